@@ -1,0 +1,166 @@
+/*
+ * ltxq.h -- C ABI of the B200 (sm_100a) quantized DiT-block hot path.
+ *
+ * Plain pointers and sizes only.  Every device pointer is caller-owned
+ * device memory; every call is asynchronous on the given CUDA stream
+ * (`stream` is a cudaStream_t passed as void*; NULL = legacy default
+ * stream).  Every entry point returns an ltxq_status; on a non-zero status
+ * ltxq_last_error() (thread-local) holds a one-line message.  There is no
+ * CPU fallback: unsupported shapes/dtypes return LTXQ_ERR_UNSUPPORTED.
+ *
+ * Reference interfaces replaced (paths inside dmlsrc/LTX-2-MLX):
+ *   ltxq_adaln_modulate  <- LTX_2_MLX/kernels/fused_ops.py:237 adaln_norm_fused
+ *                           (+ transformer.py:21-37 _adaln_inline)
+ *   ltxq_gated_add       <- LTX_2_MLX/kernels/fused_ops.py:398 gated_add_fused
+ *                           (+ transformer.py:40-50 _residual_gate_inline,
+ *                              transformer.py:387,484 text-CA gate-then-add)
+ *   ltxq_head_gate       <- LTX_2_MLX/model/transformer/attention.py:559-601
+ *   ltxq_quantize        <- mx.quantize at loader/transformer_cache.py:1255
+ *   ltxq_dequantize      <- mx.dequantize semantics of the same cache entries
+ *   ltxq_qlinear         <- nn.QuantizedLinear.__call__ /
+ *                           _PretransposedQuantizedLinear.__call__
+ *                           (loader/transformer_cache.py:177-193) with the
+ *                           block's epilogues (transformer.py:469,650,484,627)
+ *   ltxq_adaln_qlinear   <- transformer.py:458 AdaLN then attention.py:573-575
+ *                           projections (prologue-fused quantized linear)
+ *   ltxq_feed_forward    <- model/transformer/feed_forward.py:64-112
+ *                           FeedForward.__call__ + transformer.py:629-650
+ */
+#ifndef LTXQ_H
+#define LTXQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t ltxq_status;
+
+enum {
+  LTXQ_OK = 0,
+  LTXQ_ERR_INVALID = 1,     /* bad argument (null pointer, negative size, ...) */
+  LTXQ_ERR_UNSUPPORTED = 2, /* shape/dtype/mode not implemented on this path */
+  LTXQ_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  LTXQ_ERR_DEVICE = 4       /* a kernel reported a device-side error (bounded wait expired) */
+};
+
+enum { LTXQ_BF16 = 0, LTXQ_F32 = 1 };                              /* element dtypes */
+enum { LTXQ_NORM_NONE = 0, LTXQ_NORM_RMS = 1, LTXQ_NORM_LAYER = 2 }; /* prologue norm */
+enum { LTXQ_AFFINE = 0, LTXQ_MXFP8 = 1 };                           /* quantization mode */
+enum { LTXQ_LAYOUT_STD = 0, LTXQ_LAYOUT_PRETRANSPOSED = 1 };        /* packed-weight layout */
+enum {
+  LTXQ_EPI_NONE = 0,           /* out = bf16(bf16(acc) + bias)                        */
+  LTXQ_EPI_GELU = 1,           /* out = gelu_approx(bf16(bf16(acc) + bias))           */
+  LTXQ_EPI_GATED_RESIDUAL = 2, /* out = bf16(residual + gate * branch)               */
+  LTXQ_EPI_GATE_THEN_ADD = 3   /* out = bf16(residual + bf16(gate * branch))          */
+};
+enum { LTXQ_GATED_ADD = 0, LTXQ_GATE_THEN_ADD = 1 }; /* ltxq_gated_add modes */
+
+/* A quantized linear layer in the reference's MLX cache layout
+ * (loader/transformer_cache.py:1238-1267, 1436-1462).
+ *  affine:  weight uint32 [N, K*bits/32], scales/biases bf16 [N, K/gs]
+ *  mxfp8:   weight uint32 [N, K/4] (E4M3), scales uint8 E8M0 [N, K/32]
+ *  pretransposed layout: the same arrays built from W^T, i.e. weight
+ *  [K, N*bits/32] and scales [K, N/gs] (groups along N).
+ *  bias: optional bf16 [N] (the Linear bias, stored unquantized). */
+typedef struct {
+  const void* weight;
+  const void* scales;
+  const void* biases; /* affine only; NULL for mxfp8 */
+  const void* bias;   /* optional */
+  int64_t n_out;
+  int64_t k_in;
+  int32_t mode;       /* LTXQ_AFFINE / LTXQ_MXFP8 */
+  int32_t bits;       /* 4 or 8 */
+  int32_t group_size; /* 64 (affine), 32 (mxfp8) */
+  int32_t layout;     /* LTXQ_LAYOUT_STD / LTXQ_LAYOUT_PRETRANSPOSED */
+} ltxq_qweight;
+
+/* Per-channel vectors (AdaLN scale/shift/gate).  Element (row m, channel c)
+ * lives at ptr[(m / rows_per_vec) * row_stride + c] when rows_per_vec > 0,
+ * and at ptr[c] when rows_per_vec == 0 (the (B,1,C) broadcast of the
+ * reference's T2V path; rows_per_vec = T gives per-batch vectors,
+ * rows_per_vec = 1 per-token vectors). */
+typedef struct {
+  const void* ptr;
+  int32_t dtype; /* LTXQ_BF16 or LTXQ_F32 */
+  int32_t pad_;
+  int64_t rows_per_vec;
+  int64_t row_stride;
+} ltxq_vec;
+
+typedef struct {
+  int32_t kind;          /* LTXQ_EPI_* */
+  int32_t pad_;
+  ltxq_vec gate;         /* GATED_RESIDUAL / GATE_THEN_ADD */
+  const void* residual;  /* bf16 [M, N] (row stride N) for the gated kinds */
+} ltxq_epilogue;
+
+typedef struct {
+  int32_t norm; /* LTXQ_NORM_RMS / LTXQ_NORM_LAYER / LTXQ_NORM_NONE (modulate only) */
+  float eps;
+  ltxq_vec scale;
+  ltxq_vec shift;
+} ltxq_prologue;
+
+/* ---- library ---------------------------------------------------------- */
+const char* ltxq_last_error(void);
+const char* ltxq_version(void);
+/* Reads (and clears) the device-side error word written by kernels whose
+ * bounded waits expired.  Synchronizes the device.  0 = no error. */
+ltxq_status ltxq_device_error(int32_t* code_out);
+
+/* ---- bandwidth kernels ------------------------------------------------ */
+/* out[m, :] = modulate(norm(x[m, :])) for m < rows; x/out dtype x_dtype
+ * (bf16 or f32), C % 8 == 0, C <= 8192.  norm = LTXQ_NORM_NONE gives the
+ * norm-free context modulation of transformer.py:379. */
+ltxq_status ltxq_adaln_modulate(const void* x, int32_t x_dtype, int64_t rows, int64_t C,
+                                const ltxq_prologue* pro, void* out, void* stream);
+
+/* out = residual + gate * branch (mode LTXQ_GATED_ADD, one rounding) or
+ * residual + bf16(gate * branch) (LTXQ_GATE_THEN_ADD).  bf16 tensors [rows, C]. */
+ltxq_status ltxq_gated_add(const void* residual, const void* branch, const ltxq_vec* gate,
+                           int64_t rows, int64_t C, int32_t mode, void* out, void* stream);
+
+/* out[m, h*d:(h+1)*d] = o[m, ...] * (2*sigmoid(logits[m, h])), bf16. */
+ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int64_t heads,
+                           int64_t head_dim, void* out, void* stream);
+
+/* ---- quantized weights ------------------------------------------------ */
+/* Quantize a bf16 weight [N, K] into the MLX cache layout described by `w`
+ * (w->weight/scales/biases are outputs here; w->bias is ignored). */
+ltxq_status ltxq_quantize(const void* w_bf16, const ltxq_qweight* w, void* stream);
+/* Dequantize `w` to bf16 [N, K] (standard layout) or [K, N] (pretransposed). */
+ltxq_status ltxq_dequantize(const ltxq_qweight* w, void* out_bf16, void* stream);
+
+/* ---- quantized linear ------------------------------------------------- */
+/* Bytes of device workspace the calls below need for these shapes. */
+size_t ltxq_qlinear_workspace_size(int64_t M, const ltxq_qweight* w);
+size_t ltxq_adaln_qlinear_workspace_size(int64_t M, const ltxq_qweight* w);
+size_t ltxq_feed_forward_workspace_size(int64_t M, const ltxq_qweight* w_in, const ltxq_qweight* w_out);
+
+/* out[M, N] = epilogue(x[M, K] . dequant(W)^T); x, out bf16 row-major
+ * (row strides K and N). */
+ltxq_status ltxq_qlinear(const void* x, int64_t M, const ltxq_qweight* w, const ltxq_epilogue* epi,
+                         void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out = epilogue(modulate(norm(x)) . dequant(W)^T) -- the AdaLN prologue
+ * fused in front of the quantized linear. */
+ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pro,
+                               const ltxq_qweight* w, const ltxq_epilogue* epi, void* out,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* out = x + gate * project_out(gelu(project_in(modulate(norm(x))))) -- the
+ * whole FF sub-layer of transformer.py:629-668.  pro may be NULL (x is
+ * already modulated) and epi may be NULL / LTXQ_EPI_NONE (plain FF). */
+ltxq_status ltxq_feed_forward(const void* x, int64_t M, const ltxq_prologue* pro,
+                              const ltxq_qweight* w_in, const ltxq_qweight* w_out,
+                              const ltxq_epilogue* epi, void* out, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LTXQ_H */

@@ -1,0 +1,306 @@
+// elementwise.cu -- HBM-bound kernels of the block: AdaLN norm+modulate
+// (fused_ops.py:237 adaln_norm_fused / transformer.py:21-37), the gated
+// residual add (fused_ops.py:398 / transformer.py:40-50, 387) and the
+// per-head attention output gate (attention.py:559-601).
+//
+// Rounding points follow the reference composition: rms_norm/layer_norm
+// output rounded to bf16; fp32 AdaLN vectors give fp32 product and sum (no
+// FMA contraction) and one bf16 rounding; bf16 vectors round after every op.
+// Row statistics are accumulated in fp64 so that they are independent of the
+// reduction order.
+#include "common.cuh"
+
+namespace ltxq {
+
+__device__ __forceinline__ double block_sum(double v, double* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+// modulate one element: normed (bf16-exact for bf16 output) * (1+s) + t
+template <bool kVecBf16>
+__device__ __forceinline__ float modulate1(float n, float s, float t) {
+  if (kVecBf16) {
+    const float one_p = rbf16(__fadd_rn(1.0f, s));
+    return __fadd_rn(rbf16(__fmul_rn(n, one_p)), t);
+  }
+  return __fadd_rn(__fmul_rn(n, __fadd_rn(1.0f, s)), t);
+}
+
+// One CTA per row; each thread owns up to 16 consecutive channels (two
+// 16-byte chunks of bf16).  kXF32: x/out are fp32 (the reference's fp32
+// fallback keeps fp32 output without rounding).
+template <bool kXF32, bool kVecBf16>
+__global__ void __launch_bounds__(512) adaln_modulate_kernel(const void* __restrict__ x, int64_t C, int norm,
+                                                              float eps, VecArg scale, VecArg shift,
+                                                              void* __restrict__ out) {
+  __shared__ double red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t c0 = static_cast<int64_t>(threadIdx.x) * 16;
+  float v[16];
+  int nvalid = 0;
+  if (c0 < C) nvalid = (C - c0 >= 16) ? 16 : static_cast<int>(C - c0);  // 8 or 16 (C % 8 == 0)
+  if (kXF32) {
+    const float* xr = static_cast<const float*>(x) + row * C;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h * 8 < nvalid) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(xr + c0 + h * 8));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(xr + c0 + h * 8 + 4));
+        v[h * 8 + 0] = a.x; v[h * 8 + 1] = a.y; v[h * 8 + 2] = a.z; v[h * 8 + 3] = a.w;
+        v[h * 8 + 4] = b.x; v[h * 8 + 5] = b.y; v[h * 8 + 6] = b.z; v[h * 8 + 7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[h * 8 + i] = 0.f;
+      }
+    }
+  } else {
+    const uint16_t* xr = static_cast<const uint16_t*>(x) + row * C;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h * 8 < nvalid) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(xr + c0 + h * 8));
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[h * 8 + 2 * i] = lo_bf16(w[i]);
+          v[h * 8 + 2 * i + 1] = hi_bf16(w[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[h * 8 + i] = 0.f;
+      }
+    }
+  }
+
+  float mu_f = 0.f, inv = 1.f;
+  if (norm == LTXQ_NORM_RMS) {
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss += static_cast<double>(v[i]) * static_cast<double>(v[i]);
+    const double tot = block_sum(ss, red);
+    const float ms = static_cast<float>(tot / static_cast<double>(C));
+    inv = static_cast<float>(1.0 / sqrt(static_cast<double>(__fadd_rn(ms, eps))));
+  } else if (norm == LTXQ_NORM_LAYER) {
+    double s1 = 0.0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s1 += static_cast<double>(v[i]);
+    const double mu = block_sum(s1, red) / static_cast<double>(C);
+    double s2 = 0.0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < nvalid) {
+        const double d = static_cast<double>(v[i]) - mu;
+        s2 += d * d;
+      }
+    }
+    const float var = static_cast<float>(block_sum(s2, red) / static_cast<double>(C));
+    inv = static_cast<float>(1.0 / sqrt(static_cast<double>(__fadd_rn(var, eps))));
+    mu_f = static_cast<float>(mu);
+  }
+  if (nvalid == 0) return;
+
+  const char* sc = vec_row(scale, row);
+  const char* sh = vec_row(shift, row);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (h * 8 >= nvalid) break;
+    float s[8], t[8], o[8];
+    load_vec8(scale, sc, c0 + h * 8, s);
+    load_vec8(shift, sh, c0 + h * 8, t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float n = v[h * 8 + i];
+      if (norm == LTXQ_NORM_RMS) n = __fmul_rn(n, inv);
+      else if (norm == LTXQ_NORM_LAYER) n = __fmul_rn(__fsub_rn(n, mu_f), inv);
+      if (!kXF32) n = rbf16(n);
+      o[i] = modulate1<kVecBf16>(n, s[i], t[i]);
+    }
+    if (kXF32) {
+      float* orow = static_cast<float*>(out) + row * C + c0 + h * 8;
+      reinterpret_cast<float4*>(orow)[0] = make_float4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<float4*>(orow)[1] = make_float4(o[4], o[5], o[6], o[7]);
+    } else {
+      uint4 pk;
+      pk.x = pack_bf16x2(o[0], o[1]);
+      pk.y = pack_bf16x2(o[2], o[3]);
+      pk.z = pack_bf16x2(o[4], o[5]);
+      pk.w = pack_bf16x2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + row * C + c0 + h * 8) = pk;
+    }
+  }
+}
+
+// out = residual + gate * branch over bf16 [rows, C]; 8 channels per thread.
+template <bool kVecBf16, bool kTwoRound>
+__global__ void gated_add_kernel(const uint16_t* __restrict__ res, const uint16_t* __restrict__ br, VecArg gate,
+                                 int64_t rows, int64_t C, uint16_t* __restrict__ out) {
+  const int64_t chunks_per_row = C >> 3;
+  const int64_t total = rows * chunks_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / chunks_per_row;
+    const int64_t c = (i - row * chunks_per_row) << 3;
+    const uint4 r4 = __ldg(reinterpret_cast<const uint4*>(res + row * C + c));
+    const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(br + row * C + c));
+    float g[8];
+    load_vec8(gate, vec_row(gate, row), c, g);
+    const uint32_t rw[4] = {r4.x, r4.y, r4.z, r4.w};
+    const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+    uint32_t ow[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float o2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float r = h ? hi_bf16(rw[k]) : lo_bf16(rw[k]);
+        const float b = h ? hi_bf16(bw[k]) : lo_bf16(bw[k]);
+        const float p = __fmul_rn(b, g[2 * k + h]);
+        o2[h] = (kVecBf16 || kTwoRound) ? __fadd_rn(r, rbf16(p)) : __fadd_rn(p, r);
+      }
+      ow[k] = pack_bf16x2(o2[0], o2[1]);
+    }
+    *reinterpret_cast<uint4*>(out + row * C + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+}
+
+// out[m, h, :] = o[m, h, :] * bf16(2 * bf16(sigmoid(logit[m, h]))); one
+// thread per 8 channels.
+__global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ logits, int64_t rows,
+                                 int64_t heads, int64_t head_dim, uint16_t* __restrict__ out) {
+  const int64_t width = heads * head_dim;
+  const int64_t total = rows * (width >> 3);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / (width >> 3);
+    const int64_t c = (i - row * (width >> 3)) << 3;
+    const int64_t h = c / head_dim;
+    const double lg = static_cast<double>(bf16_to_f32(__ldg(logits + row * heads + h)));
+    const float sig = rbf16(static_cast<float>(1.0 / (1.0 + exp(-lg))));
+    const float g = rbf16(__fmul_rn(2.0f, sig));
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + row * width + c));
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+    uint32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r[k] = pack_bf16x2(__fmul_rn(lo_bf16(w[k]), g), __fmul_rn(hi_bf16(w[k]), g));
+    *reinterpret_cast<uint4*>(out + row * width + c) = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static ltxq_status check_vec(const ltxq_vec& v, int64_t C, const char* name) {
+  if (!v.ptr) return fail(LTXQ_ERR_INVALID, std::string(name) + " pointer is NULL");
+  if (v.dtype != LTXQ_BF16 && v.dtype != LTXQ_F32)
+    return fail(LTXQ_ERR_UNSUPPORTED, std::string(name) + " dtype must be bf16 or f32");
+  if (!aligned16(v.ptr)) return fail(LTXQ_ERR_UNSUPPORTED, std::string(name) + " must be 16-byte aligned");
+  if (v.rows_per_vec < 0) return fail(LTXQ_ERR_INVALID, std::string(name) + " rows_per_vec < 0");
+  if (v.rows_per_vec > 0) {
+    if (v.row_stride < C) return fail(LTXQ_ERR_INVALID, std::string(name) + " row_stride < C");
+    const int64_t es = v.dtype == LTXQ_F32 ? 4 : 2;
+    if ((v.row_stride * es) % 16 != 0)
+      return fail(LTXQ_ERR_UNSUPPORTED, std::string(name) + " row stride must be a multiple of 16 bytes");
+  }
+  return LTXQ_OK;
+}
+
+ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int64_t C, const ltxq_prologue& pro,
+                                  void* out, cudaStream_t stream) {
+  if (!x || !out) return fail(LTXQ_ERR_INVALID, "adaln_modulate: x/out is NULL");
+  if (rows < 0 || C <= 0) return fail(LTXQ_ERR_INVALID, "adaln_modulate: bad shape");
+  if (C % 8 != 0 || C > 8192)
+    return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: C must be a multiple of 8 and <= 8192");
+  if (x_dtype != LTXQ_BF16 && x_dtype != LTXQ_F32) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: x dtype");
+  if (pro.norm != LTXQ_NORM_NONE && pro.norm != LTXQ_NORM_RMS && pro.norm != LTXQ_NORM_LAYER)
+    return fail(LTXQ_ERR_INVALID, "adaln_modulate: unknown norm kind");
+  if (!(pro.eps >= 0.f)) return fail(LTXQ_ERR_INVALID, "adaln_modulate: eps must be >= 0");
+  if (ltxq_status st = check_vec(pro.scale, C, "scale")) return st;
+  if (ltxq_status st = check_vec(pro.shift, C, "shift")) return st;
+  if (pro.scale.dtype != pro.shift.dtype)
+    return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: scale and shift must share a dtype");
+  if (!aligned16(x) || !aligned16(out)) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: x/out not 16B aligned");
+  if (rows == 0) return LTXQ_OK;
+  if (rows > 0x7FFFFFFF) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: too many rows");
+  int threads = static_cast<int>((C + 15) / 16);
+  threads = ((threads + 31) / 32) * 32;
+  const VecArg s = to_vec(pro.scale), t = to_vec(pro.shift);
+  const bool vb = pro.scale.dtype == LTXQ_BF16;
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (x_dtype == LTXQ_F32) {
+    if (vb) adaln_modulate_kernel<true, true><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);
+    else adaln_modulate_kernel<true, false><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);
+  } else {
+    if (vb) adaln_modulate_kernel<false, true><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);
+    else adaln_modulate_kernel<false, false><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);
+  }
+  return cuda_check(cudaGetLastError(), "adaln_modulate launch");
+}
+
+ltxq_status launch_gated_add(const void* residual, const void* branch, const ltxq_vec& gate, int64_t rows,
+                             int64_t C, int mode, void* out, cudaStream_t stream) {
+  if (!residual || !branch || !out) return fail(LTXQ_ERR_INVALID, "gated_add: NULL tensor");
+  if (rows < 0 || C <= 0) return fail(LTXQ_ERR_INVALID, "gated_add: bad shape");
+  if (C % 8 != 0) return fail(LTXQ_ERR_UNSUPPORTED, "gated_add: C must be a multiple of 8");
+  if (mode != LTXQ_GATED_ADD && mode != LTXQ_GATE_THEN_ADD) return fail(LTXQ_ERR_INVALID, "gated_add: bad mode");
+  if (ltxq_status st = check_vec(gate, C, "gate")) return st;
+  if (!aligned16(residual) || !aligned16(branch) || !aligned16(out))
+    return fail(LTXQ_ERR_UNSUPPORTED, "gated_add: tensors must be 16-byte aligned");
+  if (rows == 0) return LTXQ_OK;
+  const int64_t work = rows * (C / 8);
+  const int threads = 256;
+  const int64_t want = (work + threads - 1) / threads;
+  const unsigned blocks = static_cast<unsigned>(want < num_sms() * 16 ? want : num_sms() * 16);
+  const VecArg g = to_vec(gate);
+  auto* r = static_cast<const uint16_t*>(residual);
+  auto* b = static_cast<const uint16_t*>(branch);
+  auto* o = static_cast<uint16_t*>(out);
+  const bool vb = gate.dtype == LTXQ_BF16;
+  if (vb) gated_add_kernel<true, true><<<blocks, threads, 0, stream>>>(r, b, g, rows, C, o);
+  else if (mode == LTXQ_GATE_THEN_ADD) gated_add_kernel<false, true><<<blocks, threads, 0, stream>>>(r, b, g, rows, C, o);
+  else gated_add_kernel<false, false><<<blocks, threads, 0, stream>>>(r, b, g, rows, C, o);
+  return cuda_check(cudaGetLastError(), "gated_add launch");
+}
+
+}  // namespace ltxq
+
+extern "C" {
+
+ltxq_status ltxq_adaln_modulate(const void* x, int32_t x_dtype, int64_t rows, int64_t C, const ltxq_prologue* pro,
+                                void* out, void* stream) {
+  if (!pro) return ltxq::fail(LTXQ_ERR_INVALID, "adaln_modulate: prologue is NULL");
+  return ltxq::launch_adaln_modulate(x, x_dtype, rows, C, *pro, out, static_cast<cudaStream_t>(stream));
+}
+
+ltxq_status ltxq_gated_add(const void* residual, const void* branch, const ltxq_vec* gate, int64_t rows, int64_t C,
+                           int32_t mode, void* out, void* stream) {
+  if (!gate) return ltxq::fail(LTXQ_ERR_INVALID, "gated_add: gate is NULL");
+  return ltxq::launch_gated_add(residual, branch, *gate, rows, C, mode, out, static_cast<cudaStream_t>(stream));
+}
+
+ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
+                           void* out, void* stream) {
+  if (!o || !logits || !out) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate: NULL tensor");
+  if (rows < 0 || heads <= 0 || head_dim <= 0) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate: bad shape");
+  if (head_dim % 8 != 0) return ltxq::fail(LTXQ_ERR_UNSUPPORTED, "head_gate: head_dim must be a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return ltxq::fail(LTXQ_ERR_UNSUPPORTED, "head_gate: o/out must be 16-byte aligned");
+  if (rows == 0) return LTXQ_OK;
+  const int64_t work = rows * heads * head_dim / 8;
+  const int threads = 256;
+  const int64_t want = (work + threads - 1) / threads;
+  const unsigned blocks = static_cast<unsigned>(want < ltxq::num_sms() * 16 ? want : ltxq::num_sms() * 16);
+  ltxq::head_gate_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(logits), rows, heads, head_dim,
+      static_cast<uint16_t*>(out));
+  return ltxq::cuda_check(cudaGetLastError(), "head_gate launch");
+}
+
+}  // extern "C"

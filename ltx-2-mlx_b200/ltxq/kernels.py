@@ -1,0 +1,131 @@
+"""Drop-in replacements for ``LTX_2_MLX.kernels`` (fused_ops.py).
+
+``adaln_norm_fused(x, scale, shift, eps)`` and ``gated_add_fused(residual,
+branch, gate)`` keep the reference's names, argument order and return dtype
+(fused_ops.py:237, 398).  Unlike the reference they never fall back to a
+second implementation: every supported input (bf16/fp32 ``x``, fp32/bf16
+vectors, broadcast, per-batch or per-token vectors, any eps, any C that is a
+multiple of 8) runs the CUDA kernel, and anything else raises ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DT = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
+
+
+def vec_arg(v: torch.Tensor, rows_shape: tuple[int, ...], C: int, name: str, keep: list) -> _lib.Vec:
+    """Describe a per-channel vector broadcast against activations of shape
+    ``rows_shape + (C,)``: all-singleton leading dims -> one vector for all
+    rows; (B, 1, C) -> one vector per batch entry; (B, T, C) -> per token."""
+    _require_cuda(v, name)
+    if v.dtype not in _DT:
+        raise ValueError(f"{name} dtype must be bfloat16 or float32, got {v.dtype}")
+    if v.shape[-1] != C:
+        raise ValueError(f"{name} last dim {v.shape[-1]} != {C}")
+    v = v.contiguous()
+    keep.append(v)
+    lead = tuple(v.shape[:-1])
+    numel_lead = 1
+    for d in lead:
+        numel_lead *= d
+    if numel_lead == 1:
+        return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, 0, 0)
+    rows = 1
+    for d in rows_shape:
+        rows *= d
+    if numel_lead == rows:  # (B, T, C): one vector per row
+        return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, 1, C)
+    if len(rows_shape) >= 2 and len(lead) >= 1 and lead[0] == rows_shape[0] and numel_lead == rows_shape[0]:
+        return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, rows // rows_shape[0], C)  # (B, 1, C)
+    raise ValueError(f"{name} shape {tuple(v.shape)} does not broadcast against {rows_shape + (C,)}")
+
+
+def prologue(norm: int, eps: float, scale, shift, rows_shape, C, keep) -> _lib.Prologue:
+    return _lib.Prologue(norm, float(eps), vec_arg(scale, rows_shape, C, "scale", keep),
+                         vec_arg(shift, rows_shape, C, "shift", keep))
+
+
+def adaln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
+                   norm: str = "rms") -> torch.Tensor:
+    """``bf16(norm(x) * (1 + scale) + shift)`` with norm in {"rms", "layer",
+    "none"}; "none" is the text cross-attention context modulation
+    (transformer.py:379)."""
+    _require_cuda(x, "x")
+    if x.dtype not in _DT:
+        raise ValueError(f"x dtype must be bfloat16 or float32, got {x.dtype}")
+    x = x.contiguous()
+    C = x.shape[-1]
+    rows_shape = tuple(x.shape[:-1])
+    keep: list = []
+    nk = {"rms": _lib.NORM_RMS, "layer": _lib.NORM_LAYER, "none": _lib.NORM_NONE}[norm]
+    pro = prologue(nk, eps, scale, shift, rows_shape, C, keep)
+    out = torch.empty_like(x)
+    lib = _lib.load()
+    _lib.check(lib.ltxq_adaln_modulate(x.data_ptr(), _DT[x.dtype], x.numel() // C, C, ctypes.byref(pro),
+                                       out.data_ptr(), _stream()), "adaln_modulate")
+    return out
+
+
+def adaln_norm_fused(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float) -> torch.Tensor:
+    """``(rms_norm(x) * (1 + scale) + shift).astype(x.dtype)``
+    (fused_ops.py:237 / transformer.py:21-37)."""
+    return adaln_modulate(x, scale, shift, eps, "rms")
+
+
+def gated_add_fused(residual: torch.Tensor, branch: torch.Tensor, gate: torch.Tensor,
+                    gate_then_add: bool = False) -> torch.Tensor:
+    """``(residual + branch * gate).astype(residual.dtype)``
+    (fused_ops.py:398 / transformer.py:40-50).  ``gate_then_add=True`` gives
+    the text cross-attention form ``residual + bf16(branch * gate)``
+    (transformer.py:387, 484)."""
+    _require_cuda(residual, "residual")
+    _require_cuda(branch, "branch")
+    if residual.dtype != torch.bfloat16 or branch.dtype != torch.bfloat16:
+        raise ValueError("residual and branch must be bfloat16")
+    if residual.shape != branch.shape:
+        raise ValueError(f"shape mismatch {tuple(residual.shape)} vs {tuple(branch.shape)}")
+    residual = residual.contiguous()
+    branch = branch.contiguous()
+    C = residual.shape[-1]
+    keep: list = []
+    g = vec_arg(gate, tuple(residual.shape[:-1]), C, "gate", keep)
+    out = torch.empty_like(residual)
+    mode = _lib.GATE_THEN_ADD if gate_then_add else _lib.GATED_ADD
+    _lib.check(_lib.load().ltxq_gated_add(residual.data_ptr(), branch.data_ptr(), ctypes.byref(g),
+                                          residual.numel() // C, C, mode, out.data_ptr(), _stream()),
+               "gated_add")
+    return out
+
+
+def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int) -> torch.Tensor:
+    """``out * (2 * sigmoid(gate_logits))[..., None]`` per head
+    (attention.py:559-601)."""
+    _require_cuda(out, "out")
+    _require_cuda(gate_logits, "gate_logits")
+    if out.dtype != torch.bfloat16 or gate_logits.dtype != torch.bfloat16:
+        raise ValueError("head_gate expects bfloat16 tensors")
+    out = out.contiguous()
+    gate_logits = gate_logits.contiguous()
+    width = out.shape[-1]
+    rows = out.numel() // width
+    if gate_logits.numel() != rows * heads:
+        raise ValueError("gate_logits must have one value per (row, head)")
+    res = torch.empty_like(out)
+    _lib.check(_lib.load().ltxq_head_gate(out.data_ptr(), gate_logits.data_ptr(), rows, heads, width // heads,
+                                          res.data_ptr(), _stream()), "head_gate")
+    return res

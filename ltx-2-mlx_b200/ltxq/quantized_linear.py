@@ -1,0 +1,165 @@
+"""Quantized linear layers over the reference's MLX cache layout.
+
+``QuantizedLinear`` mirrors MLX ``nn.QuantizedLinear`` as the reference uses
+it (LTX_2_MLX/loader/transformer_cache.py:1436-1462 builds the empty module,
+:1238-1267 fills ``weight``/``scales``/``biases`` from ``mx.quantize``,
+``bias`` stays bf16): the same attribute names and dtypes, the same
+``mode``/``group_size``/``bits`` semantics and defaults (:797-811), and
+``__call__(x) -> y``.  ``pretransposed=True`` gives the reference's
+``_PretransposedQuantizedLinear`` (:177-193) whose packed arrays were built
+from ``W.T``.
+
+The forward pass is one launch of the sm_100a quantized GEMM with the
+block's epilogue fused (bias, GELU, gated residual); there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from .kernels import _require_cuda, _stream, prologue, vec_arg
+
+QUANT_DEFAULTS = {"affine": (64, 4), "mxfp8": (32, 8)}
+_MODE = {"affine": _lib.AFFINE, "mxfp8": _lib.MXFP8}
+
+
+def quant_defaults(mode: str, group_size: int | None, bits: int | None) -> tuple[int, int]:
+    """``_quant_defaults`` (transformer_cache.py:797-811) for the modes this
+    path implements."""
+    if mode not in QUANT_DEFAULTS:
+        raise ValueError(f"Unsupported quantization mode: {mode}")
+    gs, b = QUANT_DEFAULTS[mode]
+    return group_size or gs, bits or b
+
+
+class QuantizedLinear:
+    def __init__(self, weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor | None = None,
+                 bias: torch.Tensor | None = None, *, group_size: int, bits: int, mode: str = "affine",
+                 pretransposed: bool = False, in_features: int | None = None, out_features: int | None = None):
+        if mode not in _MODE:
+            raise ValueError(f"Unsupported quantization mode: {mode}")
+        for t, name in ((weight, "weight"), (scales, "scales")):
+            _require_cuda(t, name)
+        self.weight = weight.contiguous()
+        self.scales = scales.contiguous()
+        self.biases = biases.contiguous() if biases is not None else None
+        self.bias = bias.contiguous() if bias is not None else None
+        self.group_size = int(group_size)
+        self.bits = int(bits)
+        self.mode = mode
+        self.pretransposed = bool(pretransposed)
+        packed_rows = self.weight.shape[0]
+        packed_len = self.weight.shape[1] * 32 // self.bits
+        if pretransposed:
+            self.in_features = in_features or packed_rows
+            self.out_features = out_features or packed_len
+        else:
+            self.out_features = out_features or packed_rows
+            self.in_features = in_features or packed_len
+        if mode == "affine" and self.biases is None:
+            raise ValueError("affine quantization needs biases")
+
+    # ------------------------------------------------------------------ build
+    @classmethod
+    def from_linear(cls, weight: torch.Tensor, bias: torch.Tensor | None = None, group_size: int | None = None,
+                    bits: int | None = None, mode: str = "affine", pretransposed: bool = False) -> "QuantizedLinear":
+        """Quantize a bf16 ``nn.Linear`` weight [out, in] on the GPU
+        (``nn.QuantizedLinear.from_linear`` / ``mx.quantize``)."""
+        _require_cuda(weight, "weight")
+        gs, b = quant_defaults(mode, group_size, bits)
+        w = weight.to(torch.bfloat16)
+        n_out, k_in = w.shape
+        src = w.t().contiguous() if pretransposed else w.contiguous()
+        rows, length = src.shape
+        packed = torch.empty((rows, length * b // 32), dtype=torch.uint32, device=w.device)
+        if mode == "affine":
+            scales = torch.empty((rows, length // gs), dtype=torch.bfloat16, device=w.device)
+            biases = torch.empty_like(scales)
+        else:
+            scales = torch.empty((rows, length // gs), dtype=torch.uint8, device=w.device)
+            biases = None
+        q = _lib.QWeight(packed.data_ptr(), scales.data_ptr(), biases.data_ptr() if biases is not None else None,
+                         None, n_out, k_in, _MODE[mode], b, gs,
+                         _lib.LAYOUT_PRETRANSPOSED if pretransposed else _lib.LAYOUT_STD)
+        _lib.check(_lib.load().ltxq_quantize(src.data_ptr(), ctypes.byref(q), _stream()), "quantize")
+        bias_bf16 = bias.to(torch.bfloat16).contiguous() if bias is not None else None
+        return cls(packed, scales, biases, bias_bf16, group_size=gs, bits=b, mode=mode,
+                   pretransposed=pretransposed, in_features=k_in, out_features=n_out)
+
+    # ------------------------------------------------------------------ views
+    def qweight(self) -> _lib.QWeight:
+        return _lib.QWeight(
+            self.weight.data_ptr(), self.scales.data_ptr(),
+            self.biases.data_ptr() if self.biases is not None else None,
+            self.bias.data_ptr() if self.bias is not None else None,
+            self.out_features, self.in_features, _MODE[self.mode], self.bits, self.group_size,
+            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD)
+
+    def dequantize(self) -> torch.Tensor:
+        """bf16 weight: [out, in] (standard) or [in, out] (pretransposed)."""
+        shape = (self.in_features, self.out_features) if self.pretransposed else (self.out_features, self.in_features)
+        out = torch.empty(shape, dtype=torch.bfloat16, device=self.weight.device)
+        q = self.qweight()
+        _lib.check(_lib.load().ltxq_dequantize(ctypes.byref(q), out.data_ptr(), _stream()), "dequantize")
+        return out
+
+    # ---------------------------------------------------------------- forward
+    def _epilogue(self, x_rows_shape, keep, gelu=False, residual=None, gate=None, gate_then_add=False):
+        epi = _lib.Epilogue()
+        if residual is not None:
+            if gate is None:
+                raise ValueError("gated epilogue needs a gate")
+            _require_cuda(residual, "residual")
+            if residual.dtype != torch.bfloat16:
+                raise ValueError("residual must be bfloat16")
+            residual = residual.contiguous()
+            keep.append(residual)
+            if residual.numel() != math.prod(x_rows_shape) * self.out_features:
+                raise ValueError("residual shape does not match the output")
+            epi.kind = _lib.EPI_GATE_THEN_ADD if gate_then_add else _lib.EPI_GATED_RESIDUAL
+            epi.gate = vec_arg(gate, x_rows_shape, self.out_features, "gate", keep)
+            epi.residual = residual.data_ptr()
+        else:
+            epi.kind = _lib.EPI_GELU if gelu else _lib.EPI_NONE
+        return epi
+
+    def __call__(self, x: torch.Tensor, *, gelu: bool = False, residual: torch.Tensor | None = None,
+                 gate: torch.Tensor | None = None, gate_then_add: bool = False,
+                 adaln: tuple | None = None) -> torch.Tensor:
+        """``y = x @ dequant(W).T + bias`` with optional fused consumers:
+        ``gelu=True`` (project_in), ``residual``/``gate`` (gated residual add),
+        and ``adaln=(scale, shift, eps[, norm])`` (the AdaLN prologue)."""
+        _require_cuda(x, "x")
+        if x.dtype != torch.bfloat16:
+            raise ValueError(f"x must be bfloat16, got {x.dtype}")
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"x last dim {x.shape[-1]} != in_features {self.in_features}")
+        x = x.contiguous()
+        rows_shape = tuple(x.shape[:-1])
+        M = x.numel() // self.in_features
+        keep: list = []
+        epi = self._epilogue(rows_shape, keep, gelu, residual, gate, gate_then_add)
+        out = torch.empty(rows_shape + (self.out_features,), dtype=torch.bfloat16, device=x.device)
+        q = self.qweight()
+        lib = _lib.load()
+        if adaln is not None:
+            scale, shift, eps = adaln[:3]
+            norm = adaln[3] if len(adaln) > 3 else "rms"
+            nk = {"rms": _lib.NORM_RMS, "layer": _lib.NORM_LAYER, "none": _lib.NORM_NONE}[norm]
+            pro = prologue(nk, eps, scale, shift, rows_shape, self.in_features, keep)
+            ws_bytes = lib.ltxq_adaln_qlinear_workspace_size(M, ctypes.byref(q))
+            ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+            _lib.check(lib.ltxq_adaln_qlinear(x.data_ptr(), M, ctypes.byref(pro), ctypes.byref(q), ctypes.byref(epi),
+                                              out.data_ptr(), ws.data_ptr(), ws_bytes, _stream()), "adaln_qlinear")
+        else:
+            _lib.check(lib.ltxq_qlinear(x.data_ptr(), M, ctypes.byref(q), ctypes.byref(epi), out.data_ptr(), None, 0,
+                                        _stream()), "qlinear")
+        return out
+
+    def __repr__(self) -> str:
+        return (f"QuantizedLinear(in={self.in_features}, out={self.out_features}, mode={self.mode}, "
+                f"bits={self.bits}, group_size={self.group_size}, pretransposed={self.pretransposed})")
