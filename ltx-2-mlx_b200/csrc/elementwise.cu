@@ -43,6 +43,7 @@ __global__ void __launch_bounds__(512) adaln_modulate_kernel(const void* __restr
                                                               float eps, VecArg scale, VecArg shift,
                                                               void* __restrict__ out) {
   __shared__ double red[32];
+  const double inv_c = 1.0 / static_cast<double>(C);
   const int64_t row = blockIdx.x;
   const int64_t c0 = static_cast<int64_t>(threadIdx.x) * 16;
   float v[16];
@@ -87,13 +88,13 @@ __global__ void __launch_bounds__(512) adaln_modulate_kernel(const void* __restr
 #pragma unroll
     for (int i = 0; i < 16; ++i) ss += static_cast<double>(v[i]) * static_cast<double>(v[i]);
     const double tot = block_sum(ss, red);
-    const float ms = static_cast<float>(tot / static_cast<double>(C));
-    inv = static_cast<float>(1.0 / sqrt(static_cast<double>(__fadd_rn(ms, eps))));
+    const float ms = static_cast<float>(tot * inv_c);
+    inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(ms, eps))));
   } else if (norm == LTXQ_NORM_LAYER) {
     double s1 = 0.0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) s1 += static_cast<double>(v[i]);
-    const double mu = block_sum(s1, red) / static_cast<double>(C);
+    const double mu = block_sum(s1, red) * inv_c;
     double s2 = 0.0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
@@ -102,8 +103,8 @@ __global__ void __launch_bounds__(512) adaln_modulate_kernel(const void* __restr
         s2 += d * d;
       }
     }
-    const float var = static_cast<float>(block_sum(s2, red) / static_cast<double>(C));
-    inv = static_cast<float>(1.0 / sqrt(static_cast<double>(__fadd_rn(var, eps))));
+    const float var = static_cast<float>(block_sum(s2, red) * inv_c);
+    inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(var, eps))));
     mu_f = static_cast<float>(mu);
   }
   if (nvalid == 0) return;
@@ -136,6 +137,141 @@ __global__ void __launch_bounds__(512) adaln_modulate_kernel(const void* __restr
       pk.w = pack_bf16x2(o[6], o[7]);
       *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + row * C + c0 + h * 8) = pk;
     }
+  }
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// kWPR warps per row for bf16 rows with C <= kWPR * 32 * 8 * kCPL: every
+// lane keeps kCPL 16-byte chunks (chunk lane + 32 * (wr + kWPR * j)) in
+// registers, so a row is read from HBM once with all loads in flight.  The
+// per-row fp64 partial sums of the kWPR warps meet in shared memory.
+// v[j] for a runtime j without dynamic register indexing (selects only)
+template <int N>
+__device__ __forceinline__ uint4 pick(const uint4 (&v)[N], int j) {
+  uint4 cur = v[0];
+#pragma unroll
+  for (int jj = 1; jj < N; ++jj)
+    if (jj == j) cur = v[jj];
+  return cur;
+}
+
+template <int kCPL, int kWPR, bool kVecBf16>
+__global__ void __launch_bounds__(256, 2) adaln_rows_kernel(const uint16_t* __restrict__ x, int64_t rows, int64_t C,
+                                                         int norm, float eps, VecArg scale, VecArg shift,
+                                                         uint16_t* __restrict__ out) {
+  __shared__ double red[8][2];
+  const double inv_c = __drcp_rn(static_cast<double>(C));
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int wr = warp % kWPR;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / kWPR) + warp / kWPR;
+  const bool live = row < rows;
+  const int nch = static_cast<int>(C >> 3);
+  const uint16_t* xr = x + (live ? row : 0) * C;
+  uint4 v[kCPL];
+#pragma unroll
+  for (int j = 0; j < kCPL; ++j) {
+    const int c = lane + 32 * (wr + kWPR * j);
+    v[j] = (live && c < nch) ? __ldg(reinterpret_cast<const uint4*>(xr) + c) : make_uint4(0, 0, 0, 0);
+  }
+  float mu_f = 0.f, inv = 1.f;
+  if (norm != LTXQ_NORM_NONE) {
+    double s1 = 0.0, s2 = 0.0;
+#pragma unroll 1
+    for (int j = 0; j < kCPL; ++j) {
+      const uint4 cur = pick(v, j);
+      const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const double a = lo_bf16(w[i]), b = hi_bf16(w[i]);
+        s1 += a + b;
+        s2 += a * a + b * b;
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (kWPR > 1) {
+      if (lane == 0) {
+        red[warp][0] = s1;
+        red[warp][1] = s2;
+      }
+      __syncthreads();
+      const int w0 = warp - wr;
+      s1 = 0.0;
+      s2 = 0.0;
+#pragma unroll
+      for (int i = 0; i < kWPR; ++i) {
+        s1 += red[w0 + i][0];
+        s2 += red[w0 + i][1];
+      }
+    }
+    if (norm == LTXQ_NORM_RMS) {
+      const float ms = static_cast<float>(s2 * inv_c);
+      inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(ms, eps))));
+    } else {
+      const double mu = s1 * inv_c;
+      double d2 = 0.0;
+#pragma unroll 1
+      for (int j = 0; j < kCPL; ++j) {
+        if (lane + 32 * (wr + kWPR * j) < nch) {
+          const uint4 cur = pick(v, j);
+          const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const double a = lo_bf16(w[i]) - mu, b = hi_bf16(w[i]) - mu;
+            d2 += a * a + b * b;
+          }
+        }
+      }
+      d2 = warp_sum(d2);
+      if (kWPR > 1) {
+        __syncthreads();
+        if (lane == 0) red[warp][0] = d2;
+        __syncthreads();
+        const int w0 = warp - wr;
+        d2 = 0.0;
+#pragma unroll
+        for (int i = 0; i < kWPR; ++i) d2 += red[w0 + i][0];
+      }
+      const float var = static_cast<float>(d2 * inv_c);
+      inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(var, eps))));
+      mu_f = static_cast<float>(mu);
+    }
+  }
+  if (!live) return;
+  const char* sc = vec_row(scale, row);
+  const char* sh = vec_row(shift, row);
+  uint16_t* orow = out + row * C;
+  // not unrolled, so that the vector loads of one chunk are not hoisted over
+  // the whole row (register pressure); the chunk is picked with selects
+#pragma unroll 1
+  for (int j = 0; j < kCPL; ++j) {
+    const int c = lane + 32 * (wr + kWPR * j);
+    if (c >= nch) break;
+    const uint4 cur = pick(v, j);
+    float s8[8], t8[8];
+    load_vec8(scale, sc, static_cast<int64_t>(c) * 8, s8);
+    load_vec8(shift, sh, static_cast<int64_t>(c) * 8, t8);
+    const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float e[2] = {lo_bf16(w[i]), hi_bf16(w[i])};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float n = e[h];
+        if (norm == LTXQ_NORM_RMS) n = rbf16(__fmul_rn(n, inv));
+        else if (norm == LTXQ_NORM_LAYER) n = rbf16(__fmul_rn(__fsub_rn(n, mu_f), inv));
+        e[h] = modulate1<kVecBf16>(n, s8[2 * i + h], t8[2 * i + h]);
+      }
+      o[i] = pack_bf16x2(e[0], e[1]);
+    }
+    reinterpret_cast<uint4*>(orow)[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -229,10 +365,25 @@ ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int6
   if (!aligned16(x) || !aligned16(out)) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: x/out not 16B aligned");
   if (rows == 0) return LTXQ_OK;
   if (rows > 0x7FFFFFFF) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: too many rows");
-  int threads = static_cast<int>((C + 15) / 16);
-  threads = ((threads + 31) / 32) * 32;
   const VecArg s = to_vec(pro.scale), t = to_vec(pro.shift);
   const bool vb = pro.scale.dtype == LTXQ_BF16;
+  if (x_dtype == LTXQ_BF16 && C <= 4096) {
+    auto* xb = static_cast<const uint16_t*>(x);
+    auto* ob = static_cast<uint16_t*>(out);
+#define LTXQ_ROWS(CPL, WPR)                                                                              \
+  do {                                                                                                    \
+    const unsigned blocks = static_cast<unsigned>((rows + (8 / WPR) - 1) / (8 / WPR));                    \
+    if (vb) adaln_rows_kernel<CPL, WPR, true><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob); \
+    else adaln_rows_kernel<CPL, WPR, false><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob);   \
+  } while (0)
+    if (C <= 1024) LTXQ_ROWS(4, 1);
+    else if (C <= 2048) LTXQ_ROWS(8, 1);
+    else LTXQ_ROWS(8, 2);
+#undef LTXQ_ROWS
+    return cuda_check(cudaGetLastError(), "adaln_modulate launch");
+  }
+  int threads = static_cast<int>((C + 15) / 16);
+  threads = ((threads + 31) / 32) * 32;
   const dim3 grid(static_cast<unsigned>(rows));
   if (x_dtype == LTXQ_F32) {
     if (vb) adaln_modulate_kernel<true, true><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);

@@ -39,36 +39,21 @@ namespace gemm {
 
 constexpr int BM = 128;  // output features per CTA (MMA M, TMEM lanes)
 constexpr int BK = 64;   // K per pipeline stage
-constexpr int kTmaWarp = 4, kMmaWarp = 5, kThreads = 192;
-constexpr int kAStages = 4;  // TMEM A-operand ring
+constexpr int kDeqWarps = 8;  // two per TMEM lane quarter; each converts one 32-wide half of a stage
+constexpr int kTmaWarp = 8, kMmaWarp = 9, kThreads = 320;
 constexpr int kStagePitch = 136;  // epilogue staging row pitch in bf16 (128 + 8 pad)
+constexpr int kPrefetch = 4;      // scale/bias register prefetch distance (stages)
 
 enum QKind { kAffine8 = 0, kAffine4 = 1, kMxfp8 = 2 };
 
 template <int QK>
 struct QTraits {
   static constexpr int kWBytes = QK == kAffine4 ? 32 : 64;  // packed bytes per row per stage
-  static constexpr CUtensorMapSwizzle kSwizzle =
-      QK == kAffine4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
-};
-
-template <int QK, int BN>
-struct Cfg {
-  static constexpr int kXStage = BN * BK * 2;
-  static constexpr int kWStage = BM * QTraits<QK>::kWBytes;
-  static constexpr int kBudget = 200 * 1024;
-  static constexpr int kStagesRaw = kBudget / (kXStage + kWStage);
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kBarOff = kStages * (kXStage + kWStage);
-  static constexpr int kSmem = 1024 + kBarOff + 256;
-  static constexpr uint32_t kTmemCols = (BN + kAStages * 32) <= 256 ? 256 : 512;
-  static constexpr uint32_t kACol = BN;  // A-operand stages follow the accumulator
-  static_assert(kStages >= 2, "pipeline needs at least two stages");
-  static_assert(BN + kAStages * 32 <= 512, "TMEM budget");
 };
 
 struct Params {
   int M, N, K, gs;
+  int vec_groups;  // group parameters of a row are 16-byte aligned blocks (see GroupCursor)
   const void* scales;
   const uint16_t* biases;
   const uint16_t* bias;
@@ -99,27 +84,327 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// 16-byte blocks of a row's group parameters (8 bf16 scales / biases for
+// affine, 16 E8M0 bytes for mxfp8) held in registers, with the next block
+// prefetched one block ahead: one vector load per 4..16 stages instead of two
+// scattered 2-byte loads per stage.
+template <int QK>
+struct GroupCursor {
+  static constexpr int kPerBlk = QK == kMxfp8 ? 16 : 8;
+  const uint4* sb;
+  const uint4* bb;
+  int nblk, cur;
+  uint4 cs, cb, ns, nb;
+  __device__ __forceinline__ void init(const Params& p, int64_t srow, bool ok) {
+    const int gpr = QK == kMxfp8 ? p.K / 32 : p.K / p.gs;
+    nblk = ok ? gpr / kPerBlk : 0;
+    sb = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.scales) + srow * (QK == kMxfp8 ? 1 : 2));
+    bb = QK == kMxfp8 ? nullptr : reinterpret_cast<const uint4*>(p.biases + srow);
+    cur = 0;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    cs = nblk > 0 ? __ldg(sb) : z;
+    cb = (QK != kMxfp8 && nblk > 0) ? __ldg(bb) : z;
+    ns = nblk > 1 ? __ldg(sb + 1) : z;
+    nb = (QK != kMxfp8 && nblk > 1) ? __ldg(bb + 1) : z;
+  }
+  // parameters of group g (monotone, advancing by at most one block per call)
+  __device__ __forceinline__ void get(int g, uint32_t& s, uint32_t& b) {
+    const int blk = g / kPerBlk;
+    if (blk != cur && nblk > 0) {
+      cs = ns;
+      cb = nb;
+      cur = blk;
+      if (blk + 1 < nblk) {
+        ns = __ldg(sb + blk + 1);
+        if (QK != kMxfp8) nb = __ldg(bb + blk + 1);
+      }
+    }
+    const int e = g - blk * kPerBlk;
+    if (QK == kMxfp8) {
+      const int wi = e >> 2;
+      const uint32_t w = wi == 0 ? cs.x : wi == 1 ? cs.y : wi == 2 ? cs.z : cs.w;
+      s = (w >> (8 * (e & 3))) & 0xFFu;
+      b = 0u;
+    } else {
+      const int wi = e >> 1;
+      const uint32_t ws_ = wi == 0 ? cs.x : wi == 1 ? cs.y : wi == 2 ? cs.z : cs.w;
+      const uint32_t wb_ = wi == 0 ? cb.x : wi == 1 ? cb.y : wi == 2 ? cb.z : cb.w;
+      const int sh = 16 * (e & 1);
+      s = bcast_bf16x2(ws_ >> sh);
+      b = bcast_bf16x2(wb_ >> sh);
+    }
+  }
+};
+
+// Group parameters of (row n, K-half starting at element k) as the packed
+// form the converters take: affine -> bf16x2 broadcast scale / bias;
+// mxfp8 -> E8M0 byte in `s`.
+template <int QK>
+__device__ __forceinline__ void load_group(const Params& p, int64_t row_off_scales, int k, bool ok, uint32_t& s,
+                                           uint32_t& b) {
+  if (!ok) {
+    s = 0u;
+    b = 0u;
+    return;
+  }
+  if (QK == kMxfp8) {
+    s = __ldg(static_cast<const uint8_t*>(p.scales) + row_off_scales + (k >> 5));
+    b = 0u;
+  } else {
+    const int g = k / p.gs;
+    s = bcast_bf16x2(__ldg(static_cast<const uint16_t*>(p.scales) + row_off_scales + g));
+    b = bcast_bf16x2(__ldg(p.biases + row_off_scales + g));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory / barrier plan of one CTA.  BNC = tokens whose activation
+// rows this CTA stages (the MMA's N in single-CTA mode; half of it in pair
+// mode).  BN = MMA N = accumulator columns.
+template <int QK, int BN, int BNC>
+struct Plan {
+  static constexpr int kXStage = BNC * BK * 2;
+  static constexpr int kWStage = BM * QTraits<QK>::kWBytes;
+  static constexpr int kStagingBytes = 2 * 32 * kStagePitch * 2;  // two epilogue staging tiles
+  static constexpr int kBudget = 200 * 1024;
+  static constexpr int kStagesRaw = kBudget / (kXStage + kWStage);
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kBarOff = kStages * (kXStage + kWStage);
+  static constexpr int kSmem = 1024 + kBarOff + 512;
+  // TMEM: fp32 accumulator (BN columns) followed by the bf16 A-operand ring
+  // (32 columns per 64-wide K stage).
+  static constexpr uint32_t kTmemCols = BN >= 256 ? 512 : 256;
+  static constexpr int kAStages =
+      (static_cast<int>(kTmemCols) - BN) / 32 > 8 ? 8 : (static_cast<int>(kTmemCols) - BN) / 32;
+  static constexpr uint32_t kACol = BN;
+  static_assert(kStages >= 2, "pipeline needs at least two stages");
+  static_assert(kAStages >= 2, "TMEM A ring needs two stages");
+  static_assert(kStagingBytes <= kStages * kXStage, "epilogue staging reuses the drained activation stages");
+};
+
+struct Bars {
+  uint64_t *x_full, *x_empty, *w_full, *w_empty, *a_full, *a_empty, *acc_full, *acc_empty;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+};
+
+template <int S, int AS>
+__device__ __forceinline__ Bars carve_bars(uint8_t* base) {
+  uint64_t* b = reinterpret_cast<uint64_t*>(base);
+  Bars r;
+  r.x_full = b;
+  r.x_empty = b + S;
+  r.w_full = b + 2 * S;
+  r.w_empty = b + 3 * S;
+  r.a_full = b + 4 * S;
+  r.a_empty = b + 4 * S + AS;
+  r.acc_full = b + 4 * S + 2 * AS;
+  r.acc_empty = b + 4 * S + 2 * AS + 1;
+  r.tmem_slot = reinterpret_cast<uint32_t*>(r.acc_empty + 1);
+  r.abort_flag = reinterpret_cast<volatile int*>(r.tmem_slot + 1);
+  return r;
+}
+
+// Dequant warps (warp 0..7): convert this CTA's 128 packed weight rows stage
+// by stage into the TMEM A ring.  `a_full_remote` != 0 means the A-full
+// barriers live in the pair leader (cluster address of a_full[0]).
+template <int QK, int S, int AS, uint32_t kACol>
+__device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, uint8_t* ws, uint32_t tmem, int warp,
+                                             int lane, int n0, int num_kb, uint32_t a_full_remote, int kb_base) {
+  constexpr int WB = QTraits<QK>::kWBytes;
+  constexpr int kWStage = BM * WB;
+  const int q = warp & 3;      // TMEM lane quarter
+  const int half = warp >> 2;  // which 32-wide half of every K stage
+  const int r = q * 32 + lane; // feature row within the tile == TMEM lane
+  const int n = n0 + r;
+  const bool row_ok = n < p.N;
+  const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+  const int64_t srow = static_cast<int64_t>(n) * (QK == kMxfp8 ? p.K / 32 : p.K / p.gs);
+  // group parameters of stage kb live in qs/qb[kb % kPrefetch]; the K loop
+  // is unrolled by kPrefetch so every register is read kPrefetch stages
+  // after its load was issued (no register moves that would wait on it)
+  const bool vec = p.vec_groups != 0;
+  GroupCursor<QK> gc;
+  if (vec) gc.init(p, srow, row_ok);
+  uint32_t qs[kPrefetch], qb[kPrefetch];
+#pragma unroll
+  for (int i = 0; i < kPrefetch; ++i)
+    load_group<QK>(p, srow, i * BK + half * 32, !vec && row_ok && i < num_kb, qs[i], qb[i]);
+  auto publish = [&](int as_done) {
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (a_full_remote) mbar_arrive_cluster(a_full_remote + 8u * static_cast<uint32_t>(as_done));
+      else mbar_arrive(&bb.a_full[as_done]);
+    }
+  };
+  // the TMEM store of stage kb is completed (wait::st) and published
+  // (a_full) only after stage kb+1 has been converted, hiding its latency
+  int pend_as = -1;
+  bool ok = true;
+  for (int kb0 = 0; kb0 < num_kb && ok; kb0 += kPrefetch) {
+#pragma unroll
+    for (int i = 0; i < kPrefetch; ++i) {
+      const int kb = kb0 + i;
+      if (kb >= num_kb) break;
+      const int g = kb_base + kb;  // position in the smem / TMEM rings
+      const int s = g % S;
+      const uint32_t ph = (g / S) & 1;
+      const int as = g % AS;
+      const uint32_t aph = (g / AS) & 1;
+      uint32_t s_cur = qs[i], b_cur = qb[i];
+      if (vec) {
+        const int k = kb * BK + half * 32;
+        gc.get(QK == kMxfp8 ? (k >> 5) : k / p.gs, s_cur, b_cur);
+        if (!row_ok) {
+          s_cur = 0u;
+          b_cur = 0u;
+        }
+      }
+      if (!mbar_wait(&bb.w_full[s], ph, bb.abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* wrow = ws + s * kWStage + r * WB;
+      uint32_t o[16];
+      if (QK == kAffine4) {
+        // 32-byte rows, 32B swizzle: 16-byte chunk c sits at c ^ ((r >> 2) & 1);
+        // this warp's half is chunk `half`
+        const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((half ^ ((r >> 2) & 1)) << 4));
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int w4 = 0; w4 < 4; ++w4) {
+          uint32_t q4[4];
+          deq_affine4_word(wv[w4], s_cur, b_cur, q4);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) o[w4 * 4 + t] = q4[t];
+        }
+      } else {
+        // 64-byte rows, 64B swizzle: 16-byte chunk c sits at c ^ ((r >> 1) & 3);
+        // this warp's half is chunks 2*half, 2*half+1
+        const float fsc = QK == kMxfp8 ? e8m0_to_f32(s_cur) : 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
+          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ ((r >> 1) & 3)) << 4));
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            if (QK == kMxfp8) deq_mxfp8_word(wv[w4], fsc, o[cc * 8 + w4 * 2], o[cc * 8 + w4 * 2 + 1]);
+            else deq_affine8_word(wv[w4], s_cur, b_cur, o[cc * 8 + w4 * 2], o[cc * 8 + w4 * 2 + 1]);
+          }
+        }
+      }
+      if (!row_ok) {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) o[t] = 0u;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bb.w_empty[s]);  // packed bytes consumed
+      if (pend_as >= 0) publish(pend_as);
+      pend_as = -1;
+      if (!mbar_wait(&bb.a_empty[as], aph ^ 1, bb.abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      tmem_st_32x32b_x16(tmem + t_lane + kACol + as * 32 + half * 16, o);
+      pend_as = as;
+      // issued late so that no arrive (release) of this stage waits for it
+      if (!vec)
+        load_group<QK>(p, srow, (kb + kPrefetch) * BK + half * 32, row_ok && kb + kPrefetch < num_kb, qs[i], qb[i]);
+    }
+  }
+  if (pend_as >= 0) publish(pend_as);
+}
+
+// Epilogue (warps 0..7): drain this CTA's 128 x BN accumulator, apply the
+// reference's bias / GELU rounding points, transpose through shared memory
+// (warps of `half` h take 32-token chunks c = h, h+2, ...) and write 16-byte
+// coalesced rows with the gated residual fused in.
+template <int BN>
+__device__ __forceinline__ void epilogue(const Params& p, uint8_t* staging, uint32_t tmem, int warp, int lane, int n0,
+                                         int m0) {
+  const int q = warp & 3;
+  const int half = warp >> 2;
+  const int r = q * 32 + lane;
+  const int n = n0 + r;
+  const bool row_ok = n < p.N;
+  const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+  uint16_t* stg = reinterpret_cast<uint16_t*>(staging) + half * 32 * kStagePitch;
+  const int tid = q * 32 + lane;  // 0..127 within the group
+  const float bias_n = (p.bias != nullptr && row_ok) ? bf16_to_f32(__ldg(p.bias + n)) : 0.f;
+  const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
+  const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+  for (int c = half; c < BN / 32; c += 2) {
+    if (m0 + c * 32 >= p.M) break;  // uniform across the group
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float a = rbf16(__uint_as_float(v[j]));
+      if (p.bias != nullptr) a = rbf16(__fadd_rn(a, bias_n));
+      if (p.epi == LTXQ_EPI_GELU) a = gelu_ref(a);
+      stg[j * kStagePitch + r] = f32_to_bf16(a);
+    }
+    named_bar_sync(1 + half, 128);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qq = i * 128 + tid;
+      const int j = qq >> 4, f = (qq & 15) * 8;
+      const int m = m0 + c * 32 + j, nf = n0 + f;
+      if (m < p.M && nf < p.N) {
+        uint4 bw = *reinterpret_cast<const uint4*>(stg + j * kStagePitch + f);
+        const int64_t off = static_cast<int64_t>(m) * p.N + nf;
+        if (gated) {
+          const uint4 rv = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
+          float g[8];
+          load_vec8(p.gate, vec_row(p.gate, m), nf, g);
+          const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+          uint32_t bwv[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float p0 = __fmul_rn(lo_bf16(bwv[k]), g[2 * k]);
+            const float p1 = __fmul_rn(hi_bf16(bwv[k]), g[2 * k + 1]);
+            const float r0 = lo_bf16(rw[k]), r1 = hi_bf16(rw[k]);
+            bwv[k] = two_round ? pack_bf16x2(__fadd_rn(r0, rbf16(p0)), __fadd_rn(r1, rbf16(p1)))
+                               : pack_bf16x2(__fadd_rn(p0, r0), __fadd_rn(p1, r1));
+          }
+          bw = make_uint4(bwv[0], bwv[1], bwv[2], bwv[3]);
+        }
+        *reinterpret_cast<uint4*>(p.out + off) = bw;
+      }
+    }
+    named_bar_sync(1 + half, 128);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Single-CTA kernel: 128 features x BN tokens per CTA (used for small token
+// counts, BN in {64, 128}).
 template <int QK, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                  const Params p) {
-  using C = Cfg<QK, BN>;
-  constexpr int S = C::kStages;
+  using P = Plan<QK, BN, BN>;
+  constexpr int S = P::kStages;
+  constexpr int AS = P::kAStages;
   constexpr int WB = QTraits<QK>::kWBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = smem;
-  uint8_t* ws = smem + S * C::kXStage;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-  uint64_t* x_full = bars;
-  uint64_t* x_empty = bars + S;
-  uint64_t* w_full = bars + 2 * S;
-  uint64_t* w_empty = bars + 3 * S;
-  uint64_t* a_full = bars + 4 * S;
-  uint64_t* a_empty = bars + 4 * S + kAStages;
-  uint64_t* acc_full = bars + 4 * S + 2 * kAStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* ws = smem + S * P::kXStage;
+  const Bars bb = carve_bars<S, AS>(smem + P::kBarOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -129,27 +414,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&x_full[s], 1);
-      mbar_init(&x_empty[s], 1);
-      mbar_init(&w_full[s], 1);
-      mbar_init(&w_empty[s], 4);
+      mbar_init(&bb.x_full[s], 1);
+      mbar_init(&bb.x_empty[s], 1);
+      mbar_init(&bb.w_full[s], 1);
+      mbar_init(&bb.w_empty[s], kDeqWarps);
     }
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], 4);
-      mbar_init(&a_empty[s], 1);
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&bb.a_full[s], kDeqWarps);
+      mbar_init(&bb.a_empty[s], 1);
     }
-    mbar_init(acc_full, 1);
-    *abort_flag = 0;
+    mbar_init(bb.acc_full, 1);
+    *bb.abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(bb.tmem_slot, P::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *bb.tmem_slot;
 
   if (warp == kTmaWarp) {
     if (lane == 0) {
@@ -159,24 +444,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < num_kb; ++kb) {
         const int s = kb % S;
         const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&x_empty[s], ph ^ 1, abort_flag, p.err)) break;
-        mbar_arrive_expect_tx(&x_full[s], C::kXStage);
-        tma_load_2d(xs + s * C::kXStage, &tmap_x, &x_full[s], kb * BK, m0);
-        if (!mbar_wait(&w_empty[s], ph ^ 1, abort_flag, p.err)) {
-          issued = kb + 1;
+        if (!mbar_wait(&bb.w_empty[s], ph ^ 1, bb.abort_flag, p.err)) break;
+        mbar_arrive_expect_tx(&bb.w_full[s], P::kWStage);
+        tma_load_2d(ws + s * P::kWStage, &tmap_w, &bb.w_full[s], kb * WB, n0);
+        if (!mbar_wait(&bb.x_empty[s], ph ^ 1, bb.abort_flag, p.err)) {
+          issued = kb;  // the weight copy of stage kb is in flight
           break;
         }
-        mbar_arrive_expect_tx(&w_full[s], C::kWStage);
-        tma_load_2d(ws + s * C::kWStage, &tmap_w, &w_full[s], kb * WB, n0);
+        mbar_arrive_expect_tx(&bb.x_full[s], P::kXStage);
+        tma_load_2d(xs + s * P::kXStage, &tmap_x, &bb.x_full[s], kb * BK, m0);
         issued = kb + 1;
       }
-      if (*abort_flag) {
+      if (*bb.abort_flag) {
         // let the copies already issued land before the CTA's smem is released
         int dummy_abort = 0;
         for (int kb = issued - 1; kb >= 0 && kb >= issued - S; --kb) {
           const int s = kb % S;
           const uint32_t ph = (kb / S) & 1;
-          mbar_wait(&x_full[s], ph, reinterpret_cast<volatile int*>(&dummy_abort), p.err);
+          mbar_wait(&bb.x_full[s], ph, reinterpret_cast<volatile int*>(&dummy_abort), p.err);
+          mbar_wait(&bb.w_full[s], ph, reinterpret_cast<volatile int*>(&dummy_abort), p.err);
         }
       }
     }
@@ -186,145 +472,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < num_kb; ++kb) {
         const int s = kb % S;
         const uint32_t ph = (kb / S) & 1;
-        const int as = kb % kAStages;
-        const uint32_t aph = (kb / kAStages) & 1;
-        if (!mbar_wait(&x_full[s], ph, abort_flag, p.err)) break;
-        if (!mbar_wait(&a_full[as], aph, abort_flag, p.err)) break;
+        const int as = kb % AS;
+        const uint32_t aph = (kb / AS) & 1;
+        if (!mbar_wait(&bb.a_full[as], aph, bb.abort_flag, p.err)) break;
+        if (!mbar_wait(&bb.x_full[s], ph, bb.abort_flag, p.err)) break;
         tc_fence_after();
-        const uint32_t xaddr = smem_u32(xs + s * C::kXStage);
+        const uint32_t xaddr = smem_u32(xs + s * P::kXStage);
 #pragma unroll
         for (int j = 0; j < BK / 16; ++j) {
           const uint64_t bdesc = smem_desc_sw128(xaddr + j * 32);
-          mma_bf16_ts(tmem, tmem + C::kACol + as * 32 + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+          mma_bf16_ts(tmem, tmem + P::kACol + as * 32 + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
         }
-        mma_commit(&x_empty[s]);
-        mma_commit(&a_empty[as]);
+        mma_commit(&bb.x_empty[s]);
+        mma_commit(&bb.a_empty[as]);
       }
-      mma_commit(acc_full);  // also drains in-flight MMAs on the abort path
-      if (*abort_flag) {
+      mma_commit(bb.acc_full);  // also drains in-flight MMAs on the abort path
+      if (*bb.abort_flag) {
         int dummy_abort = 0;
-        mbar_wait(acc_full, 0, reinterpret_cast<volatile int*>(&dummy_abort), p.err);
+        mbar_wait(bb.acc_full, 0, reinterpret_cast<volatile int*>(&dummy_abort), p.err);
       }
     }
   } else {
-    // ------------------------------------------------ dequant warps 0..3
-    const int r = warp * 32 + lane;  // feature row within the tile == TMEM lane
-    const int n = n0 + r;
-    const bool row_ok = n < p.N;
-    const uint32_t t_lane = static_cast<uint32_t>(warp * 32) << 16;
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % S;
-      const uint32_t ph = (kb / S) & 1;
-      const int as = kb % kAStages;
-      const uint32_t aph = (kb / kAStages) & 1;
-      // group parameters of this row for the two 32-wide halves of the stage
-      uint32_t s2[2] = {0u, 0u}, b2[2] = {0u, 0u};
-      float fs[2] = {0.f, 0.f};
-      if (row_ok) {
-        if (QK == kMxfp8) {
-          const uint8_t* sc = static_cast<const uint8_t*>(p.scales) + static_cast<int64_t>(n) * (p.K / 32) + kb * 2;
-          fs[0] = e8m0_to_f32(__ldg(sc));
-          fs[1] = e8m0_to_f32(__ldg(sc + 1));
-        } else {
-          const int gpr = p.K / p.gs;
-          const uint16_t* sc = static_cast<const uint16_t*>(p.scales) + static_cast<int64_t>(n) * gpr;
-          const uint16_t* bi = p.biases + static_cast<int64_t>(n) * gpr;
-          const int g0 = (kb * BK) / p.gs, g1 = (kb * BK + 32) / p.gs;
-          s2[0] = bcast_bf16x2(__ldg(sc + g0));
-          b2[0] = bcast_bf16x2(__ldg(bi + g0));
-          s2[1] = bcast_bf16x2(__ldg(sc + g1));
-          b2[1] = bcast_bf16x2(__ldg(bi + g1));
-        }
-      }
-      if (!mbar_wait(&w_full[s], ph, abort_flag, p.err)) break;
-      if (!mbar_wait(&a_empty[as], aph ^ 1, abort_flag, p.err)) break;
-      const uint8_t* wrow = ws + s * C::kWStage + r * WB;
-      uint32_t o[32];
-      if (QK == kAffine4) {
-        // 32-byte rows, 32B swizzle: 16-byte chunk c sits at c ^ ((r >> 2) & 1)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ ((r >> 2) & 1)) << 4));
-          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t q4[4];
-            deq_affine4_word(wv[i], s2[c], b2[c], q4);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) o[c * 16 + i * 4 + t] = q4[t];
-          }
-        }
-      } else {
-        // 64-byte rows, 64B swizzle: 16-byte chunk c sits at c ^ ((r >> 1) & 3)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 v = *reinterpret_cast<const uint4*>(wrow + ((c ^ ((r >> 1) & 3)) << 4));
-          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if (QK == kMxfp8) deq_mxfp8_word(wv[i], fs[c >> 1], o[c * 8 + i * 2], o[c * 8 + i * 2 + 1]);
-            else deq_affine8_word(wv[i], s2[c >> 1], b2[c >> 1], o[c * 8 + i * 2], o[c * 8 + i * 2 + 1]);
-          }
-        }
-      }
-      tmem_st_32x32b_x32(tmem + t_lane + C::kACol + as * 32, o);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[as]);
-        mbar_arrive(&w_empty[s]);
-      }
-    }
-
-    // ------------------------------------------------ epilogue
-    if (!*abort_flag && mbar_wait(acc_full, 0, abort_flag, p.err)) {
+    dequant_loop<QK, S, AS, P::kACol>(p, bb, ws, tmem, warp, lane, n0, num_kb, 0u, 0);
+    if (!*bb.abort_flag && mbar_wait(bb.acc_full, 0, bb.abort_flag, p.err)) {
       tc_fence_after();
-      uint16_t* stg = reinterpret_cast<uint16_t*>(xs);  // all stages are drained by now
-      const float bias_n = (p.bias != nullptr && row_ok) ? bf16_to_f32(__ldg(p.bias + n)) : 0.f;
-      const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
-      const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float a = rbf16(__uint_as_float(v[j]));
-          if (p.bias != nullptr) a = rbf16(__fadd_rn(a, bias_n));
-          if (p.epi == LTXQ_EPI_GELU) a = gelu_ref(a);
-          stg[j * kStagePitch + r] = f32_to_bf16(a);
-        }
-        named_bar_sync(1, 128);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int q = i * 128 + static_cast<int>(threadIdx.x);
-          const int j = q >> 4, f = (q & 15) * 8;
-          const int m = m0 + c * 32 + j, nf = n0 + f;
-          if (m < p.M && nf < p.N) {
-            uint4 bw = *reinterpret_cast<const uint4*>(stg + j * kStagePitch + f);
-            const int64_t off = static_cast<int64_t>(m) * p.N + nf;
-            if (gated) {
-              const uint4 rv = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
-              float g[8];
-              load_vec8(p.gate, vec_row(p.gate, m), nf, g);
-              const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-              uint32_t bwv[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const float p0 = __fmul_rn(lo_bf16(bwv[k]), g[2 * k]);
-                const float p1 = __fmul_rn(hi_bf16(bwv[k]), g[2 * k + 1]);
-                const float r0 = lo_bf16(rw[k]), r1 = hi_bf16(rw[k]);
-                bwv[k] = two_round ? pack_bf16x2(__fadd_rn(r0, rbf16(p0)), __fadd_rn(r1, rbf16(p1)))
-                                   : pack_bf16x2(__fadd_rn(p0, r0), __fadd_rn(p1, r1));
-              }
-              bw = make_uint4(bwv[0], bwv[1], bwv[2], bwv[3]);
-            }
-            *reinterpret_cast<uint4*>(p.out + off) = bw;
-          }
-        }
-        named_bar_sync(1, 128);
-      }
+      epilogue<BN>(p, xs, tmem, warp, lane, n0, m0);
     }
   }
 
@@ -332,20 +504,313 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    tmem_dealloc(tmem, P::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent CTA-pair kernel (cluster of 2, tcgen05 cta_group::2).  Each
+// cluster walks the output tiles (256 features x 256 tokens) in a static
+// round robin.  Per tile, CTA r of the pair dequantizes feature rows
+// [n0 + 128 r, +128) into its own TMEM and stages activation rows
+// [m0 + 128 r, +128) in its own smem, so each SM streams half of the
+// activation tile; the leader (rank 0) issues one M=256 x N=256 MMA per K
+// step and collects both CTAs' readiness on its barriers; tcgen05.commit
+// multicasts stage releases and accumulator readiness to both CTAs.
+//
+// Four epilogue warps per CTA drain the 128 x 256 fp32 accumulator into a
+// bf16 shared-memory tile (the reference's first rounding point), hand TMEM
+// back to the MMA through the leader's acc_empty barrier, and only then apply
+// bias / GELU / gated residual and store -- overlapped with the next tile's
+// main loop.  The smem and TMEM rings continue across tiles.
+constexpr int kEpiWarp0 = 10, kPairThreads = 448;  // warps 10..13: epilogue
+
+template <int QK>
+struct PairPlan {
+  static constexpr int BN = 256;
+  static constexpr int kXStage = (BN / 2) * BK * 2;  // this CTA's half of the activation tile
+  static constexpr int kWStage = BM * QTraits<QK>::kWBytes;
+  static constexpr int kEpiBytes = BN * BM * 2;      // bf16 [256 tokens][128 features]
+  static constexpr int kBudget = 224 * 1024 - kEpiBytes - 2048;
+  static constexpr int kStagesRaw = kBudget / (kXStage + kWStage);
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kEpiOff = kStages * (kXStage + kWStage);
+  static constexpr int kBarOff = kEpiOff + kEpiBytes;
+  static constexpr int kSmem = 1024 + kBarOff + 512;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kAStages = 8;
+  static constexpr uint32_t kACol = BN;
+  static_assert(kStages >= 4, "pipeline depth");
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
+};
+
+// Epilogue math for one CTA's tile from the bf16 staging tile (token-major,
+// 128 features per token row): 128 threads, thread t owns the 8-feature
+// column chunk (t & 15) and token rows (t >> 4) + 8 i.
+__device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const uint16_t* stg, int tid, int n0, int m0) {
+  const int f = (tid & 15) * 8;
+  const int nf = n0 + f;
+  if (nf >= p.N) return;
+  const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
+  const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+  float bias8[8];
+  if (p.bias != nullptr) {
+    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + nf));
+    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      bias8[2 * k] = lo_bf16(bw[k]);
+      bias8[2 * k + 1] = hi_bf16(bw[k]);
+    }
+  }
+  float g8[8];
+  const bool gate_bcast = p.gate.rows_per_vec == 0;
+  if (gated && gate_bcast) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8);
+#pragma unroll 2
+  for (int i = 0; i < 32; ++i) {
+    const int j = (tid >> 4) + 8 * i;
+    const int m = m0 + j;
+    if (m >= p.M) break;
+    const uint4 av = *reinterpret_cast<const uint4*>(stg + j * BM + f);
+    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+    float a[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      a[2 * k] = lo_bf16(aw[k]);
+      a[2 * k + 1] = hi_bf16(aw[k]);
+    }
+    if (p.bias != nullptr) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = rbf16(__fadd_rn(a[k], bias8[k]));
+    }
+    if (p.epi == LTXQ_EPI_GELU) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = gelu_ref(a[k]);
+    }
+    const int64_t off = static_cast<int64_t>(m) * p.N + nf;
+    if (gated) {
+      const uint4 rv = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+      if (!gate_bcast) load_vec8(p.gate, vec_row(p.gate, m), nf, g8);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float pr = __fmul_rn(a[2 * k + h], g8[2 * k + h]);
+          const float rr = h ? hi_bf16(rw[k]) : lo_bf16(rw[k]);
+          a[2 * k + h] = two_round ? __fadd_rn(rr, rbf16(pr)) : __fadd_rn(pr, rr);
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(p.out + off) =
+        make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+  }
+}
+
+template <int QK>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    qgemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                      const Params p) {
+  using P = PairPlan<QK>;
+  constexpr int BN = P::BN;
+  constexpr int S = P::kStages;
+  constexpr int AS = P::kAStages;
+  constexpr int WB = QTraits<QK>::kWBytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* xs = smem;
+  uint8_t* ws = smem + S * P::kXStage;
+  uint16_t* stg = reinterpret_cast<uint16_t*>(smem + P::kEpiOff);
+  const Bars bb = carve_bars<S, AS>(smem + P::kBarOff);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_kb = p.K / BK;
+  const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
+  const int tiles = n_pt * ((p.M + BN - 1) / BN);
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int n_clusters = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bb.x_full[s], 1);
+      mbar_init(&bb.x_empty[s], 1);
+      mbar_init(&bb.w_full[s], 1);
+      mbar_init(&bb.w_empty[s], kDeqWarps);
+    }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&bb.a_full[s], 2 * kDeqWarps);  // both CTAs' dequant warps (the leader's copy is used)
+      mbar_init(&bb.a_empty[s], 1);
+    }
+    mbar_init(bb.acc_full, 1);
+    mbar_init(bb.acc_empty, 2);  // both CTAs' epilogue groups (the leader's copy is used)
+    *bb.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(bb.tmem_slot, P::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialized, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *bb.tmem_slot;
+  const uint32_t leader_x_full = mapa_shared(smem_u32(bb.x_full), 0);
+  const uint32_t leader_a_full = mapa_shared(smem_u32(bb.a_full), 0);
+  const uint32_t leader_acc_empty = mapa_shared(smem_u32(bb.acc_empty), 0);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
+      tma_prefetch_desc(&tmap_w);
+      bool ok = true;
+      for (int tile = cluster_id, it = 0; tile < tiles && ok; tile += n_clusters, ++it) {
+        const int n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
+        const int m0 = (tile / n_pt) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int g = it * num_kb + kb;
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!mbar_wait(&bb.w_empty[s], ph ^ 1, bb.abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bb.w_full[s], P::kWStage);
+          tma_load_2d(ws + s * P::kWStage, &tmap_w, &bb.w_full[s], kb * WB, n0);
+          if (!mbar_wait(&bb.x_empty[s], ph ^ 1, bb.abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          // the leader expects both halves; each CTA's copy completes on the leader's barrier
+          if (leader) mbar_arrive_expect_tx(&bb.x_full[s], 2 * P::kXStage);
+          tma_load_2d_pair(xs + s * P::kXStage, &tmap_x, leader_x_full + 8u * s, kb * BK,
+                           m0 + static_cast<int>(rank) * (BN / 2));
+        }
+      }
+      if (*bb.abort_flag) {
+        // give copies already in flight time to land before smem is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(2 * BM, BN);
+      bool ok = true;
+        int it = 0;
+      for (int tile = cluster_id; tile < tiles && ok; tile += n_clusters, ++it) {
+        // both epilogue groups must have drained the previous tile's accumulator
+        if (!mbar_wait(bb.acc_empty, (it & 1) ^ 1, bb.abort_flag, p.err)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int g = it * num_kb + kb;
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          const int as = g % AS;
+          const uint32_t aph = (g / AS) & 1;
+          if (!mbar_wait(&bb.a_full[as], aph, bb.abort_flag, p.err) ||
+              !mbar_wait(&bb.x_full[s], ph, bb.abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(xs + s * P::kXStage);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            const uint64_t bdesc = smem_desc_sw128(xaddr + j * 32);
+            mma_bf16_ts_pair(tmem, tmem + P::kACol + as * 32 + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&bb.x_empty[s], 0x3);
+          mma_commit_pair(&bb.a_empty[as], 0x3);
+        }
+        mma_commit_pair(bb.acc_full, 0x3);  // accumulator of this tile ready in both CTAs
+      }
+      if (*bb.abort_flag) {
+        // give MMAs already issued time to complete before TMEM is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
+    }
+  } else if (warp < kDeqWarps) {
+    for (int tile = cluster_id, it = 0; tile < tiles && !*bb.abort_flag; tile += n_clusters, ++it) {
+      const int n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
+      dequant_loop<QK, S, AS, P::kACol>(p, bb, ws, tmem, warp, lane, n0, num_kb, leader_a_full, it * num_kb);
+    }
+  } else {
+    // ------------------------------------------------ epilogue warps 10..13
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;
+    const int tid = (warp - kEpiWarp0) * 32 + lane;  // 0..127
+    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    for (int tile = cluster_id, it = 0; tile < tiles; tile += n_clusters, ++it) {
+      const int n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
+      const int m0 = (tile / n_pt) * BN;
+      if (!mbar_wait(bb.acc_full, it & 1, bb.abort_flag, p.err)) break;
+      tc_fence_after();
+      // drain: accumulator column j of TMEM lane r -> staging[j][r] as bf16(acc)
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stg[(c * 32 + j) * BM + r] = f32_to_bf16(__uint_as_float(v[j]));
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (tid == 0) mbar_arrive_cluster(leader_acc_empty);  // TMEM accumulator may be overwritten
+      epilogue_tile_from_smem(p, stg, tid, n0, m0);
+      named_bar_sync(1, 128);  // staging tile consumed
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal or read it
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, P::kTmemCols);
   }
 }
 
 template <int QK, int BN>
 static ltxq_status launch_cfg(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, cudaStream_t stream) {
-  using C = Cfg<QK, BN>;
+  using PL = Plan<QK, BN, BN>;
   auto kern = qgemm_kernel<QK, BN>;
   ltxq_status st =
-      cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem), "smem attribute");
+      cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem), "smem attribute");
   if (st) return st;
   const dim3 grid((p.N + BM - 1) / BM, (p.M + BN - 1) / BN);
-  kern<<<grid, kThreads, C::kSmem, stream>>>(tx, tw, p);
+  kern<<<grid, kThreads, PL::kSmem, stream>>>(tx, tw, p);
   return cuda_check(cudaGetLastError(), "qgemm launch");
+}
+
+template <int QK>
+static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, cudaStream_t stream) {
+  using PL = PairPlan<QK>;
+  auto kern = qgemm_pair_kernel<QK>;
+  ltxq_status st =
+      cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem), "smem attribute");
+  if (st) return st;
+  const int tiles = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + 255) / 256);
+  const int max_clusters = num_sms() / 2;
+  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kPairThreads);
+  cfg.dynamicSmemBytes = PL::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kern, tx, tw, p), "qgemm pair launch");
 }
 
 template <int QK>
@@ -353,7 +818,7 @@ static ltxq_status launch_qk(int bn, const CUtensorMap& tx, const CUtensorMap& t
                              cudaStream_t stream) {
   if (bn == 64) return launch_cfg<QK, 64>(tx, tw, p, stream);
   if (bn == 128) return launch_cfg<QK, 128>(tx, tw, p, stream);
-  return launch_cfg<QK, 256>(tx, tw, p, stream);
+  return launch_pair<QK>(tx, tw, p, stream);
 }
 
 }  // namespace gemm
@@ -399,14 +864,16 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
     return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: dimension too large");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
     return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: x/out must be 16-byte aligned");
-  if (w.bias && (reinterpret_cast<uintptr_t>(w.bias) & 1u)) return fail(LTXQ_ERR_INVALID, "qlinear: bias misaligned");
+  if (w.bias && (reinterpret_cast<uintptr_t>(w.bias) & 15u))
+    return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: bias must be 16-byte aligned");
   if (ltxq_status st = check_epilogue(epi, M, N)) return st;
   if (M == 0) return LTXQ_OK;
 
   const int qk = w.mode == LTXQ_MXFP8 ? gemm::kMxfp8 : (w.bits == 8 ? gemm::kAffine8 : gemm::kAffine4);
   const int bn = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
   CUtensorMap tx, tw;
-  if (ltxq_status st = encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, K * 2, gemm::BK, bn,
+  const uint32_t xbox = bn == 256 ? 128 : static_cast<uint32_t>(bn);  // the pair kernel stages half a tile per CTA
+  if (ltxq_status st = encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, K * 2, gemm::BK, xbox,
                                       CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
   const int wbytes_row = static_cast<int>(K * w.bits / 8);
@@ -433,6 +900,13 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
     p.residual = nullptr;
   }
   p.out = static_cast<uint16_t*>(out);
+  {
+    const int64_t gpr = w.mode == LTXQ_MXFP8 ? K / 32 : K / w.group_size;
+    const int64_t per_blk = w.mode == LTXQ_MXFP8 ? 16 : 8;
+    const bool al = (reinterpret_cast<uintptr_t>(w.scales) & 15u) == 0 &&
+                    (w.mode == LTXQ_MXFP8 || (reinterpret_cast<uintptr_t>(w.biases) & 15u) == 0);
+    p.vec_groups = (gpr % per_blk == 0 && al) ? 1 : 0;
+  }
   p.err = dev_error_word();
   if (!p.err) return fail(LTXQ_ERR_CUDA, "qlinear: device error word unavailable");
   switch (qk) {

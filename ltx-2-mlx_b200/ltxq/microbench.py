@@ -1,0 +1,85 @@
+"""Quantized-linear microbenchmark (the analogue of the reference's
+scripts/bench_ff_microbench.py ``quant_matmul``, :451-551).
+
+    python -m ltxq.microbench --shapes 9216x4096x4096 --modes affine4,mxfp8
+    python -m ltxq.microbench --cublas            # also time torch bf16 F.linear
+
+Each shape is MxKxN (tokens x in x out).  Prints one JSON line per shape
+with ms and TFLOP/s (2*M*N*K / time) per mode; the L2 is flushed (256 MiB
+write) before every timed launch and each number is the median of
+``--iters`` CUDA-event timings.  ``--iters 1 --warmup 1`` gives a short
+launch sequence suitable for an ncu capture.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib
+from .quantized_linear import QuantizedLinear
+
+DEFAULT_SHAPES = ["1024x4096x4096", "3456x4096x16384", "3456x16384x4096", "9216x4096x12288", "9216x4096x4096",
+                  "9216x16384x4096", "126x2048x8192", "201x4096x2048"]
+MODES = {"affine8": ("affine", 8), "affine4": ("affine", 4), "mxfp8": ("mxfp8", 8)}
+
+
+def _time(fn, flush, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--shapes", default=",".join(DEFAULT_SHAPES))
+    ap.add_argument("--modes", default="affine8,affine4,mxfp8")
+    ap.add_argument("--epilogue", choices=["none", "gelu", "gated"], default="none")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--cublas", action="store_true")
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for spec in args.shapes.split(","):
+        M, K, N = (int(v) for v in spec.split("x"))
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        b = (torch.randn(N, device=dev, generator=g) * 0.01).to(torch.bfloat16)
+        res = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
+        gate = torch.randn(N, device=dev, generator=g) * 0.1
+        row = {"M": M, "K": K, "N": N, "epilogue": args.epilogue}
+        flops = 2.0 * M * N * K
+        if args.cublas:
+            t = _time(lambda: torch.nn.functional.linear(x, w, b), flush, args.iters, args.warmup)
+            row["cublas_bf16"] = {"ms": t, "tflops": flops / t / 1e9}
+        for name in args.modes.split(","):
+            mode, bits = MODES[name]
+            ql = QuantizedLinear.from_linear(w, b, mode=mode, bits=bits)
+            kw = {"gelu": True} if args.epilogue == "gelu" else (
+                {"residual": res, "gate": gate} if args.epilogue == "gated" else {})
+            t = _time(lambda: ql(x, **kw), flush, args.iters, args.warmup)
+            row[name] = {"ms": t, "tflops": flops / t / 1e9}
+        print(json.dumps(row), flush=True)
+    err = _lib.device_error()
+    if err:
+        raise SystemExit(f"device error word {err}")
+
+
+if __name__ == "__main__":
+    main()

@@ -32,6 +32,7 @@ from .bf16 import (
     e4m3_decode,
     e4m3_encode,
     f32_to_bf16_bits,
+    rbf16,
     rbf16_exact,
 )
 
@@ -107,6 +108,20 @@ def affine_dequantize(weight_u32, scales_u16, biases_u16, k: int, group_size: in
     s = np.repeat(s, group_size, axis=1)[:, :k]
     b = np.repeat(b, group_size, axis=1)[:, :k]
     return rbf16_exact(s * q + b).reshape(n, k)
+
+
+def affine_dequantize_fast(weight_u32, scales_u16, biases_u16, k: int, group_size: int = 64, bits: int = 8):
+    """float32 evaluation of the same dequantization for the timed CPU
+    baseline: ``rbf16(fp32 fma-free scale*q + bias)``.  It equals
+    ``affine_dequantize`` whenever scale*q + bias is exact in fp32 (the
+    exponents of the two terms within 2**8 of each other, true for every
+    group ``affine_quantize`` produces from finite weights)."""
+    q = unpack_bits(np.asarray(weight_u32), bits, k).astype(np.float32)
+    n = q.shape[0]
+    s = bf16_bits_to_f32(scales_u16)[:, :, None]
+    b = bf16_bits_to_f32(biases_u16)[:, :, None]
+    g = q.reshape(n, -1, group_size)
+    return rbf16((g * s + b).astype(np.float32)).reshape(n, k)
 
 
 # --------------------------------------------------------------------------

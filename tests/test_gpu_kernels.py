@@ -315,3 +315,19 @@ def test_no_device_error_after_suite(cuda):
     from ltxq import _lib
 
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("gs,K,bits", [(32, 512, 8), (128, 1024, 4), (64, 320, 8), (64, 448, 4)])
+def test_qlinear_group_sizes_and_unaligned_group_rows(cuda, gs, K, bits):
+    """Group sizes 32/128 and K whose group-parameter rows are not 16-byte
+    blocks (the scalar group-load path)."""
+    M, N = 300, 256
+    g = rng(13)
+    x = normal_bf16(g, (M, K))
+    W = normal_bf16(g, (N, K), 0.02)
+    bias = normal_bf16(g, (N,), 0.01)
+    q = oq.quantize(W, "affine", gs, bits)
+    deq = oq.dequantize(q, K)
+    out = from_dev_bf16(qlinear_from_oracle(q, bias, N, K)(to_dev_bf16(x)))
+    assert_close(out, ro.linear(x, deq, bias), f"gs={gs} K={K}")
+    assert (ulp_diff_bf16(out, ro.linear(x, deq, bias)) > 0).mean() < 0.01
