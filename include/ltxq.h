@@ -152,6 +152,21 @@ ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pr
                                const ltxq_qweight* w, const ltxq_epilogue* epi, void* out,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* ltxq_adaln_qlinear without a workspace argument and without allocating.
+ * No counterpart in the reference.  For hosts that cannot let a library
+ * allocate device memory (a runtime that owns the whole GPU's memory
+ * through its own pool, a plugin inside another framework's allocator, a
+ * latency-critical loop where cudaMalloc/cudaFree would synchronize the
+ * device).  The scratch is a fixed 8 MiB array inside the library's device
+ * image, held by every GPU that loads the library until exit: M * K must be
+ * <= 4194304 (else LTXQ_ERR_UNSUPPORTED, nothing launched).  All calls share
+ * that array, so calls that overlap on the GPU race; serialize them.  The
+ * first call on a device looks the array's address up (make it before any
+ * stream capture).  No cudaMalloc/cudaFree or allocating routine is used. */
+ltxq_status ltxq_adaln_qlinear_noalloc(const void* x, int64_t M, const ltxq_prologue* pro,
+                                       const ltxq_qweight* w, const ltxq_epilogue* epi, void* out,
+                                       void* stream);
+
 /* out = x + gate * project_out(gelu(project_in(modulate(norm(x))))) -- the
  * whole FF sub-layer of transformer.py:629-668.  pro may be NULL (x is
  * already modulated) and epi may be NULL / LTXQ_EPI_NONE (plain FF). */

@@ -73,6 +73,8 @@ SIGNATURES = {
                                c_size_t, c_void_p]),
     "ltxq_adaln_qlinear": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(Epilogue),
                                      c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ltxq_adaln_qlinear_noalloc": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight),
+                                             POINTER(Epilogue), c_void_p, c_void_p]),
     "ltxq_feed_forward": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(QWeight),
                                     POINTER(Epilogue), c_void_p, c_void_p, c_size_t, c_void_p]),
 }
