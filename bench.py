@@ -1,25 +1,33 @@
 """Benchmark of the quantized DiT-block hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload step|ff]
 
-Workload ("config 2"): the video feed-forward
-sub-layer of the 22B block -- AdaLN (RMSNorm + modulate) prologue, Linear
-4096->16384 with GELU-tanh, Linear 16384->4096, gated residual -- on
-3456 tokens x 4096 bf16 (~N(0,1)), weights ~N(0, 0.02) quantized affine int4
-group 64 on the GPU, biases ~N(0, 0.01), AdaLN vectors ~N(0, 0.1) fp32.
+Default workload "step" (the metric's own
+configuration): one 22B-shaped denoise step -- 48 random-init audio-video
+blocks, every block linear quantized mxfp8 (group 32, E8M0 scales) on the
+GPU from bf16 weights ~N(0, 0.02), 1024x576x121 frames -> 9216 video tokens
+(d 4096, 32 heads x 128), 201 audio tokens (d 2048, 32 x 64), 1024 text tokens
+per stream, batch 1; AdaLN vectors ~N(0, 0.1) fp32 (the sigma schedule only
+changes their values, not the cost); RoPE tables from synthetic positions.
 Synthetic, seeded data (the reference uses no dataset).
 
-A step is one pass of the sub-layer.  ``value`` is whole-job quantized-GEMM
-throughput (2*M*N*K of both linears / step time, summed over ranks) with the
-inputs resident in HBM; the L2 is flushed (a 256 MiB write) before every
-timed step, outside the timed events.  ``e2e`` is the same metric through the
-public API (``FeedForward.sublayer`` -> ``ltxq_feed_forward``) with the input
-copied from pinned host memory and the output copied back inside the timed
-region.  ``roofline`` describes the dominant kernel (the project_in GEMM).
-Under torchrun every rank runs its own sub-layer (weak scaling, no
-collective on this workload); timings are max over ranks.
+``value`` is ms per denoise step (lower is better), max over ranks, inputs
+resident in HBM; the 19 GB of packed weights streamed every step are far
+larger than the L2, so no flush is needed.  Under torchrun (N > 1) the video
+tokens are row-sharded over the ranks (9216 / N rows each), weights are
+replicated, audio and text streams are replicated, and the K/V of video
+self-attention and of video->audio cross-attention are all-gathered with NCCL
+(strong scaling: the job is fixed).  ``e2e`` is the same metric through the
+public block API with this step's latent rows copied from pinned host memory
+and the results copied back inside the timed region.  ``roofline`` describes
+the dominant kernel, the video FF project_in GEMM (mxfp8 CTA-pair GEMM,
+9216/N x 4096 -> 16384 with the GELU epilogue), timed with CUDA events around
+its launches inside the timed steps.
 
-``--impl reference`` times the reference composition on the host CPU (the
+Workload "ff": the video FF sub-layer, int4 g64, 3456 tokens,
+reported in quantized-GEMM TFLOP/s.
+
+``--impl reference`` times the reference's composition on the host CPU (the
 numpy restatement in oracle/, all host threads) on a bounded sample of the
 same workload and prints the same metric.
 """
@@ -27,8 +35,8 @@ same workload and prints the same metric.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
-import math
 import os
 import subprocess
 import sys
@@ -39,10 +47,30 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "ltx-2-mlx_b200"))
 
 METRIC = "ms/denoise step (22B shape, 8xB200) + quantized-GEMM TFLOP/s vs peak, 1/2/4/8 GPU"
-WORKLOAD = "config2_video_ff_sublayer_int4g64_3456tok"
-T, D, H = 3456, 4096, 16384
-FLOPS = 2.0 * T * D * H * 2  # both linears (927.7 GFLOP)
-BITS, GS = 4, 64
+
+# ---- config 4: 22B-shaped denoise step
+STEP_T, STEP_A, STEP_L, STEP_BLOCKS = 9216, 201, 1024, 48
+VD, AD = 4096, 2048
+
+
+def step_linear_flops(t_video: int, t_audio: int, t_text: int) -> float:
+    """2*M*N*K over every block linear (which rows each projection reads:
+    transformer.py:447-668, attention.py:560-602)."""
+    V, A, L = t_video, t_audio, t_text
+    f = 0.0
+    f += 2 * V * VD * (3 * VD + 32) + 2 * V * VD * VD                  # attn1 qkv+gate, out
+    f += 2 * V * VD * (VD + 32) + 2 * L * VD * 2 * VD + 2 * V * VD * VD  # attn2 q+gate, kv (text), out
+    f += 2 * A * AD * (3 * AD + 32) + 2 * A * AD * AD                  # audio_attn1
+    f += 2 * A * AD * (AD + 32) + 2 * L * AD * 2 * AD + 2 * A * AD * AD  # audio_attn2
+    f += 2 * V * VD * (AD + 32) + 2 * A * AD * 2 * AD + 2 * V * AD * VD  # a2v: q(video) kv(audio) out
+    f += 2 * A * AD * (AD + 32) + 2 * V * VD * 2 * AD + 2 * A * AD * AD  # v2a: q(audio) kv(video) out
+    f += 2 * V * VD * 4 * VD * 2 + 2 * A * AD * 4 * AD * 2              # feed-forwards
+    return f
+
+
+# ---- config 2: video FF sub-layer
+FF_T, FF_D, FF_H = 3456, 4096, 16384
+FF_FLOPS = 2.0 * FF_T * FF_D * FF_H * 2
 
 
 def _peaks():
@@ -65,7 +93,7 @@ def _traffic(kernel_key: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """nvidia-smi clocks / throttle-reason sampling while the benchmark runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -76,13 +104,12 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
-            self._t.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except Exception:
             self.proc = None
         return self
@@ -91,7 +118,7 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def __exit__(self, *a):
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -121,116 +148,309 @@ class ClockSampler:
 
 
 def _dist():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
 
 
-# ---------------------------------------------------------------------------- reference arm (CPU)
+# ============================================================================ CPU legs (oracle)
+
+
+class CpuStepSample:
+    """One full-width block on ``video_tokens`` video rows (+ 201 audio, 1024
+    text) through the oracle.  The packed mxfp8 weights are prepared once;
+    each timed run dequantizes them (the reference's quantized matmul works
+    from packed weights every call) and runs the block composition."""
+
+    def __init__(self, video_tokens: int, seed: int = 0):
+        import numpy as np
+
+        from ltxq.block import AUDIO_22B, VIDEO_22B, linear_specs, table_specs
+        from oracle import quant as oq
+        from oracle.bf16 import rbf16
+
+        self.video_tokens = video_tokens
+        g = np.random.default_rng(seed)
+        self.q = {}
+        for name, (n, k) in linear_specs().items():
+            # packed mxfp8 drawn directly (finite E4M3 codes of either sign, E8M0
+            # scales around 2^-9): the timed work does not depend on the values
+            codes = (g.integers(0, 0x7F, size=(n, k), dtype=np.uint8) | (g.integers(0, 2, size=(n, k), dtype=np.uint8) << 7))
+            qq = {"mode": "mxfp8", "group_size": 32, "bits": 8,
+                  "weight": codes.view(np.uint32).reshape(n, k // 4),
+                  "scales": g.integers(112, 120, size=(n, k // 32), dtype=np.uint8)}
+            self.q[name] = (qq, rbf16(g.standard_normal(n, dtype=np.float32) * np.float32(0.01)), k)
+        self.tabs = {k: (g.standard_normal(s, dtype=np.float32) * np.float32(0.1)
+                         + np.float32(1.0 if k.endswith("norm.weight") else 0.0)) for k, s in table_specs().items()}
+
+        def stream(cfg, t, cross_heads, cross_d):
+            ang = g.uniform(0, 6.28, (cfg.heads, t, cfg.d_head // 2)).astype(np.float32)
+            cang = g.uniform(0, 6.28, (cross_heads, t, cross_d // 2)).astype(np.float32)
+            return {"x": rbf16(g.standard_normal((t, cfg.dim), dtype=np.float32)),
+                    "context": rbf16(g.standard_normal((STEP_L, cfg.context_dim), dtype=np.float32)),
+                    "timesteps": (g.standard_normal((9, cfg.dim)) * 0.1).astype(np.float32),
+                    "prompt": (g.standard_normal((2, cfg.dim)) * 0.1).astype(np.float32),
+                    "cross_ss": (g.standard_normal((4, cfg.dim)) * 0.1).astype(np.float32),
+                    "cross_gate": (g.standard_normal((1, cfg.dim)) * 0.1).astype(np.float32),
+                    "pe": (np.cos(ang), np.sin(ang)), "cross_pe": (np.cos(cang), np.sin(cang))}
+
+        self.vs = stream(VIDEO_22B, video_tokens, AUDIO_22B.heads, AUDIO_22B.d_head)
+        self.as_ = stream(AUDIO_22B, STEP_A, AUDIO_22B.heads, AUDIO_22B.d_head)
+        self.flops = step_linear_flops(video_tokens, STEP_A, STEP_L)
+
+    def run(self) -> float:
+        from oracle import block as ob
+        from oracle import quant as oq
+
+        t0 = time.perf_counter()
+        p = dict(self.tabs)
+        for name, (qq, b, k) in self.q.items():
+            p[f"{name}.weight"] = oq.dequantize_fast(qq, k)
+            p[f"{name}.bias"] = b
+        ob.block(p, self.vs, self.as_)
+        return time.perf_counter() - t0
+
+
+def _cpu_ff_sample(sample: int, seed: int = 1):
+    import numpy as np
+
+    from oracle import quant as oq
+    from oracle import ref_ops as ro
+    from oracle.bf16 import rbf16
+
+    g = np.random.default_rng(seed)
+    x = rbf16(g.standard_normal((1, sample, FF_D)).astype(np.float32))
+    w_in = rbf16((g.standard_normal((FF_H, FF_D)) * 0.02).astype(np.float32))
+    w_out = rbf16((g.standard_normal((FF_D, FF_H)) * 0.02).astype(np.float32))
+    b_in = rbf16((g.standard_normal(FF_H) * 0.01).astype(np.float32))
+    b_out = rbf16((g.standard_normal(FF_D) * 0.01).astype(np.float32))
+    v = (g.standard_normal((3, 1, 1, FF_D)) * 0.1).astype(np.float32)
+    qi = oq.quantize(w_in, "affine", 64, 4)
+    qo = oq.quantize(w_out, "affine", 64, 4)
+    t0 = time.perf_counter()
+    wi = oq.dequantize_fast(qi, FF_D)
+    wo = oq.dequantize_fast(qo, FF_H)
+    ro.ff_sublayer(x, v[0], v[1], v[2], wi, b_in, wo, b_out)
+    return time.perf_counter() - t0, 2.0 * sample * FF_D * FF_H * 2
+
+
+def cpu_baseline(workload: str):
+    """Bounded CPU measurement (~10-30 s) for the cpu_baseline field."""
+    if workload == "step":
+        smp = CpuStepSample(64)
+        sec = min(smp.run() for _ in range(2))
+        tflops = smp.flops / sec / 1e12
+        ms_step = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS / (tflops * 1e12) * 1e3
+        return {"value": ms_step, "unit": "ms/step", "cores": os.cpu_count() or 1, "kind": "port",
+                "sample": f"one full-width mxfp8 block on 64 of the 9216 video tokens (+201 audio, 1024 text), "
+                          f"oracle/ numpy restatement with weights dequantized per call; {tflops * 1e3:.2f} "
+                          f"GFLOP/s of linear work, extrapolated to 48 blocks x 9216 tokens by linear FLOPs "
+                          f"(attention excluded)"}
+    sec, flops = _cpu_ff_sample(256)
+    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"256 of the {FF_T} tokens (dequantize + numpy fp32 BLAS with the reference's bf16 rounding points)"}
 
 
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return
-    import numpy as np
-
-    from oracle import quant as oq
-    from oracle import ref_ops as ro
-    from oracle.bf16 import rbf16
-
-    cores = os.cpu_count() or 1
-    g = np.random.default_rng(0)
     sample = args.cpu_sample
-    x = rbf16(g.standard_normal((1, sample, D)).astype(np.float32))
-    w_in = rbf16((g.standard_normal((H, D)) * 0.02).astype(np.float32))
-    w_out = rbf16((g.standard_normal((D, H)) * 0.02).astype(np.float32))
-    b_in = rbf16((g.standard_normal(H) * 0.01).astype(np.float32))
-    b_out = rbf16((g.standard_normal(D) * 0.01).astype(np.float32))
-    s = (g.standard_normal((1, 1, D)) * 0.1).astype(np.float32)
-    t = (g.standard_normal((1, 1, D)) * 0.1).astype(np.float32)
-    gate = (g.standard_normal((1, 1, D)) * 0.1).astype(np.float32)
-    qi = oq.quantize(w_in, "affine", GS, BITS)
-    qo = oq.quantize(w_out, "affine", GS, BITS)
-
-    def step():
-        # the reference keeps only the packed weights: the composition
-        # dequantizes (inside mx.quantized_matmul) every call
-        wi = oq.affine_dequantize_fast(qi["weight"], qi["scales"], qi["biases"], D, GS, BITS)
-        wo = oq.affine_dequantize_fast(qo["weight"], qo["scales"], qo["biases"], H, GS, BITS)
-        return ro.ff_sublayer(x, s, t, gate, wi, b_in, wo, b_out)
-
-    for _ in range(args.warmup):
-        step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times)
-    flops = 2.0 * sample * D * H * 2
-    val = flops / sec / 1e12
+    if args.workload == "ff":
+        run = lambda i: _cpu_ff_sample(sample, i)
+    else:
+        smp = CpuStepSample(sample)
+        run = lambda i: (smp.run(), smp.flops)
+    for i in range(args.warmup):
+        run(100 + i)
+    secs, flops = [], 0.0
+    for i in range(args.steps):
+        s, flops = run(i)
+        secs.append(s)
+    sec = sum(secs) / len(secs)
+    tflops = flops / sec / 1e12
+    if args.workload == "step":
+        value = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS / (tflops * 1e12) * 1e3
+        unit, hib, cfg, scaling = "ms/step", False, _step_config(world), "strong"
+        desc = (f"one full-width block on {sample} of 9216 video tokens per step, extrapolated to 48 blocks x "
+                f"9216 tokens by linear FLOPs (attention excluded)")
+    else:
+        value, unit, hib, cfg, scaling = tflops, "TFLOP/s", True, _ff_config(world), "weak"
+        desc = f"{sample} of {FF_T} tokens per step"
     line = {
-        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3 * (T / sample),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "tokens": T, "d": D, "inner": H, "quant": f"affine int{BITS} g{GS}"},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": f"{sample} of {T} tokens per step (oracle/ numpy restatement: dequantize + "
-                                   f"fp32 BLAS with bf16 rounding points), ms_per_step scaled by tokens"},
-        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": value if unit == "ms/step" else sec * 1e3, "higher_is_better": hib,
+        "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+        "cpu_baseline": {"value": value, "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": desc + " (oracle/ numpy restatement of the reference composition)"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_sample(seconds_budget: float = 20.0):
-    """Bounded CPU measurement for the main arm's cpu_baseline field."""
-    import numpy as np
-
-    from oracle import quant as oq
-    from oracle import ref_ops as ro
-    from oracle.bf16 import rbf16
-
-    g = np.random.default_rng(1)
-    sample = 256
-    x = rbf16(g.standard_normal((1, sample, D)).astype(np.float32))
-    w_in = rbf16((g.standard_normal((H, D)) * 0.02).astype(np.float32))
-    w_out = rbf16((g.standard_normal((D, H)) * 0.02).astype(np.float32))
-    b_in = rbf16((g.standard_normal(H) * 0.01).astype(np.float32))
-    b_out = rbf16((g.standard_normal(D) * 0.01).astype(np.float32))
-    v = (g.standard_normal((3, 1, 1, D)) * 0.1).astype(np.float32)
-    qi = oq.quantize(w_in, "affine", GS, BITS)
-    qo = oq.quantize(w_out, "affine", GS, BITS)
-    times = []
-    t_start = time.perf_counter()
-    while not times or (time.perf_counter() - t_start < seconds_budget and len(times) < 5):
-        t0 = time.perf_counter()
-        wi = oq.affine_dequantize_fast(qi["weight"], qi["scales"], qi["biases"], D, GS, BITS)
-        wo = oq.affine_dequantize_fast(qo["weight"], qo["scales"], qo["biases"], H, GS, BITS)
-        ro.ff_sublayer(x, v[0], v[1], v[2], wi, b_in, wo, b_out)
-        times.append(time.perf_counter() - t0)
-    sec = sorted(times)[len(times) // 2]
-    return {"value": 2.0 * sample * D * H * 2 / sec / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count() or 1,
-            "kind": "port", "sample": f"{sample} tokens of the {T}-token sub-layer, median of {len(times)} "
-                                      f"(dequantize + numpy fp32 BLAS with the reference's bf16 rounding points)"}
+# ============================================================================ GPU arm
 
 
-# ---------------------------------------------------------------------------- our arm (GPU)
+def _step_config(world):
+    return {"workload": "config4_22b_denoise_step_mxfp8g32", "blocks": STEP_BLOCKS, "video_tokens": STEP_T,
+            "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
+            "quant": "mxfp8 g32 (E4M3, E8M0 scales), all block linears",
+            "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL)",
+            "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
 
 
-def run_ours(args):
+def _ff_config(world):
+    return {"workload": "config2_video_ff_sublayer_int4g64_3456tok", "tokens": FF_T, "d": FF_D, "inner": FF_H,
+            "quant": "affine int4 g64", "global_batch": world, "seq_len": FF_T, "parallelism": f"replicas{world}",
+            "l2": "flushed before every timed step (256 MiB write, outside the events)"}
+
+
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
     import torch
 
-    world, rank, local = _dist()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_step(args, world, rank, local, dev):
+    import torch
+
+    from ltxq import _lib
+    from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, RowShard, TransformerArgs
+
+    if STEP_T % world:
+        raise SystemExit(f"{STEP_T} video tokens do not split over {world} ranks")
+    tl = STEP_T // world
+    shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2026)  # identical on every rank: weights are replicated
+    blocks = [BasicAVTransformerBlock.random(gen, dev, mode="mxfp8") for _ in range(STEP_BLOCKS)]
+    weight_bytes = sum(b.nbytes() for b in blocks)
+
+    def rnd(*shape, std=1.0, dtype=torch.float32):
+        return (torch.randn(*shape, generator=gen, device=dev) * std).to(dtype)
+
+    def rope(heads, t, d):
+        ang = torch.rand(1, heads, t, d // 2, generator=gen, device=dev) * 6.2831853
+        return torch.cos(ang), torch.sin(ang)
+
+    vx_full = rnd(1, STEP_T, VD, dtype=torch.bfloat16)
+    ax = rnd(1, STEP_A, AD, dtype=torch.bfloat16)
+    pe_v = rope(VIDEO_22B.heads, STEP_T, VIDEO_22B.d_head)
+    cpe_v = rope(AUDIO_22B.heads, STEP_T, AUDIO_22B.d_head)
+    rows = slice(rank * tl, (rank + 1) * tl)
+    video = TransformerArgs(
+        x=vx_full[:, rows].contiguous(), context=rnd(1, STEP_L, VD, dtype=torch.bfloat16),
+        timesteps=rnd(1, 1, 9, VD, std=0.1), positional_embeddings=tuple(c[:, :, rows].contiguous() for c in pe_v),
+        cross_positional_embeddings=tuple(c[:, :, rows].contiguous() for c in cpe_v),
+        cross_scale_shift_timestep=rnd(1, 1, 4, VD, std=0.1), cross_gate_timestep=rnd(1, 1, 1, VD, std=0.1),
+        prompt_timestep=rnd(1, 1, 2, VD, std=0.1))
+    audio = TransformerArgs(
+        x=ax, context=rnd(1, STEP_L, AD, dtype=torch.bfloat16), timesteps=rnd(1, 1, 9, AD, std=0.1),
+        positional_embeddings=rope(AUDIO_22B.heads, STEP_A, AUDIO_22B.d_head),
+        cross_positional_embeddings=rope(AUDIO_22B.heads, STEP_A, AUDIO_22B.d_head),
+        cross_scale_shift_timestep=rnd(1, 1, 4, AD, std=0.1), cross_gate_timestep=rnd(1, 1, 1, AD, std=0.1),
+        prompt_timestep=rnd(1, 1, 2, AD, std=0.1))
+    del vx_full, pe_v, cpe_v
+    stream = torch.cuda.current_stream()
+    ff_events: list = []
+
+    def probe(tag):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        ff_events.append(e)
+
+    def step(v, a):
+        for b in blocks:
+            v, a = b(v, a, shard)
+        return v, a
+
+    clk = ClockSampler(local).start()
+    for _ in range(args.warmup):
+        step(video, audio)
+    torch.cuda.synchronize()
     if world > 1:
-        import datetime
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for b in blocks:
+        b.probe = probe
+    evs = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step(video, audio)
+        e1.record(stream)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    clk.stop()
+    for b in blocks:
+        b.probe = None
+    if world > 1:
+        torch.distributed.barrier()
+    total_ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in evs), world, dev)
+    ms_step = total_ms / args.steps
+    ff_ms = [ff_events[i].elapsed_time(ff_events[i + 1]) for i in range(0, len(ff_events), 2)]
+    ff_avg = sum(ff_ms) / len(ff_ms)
 
-        import torch.distributed as dist
+    # ---- e2e through the public block API with host buffers
+    vx_host = video.x.cpu().pin_memory()
+    ax_host = audio.x.cpu().pin_memory()
+    vo_host, ao_host = torch.empty_like(vx_host).pin_memory(), torch.empty_like(ax_host).pin_memory()
+    vdev, adev = torch.empty_like(video.x), torch.empty_like(audio.x)
+    e2e = []
+    for i in range(args.steps + 1):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        vdev.copy_(vx_host, non_blocking=True)
+        adev.copy_(ax_host, non_blocking=True)
+        vo, ao = step(video.replace(x=vdev), audio.replace(x=adev))
+        vo_host.copy_(vo.x, non_blocking=True)
+        ao_host.copy_(ao.x, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if i:  # the first pass warms the copy path
+            e2e.append(e0.elapsed_time(e1))
+    e2e_ms = _max_over_ranks(sum(e2e), world, dev) / len(e2e)
+    dev_err = _lib.device_error()
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if rank == 0:
+        hbm, tf_burst, tf_sust, peak_kind = _peaks()
+        lin_flops = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS
+        ff_flops = 2.0 * tl * VD * 4 * VD
+        achieved = ff_flops / (ff_avg / 1e3) / 1e12
+        h2d = vx_host.numel() * 2 + ax_host.numel() * 2
+        line = {
+            "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world),
+            "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
+                               "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
+                               "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
+                               "frac_of_bf16_burst_peak": achieved / tf_burst},
+            "roofline": {"bound": "tensor", "kernel": "qgemm_pair_kernel<mxfp8> (video FF project_in, GELU epilogue)",
+                         "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
+                         "peak_kind": (f"{peak_kind} bf16 sustained (kernel timed inside a long step)"
+                                       if peak_kind == "measured" else "fallback 1400 TFLOP/s sustained"),
+                         "traffic": _traffic(f"qgemm_pair_mxfp8_ff_in_{tl}x16384x4096"),
+                         "algorithmic_per_launch": {"flops": ff_flops,
+                                                    "bytes": tl * VD * 2 + 4 * VD * VD + 4 * VD * VD // 32
+                                                    + tl * 4 * VD * 2}},
+            "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
+                    "api": "ltxq.block.BasicAVTransformerBlock x48 (C ABI: ltxq_adaln_modulate, ltxq_qlinear, "
+                           "ltxq_head_gate)"},
+            "gpu_launches": args.steps * STEP_BLOCKS * 32,
+            "weights_gb": weight_bytes / 1e9,
+            "clocks": clk.summary(),
+            "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline("step"),
+            "device_error": dev_err,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_ff(args, world, rank, local, dev):
+    import torch
+
     import ltxq
     from ltxq import _lib
 
@@ -240,19 +460,14 @@ def run_ours(args):
     def randn(*shape, std=1.0, dtype=torch.bfloat16):
         return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * std).to(dtype)
 
-    x = randn(1, T, D)
-    ff = ltxq.FeedForward.from_linear(randn(H, D, std=0.02), randn(H, std=0.01), randn(D, H, std=0.02),
-                                      randn(D, std=0.01), mode="affine", group_size=GS, bits=BITS)
-    scale = randn(1, 1, D, std=0.1, dtype=torch.float32)
-    shift = randn(1, 1, D, std=0.1, dtype=torch.float32)
-    gate = randn(1, 1, D, std=0.1, dtype=torch.float32)
+    x = randn(1, FF_T, FF_D)
+    ff = ltxq.FeedForward.from_linear(randn(FF_H, FF_D, std=0.02), randn(FF_H, std=0.01), randn(FF_D, FF_H, std=0.02),
+                                      randn(FF_D, std=0.01), mode="affine", group_size=64, bits=4)
+    scale, shift, gate = (randn(1, 1, FF_D, std=0.1, dtype=torch.float32) for _ in range(3))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    torch.cuda.synchronize()
-
     stream = torch.cuda.current_stream()
 
     def step_kernels(evs):
-        # the three launches of the sub-layer, events between them
         evs[0].record(stream)
         a = ltxq.adaln_modulate(x, scale, shift, 1e-6, "rms")
         evs[1].record(stream)
@@ -262,53 +477,29 @@ def run_ours(args):
         evs[3].record(stream)
         return y
 
-    def make_evs():
-        return [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-
-    clk = ClockSampler(local).__enter__()  # runs from warm-up through the timed region
+    mk = lambda: [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    clk = ClockSampler(local).start()
     for _ in range(args.warmup):
         flush.fill_(1)
-        step_kernels(make_evs())
+        step_kernels(mk())
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    torch.cuda.synchronize()
-
     all_evs = []
-    if True:
-        for _ in range(args.steps):
-            flush.fill_(1)
-            evs = make_evs()
-            step_kernels(evs)
-            all_evs.append(evs)
-        torch.cuda.synchronize()
-    clk.__exit__(None, None, None)
-    if world > 1:
-        torch.distributed.barrier()
+    for _ in range(args.steps):
+        flush.fill_(1)
+        evs = mk()
+        step_kernels(evs)
+        all_evs.append(evs)
     torch.cuda.synchronize()
-    step_ms = [e[0].elapsed_time(e[3]) for e in all_evs]
-    gin_ms = [e[1].elapsed_time(e[2]) for e in all_evs]
-    gout_ms = [e[2].elapsed_time(e[3]) for e in all_evs]
-    mod_ms = [e[0].elapsed_time(e[1]) for e in all_evs]
-    total_ms = sum(step_ms)
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms = float(t.item())
-    ms_per_step = total_ms / args.steps
-    value = world * FLOPS * args.steps / (total_ms / 1e3) / 1e12
-
-    # ---- e2e through the public API with host buffers
+    clk.stop()
+    total = _max_over_ranks(sum(e[0].elapsed_time(e[3]) for e in all_evs), world, dev)
+    gin = sum(e[1].elapsed_time(e[2]) for e in all_evs) / len(all_evs)
     x_host = x.cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
     x_dev = torch.empty_like(x)
-    for _ in range(max(1, args.warmup)):
-        x_dev.copy_(x_host, non_blocking=True)
-        y = ff.sublayer(x_dev, scale, shift, gate)
-        out_host.copy_(y, non_blocking=True)
-    torch.cuda.synchronize()
-    e2e_ms = []
-    for _ in range(args.steps):
+    e2e = []
+    for i in range(args.steps + 1):
         flush.fill_(1)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -317,61 +508,68 @@ def run_ours(args):
         out_host.copy_(y, non_blocking=True)
         e1.record(stream)
         e1.synchronize()
-        e2e_ms.append(e0.elapsed_time(e1))
-    e2e_total = sum(e2e_ms)
-    if world > 1:
-        t = torch.tensor([e2e_total], device=dev, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_total = float(t.item())
-    e2e_value = world * FLOPS * args.steps / (e2e_total / 1e3) / 1e12
+        if i:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_total = _max_over_ranks(sum(e2e), world, dev)
     dev_err = _lib.device_error()
-
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = _peaks()
-        gin_avg = sum(gin_ms) / len(gin_ms)
-        gin_flops = 2.0 * T * D * H
-        achieved = gin_flops / (gin_avg / 1e3) / 1e12
-        traffic = _traffic("qgemm_affine4_ff_in_3456x16384x4096")
-        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline_sample()
-        clocks = clk.summary()
+        achieved = 2.0 * FF_T * FF_D * FF_H / (gin / 1e3) / 1e12
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": T, "d": D, "inner": H, "quant": f"affine int{BITS} g{GS}",
-                       "global_batch": world, "seq_len": T, "parallelism": f"replicas{world}",
-                       "l2": "flushed before every timed step (256 MiB write, outside the events)"},
-            "breakdown_ms": {"adaln_modulate": sum(mod_ms) / len(mod_ms), "qgemm_ff_in_gelu": gin_avg,
-                             "qgemm_ff_out_gated": sum(gout_ms) / len(gout_ms)},
-            "roofline": {"bound": "tensor", "kernel": "qgemm_kernel<affine4,256> (project_in, GELU epilogue)",
+            "metric": METRIC, "value": world * FF_FLOPS * args.steps / (total / 1e3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": _ff_config(world),
+            "roofline": {"bound": "tensor", "kernel": "qgemm_pair_kernel<affine4> (project_in, GELU epilogue)",
                          "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s", "frac": achieved / tf_burst,
-                         "peak_kind": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json)" if peak_kind == "measured"
-                         else "fallback 1590 TFLOP/s", "traffic": traffic,
-                         "algorithmic_per_launch": {"flops": gin_flops,
-                                                    "bytes": T * D * 2 + H * D // 2 + H * D // GS * 4 + T * H * 2}},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": x.numel() * 2,
-                    "d2h_bytes_per_step": x.numel() * 2, "api": "ltxq.FeedForward.sublayer -> ltxq_feed_forward"},
-            "gpu_launches": 3 * args.steps,
-            "clocks": clocks,
-            "cpu_baseline": cpu,
+                         "peak_kind": f"{peak_kind} bf16 burst",
+                         "traffic": _traffic("qgemm_pair_affine4_ff_in_3456x16384x4096")},
+            "e2e": {"value": world * FF_FLOPS * len(e2e) / (e2e_total / 1e3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                    "api": "ltxq.FeedForward.sublayer -> ltxq_feed_forward"},
+            "gpu_launches": 3 * args.steps, "clocks": clk.summary(),
+            "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline("ff"),
             "device_error": dev_err,
         }
         print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
-        torch.distributed.destroy_process_group()
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    try:
+        if args.workload == "ff":
+            run_ff(args, world, rank, local, dev)
+        else:
+            run_step(args, world, rank, local, dev)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--workload", choices=["step", "ff"], default="step")
+    ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3)
+    if args.cpu_sample is None:
+        args.cpu_sample = 64 if args.workload == "step" else 256
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -1,0 +1,386 @@
+"""The LTX-2 audio-video transformer block on the ltxq hot path.
+
+``BasicAVTransformerBlock`` mirrors LTX_2_MLX/model/transformer/transformer.py
+:160-674 (same sub-layer order, AdaLN table slicing and residual forms) with
+every linear layer a quantized GEMM from the C ABI:
+
+* the AdaLN modulate of a sub-layer's input is computed once
+  (``ltxq_adaln_modulate``) and feeds one GEMM whose weight is the
+  concatenation of the projections reading that input (self-attention
+  Q|K|V|gate-logits; cross-attention Q|gate-logits on the query side and
+  K|V on the context side).  Concatenating packed rows along the output
+  dimension is exact: every row keeps its own groups;
+* the residual updates are GEMM epilogues of ``to_out`` / ``project_out``:
+  gated residual (transformer.py:40-50, 469, 610-627, 650) or the text
+  cross-attention gate-then-add (transformer.py:387, 484);
+* the FF sub-layer is one ``ltxq_feed_forward`` call (GELU in project_in's
+  epilogue).
+
+QK RMSNorm, split RoPE (rope.py:53-90) and scaled-dot-product attention
+(attention.py:170-302) run through torch (cuDNN/flash SDPA); they are the
+attention core, outside the quantized-linear path.
+
+Parameter names follow the reference's cache key scheme
+(loader/transformer_cache.py:35-59): ``attn1.to_q``, ``audio_ff.project_out``, ...
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+from .quantized_linear import QuantizedLinear
+
+
+@dataclass(frozen=True)
+class StreamConfig:
+    """TransformerConfig (transformer.py:113-122) of one stream."""
+
+    dim: int
+    heads: int
+    d_head: int
+    context_dim: int
+
+
+VIDEO_22B = StreamConfig(4096, 32, 128, 4096)   # model.py:514-515, 622-627
+AUDIO_22B = StreamConfig(2048, 32, 64, 2048)
+
+ATTN_PROJECTIONS = ("to_q", "to_k", "to_v", "to_out", "to_gate_logits")
+
+
+def attention_dims(name: str, v: StreamConfig, a: StreamConfig):
+    """(query_dim, context_dim, heads, d_head) of each attention module
+    (transformer.py:183-269)."""
+    return {
+        "attn1": (v.dim, v.dim, v.heads, v.d_head),
+        "attn2": (v.dim, v.context_dim, v.heads, v.d_head),
+        "audio_attn1": (a.dim, a.dim, a.heads, a.d_head),
+        "audio_attn2": (a.dim, a.context_dim, a.heads, a.d_head),
+        "audio_to_video_attn": (v.dim, a.dim, a.heads, a.d_head),
+        "video_to_audio_attn": (a.dim, v.dim, a.heads, a.d_head),
+    }[name]
+
+
+def linear_specs(v: StreamConfig = VIDEO_22B, a: StreamConfig = AUDIO_22B) -> dict[str, tuple[int, int]]:
+    """Every quantized linear of a block: base name -> (out, in), in the
+    cache's ``_CACHE_QUANTIZED_BLOCK_LINEAR_BASES`` order."""
+    specs: dict[str, tuple[int, int]] = {}
+    for name in ("attn1", "attn2", "audio_attn1", "audio_attn2", "audio_to_video_attn", "video_to_audio_attn"):
+        qd, cd, h, d = attention_dims(name, v, a)
+        inner = h * d
+        specs[f"{name}.to_q"] = (inner, qd)
+        specs[f"{name}.to_k"] = (inner, cd)
+        specs[f"{name}.to_v"] = (inner, cd)
+        specs[f"{name}.to_out"] = (qd, inner)
+        specs[f"{name}.to_gate_logits"] = (h, qd)
+    specs["ff.project_in.proj"] = (4 * v.dim, v.dim)
+    specs["ff.project_out"] = (v.dim, 4 * v.dim)
+    specs["audio_ff.project_in.proj"] = (4 * a.dim, a.dim)
+    specs["audio_ff.project_out"] = (a.dim, 4 * a.dim)
+    return specs
+
+
+def table_specs(v: StreamConfig = VIDEO_22B, a: StreamConfig = AUDIO_22B) -> dict[str, tuple[int, ...]]:
+    """fp32 AdaLN tables and QK-norm weights (transformer.py:210-269)."""
+    t = {
+        "scale_shift_table": (9, v.dim),
+        "audio_scale_shift_table": (9, a.dim),
+        "prompt_scale_shift_table": (2, v.dim),
+        "audio_prompt_scale_shift_table": (2, a.dim),
+        "scale_shift_table_a2v_ca_audio": (5, a.dim),
+        "scale_shift_table_a2v_ca_video": (5, v.dim),
+    }
+    for name in ("attn1", "attn2", "audio_attn1", "audio_attn2", "audio_to_video_attn", "video_to_audio_attn"):
+        _, _, h, d = attention_dims(name, v, a)
+        t[f"{name}.q_norm.weight"] = (h * d,)
+        t[f"{name}.k_norm.weight"] = (h * d,)
+    return t
+
+
+@dataclass
+class TransformerArgs:
+    """Per-stream inputs (transformer.py:125-157); batch entries share the
+    rows dimension (x is (B, T, C)).  AdaLN tensors are fp32 with a broadcast
+    token dimension: timesteps (B, 1, 9, C), prompt_timestep (B, 1, 2, C),
+    cross_scale_shift_timestep (B, 1, 4, C), cross_gate_timestep (B, 1, 1, C).
+    RoPE tables are (cos, sin), each (B, H, T, D/2) fp32."""
+
+    x: torch.Tensor
+    context: torch.Tensor
+    timesteps: torch.Tensor
+    positional_embeddings: tuple | None = None
+    context_mask: torch.Tensor | None = None
+    embedded_timestep: torch.Tensor | None = None
+    cross_positional_embeddings: tuple | None = None
+    cross_scale_shift_timestep: torch.Tensor | None = None
+    cross_gate_timestep: torch.Tensor | None = None
+    enabled: bool = True
+    prompt_timestep: torch.Tensor | None = None
+
+    def replace(self, **kw) -> "TransformerArgs":
+        d = dict(self.__dict__)
+        d.update(kw)
+        return TransformerArgs(**d)
+
+
+def rms_norm_weighted(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """QK RMSNorm (attention.py:320-329): fp32 math, cast back to bf16."""
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * inv * w.float()).to(torch.bfloat16)
+
+
+def apply_split_rope(x: torch.Tensor, pe: tuple, heads: int) -> torch.Tensor:
+    """rope.py:53-90 on (B, T, H*D) with cos/sin (B, H, T, D/2) fp32 ->
+    (B, T, H*D) bf16 (token-major, so that rows can be all-gathered)."""
+    b, t, width = x.shape
+    d = width // heads
+    xh = x.view(b, t, heads, d).float()
+    x1, x2 = xh[..., : d // 2], xh[..., d // 2:]
+    cos, sin = (c.transpose(1, 2) for c in pe)
+    out = torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1).to(torch.bfloat16)
+    return out.reshape(b, t, width)
+
+
+def _heads(x: torch.Tensor, heads: int) -> torch.Tensor:
+    b, t, width = x.shape
+    return x.view(b, t, heads, width // heads).transpose(1, 2)
+
+
+@dataclass
+class RowShard:
+    """Video-token row sharding over a process group (one rank per GPU):
+    every linear, modulate and residual is row-local; attention K/V computed
+    from video rows are all-gathered (NCCL over NVLink) before the attention
+    that reads all video keys -- video self-attention and video->audio
+    cross-attention.  Audio and text rows are replicated."""
+
+    group: object = None
+    world: int = 1
+    rank: int = 0
+
+    def gather_rows(self, x: torch.Tensor) -> torch.Tensor:
+        """(B, T_local, C) on every rank -> (B, world * T_local, C)."""
+        if self.world == 1:
+            return x
+        import torch.distributed as dist
+
+        x = x.contiguous()
+        out = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x, group=self.group)
+        b, t, c = x.shape
+        return out.permute(1, 0, 2, 3).reshape(b, self.world * t, c)
+
+
+@dataclass
+class QAttention:
+    """Attention (attention.py:360-603) with fused quantized projections."""
+
+    name: str
+    heads: int
+    d_head: int
+    self_attention: bool
+    q_proj: QuantizedLinear        # self: Q|K|V|gate ; cross: Q|gate
+    kv_proj: QuantizedLinear | None  # cross: K|V over the context
+    to_out: QuantizedLinear
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    eps: float = 1e-6
+
+    def project(self, x_mod: torch.Tensor, ctx_mod: torch.Tensor | None):
+        inner = self.heads * self.d_head
+        y = self.q_proj(x_mod)
+        if self.self_attention:
+            q, k, v, gl = y[..., :inner], y[..., inner:2 * inner], y[..., 2 * inner:3 * inner], y[..., 3 * inner:]
+        else:
+            kv = self.kv_proj(ctx_mod)
+            q, gl = y[..., :inner], y[..., inner:]
+            k, v = kv[..., :inner], kv[..., inner:]
+        return q, k, v, gl
+
+    def core(self, q, k, v, gl, pe=None, k_pe=None, gather_kv: RowShard | None = None) -> torch.Tensor:
+        """QK norm, RoPE, SDPA, per-head gate -> (B, T, inner) bf16.  With
+        ``gather_kv`` the (rotated) K and V rows of every rank are
+        all-gathered first."""
+        q = rms_norm_weighted(q, self.q_norm, self.eps)
+        k = rms_norm_weighted(k, self.k_norm, self.eps)
+        if pe is not None:
+            q = apply_split_rope(q, pe, self.heads)
+            k = apply_split_rope(k, pe if k_pe is None else k_pe, self.heads)
+        if gather_kv is not None and gather_kv.world > 1:
+            k = gather_kv.gather_rows(k)
+            v = gather_kv.gather_rows(v)
+        qh, kh, vh = _heads(q, self.heads), _heads(k, self.heads), _heads(v, self.heads)
+        o = F.scaled_dot_product_attention(qh, kh, vh, scale=1.0 / math.sqrt(self.d_head))
+        b, h, t, d = o.shape
+        o = o.transpose(1, 2).reshape(b, t, h * d)
+        return K.head_gate(o, gl.contiguous(), self.heads)
+
+
+def _cat_linears(parts: list[QuantizedLinear]) -> QuantizedLinear:
+    """Concatenate quantized linears along the output dimension (exact: each
+    packed row keeps its own groups)."""
+    p0 = parts[0]
+    for p in parts[1:]:
+        assert p.in_features == p0.in_features and p.mode == p0.mode and p.bits == p0.bits
+        assert p.group_size == p0.group_size and not p.pretransposed
+    bias = None
+    if any(p.bias is not None for p in parts):
+        bias = torch.cat([p.bias if p.bias is not None else torch.zeros(p.out_features, dtype=torch.bfloat16,
+                                                                         device=p.weight.device) for p in parts])
+    return QuantizedLinear(
+        torch.cat([p.weight for p in parts]), torch.cat([p.scales for p in parts]),
+        torch.cat([p.biases for p in parts]) if p0.biases is not None else None, bias,
+        group_size=p0.group_size, bits=p0.bits, mode=p0.mode, in_features=p0.in_features,
+        out_features=sum(p.out_features for p in parts))
+
+
+class BasicAVTransformerBlock:
+    """transformer.py:160-674 over quantized weights."""
+
+    def __init__(self, linears: dict[str, QuantizedLinear], tables: dict[str, torch.Tensor],
+                 video: StreamConfig = VIDEO_22B, audio: StreamConfig = AUDIO_22B, norm_eps: float = 1e-6):
+        self.video_cfg, self.audio_cfg, self.norm_eps = video, audio, norm_eps
+        self.linears = linears
+        self.tables = {k: v.float().contiguous() for k, v in tables.items()}
+        self.attn = {}
+        for name in ("attn1", "attn2", "audio_attn1", "audio_attn2", "audio_to_video_attn", "video_to_audio_attn"):
+            _, _, h, d = attention_dims(name, video, audio)
+            l = {p: linears[f"{name}.{p}"] for p in ATTN_PROJECTIONS}
+            self_attn = name in ("attn1", "audio_attn1")
+            if self_attn:
+                q_proj, kv_proj = _cat_linears([l["to_q"], l["to_k"], l["to_v"], l["to_gate_logits"]]), None
+            else:
+                q_proj = _cat_linears([l["to_q"], l["to_gate_logits"]])
+                kv_proj = _cat_linears([l["to_k"], l["to_v"]])
+            self.attn[name] = QAttention(name, h, d, self_attn, q_proj, kv_proj, l["to_out"],
+                                         self.tables[f"{name}.q_norm.weight"], self.tables[f"{name}.k_norm.weight"],
+                                         norm_eps)
+        self.ff = (linears["ff.project_in.proj"], linears["ff.project_out"])
+        self.audio_ff = (linears["audio_ff.project_in.proj"], linears["audio_ff.project_out"])
+        # the fused projections own the packed rows now; drop the per-projection
+        # copies so that a block holds its weights once
+        self.linears = {k: v for k, v in linears.items()
+                        if not k.endswith((".to_q", ".to_k", ".to_v", ".to_gate_logits"))}
+        self.probe = None  # optional callable(tag) recording events around the FF project_in GEMM
+
+    # -------------------------------------------------------------- building
+    @classmethod
+    def random(cls, gen: torch.Generator, device, mode: str = "affine", bits: int = 8, group_size: int | None = None,
+               video: StreamConfig = VIDEO_22B, audio: StreamConfig = AUDIO_22B, w_std: float = 0.02,
+               b_std: float = 0.01, t_std: float = 0.1) -> "BasicAVTransformerBlock":
+        """Random-init block: weights ~N(0, w_std) quantized on the GPU, biases
+        ~N(0, b_std), AdaLN tables ~N(0, t_std), QK-norm weights 1 + N(0, t_std)."""
+        lin = {}
+        for name, (n, k) in linear_specs(video, audio).items():
+            w = (torch.randn(n, k, generator=gen, device=device) * w_std).to(torch.bfloat16)
+            b = (torch.randn(n, generator=gen, device=device) * b_std).to(torch.bfloat16)
+            lin[name] = QuantizedLinear.from_linear(w, b, group_size=group_size, bits=bits, mode=mode)
+            del w
+        tabs = {}
+        for name, shape in table_specs(video, audio).items():
+            t = torch.randn(*shape, generator=gen, device=device) * t_std
+            tabs[name] = (1.0 + t) if name.endswith("norm.weight") else t
+        return cls(lin, tabs, video, audio)
+
+    def quantized_modules(self) -> list[QuantizedLinear]:
+        mods = list(self.linears.values())
+        for at in self.attn.values():
+            mods.append(at.q_proj)
+            if at.kv_proj is not None:
+                mods.append(at.kv_proj)
+        return mods
+
+    def nbytes(self) -> int:
+        """Bytes of packed weights, group parameters and biases held."""
+        total = 0
+        for ql in self.quantized_modules():
+            for t in (ql.weight, ql.scales, ql.biases, ql.bias):
+                if t is not None:
+                    total += t.numel() * t.element_size()
+        return total
+
+    # -------------------------------------------------------------- forward
+    def _ada(self, table: str, ts: torch.Tensor, start: int, end: int):
+        """get_ada_values (transformer.py:286-309) -> list of (B, 1, C) fp32."""
+        t = self.tables[table][start:end]
+        vals = t[None, None] + ts[:, :, start:end]
+        return [vals[:, :, i].contiguous() for i in range(end - start)]
+
+    def __call__(self, video: TransformerArgs, audio: TransformerArgs, shard: RowShard | None = None):
+        """One block.  With ``shard``, ``video`` holds this rank's rows (and
+        the matching rows of its RoPE tables); the result keeps that split."""
+        eps = self.norm_eps
+        vx, ax = video.x.contiguous(), audio.x.contiguous()
+
+        # video self-attention (transformer.py:447-471)
+        sh, sc, g = self._ada("scale_shift_table", video.timesteps, 0, 3)
+        at = self.attn["attn1"]
+        q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
+        o = at.core(q, k, v, gl, video.positional_embeddings, gather_kv=shard)
+        vx = at.to_out(o, residual=vx, gate=g)
+
+        # video text cross-attention (transformer.py:344-387, 473-486)
+        vx = self._text_ca(vx, video, "attn2", "scale_shift_table", "prompt_scale_shift_table")
+
+        # audio self-attention + text cross-attention (transformer.py:488-527)
+        sh, sc, g = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
+        at = self.attn["audio_attn1"]
+        q, k, v, gl = at.project(K.adaln_modulate(ax, sc, sh, eps), None)
+        o = at.core(q, k, v, gl, audio.positional_embeddings)
+        ax = at.to_out(o, residual=ax, gate=g)
+        ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
+
+        # audio <-> video cross attention (transformer.py:529-627); both read
+        # the norms of vx / ax taken before either residual update
+        a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_audio", audio)
+        g_v2a = (self.tables["scale_shift_table_a2v_ca_audio"][4][None, None] + audio.cross_gate_timestep[:, :, 0])
+        v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_video", video)
+        g_a2v = (self.tables["scale_shift_table_a2v_ca_video"][4][None, None] + video.cross_gate_timestep[:, :, 0])
+        at = self.attn["audio_to_video_attn"]
+        q, k, v, gl = at.project(K.adaln_modulate(vx, v_sc_a2v, v_sh_a2v, eps),
+                                 K.adaln_modulate(ax, a_sc_a2v, a_sh_a2v, eps))
+        o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
+        at2 = self.attn["video_to_audio_attn"]
+        q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
+                                      K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
+        vx = at.to_out(o, residual=vx, gate=g_a2v.contiguous())
+        o2 = at2.core(q2, k2, v2, gl2, audio.cross_positional_embeddings, video.cross_positional_embeddings,
+                      gather_kv=shard)
+        ax = at2.to_out(o2, residual=ax, gate=g_v2a.contiguous())
+
+        # feed-forwards (transformer.py:629-668)
+        vx = self._ff(vx, video, "scale_shift_table", self.ff)
+        ax = self._ff(ax, audio, "audio_scale_shift_table", self.audio_ff)
+        return video.replace(x=vx), audio.replace(x=ax)
+
+    def _ada_cross(self, table: str, args: TransformerArgs):
+        """get_av_ca_ada_values (transformer.py:311-342) scale/shift rows."""
+        t = self.tables[table][:4][None, None] + args.cross_scale_shift_timestep
+        return [t[:, :, i].contiguous() for i in range(4)]
+
+    def _text_ca(self, x, args: TransformerArgs, name: str, table: str, prompt_table: str):
+        eps = self.norm_eps
+        sh_q, sc_q, g = self._ada(table, args.timesteps, 6, 9)
+        kv = self.tables[prompt_table][None, None] + args.prompt_timestep
+        shift_kv, scale_kv = kv[:, :, 0].contiguous(), kv[:, :, 1].contiguous()
+        at = self.attn[name]
+        q, k, v, gl = at.project(K.adaln_modulate(x, sc_q, sh_q, eps),
+                                 K.adaln_modulate(args.context, scale_kv, shift_kv, eps, "none"))
+        o = at.core(q, k, v, gl)
+        return at.to_out(o, residual=x, gate=g, gate_then_add=True)
+
+    def _ff(self, x, args: TransformerArgs, table: str, ff):
+        sh, sc, g = self._ada(table, args.timesteps, 3, 6)
+        probe = self.probe if ff is self.ff else None
+        a = K.adaln_modulate(x, sc, sh, self.norm_eps)
+        if probe is not None:
+            probe("ff_in_start")
+        h = ff[0](a, gelu=True)
+        if probe is not None:
+            probe("ff_in_end")
+        return ff[1](h, residual=x, gate=g)

@@ -1,0 +1,138 @@
+"""The reference's audio-video transformer block, restated in numpy.
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
+
+Follows LTX_2_MLX/model/transformer/transformer.py:389-674
+(BasicAVTransformerBlock.__call__), attention.py:528-603 (Attention.__call__:
+gate logits, V, Q, K projections; QK RMSNorm; split RoPE; SDPA; per-head gate;
+to_out) and rope.py:53-90 (split rotary embedding, fp32 cos/sin, cast back to
+bf16), with the rounding points of ref_ops.  Weights are given already
+dequantized (bf16 values) so that the same function checks any quantization.
+
+``p`` maps the reference's parameter names (the cache's key scheme,
+loader/transformer_cache.py:35-59) to arrays:
+``attn1.to_q.weight``, ``attn1.to_q.bias``, ``attn1.q_norm.weight``, ...,
+``ff.project_in.proj.weight``, ``scale_shift_table`` ...
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import ref_ops as ro
+from .bf16 import rbf16
+
+ATTN_MODULES = ("attn1", "attn2", "audio_attn1", "audio_attn2", "audio_to_video_attn", "video_to_audio_attn")
+
+
+def rms_norm_weighted(x, w, eps=1e-6):
+    """``RMSNorm`` module (attention.py:320-329): ``mx.fast.rms_norm(x, w, eps)``
+    (fp32 math) cast back to bf16."""
+    x = np.asarray(x, np.float32)
+    ms = (x.astype(np.float64) ** 2).mean(-1, keepdims=True).astype(np.float32)
+    inv = (1.0 / np.sqrt((ms + np.float32(eps)).astype(np.float64))).astype(np.float32)
+    return rbf16(x * inv * np.asarray(w, np.float32))
+
+
+def apply_split_rope(x, cos, sin, heads):
+    """rope.py:53-90 on (T, H*D) bf16 with cos/sin (H, T, D/2) fp32."""
+    t, width = x.shape
+    d = width // heads
+    xh = np.asarray(x, np.float32).reshape(t, heads, d).transpose(1, 0, 2)
+    x1, x2 = xh[..., : d // 2], xh[..., d // 2 :]
+    out = np.concatenate([x1 * cos - x2 * sin, x1 * sin + x2 * cos], axis=-1)
+    return rbf16(out.astype(np.float32)).transpose(1, 0, 2).reshape(t, width)
+
+
+def sdpa(q, k, v, heads):
+    """mx.fast.scaled_dot_product_attention, no mask: fp32 softmax, bf16 out."""
+    tq, width = q.shape
+    tk = k.shape[0]
+    d = width // heads
+    qh = np.asarray(q, np.float32).reshape(tq, heads, d).transpose(1, 0, 2)
+    kh = np.asarray(k, np.float32).reshape(tk, heads, d).transpose(1, 0, 2)
+    vh = np.asarray(v, np.float32).reshape(tk, heads, d).transpose(1, 0, 2)
+    s = (qh @ kh.transpose(0, 2, 1)) * np.float32(1.0 / np.sqrt(d))
+    s = s - s.max(-1, keepdims=True)
+    e = np.exp(s)
+    o = (e / e.sum(-1, keepdims=True)) @ vh
+    return rbf16(o.astype(np.float32)).transpose(1, 0, 2).reshape(tq, width)
+
+
+def attention(p, name, x, context=None, pe=None, k_pe=None, heads=32, eps=1e-6):
+    """Attention.__call__ (attention.py:528-603) for one batch row."""
+    lin = lambda base, inp: ro.linear(inp, p[f"{name}.{base}.weight"], p.get(f"{name}.{base}.bias"))
+    ctx = x if context is None else context
+    gate_logits = lin("to_gate_logits", x)
+    v = lin("to_v", ctx)
+    q = lin("to_q", x)
+    k = lin("to_k", ctx)
+    q = rms_norm_weighted(q, p[f"{name}.q_norm.weight"], eps)
+    k = rms_norm_weighted(k, p[f"{name}.k_norm.weight"], eps)
+    if pe is not None:
+        q = apply_split_rope(q, pe[0], pe[1], heads)
+        kp = pe if k_pe is None else k_pe
+        k = apply_split_rope(k, kp[0], kp[1], heads)
+    out = sdpa(q, k, v, heads)
+    out = ro.head_gate(out, gate_logits, heads)
+    return lin("to_out", out)
+
+
+def ada(table, ts, start, end):
+    """get_ada_values (transformer.py:286-309): fp32 table rows + timestep rows."""
+    return [np.asarray(table[i], np.float32) + np.asarray(ts[i], np.float32) for i in range(start, end)]
+
+
+def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
+    """BasicAVTransformerBlock.__call__ for one batch row.
+
+    video / audio: dicts with x (T, C), context (L, Cctx), timesteps (9, C),
+    pe (cos, sin), cross_pe (cos, sin), cross_ss (4, C), cross_gate (1, C),
+    prompt (2, C).  Returns (vx, ax)."""
+    vx, ax = video["x"], audio["x"]
+    # video self-attention (transformer.py:447-471)
+    sh, sc, g = ada(p["scale_shift_table"], video["timesteps"], 0, 3)
+    nv = ro.adaln(vx, sc, sh, eps)
+    vx = ro.gated_add(vx, attention(p, "attn1", nv, pe=video["pe"], heads=heads_v, eps=eps), g)
+    # video text cross-attention (transformer.py:344-387, 473-486)
+    sh_q, sc_q, g = ada(p["scale_shift_table"], video["timesteps"], 6, 9)
+    kv = [np.asarray(p["prompt_scale_shift_table"][i], np.float32) + video["prompt"][i] for i in range(2)]
+    a_in = ro.adaln(vx, sc_q, sh_q, eps)
+    enc = ro.modulate(video["context"], kv[1], kv[0])
+    vx = ro.gate_then_add(vx, attention(p, "attn2", a_in, context=enc, heads=heads_v, eps=eps), g)
+    # audio self-attention + text cross-attention (transformer.py:488-527)
+    sh, sc, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 0, 3)
+    na = ro.adaln(ax, sc, sh, eps)
+    ax = ro.gated_add(ax, attention(p, "audio_attn1", na, pe=audio["pe"], heads=heads_a, eps=eps), g)
+    sh_q, sc_q, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 6, 9)
+    kv = [np.asarray(p["audio_prompt_scale_shift_table"][i], np.float32) + audio["prompt"][i] for i in range(2)]
+    a_in = ro.adaln(ax, sc_q, sh_q, eps)
+    enc = ro.modulate(audio["context"], kv[1], kv[0])
+    ax = ro.gate_then_add(ax, attention(p, "audio_attn2", a_in, context=enc, heads=heads_a, eps=eps), g)
+    # audio <-> video cross attention (transformer.py:529-627)
+    vn3 = ro.rms_norm(vx, eps)
+    an3 = ro.rms_norm(ax, eps)
+    ta, tv = p["scale_shift_table_a2v_ca_audio"], p["scale_shift_table_a2v_ca_video"]
+    a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = [ta[i] + audio["cross_ss"][i] for i in range(4)]
+    g_v2a = ta[4] + audio["cross_gate"][0]
+    v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = [tv[i] + video["cross_ss"][i] for i in range(4)]
+    g_a2v = tv[4] + video["cross_gate"][0]
+    vxs = ro.modulate(vn3, v_sc_a2v, v_sh_a2v)
+    axs = ro.modulate(an3, a_sc_a2v, a_sh_a2v)
+    out = attention(p, "audio_to_video_attn", vxs, context=axs, pe=video["cross_pe"], k_pe=audio["cross_pe"],
+                    heads=heads_a, eps=eps)
+    vx_new = ro.gated_add(vx, out, g_a2v)
+    axs = ro.modulate(an3, a_sc_v2a, a_sh_v2a)
+    vxs = ro.modulate(vn3, v_sc_v2a, v_sh_v2a)
+    out = attention(p, "video_to_audio_attn", axs, context=vxs, pe=audio["cross_pe"], k_pe=video["cross_pe"],
+                    heads=heads_a, eps=eps)
+    ax = ro.gated_add(ax, out, g_v2a)
+    vx = vx_new
+    # feed-forwards (transformer.py:629-668)
+    sh, sc, g = ada(p["scale_shift_table"], video["timesteps"], 3, 6)
+    vx = ro.ff_sublayer(vx, sc, sh, g, p["ff.project_in.proj.weight"], p["ff.project_in.proj.bias"],
+                        p["ff.project_out.weight"], p["ff.project_out.bias"], eps)
+    sh, sc, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 3, 6)
+    ax = ro.ff_sublayer(ax, sc, sh, g, p["audio_ff.project_in.proj.weight"], p["audio_ff.project_in.proj.bias"],
+                        p["audio_ff.project_out.weight"], p["audio_ff.project_out.bias"], eps)
+    return vx, ax

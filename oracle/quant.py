@@ -156,6 +156,28 @@ def mxfp8_dequantize(weight_u32, scales_u8, k: int, group_size: int = 32):
     return rbf16_exact(v * s).reshape(n, k)
 
 
+_E4M3_F32 = e4m3_decode(np.arange(256, dtype=np.uint8)).astype(np.float32)
+
+
+def mxfp8_dequantize_fast(weight_u32, scales_u8, k: int, group_size: int = 32):
+    """float32 evaluation for the timed CPU baseline: an E4M3 value times a
+    power of two is exact in fp32 wherever the product is a normal fp32
+    number, so this equals ``mxfp8_dequantize`` for every scale an
+    ``mxfp8_quantize`` of finite bf16 weights produces."""
+    w = np.ascontiguousarray(np.asarray(weight_u32, dtype=np.uint32))
+    n = w.shape[0]
+    v = _E4M3_F32[w.view(np.uint8).reshape(n, -1)[:, :k]].reshape(n, -1, group_size)
+    s = np.ldexp(np.float32(1.0), np.asarray(scales_u8, dtype=np.int32) - 127).astype(np.float32)[:, :, None]
+    return rbf16((v * s).astype(np.float32)).reshape(n, k)
+
+
+def dequantize_fast(q: dict, k: int) -> np.ndarray:
+    """float32 dequantization used only by the timed CPU baselines."""
+    if q["mode"] == "affine":
+        return affine_dequantize_fast(q["weight"], q["scales"], q["biases"], k, q["group_size"], q["bits"])
+    return mxfp8_dequantize_fast(q["weight"], q["scales"], k, q["group_size"])
+
+
 # --------------------------------------------------------------------------
 # generic entry points mirroring the reference's (mode, group_size, bits)
 
