@@ -15,6 +15,7 @@
  *                           (+ transformer.py:40-50 _residual_gate_inline,
  *                              transformer.py:387,484 text-CA gate-then-add)
  *   ltxq_head_gate       <- LTX_2_MLX/model/transformer/attention.py:559-601
+ *   ltxq_qk_norm_rope    <- attention.py:320-329, 580-587 + rope.py:53-90
  *   ltxq_quantize        <- mx.quantize at loader/transformer_cache.py:1255
  *   ltxq_dequantize      <- mx.dequantize semantics of the same cache entries
  *   ltxq_qlinear         <- nn.QuantizedLinear.__call__ /
@@ -127,6 +128,19 @@ ltxq_status ltxq_gated_add(const void* residual, const void* branch, const ltxq_
 /* out[m, h*d:(h+1)*d] = o[m, ...] * (2*sigmoid(logits[m, h])), bf16. */
 ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int64_t heads,
                            int64_t head_dim, void* out, void* stream);
+
+/* QK RMSNorm + split rotary embedding of one attention operand
+ * (attention.py:320-329 q_norm/k_norm, then rope.py:53-90):
+ *   y = bf16(x * rsqrt(mean(x^2) + eps) * weight)   over each row of heads*head_dim,
+ *   out[h] = bf16([y1 * cos - y2 * sin, y1 * sin + y2 * cos]) per head (y1/y2: halves).
+ * x: bf16 rows with row stride row_stride elements (a column slice of a fused
+ * projection output is fine); weight: f32 [heads*head_dim]; cos/sin: f32
+ * [B, heads, pe_tokens, head_dim/2] with rows = B * pe_tokens, or both NULL
+ * for the norm alone; out: contiguous bf16 [rows, heads*head_dim].
+ * head_dim 64 or 128, heads <= 32. */
+ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t row_stride, int64_t heads,
+                              int64_t head_dim, const float* weight, float eps, const float* cos_table,
+                              const float* sin_table, int64_t pe_tokens, void* out, void* stream);
 
 /* ---- quantized weights ------------------------------------------------ */
 /* Quantize a bf16 weight [N, K] into the MLX cache layout described by `w`

@@ -455,3 +455,131 @@ ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int6
 }
 
 }  // extern "C"
+
+namespace ltxq {
+
+// ---------------------------------------------------------------------------
+// QK RMSNorm (weighted, attention.py:320-329) followed by the split rotary
+// embedding (rope.py:53-90): y = bf16(x * rsqrt(mean(x^2) + eps) * w), then
+// per head, with h1/h2 the two halves of the head vector,
+//   out = bf16([h1 * cos - h2 * sin, h1 * sin + h2 * cos])      (fp32 math).
+// One warp per row.  For head_dim D each head is D/16 lanes wide: lane l
+// owns the 8-element chunk (l % (D/16)) of both halves of heads
+// l / (D/16) + (512 / D) * i, so the rotation pairs stay in registers.  x may
+// be a column slice of a wider row (row_stride elements); out is contiguous.
+template <int kD, int kHeadsPerLane>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const uint16_t* __restrict__ x, int64_t rows,
+                                                           int64_t row_stride, int heads, const float* __restrict__ w,
+                                                           float eps, const float* __restrict__ cosv,
+                                                           const float* __restrict__ sinv, int64_t pe_tokens,
+                                                           uint16_t* __restrict__ out) {
+  constexpr int kLanesPerHead = kD / 16;
+  constexpr int kHeadStep = 32 / kLanesPerHead;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int c = lane % kLanesPerHead;  // chunk within each half
+  const int h0 = lane / kLanesPerHead;
+  const uint16_t* xr = x + row * row_stride;
+  uint4 lo[kHeadsPerLane], hi[kHeadsPerLane];
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < kHeadsPerLane; ++i) {
+    const int h = h0 + kHeadStep * i;
+    if (h < heads) {
+      lo[i] = __ldg(reinterpret_cast<const uint4*>(xr + h * kD + 8 * c));
+      hi[i] = __ldg(reinterpret_cast<const uint4*>(xr + h * kD + kD / 2 + 8 * c));
+    } else {
+      lo[i] = make_uint4(0, 0, 0, 0);
+      hi[i] = make_uint4(0, 0, 0, 0);
+    }
+    const uint32_t a[8] = {lo[i].x, lo[i].y, lo[i].z, lo[i].w, hi[i].x, hi[i].y, hi[i].z, hi[i].w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const double e0 = lo_bf16(a[k]), e1 = hi_bf16(a[k]);
+      ss += e0 * e0 + e1 * e1;
+    }
+  }
+  ss = warp_sum(ss);
+  const float ms = static_cast<float>(ss / static_cast<double>(heads * kD));
+  const float inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(ms, eps))));
+  const int64_t b = cosv != nullptr ? row / pe_tokens : 0;
+  const int64_t t = cosv != nullptr ? row - b * pe_tokens : 0;
+  uint16_t* orow = out + row * static_cast<int64_t>(heads) * kD;
+#pragma unroll
+  for (int i = 0; i < kHeadsPerLane; ++i) {
+    const int h = h0 + kHeadStep * i;
+    if (h >= heads) break;
+    const uint32_t al[4] = {lo[i].x, lo[i].y, lo[i].z, lo[i].w};
+    const uint32_t ah[4] = {hi[i].x, hi[i].y, hi[i].z, hi[i].w};
+    float y1[8], y2[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      y1[2 * k] = lo_bf16(al[k]);
+      y1[2 * k + 1] = hi_bf16(al[k]);
+      y2[2 * k] = lo_bf16(ah[k]);
+      y2[2 * k + 1] = hi_bf16(ah[k]);
+    }
+    const float* w1 = w + h * kD + 8 * c;
+    const float* w2 = w1 + kD / 2;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      y1[k] = rbf16(__fmul_rn(__fmul_rn(y1[k], inv), __ldg(w1 + k)));
+      y2[k] = rbf16(__fmul_rn(__fmul_rn(y2[k], inv), __ldg(w2 + k)));
+    }
+    if (cosv != nullptr) {
+      const int64_t off = ((b * heads + h) * pe_tokens + t) * (kD / 2) + 8 * c;
+      float cs[8], sn[8];
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(cosv + off));
+      const float4 c1 = __ldg(reinterpret_cast<const float4*>(cosv + off + 4));
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(sinv + off));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(sinv + off + 4));
+      cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float a1 = y1[k], a2 = y2[k];
+        y1[k] = __fsub_rn(__fmul_rn(a1, cs[k]), __fmul_rn(a2, sn[k]));
+        y2[k] = __fadd_rn(__fmul_rn(a1, sn[k]), __fmul_rn(a2, cs[k]));
+      }
+    }
+    uint4 o1, o2;
+    o1.x = pack_bf16x2(y1[0], y1[1]); o1.y = pack_bf16x2(y1[2], y1[3]);
+    o1.z = pack_bf16x2(y1[4], y1[5]); o1.w = pack_bf16x2(y1[6], y1[7]);
+    o2.x = pack_bf16x2(y2[0], y2[1]); o2.y = pack_bf16x2(y2[2], y2[3]);
+    o2.z = pack_bf16x2(y2[4], y2[5]); o2.w = pack_bf16x2(y2[6], y2[7]);
+    *reinterpret_cast<uint4*>(orow + h * kD + 8 * c) = o1;
+    *reinterpret_cast<uint4*>(orow + h * kD + kD / 2 + 8 * c) = o2;
+  }
+}
+
+}  // namespace ltxq
+
+extern "C" ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t row_stride, int64_t heads,
+                                         int64_t head_dim, const float* weight, float eps, const float* cos_table,
+                                         const float* sin_table, int64_t pe_tokens, void* out, void* stream) {
+  using namespace ltxq;
+  if (!x || !out || !weight) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: NULL tensor");
+  if (rows < 0 || heads <= 0 || row_stride < heads * head_dim) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: bad shape");
+  if (head_dim != 64 && head_dim != 128) return fail(LTXQ_ERR_UNSUPPORTED, "qk_norm_rope: head_dim must be 64 or 128");
+  if (heads > 32) return fail(LTXQ_ERR_UNSUPPORTED, "qk_norm_rope: at most 32 heads");
+  if ((cos_table == nullptr) != (sin_table == nullptr)) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: cos/sin pairing");
+  if (cos_table && pe_tokens <= 0) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: pe_tokens must be > 0");
+  if (cos_table && rows % pe_tokens != 0) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: rows must be a multiple of pe_tokens");
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(cos_table) |
+        reinterpret_cast<uintptr_t>(sin_table)) & 15u) || (row_stride % 8) != 0)
+    return fail(LTXQ_ERR_UNSUPPORTED, "qk_norm_rope: tensors must be 16-byte aligned (row stride a multiple of 8)");
+  if (!(eps >= 0.f)) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: eps must be >= 0");
+  if (rows == 0) return LTXQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+  auto* xi = static_cast<const uint16_t*>(x);
+  auto* o = static_cast<uint16_t*>(out);
+  const int h = static_cast<int>(heads);
+  // heads per lane: heads / (32 / (D/16)), <= 32 heads
+  if (head_dim == 128)
+    qk_norm_rope_kernel<128, 8><<<blocks, 256, 0, s>>>(xi, rows, row_stride, h, weight, eps, cos_table, sin_table, pe_tokens, o);
+  else
+    qk_norm_rope_kernel<64, 4><<<blocks, 256, 0, s>>>(xi, rows, row_stride, h, weight, eps, cos_table, sin_table, pe_tokens, o);
+  return cuda_check(cudaGetLastError(), "qk_norm_rope launch");
+}

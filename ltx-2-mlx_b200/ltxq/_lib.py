@@ -64,6 +64,8 @@ SIGNATURES = {
     "ltxq_adaln_modulate": (c_int32, [c_void_p, c_int32, c_int64, c_int64, POINTER(Prologue), c_void_p, c_void_p]),
     "ltxq_gated_add": (c_int32, [c_void_p, c_void_p, POINTER(Vec), c_int64, c_int64, c_int32, c_void_p, c_void_p]),
     "ltxq_head_gate": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+    "ltxq_qk_norm_rope": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p,
+                                    c_void_p, c_int64, c_void_p, c_void_p]),
     "ltxq_quantize": (c_int32, [c_void_p, POINTER(QWeight), c_void_p]),
     "ltxq_dequantize": (c_int32, [POINTER(QWeight), c_void_p, c_void_p]),
     "ltxq_qlinear_workspace_size": (c_size_t, [c_int64, POINTER(QWeight)]),

@@ -16,9 +16,10 @@ every linear layer a quantized GEMM from the C ABI:
 * the FF sub-layer is one ``ltxq_feed_forward`` call (GELU in project_in's
   epilogue).
 
-QK RMSNorm, split RoPE (rope.py:53-90) and scaled-dot-product attention
-(attention.py:170-302) run through torch (cuDNN/flash SDPA); they are the
-attention core, outside the quantized-linear path.
+QK RMSNorm and split RoPE (attention.py:320-329, rope.py:53-90) are one
+fused CUDA pass (``ltxq_qk_norm_rope``) reading the strided Q/K columns of
+the fused projection output; scaled-dot-product attention
+(attention.py:170-302) runs through torch (cuDNN flash SDPA).
 
 Parameter names follow the reference's cache key scheme
 (loader/transformer_cache.py:35-59): ``attn1.to_q``, ``audio_ff.project_out``, ...
@@ -206,11 +207,8 @@ class QAttention:
         """QK norm, RoPE, SDPA, per-head gate -> (B, T, inner) bf16.  With
         ``gather_kv`` the (rotated) K and V rows of every rank are
         all-gathered first."""
-        q = rms_norm_weighted(q, self.q_norm, self.eps)
-        k = rms_norm_weighted(k, self.k_norm, self.eps)
-        if pe is not None:
-            q = apply_split_rope(q, pe, self.heads)
-            k = apply_split_rope(k, pe if k_pe is None else k_pe, self.heads)
+        q = K.qk_norm_rope(q, self.q_norm, self.heads, self.eps, pe)
+        k = K.qk_norm_rope(k, self.k_norm, self.heads, self.eps, (pe if k_pe is None else k_pe) if pe is not None else None)
         if gather_kv is not None and gather_kv.world > 1:
             k = gather_kv.gather_rows(k)
             v = gather_kv.gather_rows(v)

@@ -129,3 +129,32 @@ def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int) -> torch
     _lib.check(_lib.load().ltxq_head_gate(out.data_ptr(), gate_logits.data_ptr(), rows, heads, width // heads,
                                           res.data_ptr(), _stream()), "head_gate")
     return res
+
+
+def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, heads: int, eps: float = 1e-6,
+                 pe: tuple | None = None) -> torch.Tensor:
+    """QK RMSNorm (attention.py:320-329) then split RoPE (rope.py:53-90) in one
+    pass.  x: (B, T, heads*D) bf16, any row stride with unit column stride;
+    pe: (cos, sin) fp32 (B, heads, T, D/2) or None.  Returns contiguous
+    (B, T, heads*D) bf16."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.stride(-1) != 1 or x.dim() != 3:
+        raise ValueError("x must be a (B, T, W) bfloat16 tensor with unit column stride")
+    b, t, width = x.shape
+    if x.stride(0) != t * x.stride(1):
+        x = x.contiguous()
+    d = width // heads
+    w = weight.float().contiguous()
+    out = torch.empty((b, t, width), dtype=torch.bfloat16, device=x.device)
+    cos = sin = None
+    if pe is not None:
+        cos, sin = pe[0].float().contiguous(), pe[1].float().contiguous()
+        if cos.shape != (b, heads, t, d // 2) and cos.shape != (1, heads, t, d // 2):
+            raise ValueError(f"RoPE table shape {tuple(cos.shape)} does not match {(b, heads, t, d // 2)}")
+        if cos.shape[0] != b:
+            cos, sin = cos.expand(b, -1, -1, -1).contiguous(), sin.expand(b, -1, -1, -1).contiguous()
+    _lib.check(_lib.load().ltxq_qk_norm_rope(x.data_ptr(), b * t, x.stride(1), heads, d, w.data_ptr(), float(eps),
+                                             cos.data_ptr() if cos is not None else None,
+                                             sin.data_ptr() if sin is not None else None, t, out.data_ptr(),
+                                             _stream()), "qk_norm_rope")
+    return out

@@ -331,3 +331,35 @@ def test_qlinear_group_sizes_and_unaligned_group_rows(cuda, gs, K, bits):
     out = from_dev_bf16(qlinear_from_oracle(q, bias, N, K)(to_dev_bf16(x)))
     assert_close(out, ro.linear(x, deq, bias), f"gs={gs} K={K}")
     assert (ulp_diff_bf16(out, ro.linear(x, deq, bias)) > 0).mean() < 0.01
+
+
+@pytest.mark.parametrize("heads,d,with_pe,strided", [(32, 128, True, True), (32, 64, True, False), (8, 128, False, True)])
+def test_qk_norm_rope_matches_oracle(cuda, heads, d, with_pe, strided):
+    """Fused QK RMSNorm + split RoPE against the oracle (attention.py:320-329,
+    rope.py:53-90) and against the plain torch fp32 reference."""
+    import torch
+
+    import ltxq
+    from ltxq.block import apply_split_rope, rms_norm_weighted
+    from oracle import block as ob
+
+    g = rng(14)
+    T, W = 77, heads * d
+    base = normal_bf16(g, (T, W + 40 if strided else W))
+    x = base[:, 8:8 + W] if strided else base
+    w = (1.0 + normal_f32(g, (W,), 0.1)).astype(np.float32)
+    ang = g.uniform(0, 6.28, (heads, T, d // 2)).astype(np.float32)
+    cos, sin = np.cos(ang), np.sin(ang)
+    xd = to_dev_bf16(base)[None]
+    xd = xd[:, :, 8:8 + W] if strided else xd
+    pe = (torch.from_numpy(cos)[None].cuda(), torch.from_numpy(sin)[None].cuda()) if with_pe else None
+    out = from_dev_bf16(ltxq.kernels.qk_norm_rope(xd, torch.from_numpy(w).cuda(), heads, 1e-6, pe)[0])
+    ref = ob.rms_norm_weighted(x, w)
+    if with_pe:
+        ref = ob.apply_split_rope(ref, cos, sin, heads)
+    ulps = ulp_diff_bf16(out, ref)
+    assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3, (ulps.max(), (ulps > 0).mean())
+    tref = rms_norm_weighted(xd, torch.from_numpy(w).cuda(), 1e-6)
+    if with_pe:
+        tref = apply_split_rope(tref, pe, heads)
+    assert_close(out, from_dev_bf16(tref[0]), "torch fp32 reference")
