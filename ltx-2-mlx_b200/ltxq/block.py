@@ -171,10 +171,12 @@ class RowShard:
         import torch.distributed as dist
 
         x = x.contiguous()
-        out = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
-        dist.all_gather_into_tensor(out, x, group=self.group)
         b, t, c = x.shape
-        return out.permute(1, 0, 2, 3).reshape(b, self.world * t, c)
+        out = torch.empty((self.world * b, t, c), dtype=x.dtype, device=x.device)  # rank-major blocks
+        dist.all_gather_into_tensor(out, x, group=self.group)
+        if b == 1:
+            return out.view(1, self.world * t, c)
+        return out.view(self.world, b, t, c).permute(1, 0, 2, 3).reshape(b, self.world * t, c)
 
 
 @dataclass

@@ -1,0 +1,111 @@
+"""CPU (gloo, world size 2 and 4) checks of the multi-GPU row sharding.
+
+The block shards video tokens by rows; every per-row op stays local and the
+K/V rows that attention reads from all ranks are all-gathered
+(``RowShard.gather_rows``).  These tests run the same composition as
+``QAttention.core`` on CPU ranks -- RoPE on the local rows, gather of the
+rotated K and of V, attention of the local queries -- and check that the
+concatenated per-rank outputs equal the unsharded computation, and that a
+rank that never joins makes the others fail with a timeout instead of
+hanging.
+"""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rope(x, pe, heads):
+    from ltxq.block import apply_split_rope
+
+    return apply_split_rope(x, pe, heads)
+
+
+def _attention(q, k, v, heads):
+    b, tq, w = q.shape
+    d = w // heads
+    qh = q.float().view(b, tq, heads, d).transpose(1, 2)
+    kh = k.float().view(b, k.shape[1], heads, d).transpose(1, 2)
+    vh = v.float().view(b, v.shape[1], heads, d).transpose(1, 2)
+    o = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)
+    return o.transpose(1, 2).reshape(b, tq, w)
+
+
+def _case(T=48, heads=4, d=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    w = heads * d
+    q = torch.randn(1, T, w, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, T, w, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, T, w, generator=g).to(torch.bfloat16)
+    ang = torch.rand(1, heads, T, d // 2, generator=g) * 6.28
+    return q, k, v, (torch.cos(ang), torch.sin(ang)), heads
+
+
+def _worker(rank, world, port, out_dir):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ltx-2-mlx_b200")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from ltxq.block import RowShard
+
+    q, k, v, pe, heads = _case()
+    T = q.shape[1]
+    tl = T // world
+    rows = slice(rank * tl, (rank + 1) * tl)
+    pe_l = tuple(c[:, :, rows].contiguous() for c in pe)
+    shard = RowShard(dist.group.WORLD, world, rank)
+    ql = _rope(q[:, rows], pe_l, heads)
+    kl = _rope(k[:, rows], pe_l, heads)
+    kg = shard.gather_rows(kl)
+    vg = shard.gather_rows(v[:, rows].contiguous())
+    o = _attention(ql, kg, vg, heads)
+    torch.save({"o": o, "kg": kg}, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_sharded_attention_equals_unsharded(tmp_path, world):
+    port = _free_port()
+    mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method="spawn")
+    q, k, v, pe, heads = _case()
+    ref_k = _rope(k, pe, heads)
+    ref = _attention(_rope(q, pe, heads), ref_k, v, heads)
+    outs = [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) for r in range(world)]
+    got = torch.cat([o["o"] for o in outs], dim=1)
+    assert torch.equal(outs[0]["kg"], ref_k)  # every rank sees the full rotated K
+    assert torch.allclose(got, ref, atol=1e-5, rtol=1e-5)
+
+
+def _lonely_worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    if rank == 1:
+        return  # this rank never joins
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+        open(os.path.join(out_dir, "joined"), "w").close()
+    except Exception as e:  # the rendezvous times out instead of hanging
+        with open(os.path.join(out_dir, "error"), "w") as f:
+            f.write(type(e).__name__)
+
+
+def test_missing_rank_times_out_on_host(tmp_path):
+    port = _free_port()
+    mp.start_processes(_lonely_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    assert os.path.exists(os.path.join(tmp_path, "error"))
+    assert not os.path.exists(os.path.join(tmp_path, "joined"))
