@@ -289,8 +289,8 @@ def run_reference(args):
 # ============================================================================ GPU arm
 
 
-def _step_config(world):
-    return {"workload": "config4_22b_denoise_step_mxfp8g32", "blocks": STEP_BLOCKS, "video_tokens": STEP_T,
+def _step_config(world, n_blocks=STEP_BLOCKS):
+    return {"workload": "config4_22b_denoise_step_mxfp8g32", "blocks": n_blocks, "video_tokens": STEP_T,
             "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
             "quant": "mxfp8 g32 (E4M3, E8M0 scales), all block linears",
             "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL)",
@@ -325,7 +325,8 @@ def run_step(args, world, rank, local, dev):
     shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank)
     gen = torch.Generator(device=dev)
     gen.manual_seed(2026)  # identical on every rank: weights are replicated
-    blocks = [BasicAVTransformerBlock.random(gen, dev, mode="mxfp8") for _ in range(STEP_BLOCKS)]
+    n_blocks = args.blocks
+    blocks = [BasicAVTransformerBlock.random(gen, dev, mode="mxfp8") for _ in range(n_blocks)]
     weight_bytes = sum(b.nbytes() for b in blocks)
 
     def rnd(*shape, std=1.0, dtype=torch.float32):
@@ -376,12 +377,14 @@ def run_step(args, world, rank, local, dev):
     for b in blocks:
         b.probe = probe
     evs = []
+    n_launch0 = _lib.launch_count()
     for _ in range(args.steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         step(video, audio)
         e1.record(stream)
         evs.append((e0, e1))
+    n_launches = _lib.launch_count() - n_launch0
     torch.cuda.synchronize()
     clk.stop()
     for b in blocks:
@@ -416,14 +419,14 @@ def run_step(args, world, rank, local, dev):
 
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = _peaks()
-        lin_flops = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS
+        lin_flops = step_linear_flops(STEP_T, STEP_A, STEP_L) * n_blocks
         ff_flops = 2.0 * tl * VD * 4 * VD
         achieved = ff_flops / (ff_avg / 1e3) / 1e12
         h2d = vx_host.numel() * 2 + ax_host.numel() * 2
         line = {
             "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
@@ -437,9 +440,9 @@ def run_step(args, world, rank, local, dev):
                                                     "bytes": tl * VD * 2 + 4 * VD * VD + 4 * VD * VD // 32
                                                     + tl * 4 * VD * 2}},
             "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
-                    "api": "ltxq.block.BasicAVTransformerBlock x48 (C ABI: ltxq_adaln_modulate, ltxq_qlinear, "
-                           "ltxq_head_gate)"},
-            "gpu_launches": args.steps * STEP_BLOCKS * 32,
+                    "api": f"ltxq.block.BasicAVTransformerBlock x{n_blocks} (C ABI: ltxq_adaln_modulate, ltxq_qlinear, "
+                           "ltxq_qk_norm_rope, ltxq_head_gate)"},
+            "gpu_launches": n_launches,
             "weights_gb": weight_bytes / 1e9,
             "clocks": clk.summary(),
             "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline("step"),
@@ -486,11 +489,13 @@ def run_ff(args, world, rank, local, dev):
     if world > 1:
         torch.distributed.barrier()
     all_evs = []
+    n_launch0 = _lib.launch_count()
     for _ in range(args.steps):
         flush.fill_(1)
         evs = mk()
         step_kernels(evs)
         all_evs.append(evs)
+    n_launches = _lib.launch_count() - n_launch0
     torch.cuda.synchronize()
     clk.stop()
     total = _max_over_ranks(sum(e[0].elapsed_time(e[3]) for e in all_evs), world, dev)
@@ -527,7 +532,7 @@ def run_ff(args, world, rank, local, dev):
             "e2e": {"value": world * FF_FLOPS * len(e2e) / (e2e_total / 1e3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
                     "api": "ltxq.FeedForward.sublayer -> ltxq_feed_forward"},
-            "gpu_launches": 3 * args.steps, "clocks": clk.summary(),
+            "gpu_launches": n_launches, "clocks": clk.summary(),
             "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline("ff"),
             "device_error": dev_err,
         }
@@ -566,6 +571,8 @@ def main():
     ap.add_argument("--workload", choices=["step", "ff"], default="step")
     ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,
+                    help="blocks per step (48 = the 22B model; fewer only for bounded profiler captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.cpu_sample is None:

@@ -112,6 +112,9 @@ const char* ltxq_version(void);
 /* Reads (and clears) the device-side error word written by kernels whose
  * bounded waits expired.  Synchronizes the device.  0 = no error. */
 ltxq_status ltxq_device_error(int32_t* code_out);
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads).  Host-side counter; no device synchronization. */
+uint64_t ltxq_launch_count(void);
 
 /* ---- bandwidth kernels ------------------------------------------------ */
 /* out[m, :] = modulate(norm(x[m, :])) for m < rows; x/out dtype x_dtype

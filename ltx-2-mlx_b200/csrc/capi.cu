@@ -1,5 +1,6 @@
 // capi.cu -- library-level entry points and host helpers: thread-local error
 // text, CUDA status checks, the tensor-map encoder, the device error word.
+#include <atomic>
 #include <cudaTypedefs.h>
 
 #include <cstdio>
@@ -22,6 +23,15 @@ unsigned int* dev_error_word() {
     addr[dev] = static_cast<unsigned int*>(p);
   }
   return addr[dev];
+}
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+ltxq_status launch_check(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) note_launch();
+  return cuda_check(e, what);
 }
 
 static thread_local std::string t_last_error;
@@ -82,6 +92,8 @@ int num_sms() {
 extern "C" {
 
 const char* ltxq_last_error(void) { return ltxq::t_last_error.c_str(); }
+
+uint64_t ltxq_launch_count(void) { return ltxq::g_launches.load(std::memory_order_relaxed); }
 
 const char* ltxq_version(void) { return "ltxq 0.1 (sm_100a)"; }
 

@@ -32,6 +32,10 @@ int num_sms();
 // Device error word (bounded waits that expire write a code here); kernels
 // receive its address as a parameter.
 unsigned int* dev_error_word();
+// counts one kernel launch of this library (ltxq_launch_count)
+void note_launch();
+// after a <<<>>> launch: counts it if it was accepted and returns its status
+ltxq_status launch_check(const char* what);
 
 constexpr unsigned int kErrWaitTimeout = 1;
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s: far above any launch

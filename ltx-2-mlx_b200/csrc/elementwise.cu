@@ -380,7 +380,7 @@ ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int6
     else if (C <= 2048) LTXQ_ROWS(8, 1);
     else LTXQ_ROWS(8, 2);
 #undef LTXQ_ROWS
-    return cuda_check(cudaGetLastError(), "adaln_modulate launch");
+    return launch_check("adaln_modulate launch");
   }
   int threads = static_cast<int>((C + 15) / 16);
   threads = ((threads + 31) / 32) * 32;
@@ -392,7 +392,7 @@ ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int6
     if (vb) adaln_modulate_kernel<false, true><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);
     else adaln_modulate_kernel<false, false><<<grid, threads, 0, stream>>>(x, C, pro.norm, pro.eps, s, t, out);
   }
-  return cuda_check(cudaGetLastError(), "adaln_modulate launch");
+  return launch_check("adaln_modulate launch");
 }
 
 ltxq_status launch_gated_add(const void* residual, const void* branch, const ltxq_vec& gate, int64_t rows,
@@ -417,7 +417,7 @@ ltxq_status launch_gated_add(const void* residual, const void* branch, const ltx
   if (vb) gated_add_kernel<true, true><<<blocks, threads, 0, stream>>>(r, b, g, rows, C, o);
   else if (mode == LTXQ_GATE_THEN_ADD) gated_add_kernel<false, true><<<blocks, threads, 0, stream>>>(r, b, g, rows, C, o);
   else gated_add_kernel<false, false><<<blocks, threads, 0, stream>>>(r, b, g, rows, C, o);
-  return cuda_check(cudaGetLastError(), "gated_add launch");
+  return launch_check("gated_add launch");
 }
 
 }  // namespace ltxq
@@ -451,7 +451,7 @@ ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int6
   ltxq::head_gate_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(logits), rows, heads, head_dim,
       static_cast<uint16_t*>(out));
-  return ltxq::cuda_check(cudaGetLastError(), "head_gate launch");
+  return ltxq::launch_check("head_gate launch");
 }
 
 }  // extern "C"
@@ -581,5 +581,5 @@ extern "C" ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t ro
     qk_norm_rope_kernel<128, 8><<<blocks, 256, 0, s>>>(xi, rows, row_stride, h, weight, eps, cos_table, sin_table, pe_tokens, o);
   else
     qk_norm_rope_kernel<64, 4><<<blocks, 256, 0, s>>>(xi, rows, row_stride, h, weight, eps, cos_table, sin_table, pe_tokens, o);
-  return cuda_check(cudaGetLastError(), "qk_norm_rope launch");
+  return launch_check("qk_norm_rope launch");
 }

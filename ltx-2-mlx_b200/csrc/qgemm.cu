@@ -785,7 +785,7 @@ static ltxq_status launch_cfg(const CUtensorMap& tx, const CUtensorMap& tw, cons
   if (st) return st;
   const dim3 grid((p.N + BM - 1) / BM, (p.M + BN - 1) / BN);
   kern<<<grid, kThreads, PL::kSmem, stream>>>(tx, tw, p);
-  return cuda_check(cudaGetLastError(), "qgemm launch");
+  return launch_check("qgemm launch");
 }
 
 template <int QK>
@@ -810,7 +810,9 @@ static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, con
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_check(cudaLaunchKernelEx(&cfg, kern, tx, tw, p), "qgemm pair launch");
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
+  if (e == cudaSuccess) note_launch();
+  return cuda_check(e, "qgemm pair launch");
 }
 
 template <int QK>

@@ -179,7 +179,7 @@ ltxq_status ltxq_quantize(const void* w_bf16, const ltxq_qweight* w, void* strea
     auto* sc = static_cast<uint8_t*>(const_cast<void*>(w->scales));
     mxfp8_quantize_kernel<<<blocks, threads, 0, s>>>(src, R, L, w->group_size, wq, sc);
   }
-  return cuda_check(cudaGetLastError(), "quantize launch");
+  return launch_check("quantize launch");
 }
 
 ltxq_status ltxq_dequantize(const ltxq_qweight* w, void* out_bf16, void* stream) {
@@ -200,7 +200,7 @@ ltxq_status ltxq_dequantize(const ltxq_qweight* w, void* out_bf16, void* stream)
   } else {
     dequantize_kernel<1><<<grid_for(R * L / 8, threads), threads, 0, s>>>(wq, w->scales, bi, R, L, w->group_size, o);
   }
-  return cuda_check(cudaGetLastError(), "dequantize launch");
+  return launch_check("dequantize launch");
 }
 
 }  // extern "C"

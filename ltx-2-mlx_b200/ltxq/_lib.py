@@ -61,6 +61,7 @@ SIGNATURES = {
     "ltxq_last_error": (c_char_p, []),
     "ltxq_version": (c_char_p, []),
     "ltxq_device_error": (c_int32, [POINTER(c_int32)]),
+    "ltxq_launch_count": (ctypes.c_uint64, []),
     "ltxq_adaln_modulate": (c_int32, [c_void_p, c_int32, c_int64, c_int64, POINTER(Prologue), c_void_p, c_void_p]),
     "ltxq_gated_add": (c_int32, [c_void_p, c_void_p, POINTER(Vec), c_int64, c_int64, c_int32, c_void_p, c_void_p]),
     "ltxq_head_gate": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
@@ -114,6 +115,11 @@ def check(status: int, what: str = "") -> None:
     if status in (ERR_INVALID, ERR_UNSUPPORTED):
         raise ValueError(text)
     raise LtxqError(f"[status {status}] {text}")
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process (host counter)."""
+    return int(load().ltxq_launch_count())
 
 
 def device_error() -> int:
