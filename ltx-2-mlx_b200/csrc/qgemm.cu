@@ -62,6 +62,8 @@ struct Params {
   const uint16_t* residual;
   uint16_t* out;
   unsigned int* err;
+  int splits;      // K splits (pair kernel); > 1: fp32 partials go to `partial`
+  float* partial;  // [splits][M][N] fp32, summed by splitk_reduce_kernel
 };
 
 // gelu_approx with the reference's per-op bf16 rounding (feed_forward.py:8-14;
@@ -78,6 +80,36 @@ __device__ __forceinline__ float gelu_ref(float x) {
   t = rbf16(__fadd_rn(1.0f, t));
   const float h = rbf16(__fmul_rn(0.5f, x));
   return rbf16(__fmul_rn(h, t));
+}
+
+// gelu_ref through a table.  Over all 65536 bf16 inputs gelu_ref(x) equals
+// bf16(0.5 x) for |x| < 2^-9 (its 1 + tanh term rounds to 1), x for x >= 4
+// (tanh rounds to 1), -0 for finite x <= -4 (1 + tanh rounds to 0) and NaN
+// for -inf / NaN.  Between, the result is read from a table of gelu_ref
+// values built by the kernel itself, so both forms give the same bits.
+// Magnitudes [kGeluLo, kGeluLo + kGeluN) are tabulated, positive then negative.
+constexpr uint32_t kGeluLo = 0x3B00u;  // 2^-9
+constexpr uint32_t kGeluN = 0x4080u - kGeluLo;  // up to 4.0 (exclusive)
+constexpr int kGeluTabBytes = static_cast<int>(2 * kGeluN * 2);
+
+// b: bf16 bits (low 16); returns the bf16 bits of gelu_ref
+__device__ __forceinline__ uint32_t gelu_tab_bits(uint32_t b, const uint16_t* tab) {
+  const uint32_t mag = b & 0x7FFFu, neg = b >> 15;
+  const uint32_t t = mag - kGeluLo;  // wraps for mag < kGeluLo
+  const bool in_tab = t < kGeluN;
+  const uint32_t tv = tab[in_tab ? t + neg * kGeluN : 0u];
+  const uint32_t small = f32_to_bf16(__fmul_rn(0.5f, __uint_as_float(b << 16)));
+  const uint32_t big = neg ? (mag >= 0x7F80u ? 0x7FC0u : 0x8000u) : b;
+  return in_tab ? tv : (mag < kGeluLo ? small : big);
+}
+
+// fills the table (n_threads threads, thread id tid); caller synchronizes
+__device__ __forceinline__ void gelu_tab_fill(uint16_t* tab, int tid, int n_threads) {
+  for (int i = tid; i < static_cast<int>(2 * kGeluN); i += n_threads) {
+    const uint32_t neg = static_cast<uint32_t>(i) >= kGeluN;
+    const uint32_t mag = kGeluLo + static_cast<uint32_t>(i) - (neg ? kGeluN : 0u);
+    tab[i] = f32_to_bf16(gelu_ref(__uint_as_float(((neg << 15) | mag) << 16)));
+  }
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
@@ -104,17 +136,18 @@ struct GroupCursor {
   const uint4* bb;
   int nblk, cur;
   uint4 cs, cb, ns, nb;
-  __device__ __forceinline__ void init(const Params& p, int64_t srow, bool ok) {
+  // g0: the first group get() will be asked for
+  __device__ __forceinline__ void init(const Params& p, int64_t srow, bool ok, int g0) {
     const int gpr = QK == kMxfp8 ? p.K / 32 : p.K / p.gs;
     nblk = ok ? gpr / kPerBlk : 0;
     sb = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.scales) + srow * (QK == kMxfp8 ? 1 : 2));
     bb = QK == kMxfp8 ? nullptr : reinterpret_cast<const uint4*>(p.biases + srow);
-    cur = 0;
+    cur = g0 / kPerBlk;
     const uint4 z = make_uint4(0, 0, 0, 0);
-    cs = nblk > 0 ? __ldg(sb) : z;
-    cb = (QK != kMxfp8 && nblk > 0) ? __ldg(bb) : z;
-    ns = nblk > 1 ? __ldg(sb + 1) : z;
-    nb = (QK != kMxfp8 && nblk > 1) ? __ldg(bb + 1) : z;
+    cs = cur < nblk ? __ldg(sb + cur) : z;
+    cb = (QK != kMxfp8 && cur < nblk) ? __ldg(bb + cur) : z;
+    ns = cur + 1 < nblk ? __ldg(sb + cur + 1) : z;
+    nb = (QK != kMxfp8 && cur + 1 < nblk) ? __ldg(bb + cur + 1) : z;
   }
   // parameters of group g (monotone, advancing by at most one block per call)
   __device__ __forceinline__ void get(int g, uint32_t& s, uint32_t& b) {
@@ -216,10 +249,13 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* base) {
 
 // Dequant warps (warp 0..7): convert this CTA's 128 packed weight rows stage
 // by stage into the TMEM A ring.  `a_full_remote` != 0 means the A-full
-// barriers live in the pair leader (cluster address of a_full[0]).
+// barriers live in the pair leader (cluster address of a_full[0]).  The
+// num_kb stages cover K stages [kb_first, kb_first + num_kb); kb_base is the
+// position of the first one in the smem / TMEM rings.
 template <int QK, int S, int AS, uint32_t kACol>
 __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, uint8_t* ws, uint32_t tmem, int warp,
-                                             int lane, int n0, int num_kb, uint32_t a_full_remote, int kb_base) {
+                                             int lane, int n0, int num_kb, uint32_t a_full_remote, int kb_base,
+                                             int kb_first) {
   constexpr int WB = QTraits<QK>::kWBytes;
   constexpr int kWStage = BM * WB;
   const int q = warp & 3;      // TMEM lane quarter
@@ -233,12 +269,13 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
   // is unrolled by kPrefetch so every register is read kPrefetch stages
   // after its load was issued (no register moves that would wait on it)
   const bool vec = p.vec_groups != 0;
+  const int k_first = kb_first * BK + half * 32;
   GroupCursor<QK> gc;
-  if (vec) gc.init(p, srow, row_ok);
+  if (vec) gc.init(p, srow, row_ok, QK == kMxfp8 ? (k_first >> 5) : k_first / p.gs);
   uint32_t qs[kPrefetch], qb[kPrefetch];
 #pragma unroll
   for (int i = 0; i < kPrefetch; ++i)
-    load_group<QK>(p, srow, i * BK + half * 32, !vec && row_ok && i < num_kb, qs[i], qb[i]);
+    load_group<QK>(p, srow, k_first + i * BK, !vec && row_ok && i < num_kb, qs[i], qb[i]);
   auto publish = [&](int as_done) {
     tmem_wait_st();
     tc_fence_before();
@@ -264,7 +301,7 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
       const uint32_t aph = (g / AS) & 1;
       uint32_t s_cur = qs[i], b_cur = qb[i];
       if (vec) {
-        const int k = kb * BK + half * 32;
+        const int k = k_first + kb * BK;
         gc.get(QK == kMxfp8 ? (k >> 5) : k / p.gs, s_cur, b_cur);
         if (!row_ok) {
           s_cur = 0u;
@@ -321,7 +358,7 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
       pend_as = as;
       // issued late so that no arrive (release) of this stage waits for it
       if (!vec)
-        load_group<QK>(p, srow, (kb + kPrefetch) * BK + half * 32, row_ok && kb + kPrefetch < num_kb, qs[i], qb[i]);
+        load_group<QK>(p, srow, k_first + (kb + kPrefetch) * BK, row_ok && kb + kPrefetch < num_kb, qs[i], qb[i]);
     }
   }
   if (pend_as >= 0) publish(pend_as);
@@ -493,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    dequant_loop<QK, S, AS, P::kACol>(p, bb, ws, tmem, warp, lane, n0, num_kb, 0u, 0);
+    dequant_loop<QK, S, AS, P::kACol>(p, bb, ws, tmem, warp, lane, n0, num_kb, 0u, 0, 0);
     if (!*bb.abort_flag && mbar_wait(bb.acc_full, 0, bb.abort_flag, p.err)) {
       tc_fence_after();
       epilogue<BN>(p, xs, tmem, warp, lane, n0, m0);
@@ -536,7 +573,8 @@ struct PairPlan {
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kEpiOff = kStages * (kXStage + kWStage);
   static constexpr int kBarOff = kEpiOff + kEpiBytes;
-  static constexpr int kSmem = 1024 + kBarOff + 512;
+  static constexpr int kTabOff = kBarOff + 512;  // GELU table (epilogue)
+  static constexpr int kSmem = 1024 + kTabOff + kGeluTabBytes;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kAStages = 8;
   static constexpr uint32_t kACol = BN;
@@ -544,48 +582,38 @@ struct PairPlan {
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
-// Epilogue math for one CTA's tile from the bf16 staging tile (token-major,
-// 128 features per token row): 128 threads, thread t owns the 8-feature
-// column chunk (t & 15) and token rows (t >> 4) + 8 i.
-__device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const uint16_t* stg, int tid, int n0, int m0) {
-  const int f = (tid & 15) * 8;
-  const int nf = n0 + f;
-  if (nf >= p.N) return;
-  const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
-  const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+// Epilogue state of one thread for a fixed chunk of 8 features [nf, nf + 8):
+// the linear bias and a broadcast gate are loaded once.  store() takes the
+// bf16-rounded accumulators of one token (the reference's first rounding
+// point) and applies bias / GELU / gated residual with the reference's
+// rounding points, then writes 16 bytes.
+struct Epi8 {
   float bias8[8];
-  if (p.bias != nullptr) {
-    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + nf));
-    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      bias8[2 * k] = lo_bf16(bw[k]);
-      bias8[2 * k + 1] = hi_bf16(bw[k]);
-    }
-  }
   float g8[8];
-  const bool gate_bcast = p.gate.rows_per_vec == 0;
-  if (gated && gate_bcast) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8);
-#pragma unroll 2
-  for (int i = 0; i < 32; ++i) {
-    const int j = (tid >> 4) + 8 * i;
-    const int m = m0 + j;
-    if (m >= p.M) break;
-    const uint4 av = *reinterpret_cast<const uint4*>(stg + j * BM + f);
-    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-    float a[8];
+  bool gated, two_round, gate_bcast;
+  __device__ __forceinline__ void init(const Params& p, int nf) {
+    gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
+    two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+    gate_bcast = p.gate.rows_per_vec == 0;
+    if (p.bias != nullptr) {
+      const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + nf));
+      const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      a[2 * k] = lo_bf16(aw[k]);
-      a[2 * k + 1] = hi_bf16(aw[k]);
+      for (int k = 0; k < 4; ++k) {
+        bias8[2 * k] = lo_bf16(bw[k]);
+        bias8[2 * k + 1] = hi_bf16(bw[k]);
+      }
     }
+    if (gated && gate_bcast) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8);
+  }
+  __device__ __forceinline__ void store(const Params& p, float (&a)[8], int m, int nf, const uint16_t* gtab) {
     if (p.bias != nullptr) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) a[k] = rbf16(__fadd_rn(a[k], bias8[k]));
     }
     if (p.epi == LTXQ_EPI_GELU) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) a[k] = gelu_ref(a[k]);
+      for (int k = 0; k < 8; ++k) a[k] = __uint_as_float(gelu_tab_bits(__float_as_uint(a[k]) >> 16, gtab) << 16);
     }
     const int64_t off = static_cast<int64_t>(m) * p.N + nf;
     if (gated) {
@@ -605,6 +633,73 @@ __device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const u
     *reinterpret_cast<uint4*>(p.out + off) =
         make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
   }
+};
+
+// Epilogue math for one CTA's tile from the bf16 staging tile (token-major,
+// 128 features per token row): 128 threads, thread t owns the 8-feature
+// column chunk (t & 15) and token rows (t >> 4) + 8 i.
+__device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const uint16_t* stg, const uint16_t* gtab,
+                                                        int tid, int n0, int m0) {
+  const int f = (tid & 15) * 8;
+  const int nf = n0 + f;
+  if (nf >= p.N) return;
+  Epi8 e;
+  e.init(p, nf);
+#pragma unroll 2
+  for (int i = 0; i < 32; ++i) {
+    const int j = (tid >> 4) + 8 * i;
+    const int m = m0 + j;
+    if (m >= p.M) break;
+    const uint4 av = *reinterpret_cast<const uint4*>(stg + j * BM + f);
+    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+    float a[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      a[2 * k] = lo_bf16(aw[k]);
+      a[2 * k + 1] = hi_bf16(aw[k]);
+    }
+    e.store(p, a, m, nf, gtab);
+  }
+}
+
+// Split-K: out[m, nf..nf+8) from the fp32 partial sums of the K splits,
+// added in split order (deterministic), rounded to bf16, then the same
+// epilogue as the unsplit kernel.  One thread per (token, 8 features).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
+  __shared__ uint16_t gtab[2 * kGeluN];
+  if (p.epi == LTXQ_EPI_GELU) {
+    gelu_tab_fill(gtab, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  const int chunks = p.N / 8;
+  const int64_t items = static_cast<int64_t>(p.M) * chunks;
+  const size_t plane = static_cast<size_t>(p.M) * p.N;
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(it / chunks);
+    const int nf = static_cast<int>(it - static_cast<int64_t>(m) * chunks) * 8;
+    const float* src = p.partial + static_cast<size_t>(m) * p.N + nf;
+    float a[8];
+    {
+      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src));
+      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + 4));
+      a[0] = lo.x; a[1] = lo.y; a[2] = lo.z; a[3] = lo.w;
+      a[4] = hi.x; a[5] = hi.y; a[6] = hi.z; a[7] = hi.w;
+    }
+    for (int sp = 1; sp < p.splits; ++sp) {
+      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src + sp * plane));
+      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + sp * plane + 4));
+      a[0] = __fadd_rn(a[0], lo.x); a[1] = __fadd_rn(a[1], lo.y);
+      a[2] = __fadd_rn(a[2], lo.z); a[3] = __fadd_rn(a[3], lo.w);
+      a[4] = __fadd_rn(a[4], hi.x); a[5] = __fadd_rn(a[5], hi.y);
+      a[6] = __fadd_rn(a[6], hi.z); a[7] = __fadd_rn(a[7], hi.w);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = rbf16(a[k]);
+    Epi8 e;
+    e.init(p, nf);
+    e.store(p, a, m, nf, gtab);
+  }
 }
 
 template <int QK>
@@ -621,6 +716,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* xs = smem;
   uint8_t* ws = smem + S * P::kXStage;
   uint16_t* stg = reinterpret_cast<uint16_t*>(smem + P::kEpiOff);
+  uint16_t* gtab = reinterpret_cast<uint16_t*>(smem + P::kTabOff);
   const Bars bb = carve_bars<S, AS>(smem + P::kBarOff);
 
   const int warp = threadIdx.x >> 5;
@@ -630,8 +726,20 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int num_kb = p.K / BK;
   const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
   const int tiles = n_pt * ((p.M + BN - 1) / BN);
+  // work unit u = (tile u / splits, K stages [kb_lo, kb_hi) of split u % splits);
+  // every role walks the same units in the same order
+  const int splits = p.splits;
+  const int units = tiles * splits;
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int n_clusters = static_cast<int>(gridDim.x >> 1);
+  auto unit = [&](int u, int& n0, int& m0, int& sp, int& kb_lo, int& kb_hi) {
+    const int tile = u / splits;
+    sp = u - tile * splits;
+    n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
+    m0 = (tile / n_pt) * BN;
+    kb_lo = sp * num_kb / splits;
+    kb_hi = (sp + 1) * num_kb / splits;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -666,11 +774,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tma_prefetch_desc(&tmap_x);
       tma_prefetch_desc(&tmap_w);
       bool ok = true;
-      for (int tile = cluster_id, it = 0; tile < tiles && ok; tile += n_clusters, ++it) {
-        const int n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
-        const int m0 = (tile / n_pt) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          const int g = it * num_kb + kb;
+      int g0 = 0;
+      for (int u = cluster_id; u < units && ok; u += n_clusters) {
+        int n0, m0, sp, kb_lo, kb_hi;
+        unit(u, n0, m0, sp, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          const int g = g0 + (kb - kb_lo);
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
           if (!mbar_wait(&bb.w_empty[s], ph ^ 1, bb.abort_flag, p.err)) {
@@ -688,6 +797,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tma_load_2d_pair(xs + s * P::kXStage, &tmap_x, leader_x_full + 8u * s, kb * BK,
                            m0 + static_cast<int>(rank) * (BN / 2));
         }
+        g0 += kb_hi - kb_lo;
       }
       if (*bb.abort_flag) {
         // give copies already in flight time to land before smem is released
@@ -700,13 +810,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (leader && lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(2 * BM, BN);
       bool ok = true;
-        int it = 0;
-      for (int tile = cluster_id; tile < tiles && ok; tile += n_clusters, ++it) {
-        // both epilogue groups must have drained the previous tile's accumulator
+      int it = 0, g0 = 0;
+      for (int u = cluster_id; u < units && ok; u += n_clusters, ++it) {
+        int n0, m0, sp, kb_lo, kb_hi;
+        unit(u, n0, m0, sp, kb_lo, kb_hi);
+        // both epilogue groups must have drained the previous unit's accumulator
         if (!mbar_wait(bb.acc_empty, (it & 1) ^ 1, bb.abort_flag, p.err)) break;
         tc_fence_after();
-        for (int kb = 0; kb < num_kb; ++kb) {
-          const int g = it * num_kb + kb;
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          const int g = g0 + (kb - kb_lo);
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
           const int as = g % AS;
@@ -721,12 +833,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j) {
             const uint64_t bdesc = smem_desc_sw128(xaddr + j * 32);
-            mma_bf16_ts_pair(tmem, tmem + P::kACol + as * 32 + j * 8, bdesc, idesc, (kb | j) != 0 ? 1u : 0u);
+            mma_bf16_ts_pair(tmem, tmem + P::kACol + as * 32 + j * 8, bdesc, idesc,
+                             (kb != kb_lo || j != 0) ? 1u : 0u);
           }
           mma_commit_pair(&bb.x_empty[s], 0x3);
           mma_commit_pair(&bb.a_empty[as], 0x3);
         }
-        mma_commit_pair(bb.acc_full, 0x3);  // accumulator of this tile ready in both CTAs
+        mma_commit_pair(bb.acc_full, 0x3);  // accumulator of this unit ready in both CTAs
+        g0 += kb_hi - kb_lo;
       }
       if (*bb.abort_flag) {
         // give MMAs already issued time to complete before TMEM is released
@@ -736,9 +850,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
     }
   } else if (warp < kDeqWarps) {
-    for (int tile = cluster_id, it = 0; tile < tiles && !*bb.abort_flag; tile += n_clusters, ++it) {
-      const int n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
-      dequant_loop<QK, S, AS, P::kACol>(p, bb, ws, tmem, warp, lane, n0, num_kb, leader_a_full, it * num_kb);
+    int g0 = 0;
+    for (int u = cluster_id; u < units && !*bb.abort_flag; u += n_clusters) {
+      int n0, m0, sp, kb_lo, kb_hi;
+      unit(u, n0, m0, sp, kb_lo, kb_hi);
+      dequant_loop<QK, S, AS, P::kACol>(p, bb, ws, tmem, warp, lane, n0, kb_hi - kb_lo, leader_a_full, g0, kb_lo);
+      g0 += kb_hi - kb_lo;
     }
   } else {
     // ------------------------------------------------ epilogue warps 10..13
@@ -746,11 +863,38 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int r = q * 32 + lane;
     const int tid = (warp - kEpiWarp0) * 32 + lane;  // 0..127
     const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
-    for (int tile = cluster_id, it = 0; tile < tiles; tile += n_clusters, ++it) {
-      const int n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
-      const int m0 = (tile / n_pt) * BN;
+    if (p.epi == LTXQ_EPI_GELU) {
+      gelu_tab_fill(gtab, tid, 128);  // while the first tile's main loop runs
+      named_bar_sync(1, 128);
+    }
+    for (int u = cluster_id, it = 0; u < units; u += n_clusters, ++it) {
+      int n0, m0, sp, kb_lo, kb_hi;
+      unit(u, n0, m0, sp, kb_lo, kb_hi);
       if (!mbar_wait(bb.acc_full, it & 1, bb.abort_flag, p.err)) break;
       tc_fence_after();
+      if (splits > 1) {
+        // fp32 partial of split sp: TMEM lane r = feature n0 + r, column = token
+        float* dst = p.partial + static_cast<size_t>(sp) * p.M * p.N;
+        const int n = n0 + r;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          if (m0 + c * 32 >= p.M) break;  // uniform
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v);
+          tmem_wait_ld();
+          if (n < p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int m = m0 + c * 32 + j;
+              if (m < p.M) dst[static_cast<size_t>(m) * p.N + n] = __uint_as_float(v[j]);
+            }
+          }
+        }
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (tid == 0) mbar_arrive_cluster(leader_acc_empty);
+        continue;
+      }
       // drain: accumulator column j of TMEM lane r -> staging[j][r] as bf16(acc)
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -763,7 +907,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tc_fence_before();
       named_bar_sync(1, 128);
       if (tid == 0) mbar_arrive_cluster(leader_acc_empty);  // TMEM accumulator may be overwritten
-      epilogue_tile_from_smem(p, stg, tid, n0, m0);
+      epilogue_tile_from_smem(p, stg, gtab, tid, n0, m0);
       named_bar_sync(1, 128);  // staging tile consumed
     }
   }
@@ -795,9 +939,9 @@ static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, con
   ltxq_status st =
       cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem), "smem attribute");
   if (st) return st;
-  const int tiles = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + 255) / 256);
+  const int units = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + 255) / 256) * p.splits;
   const int max_clusters = num_sms() / 2;
-  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  const int clusters = units < max_clusters ? units : max_clusters;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(kPairThreads);
@@ -812,7 +956,32 @@ static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, con
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
   if (e == cudaSuccess) note_launch();
-  return cuda_check(e, "qgemm pair launch");
+  if (ltxq_status st = cuda_check(e, "qgemm pair launch")) return st;
+  if (p.splits == 1) return LTXQ_OK;
+  const int64_t items = static_cast<int64_t>(p.M) * (p.N / 8);
+  const int64_t want = (items + 255) / 256;
+  const int cap = num_sms() * 8;
+  splitk_reduce_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(p);
+  return launch_check("split-K reduce launch");
+}
+
+// K splits of the pair kernel: used only when the output tiles alone would
+// leave more than half of the clusters idle (few tokens: the audio stream,
+// small batches).  Each split keeps at least two K stages.
+int pick_splits(int64_t M, int64_t N, int64_t K) {
+  const int64_t tiles = ((N + 2 * BM - 1) / (2 * BM)) * ((M + 255) / 256);
+  const int64_t clusters = num_sms() / 2;
+  const int64_t num_kb = K / BK;
+  if (tiles * 2 > clusters) return 1;
+  int64_t sp = clusters / tiles;
+  if (sp > num_kb / 2) sp = num_kb / 2;
+  if (sp > 32) sp = 32;
+  return sp < 2 ? 1 : static_cast<int>(sp);
+}
+
+size_t splitk_bytes(int64_t M, int64_t N, int64_t K) {
+  const int sp = pick_splits(M, N, K);
+  return sp > 1 ? static_cast<size_t>(sp) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
 }
 
 template <int QK>
@@ -851,8 +1020,10 @@ static ltxq_status check_epilogue(const ltxq_epilogue* epi, int64_t M, int64_t N
   }
 }
 
+// workspace (may be NULL): room for the split-K partials; with less than
+// splitk_bytes() the GEMM runs unsplit
 ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, const ltxq_epilogue* epi, void* out,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, void* workspace, size_t workspace_bytes) {
   int64_t R, L;
   if (ltxq_status st = check_qweight(w, true, &R, &L)) return st;
   if (!x || !out) return fail(LTXQ_ERR_INVALID, "qlinear: x/out is NULL");
@@ -872,7 +1043,11 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   if (M == 0) return LTXQ_OK;
 
   const int qk = w.mode == LTXQ_MXFP8 ? gemm::kMxfp8 : (w.bits == 8 ? gemm::kAffine8 : gemm::kAffine4);
-  const int bn = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
+  int splits = gemm::pick_splits(M, N, K);
+  if (splits > 1 && (!workspace || workspace_bytes < gemm::splitk_bytes(M, N, K) ||
+                     (reinterpret_cast<uintptr_t>(workspace) & 15u)))
+    splits = 1;
+  const int bn = splits > 1 ? 256 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
   CUtensorMap tx, tw;
   const uint32_t xbox = bn == 256 ? 128 : static_cast<uint32_t>(bn);  // the pair kernel stages half a tile per CTA
   if (ltxq_status st = encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, K * 2, gemm::BK, xbox,
@@ -911,6 +1086,8 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   }
   p.err = dev_error_word();
   if (!p.err) return fail(LTXQ_ERR_CUDA, "qlinear: device error word unavailable");
+  p.splits = splits;
+  p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   switch (qk) {
     case gemm::kAffine8: return gemm::launch_qk<gemm::kAffine8>(bn, tx, tw, p, stream);
     case gemm::kAffine4: return gemm::launch_qk<gemm::kAffine4>(bn, tx, tw, p, stream);
@@ -924,29 +1101,30 @@ static size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
 
 extern "C" {
 
+// The workspace holds the split-K partials of a GEMM with few tokens
+// (fp32 [splits][M][N]); calls given less run that GEMM unsplit.
 size_t ltxq_qlinear_workspace_size(int64_t M, const ltxq_qweight* w) {
-  (void)M;
-  (void)w;
-  return 0;
+  if (!w || M <= 0) return 0;
+  return ltxq::align_up(ltxq::gemm::splitk_bytes(M, w->n_out, w->k_in));
 }
 
 size_t ltxq_adaln_qlinear_workspace_size(int64_t M, const ltxq_qweight* w) {
   if (!w || M <= 0) return 0;
-  return ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w->k_in) * 2);
+  return ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w->k_in) * 2) +
+         ltxq_qlinear_workspace_size(M, w);
 }
 
 size_t ltxq_feed_forward_workspace_size(int64_t M, const ltxq_qweight* w_in, const ltxq_qweight* w_out) {
   if (!w_in || !w_out || M <= 0) return 0;
+  const size_t a = ltxq_qlinear_workspace_size(M, w_in), b = ltxq_qlinear_workspace_size(M, w_out);
   return ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->k_in) * 2) +
-         ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->n_out) * 2);
+         ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->n_out) * 2) + (a > b ? a : b);
 }
 
 ltxq_status ltxq_qlinear(const void* x, int64_t M, const ltxq_qweight* w, const ltxq_epilogue* epi, void* out,
                          void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (!w) return ltxq::fail(LTXQ_ERR_INVALID, "qlinear: weight is NULL");
-  return ltxq::launch_qlinear(x, M, *w, epi, out, static_cast<cudaStream_t>(stream));
+  return ltxq::launch_qlinear(x, M, *w, epi, out, static_cast<cudaStream_t>(stream), workspace, workspace_bytes);
 }
 
 ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pro, const ltxq_qweight* w,
@@ -959,7 +1137,9 @@ ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pr
   if (M == 0) return LTXQ_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w->k_in, *pro, workspace, s)) return st;
-  return ltxq::launch_qlinear(workspace, M, *w, epi, out, s);
+  const size_t a_bytes = ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w->k_in) * 2);
+  return ltxq::launch_qlinear(workspace, M, *w, epi, out, s, static_cast<char*>(workspace) + a_bytes,
+                              workspace_bytes - a_bytes);
 }
 
 ltxq_status ltxq_feed_forward(const void* x, int64_t M, const ltxq_prologue* pro, const ltxq_qweight* w_in,
@@ -981,8 +1161,11 @@ ltxq_status ltxq_feed_forward(const void* x, int64_t M, const ltxq_prologue* pro
   void* hidden = ws + ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->k_in) * 2);
   ltxq_epilogue gelu{};
   gelu.kind = LTXQ_EPI_GELU;
-  if (ltxq_status st = ltxq::launch_qlinear(a, M, *w_in, &gelu, hidden, s)) return st;
-  return ltxq::launch_qlinear(hidden, M, *w_out, epi, out, s);
+  const size_t h_bytes = ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->n_out) * 2);
+  char* part = static_cast<char*>(hidden) + h_bytes;
+  const size_t part_bytes = workspace_bytes - static_cast<size_t>(part - ws);
+  if (ltxq_status st = ltxq::launch_qlinear(a, M, *w_in, &gelu, hidden, s, part, part_bytes)) return st;
+  return ltxq::launch_qlinear(hidden, M, *w_out, epi, out, s, part, part_bytes);
 }
 
 }  // extern "C"

@@ -51,6 +51,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cublas", action="store_true")
+    ap.add_argument("--no-split-k", action="store_true", help="give the GEMM no split-K workspace")
     args = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
@@ -63,7 +64,7 @@ def main(argv=None):
         b = (torch.randn(N, device=dev, generator=g) * 0.01).to(torch.bfloat16)
         res = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
         gate = torch.randn(N, device=dev, generator=g) * 0.1
-        row = {"M": M, "K": K, "N": N, "epilogue": args.epilogue}
+        row = {"M": M, "K": K, "N": N, "epilogue": args.epilogue, "split_k": not args.no_split_k}
         flops = 2.0 * M * N * K
         if args.cublas:
             t = _time(lambda: torch.nn.functional.linear(x, w, b), flush, args.iters, args.warmup)
@@ -73,6 +74,7 @@ def main(argv=None):
             ql = QuantizedLinear.from_linear(w, b, mode=mode, bits=bits)
             kw = {"gelu": True} if args.epilogue == "gelu" else (
                 {"residual": res, "gate": gate} if args.epilogue == "gated" else {})
+            kw["split_k"] = not args.no_split_k
             t = _time(lambda: ql(x, **kw), flush, args.iters, args.warmup)
             row[name] = {"ms": t, "tflops": flops / t / 1e9}
         print(json.dumps(row), flush=True)

@@ -129,10 +129,13 @@ class QuantizedLinear:
 
     def __call__(self, x: torch.Tensor, *, gelu: bool = False, residual: torch.Tensor | None = None,
                  gate: torch.Tensor | None = None, gate_then_add: bool = False,
-                 adaln: tuple | None = None) -> torch.Tensor:
+                 adaln: tuple | None = None, split_k: bool = True) -> torch.Tensor:
         """``y = x @ dequant(W).T + bias`` with optional fused consumers:
         ``gelu=True`` (project_in), ``residual``/``gate`` (gated residual add),
-        and ``adaln=(scale, shift, eps[, norm])`` (the AdaLN prologue)."""
+        and ``adaln=(scale, shift, eps[, norm])`` (the AdaLN prologue).
+
+        ``split_k=False`` gives the library no workspace for split-K partials,
+        so a GEMM with few tokens runs unsplit (one pass over K per tile)."""
         _require_cuda(x, "x")
         if x.dtype != torch.bfloat16:
             raise ValueError(f"x must be bfloat16, got {x.dtype}")
@@ -156,8 +159,10 @@ class QuantizedLinear:
             _lib.check(lib.ltxq_adaln_qlinear(x.data_ptr(), M, ctypes.byref(pro), ctypes.byref(q), ctypes.byref(epi),
                                               out.data_ptr(), ws.data_ptr(), ws_bytes, _stream()), "adaln_qlinear")
         else:
-            _lib.check(lib.ltxq_qlinear(x.data_ptr(), M, ctypes.byref(q), ctypes.byref(epi), out.data_ptr(), None, 0,
-                                        _stream()), "qlinear")
+            ws_bytes = lib.ltxq_qlinear_workspace_size(M, ctypes.byref(q)) if split_k else 0
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+            _lib.check(lib.ltxq_qlinear(x.data_ptr(), M, ctypes.byref(q), ctypes.byref(epi), out.data_ptr(),
+                                        ws.data_ptr() if ws is not None else None, ws_bytes, _stream()), "qlinear")
         return out
 
     def __repr__(self) -> str:

@@ -13,7 +13,7 @@ import pytest
 from helpers import bf16_bits, from_dev_bf16, normal_bf16, normal_f32, rng, to_dev, to_dev_bf16, ulp_diff_bf16
 from oracle import quant as oq
 from oracle import ref_ops as ro
-from oracle.bf16 import f32_to_bf16_bits
+from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits
 
 pytestmark = pytest.mark.gpu
 
@@ -220,13 +220,17 @@ def _gemm_case(M, K, N, mode, bits, seed=9, with_bias=True):
 
 @pytest.mark.parametrize("M", [1, 64, 100, 128, 200, 256, 700])
 @pytest.mark.parametrize("qcfg", [("affine", 8), ("affine", 4), ("mxfp8", 8)])
-def test_qlinear_matches_oracle(cuda, M, qcfg):
+@pytest.mark.parametrize("split_k", [True, False])
+def test_qlinear_matches_oracle(cuda, M, qcfg, split_k):
+    """split_k=True: these shapes have few output tiles, so the pair kernel
+    splits K and splitk_reduce_kernel sums the partials; split_k=False: the
+    single-CTA kernel (M <= 128) or the unsplit pair kernel."""
     torch = _torch()
     mode, bits = qcfg
     K, N = 512, 384
     x, q, deq, bias = _gemm_case(M, K, N, mode, bits)
     ql = qlinear_from_oracle(q, bias, N, K)
-    out = from_dev_bf16(ql(to_dev_bf16(x)))
+    out = from_dev_bf16(ql(to_dev_bf16(x), split_k=split_k))
     ref = ro.linear(x, deq, bias)
     assert_close(out, ref, f"M={M} {qcfg}")
     # the only freedom is the fp32 summation order: nearly all bits agree (a
@@ -242,9 +246,10 @@ def test_qlinear_matches_oracle(cuda, M, qcfg):
 
 
 @pytest.mark.parametrize("epi", ["gelu", "gated", "gate_then_add", "nobias"])
-def test_qlinear_epilogues(cuda, epi):
+@pytest.mark.parametrize("M,split_k", [(300, True), (300, False), (96, False)])
+def test_qlinear_epilogues(cuda, epi, M, split_k):
     torch = _torch()
-    M, K, N = 300, 512, 512
+    K, N = 512, 512
     x, q, deq, bias = _gemm_case(M, K, N, "affine", 8, seed=10, with_bias=(epi != "nobias"))
     ql = qlinear_from_oracle(q, bias, N, K)
     g = rng(11)
@@ -252,16 +257,79 @@ def test_qlinear_epilogues(cuda, epi):
     gate = normal_f32(g, (1, N), 0.5)
     xd = to_dev_bf16(x)
     if epi == "gelu":
-        out = ql(xd, gelu=True)
+        out = ql(xd, gelu=True, split_k=split_k)
         ref = ro.gelu_approx(ro.linear(x, deq, bias))
     elif epi in ("gated", "gate_then_add"):
-        out = ql(xd, residual=to_dev_bf16(res), gate=torch.from_numpy(gate).cuda(), gate_then_add=(epi != "gated"))
+        out = ql(xd, residual=to_dev_bf16(res), gate=torch.from_numpy(gate).cuda(), gate_then_add=(epi != "gated"),
+                 split_k=split_k)
         y = ro.linear(x, deq, bias)
         ref = ro.gated_add(res, y, gate) if epi == "gated" else ro.gate_then_add(res, y, gate)
     else:
-        out = ql(xd)
+        out = ql(xd, split_k=split_k)
         ref = ro.linear(x, deq, None)
     assert_close(from_dev_bf16(out), ref, epi)
+
+
+def _zero_affine_linear(N, K, bias_bits):
+    """Affine int8 linear whose weights dequantize to exactly 0, with the
+    given bf16 bias bit patterns: its output is bf16(0 + bias) per feature."""
+    torch = _torch()
+    ltxq = _ltxq()
+    w = torch.zeros(N, K // 4, dtype=torch.int32, device="cuda")
+    s = torch.zeros(N, K // 64, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(N, K // 64, dtype=torch.bfloat16, device="cuda")
+    bias = torch.from_numpy(bias_bits.astype(np.uint16).view(np.int16)).cuda().view(torch.bfloat16)
+    return ltxq.QuantizedLinear(w, s, b, bias, group_size=64, bits=8, mode="affine", in_features=K, out_features=N)
+
+
+def test_gelu_epilogue_exhaustive(cuda):
+    """The GELU epilogue on every bf16 input: the pair kernel's table path,
+    the single-CTA kernel's direct evaluation and the split-K reduce kernel
+    give identical bits, and they match the oracle's gelu_approx."""
+    torch = _torch()
+    pats = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    K = 512
+    # pair kernel, unsplit (256 feature tiles > half the clusters)
+    pair = from_dev_bf16(_zero_affine_linear(0x10000, K, pats)(torch.ones(256, K, dtype=torch.bfloat16,
+                                                                              device="cuda"), gelu=True))
+    # single-CTA kernel (M <= 128, no split-K workspace)
+    single = from_dev_bf16(_zero_affine_linear(0x10000, K, pats)(torch.ones(64, K, dtype=torch.bfloat16,
+                                                                                device="cuda"), gelu=True,
+                                                                     split_k=False))
+    # split-K reduce kernel: 8192 features per call (32 tiles -> 2 splits)
+    parts = []
+    for c in range(8):
+        ql = _zero_affine_linear(8192, K, pats[c * 8192:(c + 1) * 8192])
+        parts.append(from_dev_bf16(ql(torch.ones(64, K, dtype=torch.bfloat16, device="cuda"), gelu=True)))
+    split = np.concatenate(parts, axis=1)
+    bits = lambda a: f32_to_bf16_bits(a)  # noqa: E731
+    for name, got in (("pair", pair), ("split", split)):
+        same = (bits(got[0]) == bits(single[0])) | (np.isnan(got[0]) & np.isnan(single[0]))
+        assert same.all(), (name, [hex(p) for p in pats[~same][:8]])
+    assert (bits(pair) == bits(pair[:1])).all()  # every token row alike
+    x = ro.rbf16(np.float32(0.0) + bf16_bits_to_f32(pats))
+    with np.errstate(invalid="ignore", over="ignore"):
+        ref = ro.gelu_approx(x)
+    nan_ok = np.isnan(ref) == np.isnan(single[0])
+    assert nan_ok.all(), [hex(p) for p in pats[~nan_ok][:8]]
+    fin = ~np.isnan(ref)
+    ulps = ulp_diff_bf16(single[0][fin], ref[fin])
+    # the GPU evaluates tanh in fp32 (tanhf), the oracle in fp64: a rounding
+    # boundary may separate them on a handful of inputs
+    assert ulps.max() <= 1 and (ulps > 0).sum() <= 64, ((ulps > 0).sum(), ulps.max())
+
+
+def test_split_k_deterministic(cuda):
+    """Split-K partials are summed in split order: repeated calls agree bit
+    for bit."""
+    torch = _torch()
+    x, q, deq, bias = _gemm_case(201, 2048, 2048, "mxfp8", 8, seed=21)
+    ql = qlinear_from_oracle(q, bias, 2048, 2048)
+    xd = to_dev_bf16(x)
+    a = ql(xd)
+    b = ql(xd)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert_close(from_dev_bf16(a), ro.linear(x, deq, bias), "split-K 201x2048x2048")
 
 
 def test_adaln_qlinear_gated_config1_small(cuda):
@@ -363,3 +431,42 @@ def test_qk_norm_rope_matches_oracle(cuda, heads, d, with_pe, strided):
     if with_pe:
         tref = apply_split_rope(tref, pe, heads)
     assert_close(out, from_dev_bf16(tref[0]), "torch fp32 reference")
+
+
+@pytest.mark.parametrize("mode,bits", [("mxfp8", 8), ("affine", 8), ("affine", 4)])
+@pytest.mark.parametrize("M,split_k", [(256, True), (256, False), (128, False)])
+def test_gemm_dequant_exact_through_identity(cuda, mode, bits, M, split_k):
+    """x = identity makes y[m, n] = dequant(W)[n, m] with one nonzero product
+    per output, so the in-GEMM dequantization is checked bit for bit over
+    every code: mxfp8 rows carry all finite E4M3 codes under E8M0 scales
+    10..246 (normal bf16 results, no overflow), affine rows all 2^bits codes
+    under varied bf16 scales / biases."""
+    torch = _torch()
+    ltxq = _ltxq()
+    K = N = M
+    g = rng(30)
+    if mode == "mxfp8":
+        # row n holds codes k + 128 (n % 2) (mod 256): every code appears for K >= 128
+        codes = ((np.arange(K, dtype=np.uint32)[None, :] + 128 * (np.arange(N, dtype=np.uint32)[:, None] % 2))
+                 % 256).astype(np.uint8)
+        codes[(codes & 0x7F) == 0x7F] = 0  # NaN codes: 0 * NaN would poison the row sums
+        scales = (10 + (np.arange(N * (K // 32)) * 7) % 237).astype(np.uint8).reshape(N, K // 32)
+        q = {"weight": codes.reshape(N, K // 4, 4).copy().view(np.uint32).reshape(N, K // 4), "scales": scales,
+             "group_size": 32, "bits": 8, "mode": "mxfp8"}
+    else:
+        per = 1 << bits
+        qv = np.tile(np.arange(K, dtype=np.uint32) % per, (N, 1))
+        qv = (qv + np.arange(N, dtype=np.uint32)[:, None]) % per
+        scales = f32_to_bf16_bits(normal_f32(g, (N, K // 64), 0.01))
+        biases = f32_to_bf16_bits(normal_f32(g, (N, K // 64), 0.5))
+        q = {"weight": oq.pack_bits(qv, bits), "scales": scales, "biases": biases, "group_size": 64, "bits": bits,
+             "mode": "affine"}
+    deq = oq.dequantize(q, K)
+    ql = qlinear_from_oracle(q, None, N, K)
+    eye = torch.eye(M, K, dtype=torch.bfloat16, device="cuda")
+    y = bf16_bits(ql(eye, split_k=split_k))
+    want = f32_to_bf16_bits(deq.T)
+    # +0 and -0 compare equal (a -0 weight times 1 plus +0 products sums to +0)
+    both_zero = ((y & 0x7FFF) == 0) & ((want & 0x7FFF) == 0)
+    diff = (y != want) & ~both_zero
+    assert not diff.any(), (np.argwhere(diff)[:5], y[diff][:5], want[diff][:5])
