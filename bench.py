@@ -289,8 +289,9 @@ def run_reference(args):
 # ============================================================================ GPU arm
 
 
-def _step_config(world, n_blocks=STEP_BLOCKS):
+def _step_config(world, n_blocks=STEP_BLOCKS, graph=True):
     return {"workload": "config4_22b_denoise_step_mxfp8g32", "blocks": n_blocks, "video_tokens": STEP_T,
+            "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
             "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
             "quant": "mxfp8 g32 (E4M3, E8M0 scales), all block linears",
             "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL)",
@@ -318,6 +319,7 @@ def run_step(args, world, rank, local, dev):
 
     from ltxq import _lib
     from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, RowShard, TransformerArgs
+    from ltxq.graph import StepGraph
 
     if STEP_T % world:
         raise SystemExit(f"{STEP_T} video tokens do not split over {world} ranks")
@@ -355,11 +357,13 @@ def run_step(args, world, rank, local, dev):
         prompt_timestep=rnd(1, 1, 2, AD, std=0.1))
     del vx_full, pe_v, cpe_v
     stream = torch.cuda.current_stream()
+    use_graph = not args.eager
     ff_events: list = []
 
     def probe(tag):
-        e = torch.cuda.Event(enable_timing=True)
-        e.record(stream)
+        # external: recorded as event nodes when the step is captured in a graph
+        e = torch.cuda.Event(enable_timing=True, external=use_graph)
+        e.record(torch.cuda.current_stream())
         ff_events.append(e)
 
     def step(v, a):
@@ -368,23 +372,39 @@ def run_step(args, world, rank, local, dev):
         return v, a
 
     clk = ClockSampler(local).start()
-    for _ in range(args.warmup):
+    graph = None
+    for _ in range(max(args.warmup - (1 if use_graph else 0), 0)):
         step(video, audio)
     torch.cuda.synchronize()
+    if use_graph:
+        # the last warm-up step runs inside StepGraph (before the capture)
+        for b in blocks:
+            b.probe = probe
+        graph = StepGraph(step, video, audio, warmup=1)
+        ff_events = ff_events[len(ff_events) - 2 * n_blocks:]  # the captured events
+        for b in blocks:
+            b.probe = None
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    for b in blocks:
-        b.probe = probe
-    evs = []
+    evs, ff_ms = [], []
     n_launch0 = _lib.launch_count()
     for _ in range(args.steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        step(video, audio)
-        e1.record(stream)
+        if use_graph:
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            e1.synchronize()  # read this replay's FF probes
+            ff_ms += [ff_events[i].elapsed_time(ff_events[i + 1]) for i in range(0, len(ff_events), 2)]
+        else:
+            for b in blocks:
+                b.probe = probe
+            e0.record(stream)
+            step(video, audio)
+            e1.record(stream)
         evs.append((e0, e1))
-    n_launches = _lib.launch_count() - n_launch0
+    n_launches = (graph.launches * args.steps if use_graph else _lib.launch_count() - n_launch0)
     torch.cuda.synchronize()
     clk.stop()
     for b in blocks:
@@ -393,7 +413,8 @@ def run_step(args, world, rank, local, dev):
         torch.distributed.barrier()
     total_ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in evs), world, dev)
     ms_step = total_ms / args.steps
-    ff_ms = [ff_events[i].elapsed_time(ff_events[i + 1]) for i in range(0, len(ff_events), 2)]
+    if not use_graph:
+        ff_ms = [ff_events[i].elapsed_time(ff_events[i + 1]) for i in range(0, len(ff_events), 2)]
     ff_avg = sum(ff_ms) / len(ff_ms)
 
     # ---- e2e through the public block API with host buffers
@@ -405,9 +426,15 @@ def run_step(args, world, rank, local, dev):
     for i in range(args.steps + 1):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        vdev.copy_(vx_host, non_blocking=True)
-        adev.copy_(ax_host, non_blocking=True)
-        vo, ao = step(video.replace(x=vdev), audio.replace(x=adev))
+        if use_graph:
+            # the graph reads its inputs from the tensors it was captured with
+            video.x.copy_(vx_host, non_blocking=True)
+            audio.x.copy_(ax_host, non_blocking=True)
+            vo, ao = graph.replay()
+        else:
+            vdev.copy_(vx_host, non_blocking=True)
+            adev.copy_(ax_host, non_blocking=True)
+            vo, ao = step(video.replace(x=vdev), audio.replace(x=adev))
         vo_host.copy_(vo.x, non_blocking=True)
         ao_host.copy_(ao.x, non_blocking=True)
         e1.record(stream)
@@ -416,6 +443,8 @@ def run_step(args, world, rank, local, dev):
             e2e.append(e0.elapsed_time(e1))
     e2e_ms = _max_over_ranks(sum(e2e), world, dev) / len(e2e)
     dev_err = _lib.device_error()
+    if graph is not None:
+        graph.release()  # before the process group that its collectives use goes away
 
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = _peaks()
@@ -426,7 +455,7 @@ def run_step(args, world, rank, local, dev):
         line = {
             "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks, use_graph),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
@@ -571,6 +600,8 @@ def main():
     ap.add_argument("--workload", choices=["step", "ff"], default="step")
     ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch the step op by op instead of replaying it as one captured CUDA graph")
     ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,
                     help="blocks per step (48 = the 22B model; fewer only for bounded profiler captures)")
     args = ap.parse_args()

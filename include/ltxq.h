@@ -58,6 +58,14 @@ enum {
   LTXQ_EPI_GATE_THEN_ADD = 3   /* out = bf16(residual + bf16(gate * branch))          */
 };
 enum { LTXQ_GATED_ADD = 0, LTXQ_GATE_THEN_ADD = 1 }; /* ltxq_gated_add modes */
+/* ltxq_qweight.flags: properties of the packed data, as ltxq_qweight_scan
+ * reports them.  A flag set on data that lacks the property gives wrong
+ * results (never a fault). */
+enum {
+  /* mxfp8: no NaN code (0x7F / 0xFF) and every E8M0 scale <= 134, so each
+   * element converts with integer moves and one bf16 multiply */
+  LTXQ_QW_MXFP8_FINITE = 1
+};
 
 /* A quantized linear layer in the reference's MLX cache layout
  * (loader/transformer_cache.py:1238-1267, 1436-1462).
@@ -77,6 +85,8 @@ typedef struct {
   int32_t bits;       /* 4 or 8 */
   int32_t group_size; /* 64 (affine), 32 (mxfp8) */
   int32_t layout;     /* LTXQ_LAYOUT_STD / LTXQ_LAYOUT_PRETRANSPOSED */
+  uint32_t flags;     /* LTXQ_QW_* (0 = none asserted) */
+  int32_t pad_;
 } ltxq_qweight;
 
 /* Per-channel vectors (AdaLN scale/shift/gate).  Element (row m, channel c)
@@ -151,6 +161,9 @@ ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t row_stride, i
 ltxq_status ltxq_quantize(const void* w_bf16, const ltxq_qweight* w, void* stream);
 /* Dequantize `w` to bf16 [N, K] (standard layout) or [K, N] (pretransposed). */
 ltxq_status ltxq_dequantize(const ltxq_qweight* w, void* out_bf16, void* stream);
+/* Scans the packed data of `w` and returns the LTXQ_QW_* flags it
+ * satisfies.  Synchronizes `stream` (one pass over the packed bytes). */
+ltxq_status ltxq_qweight_scan(const ltxq_qweight* w, uint32_t* flags_out, void* stream);
 
 /* ---- quantized linear ------------------------------------------------- */
 /* Bytes of device workspace the calls below need for these shapes. */

@@ -12,6 +12,12 @@
 //
 // MXFP8 (OCP MX v1.0): E4M3 bytes widened exactly through cvt.rn.f16x2.e4m3x2,
 // scaled by the E8M0 power of two in fp32 (exact) and rounded once to bf16.
+// For data without NaN codes and with scales <= 134 (LTXQ_QW_MXFP8_FINITE)
+// a shorter form gives the same bits: an E4M3 byte's sign and 7 low bits,
+// moved to bf16 bit 15 and bits 10:4, are the bf16 encoding of its value
+// times 2^-120 (normal codes keep exponent and mantissa, subnormal codes
+// become bf16 subnormals); one bf16 multiply by 2^(s-7) then scales and
+// rounds it once.
 #pragma once
 
 #include "common.cuh"
@@ -75,6 +81,24 @@ __device__ __forceinline__ void deq_mxfp8_word(uint32_t w, float scale, uint32_t
   const __half2 b = *reinterpret_cast<const __half2*>(&h23);
   o01 = pack_bf16x2(__low2float(a) * scale, __high2float(a) * scale);
   o23 = pack_bf16x2(__low2float(b) * scale, __high2float(b) * scale);
+}
+
+// bf16x2 broadcast of 2^(s - 7), the multiplier of the short mxfp8 form
+// (exact for E8M0 codes s <= 134)
+__device__ __forceinline__ uint32_t e8m0_fast_scale2(uint32_t s) { return ((s + 120u) << 7) * 0x00010001u; }
+
+// bytes (lo, hi) of w picked by a prmt selector whose high nibbles replicate
+// each byte's sign -> bf16x2 of (E4M3 value * 2^-120)
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2_m120(uint32_t w, uint32_t sel) {
+  uint32_t t;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(t) : "r"(w), "r"(sel));
+  return (t << 4) & 0x87F087F0u;
+}
+
+// mxfp8 short form (LTXQ_QW_MXFP8_FINITE data): s2 = e8m0_fast_scale2(s)
+__device__ __forceinline__ void deq_mxfp8_word_fast(uint32_t w, uint32_t s2, uint32_t& o01, uint32_t& o23) {
+  o01 = fma_bf16x2(e4m3x2_to_bf16x2_m120(w, 0x9180u), s2, 0x80008000u);
+  o23 = fma_bf16x2(e4m3x2_to_bf16x2_m120(w, 0xB3A2u), s2, 0x80008000u);
 }
 
 }  // namespace ltxq

@@ -44,7 +44,9 @@ constexpr int kTmaWarp = 8, kMmaWarp = 9, kThreads = 320;
 constexpr int kStagePitch = 136;  // epilogue staging row pitch in bf16 (128 + 8 pad)
 constexpr int kPrefetch = 4;      // scale/bias register prefetch distance (stages)
 
-enum QKind { kAffine8 = 0, kAffine4 = 1, kMxfp8 = 2 };
+// kMxfp8F: mxfp8 data flagged LTXQ_QW_MXFP8_FINITE (short conversion)
+enum QKind { kAffine8 = 0, kAffine4 = 1, kMxfp8 = 2, kMxfp8F = 3 };
+constexpr bool is_mx(int qk) { return qk == kMxfp8 || qk == kMxfp8F; }
 
 template <int QK>
 struct QTraits {
@@ -92,15 +94,23 @@ constexpr uint32_t kGeluLo = 0x3B00u;  // 2^-9
 constexpr uint32_t kGeluN = 0x4080u - kGeluLo;  // up to 4.0 (exclusive)
 constexpr int kGeluTabBytes = static_cast<int>(2 * kGeluN * 2);
 
-// b: bf16 bits (low 16); returns the bf16 bits of gelu_ref
-__device__ __forceinline__ uint32_t gelu_tab_bits(uint32_t b, const uint16_t* tab) {
+// b: bf16 bits (low 16), small: bf16 bits of bf16(0.5 b); returns the bf16
+// bits of gelu_ref(b)
+__device__ __forceinline__ uint32_t gelu_tab_sel(uint32_t b, uint32_t small, const uint16_t* tab) {
   const uint32_t mag = b & 0x7FFFu, neg = b >> 15;
   const uint32_t t = mag - kGeluLo;  // wraps for mag < kGeluLo
   const bool in_tab = t < kGeluN;
   const uint32_t tv = tab[in_tab ? t + neg * kGeluN : 0u];
-  const uint32_t small = f32_to_bf16(__fmul_rn(0.5f, __uint_as_float(b << 16)));
   const uint32_t big = neg ? (mag >= 0x7F80u ? 0x7FC0u : 0x8000u) : b;
   return in_tab ? tv : (mag < kGeluLo ? small : big);
+}
+
+// gelu_ref on both halves of a bf16x2 word (one paired conversion for the
+// small-input form)
+__device__ __forceinline__ uint32_t gelu_tab_x2(uint32_t b2, const uint16_t* tab) {
+  const uint32_t small2 = pack_bf16x2(__fmul_rn(0.5f, __uint_as_float(b2 << 16)),
+                                      __fmul_rn(0.5f, __uint_as_float(b2 & 0xFFFF0000u)));
+  return gelu_tab_sel(b2 & 0xFFFFu, small2 & 0xFFFFu, tab) | (gelu_tab_sel(b2 >> 16, small2 >> 16, tab) << 16);
 }
 
 // fills the table (n_threads threads, thread id tid); caller synchronizes
@@ -131,23 +141,23 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 // scattered 2-byte loads per stage.
 template <int QK>
 struct GroupCursor {
-  static constexpr int kPerBlk = QK == kMxfp8 ? 16 : 8;
+  static constexpr int kPerBlk = is_mx(QK) ? 16 : 8;
   const uint4* sb;
   const uint4* bb;
   int nblk, cur;
   uint4 cs, cb, ns, nb;
   // g0: the first group get() will be asked for
   __device__ __forceinline__ void init(const Params& p, int64_t srow, bool ok, int g0) {
-    const int gpr = QK == kMxfp8 ? p.K / 32 : p.K / p.gs;
+    const int gpr = is_mx(QK) ? p.K / 32 : p.K / p.gs;
     nblk = ok ? gpr / kPerBlk : 0;
-    sb = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.scales) + srow * (QK == kMxfp8 ? 1 : 2));
-    bb = QK == kMxfp8 ? nullptr : reinterpret_cast<const uint4*>(p.biases + srow);
+    sb = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.scales) + srow * (is_mx(QK) ? 1 : 2));
+    bb = is_mx(QK) ? nullptr : reinterpret_cast<const uint4*>(p.biases + srow);
     cur = g0 / kPerBlk;
     const uint4 z = make_uint4(0, 0, 0, 0);
     cs = cur < nblk ? __ldg(sb + cur) : z;
-    cb = (QK != kMxfp8 && cur < nblk) ? __ldg(bb + cur) : z;
+    cb = (!is_mx(QK) && cur < nblk) ? __ldg(bb + cur) : z;
     ns = cur + 1 < nblk ? __ldg(sb + cur + 1) : z;
-    nb = (QK != kMxfp8 && cur + 1 < nblk) ? __ldg(bb + cur + 1) : z;
+    nb = (!is_mx(QK) && cur + 1 < nblk) ? __ldg(bb + cur + 1) : z;
   }
   // parameters of group g (monotone, advancing by at most one block per call)
   __device__ __forceinline__ void get(int g, uint32_t& s, uint32_t& b) {
@@ -158,11 +168,11 @@ struct GroupCursor {
       cur = blk;
       if (blk + 1 < nblk) {
         ns = __ldg(sb + blk + 1);
-        if (QK != kMxfp8) nb = __ldg(bb + blk + 1);
+        if (!is_mx(QK)) nb = __ldg(bb + blk + 1);
       }
     }
     const int e = g - blk * kPerBlk;
-    if (QK == kMxfp8) {
+    if (is_mx(QK)) {
       const int wi = e >> 2;
       const uint32_t w = wi == 0 ? cs.x : wi == 1 ? cs.y : wi == 2 ? cs.z : cs.w;
       s = (w >> (8 * (e & 3))) & 0xFFu;
@@ -189,7 +199,7 @@ __device__ __forceinline__ void load_group(const Params& p, int64_t row_off_scal
     b = 0u;
     return;
   }
-  if (QK == kMxfp8) {
+  if (is_mx(QK)) {
     s = __ldg(static_cast<const uint8_t*>(p.scales) + row_off_scales + (k >> 5));
     b = 0u;
   } else {
@@ -264,14 +274,14 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
   const int n = n0 + r;
   const bool row_ok = n < p.N;
   const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
-  const int64_t srow = static_cast<int64_t>(n) * (QK == kMxfp8 ? p.K / 32 : p.K / p.gs);
+  const int64_t srow = static_cast<int64_t>(n) * (is_mx(QK) ? p.K / 32 : p.K / p.gs);
   // group parameters of stage kb live in qs/qb[kb % kPrefetch]; the K loop
   // is unrolled by kPrefetch so every register is read kPrefetch stages
   // after its load was issued (no register moves that would wait on it)
   const bool vec = p.vec_groups != 0;
   const int k_first = kb_first * BK + half * 32;
   GroupCursor<QK> gc;
-  if (vec) gc.init(p, srow, row_ok, QK == kMxfp8 ? (k_first >> 5) : k_first / p.gs);
+  if (vec) gc.init(p, srow, row_ok, is_mx(QK) ? (k_first >> 5) : k_first / p.gs);
   uint32_t qs[kPrefetch], qb[kPrefetch];
 #pragma unroll
   for (int i = 0; i < kPrefetch; ++i)
@@ -302,7 +312,7 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
       uint32_t s_cur = qs[i], b_cur = qb[i];
       if (vec) {
         const int k = k_first + kb * BK;
-        gc.get(QK == kMxfp8 ? (k >> 5) : k / p.gs, s_cur, b_cur);
+        gc.get(is_mx(QK) ? (k >> 5) : k / p.gs, s_cur, b_cur);
         if (!row_ok) {
           s_cur = 0u;
           b_cur = 0u;
@@ -330,6 +340,7 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
         // 64-byte rows, 64B swizzle: 16-byte chunk c sits at c ^ ((r >> 1) & 3);
         // this warp's half is chunks 2*half, 2*half+1
         const float fsc = QK == kMxfp8 ? e8m0_to_f32(s_cur) : 0.f;
+        const uint32_t s2 = QK == kMxfp8F ? e8m0_fast_scale2(s_cur) : 0u;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int c = half * 2 + cc;
@@ -338,6 +349,7 @@ __device__ __forceinline__ void dequant_loop(const Params& p, const Bars& bb, ui
 #pragma unroll
           for (int w4 = 0; w4 < 4; ++w4) {
             if (QK == kMxfp8) deq_mxfp8_word(wv[w4], fsc, o[cc * 8 + w4 * 2], o[cc * 8 + w4 * 2 + 1]);
+            else if (QK == kMxfp8F) deq_mxfp8_word_fast(wv[w4], s2, o[cc * 8 + w4 * 2], o[cc * 8 + w4 * 2 + 1]);
             else deq_affine8_word(wv[w4], s_cur, b_cur, o[cc * 8 + w4 * 2], o[cc * 8 + w4 * 2 + 1]);
           }
         }
@@ -606,14 +618,20 @@ struct Epi8 {
     }
     if (gated && gate_bcast) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8);
   }
-  __device__ __forceinline__ void store(const Params& p, float (&a)[8], int m, int nf, const uint16_t* gtab) {
+  // conversions to bf16 are paired (cvt.rn.bf16x2.f32), never one value at a time
+  __device__ __forceinline__ void store(const Params& p, const float (&a)[8], int m, int nf, const uint16_t* gtab) {
+    uint32_t u[4];
     if (p.bias != nullptr) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) a[k] = rbf16(__fadd_rn(a[k], bias8[k]));
+      for (int k = 0; k < 4; ++k)
+        u[k] = pack_bf16x2(__fadd_rn(a[2 * k], bias8[2 * k]), __fadd_rn(a[2 * k + 1], bias8[2 * k + 1]));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) u[k] = pack_bf16x2(a[2 * k], a[2 * k + 1]);  // exact: a is bf16-valued
     }
     if (p.epi == LTXQ_EPI_GELU) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) a[k] = __uint_as_float(gelu_tab_bits(__float_as_uint(a[k]) >> 16, gtab) << 16);
+      for (int k = 0; k < 4; ++k) u[k] = gelu_tab_x2(u[k], gtab);
     }
     const int64_t off = static_cast<int64_t>(m) * p.N + nf;
     if (gated) {
@@ -622,16 +640,18 @@ struct Epi8 {
       if (!gate_bcast) load_vec8(p.gate, vec_row(p.gate, m), nf, g8);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float pr = __fmul_rn(a[2 * k + h], g8[2 * k + h]);
-          const float rr = h ? hi_bf16(rw[k]) : lo_bf16(rw[k]);
-          a[2 * k + h] = two_round ? __fadd_rn(rr, rbf16(pr)) : __fadd_rn(pr, rr);
+        const float p0 = __fmul_rn(lo_bf16(u[k]), g8[2 * k]);
+        const float p1 = __fmul_rn(hi_bf16(u[k]), g8[2 * k + 1]);
+        const float r0 = lo_bf16(rw[k]), r1 = hi_bf16(rw[k]);
+        if (two_round) {
+          const uint32_t pr = pack_bf16x2(p0, p1);
+          u[k] = pack_bf16x2(__fadd_rn(r0, lo_bf16(pr)), __fadd_rn(r1, hi_bf16(pr)));
+        } else {
+          u[k] = pack_bf16x2(__fadd_rn(p0, r0), __fadd_rn(p1, r1));
         }
       }
     }
-    *reinterpret_cast<uint4*>(p.out + off) =
-        make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+    *reinterpret_cast<uint4*>(p.out + off) = make_uint4(u[0], u[1], u[2], u[3]);
   }
 };
 
@@ -695,7 +715,11 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
       a[6] = __fadd_rn(a[6], hi.z); a[7] = __fadd_rn(a[7], hi.w);
     }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) a[k] = rbf16(a[k]);
+    for (int k = 0; k < 8; k += 2) {
+      const uint32_t r = pack_bf16x2(a[k], a[k + 1]);  // the first rounding point, bf16(acc)
+      a[k] = lo_bf16(r);
+      a[k + 1] = hi_bf16(r);
+    }
     Epi8 e;
     e.init(p, nf);
     e.store(p, a, m, nf, gtab);
@@ -902,7 +926,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) stg[(c * 32 + j) * BM + r] = f32_to_bf16(__uint_as_float(v[j]));
+        for (int j = 0; j < 32; j += 2) {
+          const uint32_t h = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+          stg[(c * 32 + j) * BM + r] = static_cast<uint16_t>(h & 0xFFFFu);
+          stg[(c * 32 + j + 1) * BM + r] = static_cast<uint16_t>(h >> 16);
+        }
       }
       tc_fence_before();
       named_bar_sync(1, 128);
@@ -1042,7 +1070,8 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   if (ltxq_status st = check_epilogue(epi, M, N)) return st;
   if (M == 0) return LTXQ_OK;
 
-  const int qk = w.mode == LTXQ_MXFP8 ? gemm::kMxfp8 : (w.bits == 8 ? gemm::kAffine8 : gemm::kAffine4);
+  const int qk = w.mode == LTXQ_MXFP8 ? ((w.flags & LTXQ_QW_MXFP8_FINITE) ? gemm::kMxfp8F : gemm::kMxfp8)
+                                      : (w.bits == 8 ? gemm::kAffine8 : gemm::kAffine4);
   int splits = gemm::pick_splits(M, N, K);
   if (splits > 1 && (!workspace || workspace_bytes < gemm::splitk_bytes(M, N, K) ||
                      (reinterpret_cast<uintptr_t>(workspace) & 15u)))
@@ -1091,6 +1120,7 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   switch (qk) {
     case gemm::kAffine8: return gemm::launch_qk<gemm::kAffine8>(bn, tx, tw, p, stream);
     case gemm::kAffine4: return gemm::launch_qk<gemm::kAffine4>(bn, tx, tw, p, stream);
+    case gemm::kMxfp8F: return gemm::launch_qk<gemm::kMxfp8F>(bn, tx, tw, p, stream);
     default: return gemm::launch_qk<gemm::kMxfp8>(bn, tx, tw, p, stream);
   }
 }

@@ -8,6 +8,8 @@
 // (E8M0 shared exponent floor(log2(amax)) - 8, E4M3 RNE with saturation).
 // ltxq_dequantize produces the bf16 weight the GEMM consumes, bit for bit
 // (the same device functions as the GEMM's dequant warps).
+#include <mutex>
+
 #include "common.cuh"
 #include "dequant.cuh"
 
@@ -89,7 +91,7 @@ __global__ void mxfp8_quantize_kernel(const uint16_t* __restrict__ w, int64_t R,
 
 // One thread per packed word of a [R, L] packed matrix (L = packed-dim
 // length in elements) -> bf16 [R, L].
-template <int kKind>  // 0 affine8, 1 affine4, 2 mxfp8
+template <int kKind>  // 0 affine8, 1 affine4, 2 mxfp8, 3 mxfp8 flagged LTXQ_QW_MXFP8_FINITE
 __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const void* __restrict__ scales,
                                   const uint16_t* __restrict__ biases, int64_t R, int64_t L, int gs,
                                   uint16_t* __restrict__ out) {
@@ -107,6 +109,10 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const void* _
       const float sc = e8m0_to_f32(static_cast<const uint8_t*>(scales)[g]);
       uint32_t o01, o23;
       deq_mxfp8_word(w, sc, o01, o23);
+      *reinterpret_cast<uint2*>(out + row * L + k0) = make_uint2(o01, o23);
+    } else if (kKind == 3) {
+      uint32_t o01, o23;
+      deq_mxfp8_word_fast(w, e8m0_fast_scale2(static_cast<const uint8_t*>(scales)[g]), o01, o23);
       *reinterpret_cast<uint2*>(out + row * L + k0) = make_uint2(o01, o23);
     } else {
       const uint32_t s2 = bcast_bf16x2(static_cast<const uint16_t*>(scales)[g]);
@@ -149,6 +155,29 @@ ltxq_status check_qweight(const ltxq_qweight& w, bool need_data, int64_t* R, int
   }
   return LTXQ_OK;
 }
+
+// LTXQ_QW_MXFP8_FINITE check: sets *bad if any E4M3 byte is a NaN code or
+// any E8M0 scale exceeds 134.  `vec`: codes are 16-byte aligned (16-byte
+// loads for all but the tail).
+__global__ void mxfp8_scan_kernel(const uint8_t* __restrict__ codes, int64_t n_codes, bool vec,
+                                  const uint8_t* __restrict__ scales, int64_t n_scales, unsigned int* bad) {
+  bool b = false;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t n16 = vec ? n_codes / 16 : 0;
+  for (int64_t i = t0; i < n16; i += stride) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(codes) + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) b |= (((w[j] & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u) != 0u;
+  }
+  for (int64_t i = n16 * 16 + t0; i < n_codes; i += stride) b |= (codes[i] & 0x7Fu) == 0x7Fu;
+  for (int64_t i = t0; i < n_scales; i += stride) b |= scales[i] > 134u;
+  if (__syncthreads_or(b) && threadIdx.x == 0) atomicOr(bad, 1u);
+}
+
+__device__ unsigned int g_scan_word = 0;
+static std::mutex g_scan_mutex;
 
 static unsigned grid_for(int64_t work, int threads) {
   const int64_t want = (work + threads - 1) / threads;
@@ -193,7 +222,9 @@ ltxq_status ltxq_dequantize(const ltxq_qweight* w, void* out_bf16, void* stream)
   auto* wq = static_cast<const uint32_t*>(w->weight);
   auto* bi = static_cast<const uint16_t*>(w->biases);
   auto* o = static_cast<uint16_t*>(out_bf16);
-  if (w->mode == LTXQ_MXFP8) {
+  if (w->mode == LTXQ_MXFP8 && (w->flags & LTXQ_QW_MXFP8_FINITE)) {
+    dequantize_kernel<3><<<grid_for(R * L / 4, threads), threads, 0, s>>>(wq, w->scales, bi, R, L, w->group_size, o);
+  } else if (w->mode == LTXQ_MXFP8) {
     dequantize_kernel<2><<<grid_for(R * L / 4, threads), threads, 0, s>>>(wq, w->scales, bi, R, L, w->group_size, o);
   } else if (w->bits == 8) {
     dequantize_kernel<0><<<grid_for(R * L / 4, threads), threads, 0, s>>>(wq, w->scales, bi, R, L, w->group_size, o);
@@ -201,6 +232,32 @@ ltxq_status ltxq_dequantize(const ltxq_qweight* w, void* out_bf16, void* stream)
     dequantize_kernel<1><<<grid_for(R * L / 8, threads), threads, 0, s>>>(wq, w->scales, bi, R, L, w->group_size, o);
   }
   return launch_check("dequantize launch");
+}
+
+ltxq_status ltxq_qweight_scan(const ltxq_qweight* w, uint32_t* flags_out, void* stream) {
+  using namespace ltxq;
+  if (!w || !flags_out) return fail(LTXQ_ERR_INVALID, "qweight_scan: NULL argument");
+  int64_t R, L;
+  if (ltxq_status st = check_qweight(*w, true, &R, &L)) return st;
+  *flags_out = 0;
+  if (w->mode != LTXQ_MXFP8) return LTXQ_OK;
+  std::lock_guard<std::mutex> lock(g_scan_mutex);  // one scan word per device
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* word = nullptr;
+  if (ltxq_status st = cuda_check(cudaGetSymbolAddress(&word, g_scan_word), "scan word")) return st;
+  if (ltxq_status st = cuda_check(cudaMemsetAsync(word, 0, sizeof(unsigned int), s), "scan reset")) return st;
+  const int64_t n_codes = R * L, n_scales = R * (L / w->group_size);
+  const bool al = (reinterpret_cast<uintptr_t>(w->weight) & 15u) == 0;
+  mxfp8_scan_kernel<<<grid_for(al ? n_codes / 16 + 1 : n_codes, 256), 256, 0, s>>>(
+      static_cast<const uint8_t*>(w->weight), n_codes, al, static_cast<const uint8_t*>(w->scales), n_scales,
+      static_cast<unsigned int*>(word));
+  if (ltxq_status st = launch_check("qweight scan launch")) return st;
+  unsigned int bad = 0;
+  if (ltxq_status st = cuda_check(cudaMemcpyAsync(&bad, word, sizeof(bad), cudaMemcpyDeviceToHost, s), "scan read"))
+    return st;
+  if (ltxq_status st = cuda_check(cudaStreamSynchronize(s), "scan sync")) return st;
+  *flags_out = bad ? 0u : static_cast<uint32_t>(LTXQ_QW_MXFP8_FINITE);
+  return LTXQ_OK;
 }
 
 }  // extern "C"

@@ -19,6 +19,7 @@ BF16, F32 = 0, 1
 NORM_NONE, NORM_RMS, NORM_LAYER = 0, 1, 2
 AFFINE, MXFP8 = 0, 1
 LAYOUT_STD, LAYOUT_PRETRANSPOSED = 0, 1
+QW_MXFP8_FINITE = 1
 EPI_NONE, EPI_GELU, EPI_GATED_RESIDUAL, EPI_GATE_THEN_ADD = 0, 1, 2, 3
 GATED_ADD, GATE_THEN_ADD = 0, 1
 
@@ -35,6 +36,8 @@ class QWeight(ctypes.Structure):
         ("bits", c_int32),
         ("group_size", c_int32),
         ("layout", c_int32),
+        ("flags", ctypes.c_uint32),
+        ("pad_", c_int32),
     ]
 
 
@@ -62,6 +65,7 @@ SIGNATURES = {
     "ltxq_version": (c_char_p, []),
     "ltxq_device_error": (c_int32, [POINTER(c_int32)]),
     "ltxq_launch_count": (ctypes.c_uint64, []),
+    "ltxq_qweight_scan": (c_int32, [POINTER(QWeight), POINTER(ctypes.c_uint32), c_void_p]),
     "ltxq_adaln_modulate": (c_int32, [c_void_p, c_int32, c_int64, c_int64, POINTER(Prologue), c_void_p, c_void_p]),
     "ltxq_gated_add": (c_int32, [c_void_p, c_void_p, POINTER(Vec), c_int64, c_int64, c_int32, c_void_p, c_void_p]),
     "ltxq_head_gate": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),

@@ -9,6 +9,12 @@ with ms and TFLOP/s (2*M*N*K / time) per mode; the L2 is flushed (256 MiB
 write) before every timed launch and each number is the median of
 ``--iters`` CUDA-event timings.  ``--iters 1 --warmup 1`` gives a short
 launch sequence suitable for an ncu capture.
+
+``--graph`` times device work only: the calls are captured in a CUDA graph
+over enough copies of the packed weight to exceed the L2 (each call reads
+its weight from HBM, as in a block), and the graph's time is divided by the
+number of calls.  Without it, a GEMM shorter than the host-side cost of one
+call (Python, ctypes, tensor-map encoding, launch) measures that cost.
 """
 
 from __future__ import annotations
@@ -43,6 +49,30 @@ def _time(fn, flush, iters, warmup):
     return ts[len(ts) // 2]
 
 
+def _time_graph(fns, iters):
+    """Device time per call of a list of calls captured back to back."""
+    for f in fns:  # first calls do one-time host work (data-flag scans) outside the capture
+        f()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in fns:
+            f()
+    graph.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b) / len(fns))
+    ts.sort()
+    del graph
+    return ts[len(ts) // 2]
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(DEFAULT_SHAPES))
@@ -52,6 +82,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cublas", action="store_true")
     ap.add_argument("--no-split-k", action="store_true", help="give the GEMM no split-K workspace")
+    ap.add_argument("--graph", action="store_true", help="device time per call from a captured CUDA graph")
     args = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
@@ -75,7 +106,18 @@ def main(argv=None):
             kw = {"gelu": True} if args.epilogue == "gelu" else (
                 {"residual": res, "gate": gate} if args.epilogue == "gated" else {})
             kw["split_k"] = not args.no_split_k
-            t = _time(lambda: ql(x, **kw), flush, args.iters, args.warmup)
+            if args.graph:
+                wbytes = ql.weight.numel() * ql.weight.element_size()
+                copies = max(1, min(64, -(-(256 << 20) // max(wbytes, 1))))
+                qls = [ql] + [QuantizedLinear(ql.weight.clone(), ql.scales.clone(),
+                                              None if ql.biases is None else ql.biases.clone(), ql.bias,
+                                              group_size=ql.group_size, bits=ql.bits, mode=ql.mode,
+                                              in_features=ql.in_features, out_features=ql.out_features)
+                              for _ in range(copies - 1)]
+                t = _time_graph([lambda q=q: q(x, **kw) for q in qls], args.iters)
+                row["graph_calls"] = copies
+            else:
+                t = _time(lambda: ql(x, **kw), flush, args.iters, args.warmup)
             row[name] = {"ms": t, "tflops": flops / t / 1e9}
         print(json.dumps(row), flush=True)
     err = _lib.device_error()

@@ -97,7 +97,26 @@ class QuantizedLinear:
             self.biases.data_ptr() if self.biases is not None else None,
             self.bias.data_ptr() if self.bias is not None else None,
             self.out_features, self.in_features, _MODE[self.mode], self.bits, self.group_size,
-            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD)
+            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD, self.data_flags())
+
+    def data_flags(self) -> int:
+        """LTXQ_QW_* flags of the packed data (``ltxq_qweight_scan``), cached
+        until the weight or scale tensors change (torch's in-place version
+        counters).  ``fast_path = False`` asserts none (the general
+        conversion everywhere)."""
+        if self.mode != "mxfp8" or not getattr(self, "fast_path", True):
+            return 0
+        key = (self.weight.data_ptr(), self.weight._version, self.scales.data_ptr(), self.scales._version)
+        cached = getattr(self, "_flags_cache", None)
+        if cached is None or cached[0] != key:
+            q = _lib.QWeight(self.weight.data_ptr(), self.scales.data_ptr(), None, None, self.out_features,
+                             self.in_features, _MODE[self.mode], self.bits, self.group_size,
+                             _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD, 0)
+            flags = ctypes.c_uint32(0)
+            _lib.check(_lib.load().ltxq_qweight_scan(ctypes.byref(q), ctypes.byref(flags), _stream()), "qweight_scan")
+            cached = (key, int(flags.value))
+            self._flags_cache = cached
+        return cached[1]
 
     def dequantize(self) -> torch.Tensor:
         """bf16 weight: [out, in] (standard) or [in, out] (pretransposed)."""

@@ -94,3 +94,58 @@ def test_av_block_matches_oracle(cuda, mode, bits):
         mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
         assert mar <= 2e-2 and cos >= 0.9995, f"{what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
     assert ltxq._lib.device_error() == 0
+
+
+def test_step_graph_replay_matches_eager(cuda):
+    """A two-block step captured by ltxq.graph.StepGraph and replayed on new
+    inputs (copied into the captured input tensors) gives the eager step's
+    bits."""
+    import torch
+
+    import ltxq
+    from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
+    from ltxq.graph import StepGraph
+
+    video = StreamConfig(1024, 8, 128, 1024)
+    audio = StreamConfig(512, 8, 64, 512)
+    T, A, L = 96, 40, 32
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    blocks = [BasicAVTransformerBlock.random(gen, "cuda", mode="mxfp8", video=video, audio=audio) for _ in range(2)]
+
+    def rnd(*shape, std=1.0, dtype=torch.float32):
+        return (torch.randn(*shape, generator=gen, device="cuda") * std).to(dtype)
+
+    def rope(heads, t, d):
+        ang = torch.rand(1, heads, t, d // 2, generator=gen, device="cuda") * 6.28
+        return torch.cos(ang), torch.sin(ang)
+
+    def args(cfg, t):
+        return TransformerArgs(x=rnd(1, t, cfg.dim, dtype=torch.bfloat16),
+                               context=rnd(1, L, cfg.context_dim, dtype=torch.bfloat16),
+                               timesteps=rnd(1, 1, 9, cfg.dim, std=0.1), positional_embeddings=rope(cfg.heads, t, cfg.d_head),
+                               cross_positional_embeddings=rope(audio.heads, t, audio.d_head),
+                               cross_scale_shift_timestep=rnd(1, 1, 4, cfg.dim, std=0.1),
+                               cross_gate_timestep=rnd(1, 1, 1, cfg.dim, std=0.1),
+                               prompt_timestep=rnd(1, 1, 2, cfg.dim, std=0.1))
+
+    v, a = args(video, T), args(audio, A)
+
+    def step(v, a):
+        for b in blocks:
+            v, a = b(v, a)
+        return v, a
+
+    g = StepGraph(step, v, a)
+    assert g.launches > 0
+    new_v = rnd(1, T, video.dim, dtype=torch.bfloat16)
+    new_a = rnd(1, A, audio.dim, dtype=torch.bfloat16)
+    v.x.copy_(new_v)
+    a.x.copy_(new_a)
+    gv, ga = g.replay()
+    gv_x, ga_x = gv.x.clone(), ga.x.clone()
+    ev, ea = step(v, a)
+    assert torch.equal(gv_x.view(torch.int16), ev.x.view(torch.int16))
+    assert torch.equal(ga_x.view(torch.int16), ea.x.view(torch.int16))
+    g.release()
+    assert ltxq._lib.device_error() == 0

@@ -119,9 +119,55 @@ def test_mxfp8_dequantize_bit_exact(cuda):
     q["weight"] = wb.reshape(256, 128, 4).copy().view(np.uint32).reshape(256, 128)
     q["scales"][1, :8] = np.array([0, 1, 100, 127, 130, 200, 240, 246], dtype=np.uint8)
     ql = qlinear_from_oracle(q)
+    assert ql.data_flags() == 0  # scales above 134: the general conversion
     deq = ql.dequantize()
     ref = oq.dequantize(q, 512)
     assert np.array_equal(bf16_bits(deq), f32_to_bf16_bits(ref))
+
+
+def test_mxfp8_short_conversion_exhaustive(cuda):
+    """Every finite E4M3 code under every E8M0 scale the short conversion
+    accepts (0..134, bf16-subnormal results included) dequantizes to the
+    oracle's bits; the same data with NaN codes takes the general path."""
+    from ltxq import _lib
+
+    rows = 135
+    codes = np.tile(np.arange(256, dtype=np.uint8), (rows, 1))
+    codes[(codes & 0x7F) == 0x7F] = 0x00
+    scales = np.repeat(np.arange(rows, dtype=np.uint8)[:, None], 256 // 32, axis=1)
+    q = {"weight": codes.reshape(rows, 64, 4).copy().view(np.uint32).reshape(rows, 64), "scales": scales,
+         "group_size": 32, "bits": 8, "mode": "mxfp8"}
+    ql = qlinear_from_oracle(q)
+    assert ql.data_flags() == _lib.QW_MXFP8_FINITE
+    ref = f32_to_bf16_bits(oq.dequantize(q, 256))
+    assert np.array_equal(bf16_bits(ql.dequantize()), ref)
+    ql.fast_path = False
+    assert np.array_equal(bf16_bits(ql.dequantize()), ref)
+
+
+@pytest.mark.parametrize("plant", ["none", "nan_code_pos", "nan_code_neg", "scale_135", "scale_134"])
+def test_qweight_scan_flags(cuda, plant):
+    from ltxq import _lib
+
+    W = normal_bf16(rng(5), (64, 1024), 0.05)
+    q = oq.quantize(W, "mxfp8")
+    wb = q["weight"].view(np.uint8).reshape(64, 1024)
+    if plant == "nan_code_pos":
+        wb[63, 1023] = 0x7F
+    elif plant == "nan_code_neg":
+        wb[17, 5] = 0xFF
+    elif plant == "scale_135":
+        q["scales"][40, 31] = 135
+    elif plant == "scale_134":
+        q["scales"][40, 31] = 134
+    q["weight"] = wb.reshape(64, 256, 4).copy().view(np.uint32).reshape(64, 256)
+    ql = qlinear_from_oracle(q)
+    want = _lib.QW_MXFP8_FINITE if plant in ("none", "scale_134") else 0
+    assert ql.data_flags() == want
+    got, ref = bf16_bits(ql.dequantize()), f32_to_bf16_bits(oq.dequantize(q, 1024))
+    nan = lambda b: ((b & 0x7F80) == 0x7F80) & ((b & 0x7F) != 0)  # noqa: E731  (any NaN payload)
+    assert np.array_equal(nan(got), nan(ref))
+    assert np.array_equal(got[~nan(ref)], ref[~nan(ref)])
 
 
 # ----------------------------------------------------------------- elementwise
@@ -433,14 +479,15 @@ def test_qk_norm_rope_matches_oracle(cuda, heads, d, with_pe, strided):
     assert_close(out, from_dev_bf16(tref[0]), "torch fp32 reference")
 
 
-@pytest.mark.parametrize("mode,bits", [("mxfp8", 8), ("affine", 8), ("affine", 4)])
+@pytest.mark.parametrize("mode,bits,smax", [("mxfp8", 8, 134), ("mxfp8", 8, 246), ("affine", 8, 0), ("affine", 4, 0)])
 @pytest.mark.parametrize("M,split_k", [(256, True), (256, False), (128, False)])
-def test_gemm_dequant_exact_through_identity(cuda, mode, bits, M, split_k):
+def test_gemm_dequant_exact_through_identity(cuda, mode, bits, smax, M, split_k):
     """x = identity makes y[m, n] = dequant(W)[n, m] with one nonzero product
     per output, so the in-GEMM dequantization is checked bit for bit over
     every code: mxfp8 rows carry all finite E4M3 codes under E8M0 scales
-    10..246 (normal bf16 results, no overflow), affine rows all 2^bits codes
-    under varied bf16 scales / biases."""
+    10..smax (normal bf16 results, no overflow; smax 134 takes the short
+    conversion, 246 the general one), affine rows all 2^bits codes under
+    varied bf16 scales / biases."""
     torch = _torch()
     ltxq = _ltxq()
     K = N = M
@@ -450,7 +497,7 @@ def test_gemm_dequant_exact_through_identity(cuda, mode, bits, M, split_k):
         codes = ((np.arange(K, dtype=np.uint32)[None, :] + 128 * (np.arange(N, dtype=np.uint32)[:, None] % 2))
                  % 256).astype(np.uint8)
         codes[(codes & 0x7F) == 0x7F] = 0  # NaN codes: 0 * NaN would poison the row sums
-        scales = (10 + (np.arange(N * (K // 32)) * 7) % 237).astype(np.uint8).reshape(N, K // 32)
+        scales = (10 + (np.arange(N * (K // 32)) * 7) % (smax - 9)).astype(np.uint8).reshape(N, K // 32)
         q = {"weight": codes.reshape(N, K // 4, 4).copy().view(np.uint32).reshape(N, K // 4), "scales": scales,
              "group_size": 32, "bits": 8, "mode": "mxfp8"}
     else:
@@ -463,6 +510,8 @@ def test_gemm_dequant_exact_through_identity(cuda, mode, bits, M, split_k):
              "mode": "affine"}
     deq = oq.dequantize(q, K)
     ql = qlinear_from_oracle(q, None, N, K)
+    if mode == "mxfp8":
+        assert ql.data_flags() == (1 if smax <= 134 else 0)
     eye = torch.eye(M, K, dtype=torch.bfloat16, device="cuda")
     y = bf16_bits(ql(eye, split_k=split_k))
     want = f32_to_bf16_bits(deq.T)
