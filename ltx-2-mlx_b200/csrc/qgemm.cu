@@ -64,8 +64,18 @@ struct Params {
   const uint16_t* residual;
   uint16_t* out;
   unsigned int* err;
-  int splits;      // K splits (pair kernel); > 1: fp32 partials go to `partial`
-  float* partial;  // [splits][M][N] fp32, summed by splitk_reduce_kernel
+  // pair-kernel schedule: output tiles [0, dp_tiles) are computed whole; each
+  // later tile is split into `splits` K ranges whose fp32 partials go to
+  // `partial` ([tile - dp_tiles][split][256 tokens][256 features], tile-local)
+  // and are summed by splitk_reduce_kernel
+  int dp_tiles;
+  int splits;
+  float* partial;
+};
+
+// output tiles of the pair kernel, how many stay whole, K splits of the rest
+struct Sched {
+  int tiles, dp, splits;
 };
 
 // gelu_approx with the reference's per-op bf16 rounding (feed_forward.py:8-14;
@@ -682,23 +692,31 @@ __device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const u
   }
 }
 
-// Split-K: out[m, nf..nf+8) from the fp32 partial sums of the K splits,
-// added in split order (deterministic), rounded to bf16, then the same
-// epilogue as the unsplit kernel.  One thread per (token, 8 features).
+// Split tiles: out[m, nf..nf+8) from the fp32 partial sums of a split
+// tile's K ranges, added in split order (deterministic), rounded to bf16,
+// then the same epilogue as whole tiles.  One thread per (split tile,
+// token row, 8 features).
+constexpr int kPairTile = 256;  // features and tokens per pair-kernel tile
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
   __shared__ uint16_t gtab[2 * kGeluN];
   if (p.epi == LTXQ_EPI_GELU) {
     gelu_tab_fill(gtab, threadIdx.x, blockDim.x);
     __syncthreads();
   }
-  const int chunks = p.N / 8;
-  const int64_t items = static_cast<int64_t>(p.M) * chunks;
-  const size_t plane = static_cast<size_t>(p.M) * p.N;
+  const int n_pt = (p.N + kPairTile - 1) / kPairTile;
+  const int tiles = n_pt * ((p.M + kPairTile - 1) / kPairTile);
+  const int64_t items = static_cast<int64_t>(tiles - p.dp_tiles) * kPairTile * (kPairTile / 8);
+  constexpr size_t kTileElems = static_cast<size_t>(kPairTile) * kPairTile;
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int m = static_cast<int>(it / chunks);
-    const int nf = static_cast<int>(it - static_cast<int64_t>(m) * chunks) * 8;
-    const float* src = p.partial + static_cast<size_t>(m) * p.N + nf;
+    const int ti = static_cast<int>(it / (kPairTile * (kPairTile / 8)));
+    const int rem = static_cast<int>(it - static_cast<int64_t>(ti) * (kPairTile * (kPairTile / 8)));
+    const int j = rem / (kPairTile / 8), f = (rem % (kPairTile / 8)) * 8;
+    const int tile = p.dp_tiles + ti;
+    const int m = (tile / n_pt) * kPairTile + j;
+    const int nf = (tile % n_pt) * kPairTile + f;
+    if (m >= p.M || nf >= p.N) continue;
+    const float* src = p.partial + static_cast<size_t>(ti) * p.splits * kTileElems + j * kPairTile + f;
     float a[8];
     {
       const float4 lo = __ldcg(reinterpret_cast<const float4*>(src));
@@ -707,8 +725,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
       a[4] = hi.x; a[5] = hi.y; a[6] = hi.z; a[7] = hi.w;
     }
     for (int sp = 1; sp < p.splits; ++sp) {
-      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src + sp * plane));
-      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + sp * plane + 4));
+      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src + sp * kTileElems));
+      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + sp * kTileElems + 4));
       a[0] = __fadd_rn(a[0], lo.x); a[1] = __fadd_rn(a[1], lo.y);
       a[2] = __fadd_rn(a[2], lo.z); a[3] = __fadd_rn(a[3], lo.w);
       a[4] = __fadd_rn(a[4], hi.x); a[5] = __fadd_rn(a[5], hi.y);
@@ -750,19 +768,28 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int num_kb = p.K / BK;
   const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
   const int tiles = n_pt * ((p.M + BN - 1) / BN);
-  // work unit u = (tile u / splits, K stages [kb_lo, kb_hi) of split u % splits);
-  // every role walks the same units in the same order
+  // work unit u < dp: whole tile u; u >= dp: K range sp of tile
+  // dp + (u - dp) / splits.  Every role walks the same units in the same order.
+  const int dp = p.dp_tiles;
   const int splits = p.splits;
-  const int units = tiles * splits;
+  const int units = dp + (tiles - dp) * splits;
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int n_clusters = static_cast<int>(gridDim.x >> 1);
   auto unit = [&](int u, int& n0, int& m0, int& sp, int& kb_lo, int& kb_hi) {
-    const int tile = u / splits;
-    sp = u - tile * splits;
+    int tile;
+    if (u < dp) {
+      tile = u;
+      sp = -1;
+      kb_lo = 0;
+      kb_hi = num_kb;
+    } else {
+      tile = dp + (u - dp) / splits;
+      sp = (u - dp) - (tile - dp) * splits;
+      kb_lo = sp * num_kb / splits;
+      kb_hi = (sp + 1) * num_kb / splits;
+    }
     n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
     m0 = (tile / n_pt) * BN;
-    kb_lo = sp * num_kb / splits;
-    kb_hi = (sp + 1) * num_kb / splits;
   };
 
   if (threadIdx.x == 0) {
@@ -896,9 +923,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       unit(u, n0, m0, sp, kb_lo, kb_hi);
       if (!mbar_wait(bb.acc_full, it & 1, bb.abort_flag, p.err)) break;
       tc_fence_after();
-      if (splits > 1) {
-        // fp32 partial of split sp: TMEM lane r = feature n0 + r, column = token
-        float* dst = p.partial + static_cast<size_t>(sp) * p.M * p.N;
+      if (sp >= 0) {
+        // fp32 partial of split sp of this tile: TMEM lane r = feature n0 + r,
+        // column = token; tile-local [token][feature] layout
+        const int tile_i = (u - dp) / splits;
+        float* dst = p.partial + (static_cast<size_t>(tile_i) * splits + sp) * (kPairTile * kPairTile) +
+                     static_cast<int>(rank) * BM + r;
         const int n = n0 + r;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -910,7 +940,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int m = m0 + c * 32 + j;
-              if (m < p.M) dst[static_cast<size_t>(m) * p.N + n] = __uint_as_float(v[j]);
+              if (m < p.M) dst[(c * 32 + j) * kPairTile] = __uint_as_float(v[j]);
             }
           }
         }
@@ -967,7 +997,8 @@ static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, con
   ltxq_status st =
       cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem), "smem attribute");
   if (st) return st;
-  const int units = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + 255) / 256) * p.splits;
+  const int tiles = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + 255) / 256);
+  const int units = p.dp_tiles + (tiles - p.dp_tiles) * p.splits;
   const int max_clusters = num_sms() / 2;
   const int clusters = units < max_clusters ? units : max_clusters;
   cudaLaunchConfig_t cfg = {};
@@ -985,31 +1016,39 @@ static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, con
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
   if (e == cudaSuccess) note_launch();
   if (ltxq_status st = cuda_check(e, "qgemm pair launch")) return st;
-  if (p.splits == 1) return LTXQ_OK;
-  const int64_t items = static_cast<int64_t>(p.M) * (p.N / 8);
+  if (p.dp_tiles >= tiles) return LTXQ_OK;
+  const int64_t items = static_cast<int64_t>(tiles - p.dp_tiles) * kPairTile * (kPairTile / 8);
   const int64_t want = (items + 255) / 256;
   const int cap = num_sms() * 8;
   splitk_reduce_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(p);
   return launch_check("split-K reduce launch");
 }
 
-// K splits of the pair kernel: used only when the output tiles alone would
-// leave more than half of the clusters idle (few tokens: the audio stream,
-// small batches).  Each split keeps at least two K stages.
-int pick_splits(int64_t M, int64_t N, int64_t K) {
-  const int64_t tiles = ((N + 2 * BM - 1) / (2 * BM)) * ((M + 255) / 256);
-  const int64_t clusters = num_sms() / 2;
-  const int64_t num_kb = K / BK;
-  if (tiles * 2 > clusters) return 1;
-  int64_t sp = clusters / tiles;
+// Pair-kernel schedule.  The clusters take the output tiles in waves; when
+// the last wave would leave at least half of the clusters idle (few tokens:
+// the audio stream, or the video rows of one of several GPUs), its tiles are
+// split along K so that every cluster gets a share: the first tiles stay
+// whole (dp), the rest split into `splits` K ranges (>= 2 stages each).
+Sched plan_schedule(int64_t M, int64_t N, int64_t K) {
+  const int tiles = static_cast<int>(((N + 2 * BM - 1) / (2 * BM)) * ((M + 255) / 256));
+  Sched sc{tiles, tiles, 1};
+  const int clusters = num_sms() / 2;
+  const int num_kb = static_cast<int>(K / BK);
+  if (clusters <= 0) return sc;
+  const int rem = tiles % clusters;
+  if (rem == 0 || rem * 2 > clusters) return sc;
+  int sp = clusters / rem;
   if (sp > num_kb / 2) sp = num_kb / 2;
   if (sp > 32) sp = 32;
-  return sp < 2 ? 1 : static_cast<int>(sp);
+  if (sp < 2) return sc;
+  sc.dp = tiles - rem;
+  sc.splits = sp;
+  return sc;
 }
 
 size_t splitk_bytes(int64_t M, int64_t N, int64_t K) {
-  const int sp = pick_splits(M, N, K);
-  return sp > 1 ? static_cast<size_t>(sp) * static_cast<size_t>(M) * static_cast<size_t>(N) * 4 : 0;
+  const Sched sc = plan_schedule(M, N, K);
+  return sc.splits > 1 ? static_cast<size_t>(sc.tiles - sc.dp) * sc.splits * kPairTile * kPairTile * 4 : 0;
 }
 
 template <int QK>
@@ -1072,10 +1111,11 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
 
   const int qk = w.mode == LTXQ_MXFP8 ? ((w.flags & LTXQ_QW_MXFP8_FINITE) ? gemm::kMxfp8F : gemm::kMxfp8)
                                       : (w.bits == 8 ? gemm::kAffine8 : gemm::kAffine4);
-  int splits = gemm::pick_splits(M, N, K);
-  if (splits > 1 && (!workspace || workspace_bytes < gemm::splitk_bytes(M, N, K) ||
-                     (reinterpret_cast<uintptr_t>(workspace) & 15u)))
-    splits = 1;
+  gemm::Sched sched = gemm::plan_schedule(M, N, K);
+  if (sched.splits > 1 && (!workspace || workspace_bytes < gemm::splitk_bytes(M, N, K) ||
+                           (reinterpret_cast<uintptr_t>(workspace) & 15u)))
+    sched = gemm::Sched{sched.tiles, sched.tiles, 1};
+  const int splits = sched.splits;
   const int bn = splits > 1 ? 256 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
   CUtensorMap tx, tw;
   const uint32_t xbox = bn == 256 ? 128 : static_cast<uint32_t>(bn);  // the pair kernel stages half a tile per CTA
@@ -1115,6 +1155,7 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   }
   p.err = dev_error_word();
   if (!p.err) return fail(LTXQ_ERR_CUDA, "qlinear: device error word unavailable");
+  p.dp_tiles = sched.dp;
   p.splits = splits;
   p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   switch (qk) {
@@ -1131,8 +1172,9 @@ static size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
 
 extern "C" {
 
-// The workspace holds the split-K partials of a GEMM with few tokens
-// (fp32 [splits][M][N]); calls given less run that GEMM unsplit.
+// The workspace holds the fp32 partials of the GEMM's K-split tiles (a GEMM
+// whose last wave of tiles would leave most clusters idle); calls given less
+// run every tile whole.
 size_t ltxq_qlinear_workspace_size(int64_t M, const ltxq_qweight* w) {
   if (!w || M <= 0) return 0;
   return ltxq::align_up(ltxq::gemm::splitk_bytes(M, w->n_out, w->k_in));

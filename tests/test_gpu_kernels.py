@@ -519,3 +519,31 @@ def test_gemm_dequant_exact_through_identity(cuda, mode, bits, smax, M, split_k)
     both_zero = ((y & 0x7FFF) == 0) & ((want & 0x7FFF) == 0)
     diff = (y != want) & ~both_zero
     assert not diff.any(), (np.argwhere(diff)[:5], y[diff][:5], want[diff][:5])
+
+
+@pytest.mark.parametrize("epi", ["none", "gelu", "gated_per_token"])
+def test_qlinear_hybrid_schedule(cuda, epi):
+    """1152 tokens x 4096 features: 80 output tiles on 74 clusters, so the
+    first tiles run whole and the last ones are split along K (the video rows
+    of one rank of 8).  Matches the oracle, equals the unsplit run to within
+    fp32 summation order, and repeats bit for bit."""
+    torch = _torch()
+    M, K, N = 1152, 1536, 4096
+    x, q, deq, bias = _gemm_case(M, K, N, "mxfp8", 8, seed=40)
+    ql = qlinear_from_oracle(q, bias, N, K)
+    xd = to_dev_bf16(x)
+    kw, ref = {}, ro.linear(x, deq, bias)
+    if epi == "gelu":
+        kw, ref = {"gelu": True}, ro.gelu_approx(ref)
+    elif epi == "gated_per_token":
+        g = rng(41)
+        res = normal_bf16(g, (M, N))
+        gate = normal_f32(g, (M, N), 0.5)
+        kw = {"residual": to_dev_bf16(res), "gate": torch.from_numpy(gate).cuda()}
+        ref = ro.gated_add(res, ref, gate)
+    a = ql(xd, **kw)
+    b = ql(xd, **kw)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert_close(from_dev_bf16(a), ref, f"hybrid {epi}")
+    whole = from_dev_bf16(ql(xd, split_k=False, **kw))
+    assert (ulp_diff_bf16(from_dev_bf16(a), whole) > 0).mean() < 0.02
