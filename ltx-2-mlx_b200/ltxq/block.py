@@ -275,6 +275,15 @@ class BasicAVTransformerBlock:
                b_std: float = 0.01, t_std: float = 0.1) -> "BasicAVTransformerBlock":
         """Random-init block: weights ~N(0, w_std) quantized on the GPU, biases
         ~N(0, b_std), AdaLN tables ~N(0, t_std), QK-norm weights 1 + N(0, t_std)."""
+        lin, tabs = cls.random_parts(gen, device, mode, bits, group_size, video, audio, w_std, b_std, t_std)
+        return cls(lin, tabs, video, audio)
+
+    @staticmethod
+    def random_parts(gen: torch.Generator, device, mode: str = "affine", bits: int = 8, group_size: int | None = None,
+                     video: StreamConfig = VIDEO_22B, audio: StreamConfig = AUDIO_22B, w_std: float = 0.02,
+                     b_std: float = 0.01, t_std: float = 0.1):
+        """The per-projection quantized linears (cache base name ->
+        QuantizedLinear) and fp32 tables of a random block."""
         lin = {}
         for name, (n, k) in linear_specs(video, audio).items():
             w = (torch.randn(n, k, generator=gen, device=device) * w_std).to(torch.bfloat16)
@@ -285,7 +294,7 @@ class BasicAVTransformerBlock:
         for name, shape in table_specs(video, audio).items():
             t = torch.randn(*shape, generator=gen, device=device) * t_std
             tabs[name] = (1.0 + t) if name.endswith("norm.weight") else t
-        return cls(lin, tabs, video, audio)
+        return lin, tabs
 
     def quantized_modules(self) -> list[QuantizedLinear]:
         mods = list(self.linears.values())

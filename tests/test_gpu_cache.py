@@ -1,0 +1,63 @@
+"""GPU: blocks loaded from a cache on disk (the reference's key scheme,
+shards, metadata.json) compute the same bits as the blocks they were written
+from."""
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("mode,bits,payload_mode", [("mxfp8", 8, "mxfp8-blocks"), ("affine", 8, "off")])
+def test_blocks_from_cache_match_source(cuda, tmp_path, mode, bits, payload_mode):
+    import torch
+
+    import ltxq
+    from ltxq import cache as C
+    from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
+
+    video = StreamConfig(1024, 8, 128, 1024)
+    audio = StreamConfig(512, 8, 64, 512)
+    T, A, L = 80, 40, 24
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11)
+    parts = [BasicAVTransformerBlock.random_parts(gen, "cuda", mode=mode, bits=bits, video=video, audio=audio)
+             for _ in range(2)]
+    state = {}
+    for i, (lin, tabs) in enumerate(parts):
+        state.update(C.block_state(i, lin, tabs))
+    cache_file = tmp_path / "transformer.safetensors"
+    shards = C.write_cache_weights(cache_file, state, shard_limit_bytes=8 << 20)
+    assert len(shards) > 1
+    extra = {"video_ff_quantize_bits": bits} if mode == "affine" else {}
+    C.write_metadata(tmp_path, C.cache_payload(payload_mode, **extra))
+    loaded = C.blocks_from_cache(cache_file, "cuda", video, audio)
+    direct = [BasicAVTransformerBlock(lin, tabs, video, audio) for lin, tabs in parts]
+    assert len(loaded) == 2
+
+    def rnd(*shape, std=1.0, dtype=torch.float32):
+        return (torch.randn(*shape, generator=gen, device="cuda") * std).to(dtype)
+
+    def rope(heads, t, d):
+        ang = torch.rand(1, heads, t, d // 2, generator=gen, device="cuda") * 6.28
+        return torch.cos(ang), torch.sin(ang)
+
+    def args(cfg, t):
+        return TransformerArgs(x=rnd(1, t, cfg.dim, dtype=torch.bfloat16),
+                               context=rnd(1, L, cfg.context_dim, dtype=torch.bfloat16),
+                               timesteps=rnd(1, 1, 9, cfg.dim, std=0.1),
+                               positional_embeddings=rope(cfg.heads, t, cfg.d_head),
+                               cross_positional_embeddings=rope(audio.heads, t, audio.d_head),
+                               cross_scale_shift_timestep=rnd(1, 1, 4, cfg.dim, std=0.1),
+                               cross_gate_timestep=rnd(1, 1, 1, cfg.dim, std=0.1),
+                               prompt_timestep=rnd(1, 1, 2, cfg.dim, std=0.1))
+
+    v, a = args(video, T), args(audio, A)
+    outs = []
+    for blocks in (direct, loaded):
+        vv, aa = v, a
+        for b in blocks:
+            vv, aa = b(vv, aa)
+        outs.append((vv.x.clone(), aa.x.clone()))
+    assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
+    assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
+    assert ltxq._lib.device_error() == 0
