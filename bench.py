@@ -389,6 +389,8 @@ def run_step(args, world, rank, local, dev):
     torch.cuda.synchronize()
     evs, ff_ms = [], []
     n_launch0 = _lib.launch_count()
+    if args.profile_range:
+        torch.cuda.cudart().cudaProfilerStart()
     for _ in range(args.steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if use_graph:
@@ -404,6 +406,8 @@ def run_step(args, world, rank, local, dev):
             step(video, audio)
             e1.record(stream)
         evs.append((e0, e1))
+    if args.profile_range:
+        torch.cuda.cudart().cudaProfilerStop()
     n_launches = (graph.launches * args.steps if use_graph else _lib.launch_count() - n_launch0)
     torch.cuda.synchronize()
     clk.stop()
@@ -600,6 +604,8 @@ def main():
     ap.add_argument("--workload", choices=["step", "ff"], default="step")
     ap.add_argument("--cpu-sample", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step op by op instead of replaying it as one captured CUDA graph")
     ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,
