@@ -949,17 +949,22 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (tid == 0) mbar_arrive_cluster(leader_acc_empty);
         continue;
       }
-      // drain: accumulator column j of TMEM lane r -> staging[j][r] as bf16(acc)
+      // drain: accumulator column j of TMEM lane r -> staging[j][r] as bf16(acc);
+      // two 32-column loads in flight per wait (the MMA waits on this drain)
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v);
+      for (int c = 0; c < BN / 32; c += 2) {
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v[0]);
+        tmem_ld_32x32b_x32(tmem + t_lane + (c + 1) * 32, v[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const uint32_t h = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
-          stg[(c * 32 + j) * BM + r] = static_cast<uint16_t>(h & 0xFFFFu);
-          stg[(c * 32 + j + 1) * BM + r] = static_cast<uint16_t>(h >> 16);
+        for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const uint32_t h = pack_bf16x2(__uint_as_float(v[h2][j]), __uint_as_float(v[h2][j + 1]));
+            stg[((c + h2) * 32 + j) * BM + r] = static_cast<uint16_t>(h & 0xFFFFu);
+            stg[((c + h2) * 32 + j + 1) * BM + r] = static_cast<uint16_t>(h >> 16);
+          }
         }
       }
       tc_fence_before();
