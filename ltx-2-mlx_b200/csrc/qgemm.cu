@@ -983,6 +983,424 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pretransposed mxfp8 weights (the cache's `mxfp8-blocks-pretranspose` mode,
+// loader/transformer_cache.py:177-193, 1240-1244): the packed array is W^T,
+// [K rows][N bytes] of E4M3 codes with E8M0 scales [K, N/32] (groups along N).
+// Persistent CTA-pair kernel as qgemm_pair_kernel, but the A operand is built
+// in shared memory: TMA brings a [64 K][128 N] byte tile per stage, the
+// dequant warps write it as an MN-major 128B-swizzled bf16 tile, and the MMA
+// reads A through an MN-major descriptor (`tcgen05.mma ... [d], a_desc,
+// b_desc` with the A-transpose bit).  With A out of TMEM, all 512 columns hold
+// two 256-column accumulators: the epilogue of tile i reads accumulator i & 1
+// straight from TMEM while the MMAs of tile i + 1 fill the other one.
+// (For the standard layout this form measured slower than qgemm_pair_kernel:
+// it adds 32 KB of shared-memory traffic per stage per SM.)
+//
+// Epilogue (warps 10-13, warp w owns TMEM lanes 32w..32w+31 = features): per
+// 32-token chunk, bf16(acc), bias and GELU are applied in registers (thread =
+// feature, registers = tokens), the 32 x 32 block is transposed through a
+// 2 KB per-warp shared tile, and rows of 32 features are written with 16-byte
+// stores (the gated residual fused in on that side).
+template <int QK>
+struct PairPlanPT {
+  static constexpr int BN = 256;
+  static constexpr int kXStage = (BN / 2) * BK * 2;  // this CTA's half of the activation tile
+  static constexpr int kWStage = BK * BM;  // [64 K][128 N] E4M3 bytes
+  static constexpr int kAStage = BM * BK * 2;        // bf16 A tile, 128B-swizzled K-major
+  static constexpr int kAStages = 4;
+  static constexpr int kStgBytes = 4 * 32 * 32 * 2;  // per-warp 32 x 32 transpose tiles
+  static constexpr int kFixed = 1024 + kAStages * kAStage + kStgBytes + 512 + kGeluTabBytes;
+  static constexpr int kStagesRaw = (227 * 1024 - kFixed) / (kXStage + kWStage);
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kAOff = kStages * kXStage;            // 1024-aligned (16 KB stages)
+  static constexpr int kWOff = kAOff + kAStages * kAStage;
+  static constexpr int kStgOff = kWOff + kStages * kWStage;
+  static constexpr int kBarOff = kStgOff + kStgBytes;
+  static constexpr int kTabOff = kBarOff + 512;
+  static constexpr int kSmem = 1024 + kTabOff + kGeluTabBytes;
+  static constexpr uint32_t kTmemCols = 512;  // two accumulators
+  static_assert(kStages >= 4, "pipeline depth");
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
+  static_assert(kXStage % 1024 == 0 && kAStage % 1024 == 0, "128B-swizzle atoms need 1024-byte alignment");
+};
+
+template <int S, int AS>
+__device__ __forceinline__ Bars carve_bars_pt(uint8_t* base, uint64_t*& acc_full2, uint64_t*& acc_empty2) {
+  uint64_t* b = reinterpret_cast<uint64_t*>(base);
+  Bars r;
+  r.x_full = b;
+  r.x_empty = b + S;
+  r.w_full = b + 2 * S;
+  r.w_empty = b + 3 * S;
+  r.a_full = b + 4 * S;
+  r.a_empty = b + 4 * S + AS;
+  acc_full2 = b + 4 * S + 2 * AS;       // [2]
+  acc_empty2 = b + 4 * S + 2 * AS + 2;  // [2]
+  r.acc_full = acc_full2;
+  r.acc_empty = acc_empty2;
+  r.tmem_slot = reinterpret_cast<uint32_t*>(b + 4 * S + 2 * AS + 4);
+  r.abort_flag = reinterpret_cast<volatile int*>(r.tmem_slot + 1);
+  return r;
+}
+
+// Row side of the smem-A epilogue: u = bf16x2 words of 8 consecutive
+// features (bias / GELU already applied); gated residual, then a 16-byte store.
+__device__ __forceinline__ void epi_row_store(const Params& p, uint32_t (&u)[4], int m, int nf, const float (&g8b)[8],
+                                              bool gated, bool two_round, bool gate_bcast) {
+  const int64_t off = static_cast<int64_t>(m) * p.N + nf;
+  if (gated) {
+    const uint4 rv = __ldg(reinterpret_cast<const uint4*>(p.residual + off));
+    const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+    float g8[8];
+    if (gate_bcast) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) g8[k] = g8b[k];
+    } else {
+      load_vec8(p.gate, vec_row(p.gate, m), nf, g8);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float p0 = __fmul_rn(lo_bf16(u[k]), g8[2 * k]);
+      const float p1 = __fmul_rn(hi_bf16(u[k]), g8[2 * k + 1]);
+      const float r0 = lo_bf16(rw[k]), r1 = hi_bf16(rw[k]);
+      if (two_round) {
+        const uint32_t pr = pack_bf16x2(p0, p1);
+        u[k] = pack_bf16x2(__fadd_rn(r0, lo_bf16(pr)), __fadd_rn(r1, hi_bf16(pr)));
+      } else {
+        u[k] = pack_bf16x2(__fadd_rn(p0, r0), __fadd_rn(p1, r1));
+      }
+    }
+  }
+  *reinterpret_cast<uint4*>(p.out + off) = make_uint4(u[0], u[1], u[2], u[3]);
+}
+
+// Dequant warps of the pretransposed form.  Thread t (0..255) converts K row
+// t >> 2 of the stage for feature group t & 3 (32 features = one E8M0
+// scale): 32 bytes of the [64 K][128 N] packed tile -> four 16-byte chunks of
+// the MN-major A tile (64-feature blocks 1024 B apart, 8-row K groups 2048 B
+// apart, chunk c of K row r at c ^ (r & 7)).
+template <int QK, int S, int AS>
+__device__ __forceinline__ void dequant_loop_pt(const Params& p, const Bars& bb, uint8_t* ws, uint8_t* a_smem,
+                                                int warp, int lane, int n0, int num_kb, uint32_t a_full_remote,
+                                                int kb_base, int kb_first) {
+  constexpr int kWStage = BK * BM;
+  constexpr int kAStage = BM * BK * 2;
+  const int t = warp * 32 + lane;
+  const int kr = t >> 2, grp = t & 3;
+  const int nq = n0 + grp * 32;  // first feature of this thread's group
+  const bool col_ok = nq < p.N;
+  const int64_t gpr = p.N / 32;  // scale bytes per K row
+  const uint8_t* sc = static_cast<const uint8_t*>(p.scales);
+  bool ok = true;
+  for (int kb = 0; kb < num_kb && ok; ++kb) {
+    const int g = kb_base + kb;
+    const int s = g % S;
+    const uint32_t ph = (g / S) & 1;
+    const int as = g % AS;
+    const uint32_t aph = (g / AS) & 1;
+    const int64_t k = static_cast<int64_t>(kb_first + kb) * BK + kr;  // absolute K row
+    const uint32_t sbyte = col_ok ? __ldg(sc + k * gpr + nq / 32) : 0u;
+    if (!mbar_wait(&bb.w_full[s], ph, bb.abort_flag, p.err)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* wrow = ws + s * kWStage + kr * BM + grp * 32;
+    const uint4 v0 = *reinterpret_cast<const uint4*>(wrow);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(wrow + 16);
+    const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t o[16];
+    if (QK == kMxfp8F) {
+      const uint32_t s2 = e8m0_fast_scale2(sbyte);
+#pragma unroll
+      for (int w = 0; w < 8; ++w) deq_mxfp8_word_fast(wv[w], s2, o[2 * w], o[2 * w + 1]);
+    } else {
+      const float fsc = e8m0_to_f32(sbyte);
+#pragma unroll
+      for (int w = 0; w < 8; ++w) deq_mxfp8_word(wv[w], fsc, o[2 * w], o[2 * w + 1]);
+    }
+    if (!col_ok) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = 0u;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bb.w_empty[s]);  // packed bytes consumed
+    if (!mbar_wait(&bb.a_empty[as], aph ^ 1, bb.abort_flag, p.err)) {
+      ok = false;
+      break;
+    }
+    uint8_t* abase = a_smem + as * kAStage + (kr >> 3) * 2048 + (grp >> 1) * 1024 + (kr & 7) * 128;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<uint4*>(abase + (((4 * (grp & 1) + i) ^ (kr & 7)) << 4)) =
+          make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(a_full_remote + 8u * static_cast<uint32_t>(as));
+  }
+}
+
+template <int QK>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    qgemm_pair_pt_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                         const Params p) {
+  using P = PairPlanPT<QK>;
+  constexpr int BN = P::BN;
+  constexpr int S = P::kStages;
+  constexpr int AS = P::kAStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* xs = smem;
+  uint8_t* as_base = smem + P::kAOff;
+  uint8_t* ws = smem + P::kWOff;
+  uint16_t* gtab = reinterpret_cast<uint16_t*>(smem + P::kTabOff);
+  uint64_t *acc_full2, *acc_empty2;
+  const Bars bb = carve_bars_pt<S, AS>(smem + P::kBarOff, acc_full2, acc_empty2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_kb = p.K / BK;
+  const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
+  const int tiles = n_pt * ((p.M + BN - 1) / BN);
+  // work unit u < dp: whole tile u; u >= dp: K range sp of tile
+  // dp + (u - dp) / splits.  Every role walks the same units in the same order.
+  const int dp = p.dp_tiles;
+  const int splits = p.splits;
+  const int units = dp + (tiles - dp) * splits;
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int n_clusters = static_cast<int>(gridDim.x >> 1);
+  auto unit = [&](int u, int& n0, int& m0, int& sp, int& kb_lo, int& kb_hi) {
+    int tile;
+    if (u < dp) {
+      tile = u;
+      sp = -1;
+      kb_lo = 0;
+      kb_hi = num_kb;
+    } else {
+      tile = dp + (u - dp) / splits;
+      sp = (u - dp) - (tile - dp) * splits;
+      kb_lo = sp * num_kb / splits;
+      kb_hi = (sp + 1) * num_kb / splits;
+    }
+    n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
+    m0 = (tile / n_pt) * BN;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bb.x_full[s], 1);
+      mbar_init(&bb.x_empty[s], 1);
+      mbar_init(&bb.w_full[s], 1);
+      mbar_init(&bb.w_empty[s], kDeqWarps);
+    }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&bb.a_full[s], 2 * kDeqWarps);  // both CTAs' dequant warps (the leader's copy is used)
+      mbar_init(&bb.a_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full2[b], 1);
+      mbar_init(&acc_empty2[b], 2);  // both CTAs' epilogue groups (the leader's copy is used)
+    }
+    *bb.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(bb.tmem_slot, P::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialized, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *bb.tmem_slot;
+  const uint32_t leader_x_full = mapa_shared(smem_u32(bb.x_full), 0);
+  const uint32_t leader_a_full = mapa_shared(smem_u32(bb.a_full), 0);
+  const uint32_t leader_acc_empty = mapa_shared(smem_u32(acc_empty2), 0);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
+      tma_prefetch_desc(&tmap_w);
+      bool ok = true;
+      int g0 = 0;
+      for (int u = cluster_id; u < units && ok; u += n_clusters) {
+        int n0, m0, sp, kb_lo, kb_hi;
+        unit(u, n0, m0, sp, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          const int g = g0 + (kb - kb_lo);
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!mbar_wait(&bb.w_empty[s], ph ^ 1, bb.abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bb.w_full[s], P::kWStage);
+          tma_load_2d(ws + s * P::kWStage, &tmap_w, &bb.w_full[s], n0, kb * BK);  // [K][N] bytes
+          if (!mbar_wait(&bb.x_empty[s], ph ^ 1, bb.abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          // the leader expects both halves; each CTA's copy completes on the leader's barrier
+          if (leader) mbar_arrive_expect_tx(&bb.x_full[s], 2 * P::kXStage);
+          tma_load_2d_pair(xs + s * P::kXStage, &tmap_x, leader_x_full + 8u * s, kb * BK,
+                           m0 + static_cast<int>(rank) * (BN / 2));
+        }
+        g0 += kb_hi - kb_lo;
+      }
+      if (*bb.abort_flag) {
+        // give copies already in flight time to land before smem is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(2 * BM, BN) | (1u << 15);  // A MN-major
+      bool ok = true;
+      int it = 0, g0 = 0;
+      for (int u = cluster_id; u < units && ok; u += n_clusters, ++it) {
+        int n0, m0, sp, kb_lo, kb_hi;
+        unit(u, n0, m0, sp, kb_lo, kb_hi);
+        const int buf = it & 1;
+        // both epilogue groups must be done with this accumulator's previous use
+        if (!mbar_wait(&acc_empty2[buf], ((it >> 1) & 1) ^ 1, bb.abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
+          const int g = g0 + (kb - kb_lo);
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          const int as = g % AS;
+          const uint32_t aph = (g / AS) & 1;
+          if (!mbar_wait(&bb.a_full[as], aph, bb.abort_flag, p.err) ||
+              !mbar_wait(&bb.x_full[s], ph, bb.abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xaddr = smem_u32(xs + s * P::kXStage);
+          const uint32_t aaddr = smem_u32(as_base + as * P::kAStage);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)
+            mma_bf16_ss_pair(d, smem_desc_sw128_mn(aaddr + j * 4096, 1024, 2048),  // 16 K rows = 2 row groups
+                             smem_desc_sw128(xaddr + j * 32), idesc, (kb != kb_lo || j != 0) ? 1u : 0u);
+          mma_commit_pair(&bb.x_empty[s], 0x3);
+          mma_commit_pair(&bb.a_empty[as], 0x3);
+        }
+        mma_commit_pair(&acc_full2[buf], 0x3);  // accumulator of this unit ready in both CTAs
+        g0 += kb_hi - kb_lo;
+      }
+      if (*bb.abort_flag) {
+        // give MMAs already issued time to complete before TMEM is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
+    }
+  } else if (warp < kDeqWarps) {
+    int g0 = 0;
+    for (int u = cluster_id; u < units && !*bb.abort_flag; u += n_clusters) {
+      int n0, m0, sp, kb_lo, kb_hi;
+      unit(u, n0, m0, sp, kb_lo, kb_hi);
+      dequant_loop_pt<QK, S, AS>(p, bb, ws, as_base, warp, lane, n0, kb_hi - kb_lo, leader_a_full, g0, kb_lo);
+      g0 += kb_hi - kb_lo;
+    }
+  } else {
+    // ------------------------------------------------ epilogue warps 10..13
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;
+    const int tid = (warp - kEpiWarp0) * 32 + lane;  // 0..127
+    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    uint16_t* stw = reinterpret_cast<uint16_t*>(smem + P::kStgOff) + q * (32 * 32);
+    const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
+    const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+    const bool gate_bcast = p.gate.rows_per_vec == 0;
+    if (p.epi == LTXQ_EPI_GELU) {
+      gelu_tab_fill(gtab, tid, 128);  // while the first tile's main loop runs
+      named_bar_sync(1, 128);
+    }
+    for (int u = cluster_id, it = 0; u < units; u += n_clusters, ++it) {
+      int n0, m0, sp, kb_lo, kb_hi;
+      unit(u, n0, m0, sp, kb_lo, kb_hi);
+      const int buf = it & 1;
+      if (!mbar_wait(&acc_full2[buf], (it >> 1) & 1, bb.abort_flag, p.err)) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem + t_lane + static_cast<uint32_t>(buf * BN);
+      const int n = n0 + r;  // register side: this thread's feature
+      if (sp >= 0) {
+        // fp32 partial of split sp of this tile, tile-local [token][feature]
+        const int tile_i = (u - dp) / splits;
+        float* dst = p.partial + (static_cast<size_t>(tile_i) * splits + sp) * (kPairTile * kPairTile) +
+                     static_cast<int>(rank) * BM + r;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          if (m0 + c * 32 >= p.M) break;  // uniform
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tacc + c * 32, v);
+          tmem_wait_ld();
+          if (n < p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (m0 + c * 32 + j < p.M) dst[(c * 32 + j) * kPairTile] = __uint_as_float(v[j]);
+            }
+          }
+        }
+      } else {
+        const float bias_n = (p.bias != nullptr && n < p.N) ? bf16_to_f32(__ldg(p.bias + n)) : 0.f;
+        // row side: 8 features [nf, nf + 8) of token rows (lane >> 2) + 8 i
+        const int nf = n0 + q * 32 + (lane & 3) * 8;
+        float g8b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (gated && gate_bcast && nf < p.N) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8b);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c += 2) {
+          if (m0 + c * 32 >= p.M) break;  // uniform
+          uint32_t v[2][32];
+          tmem_ld_32x32b_x32(tacc + c * 32, v[0]);
+          tmem_ld_32x32b_x32(tacc + (c + 1) * 32, v[1]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int m_c = m0 + (c + h2) * 32;
+            if (m_c >= p.M) break;  // uniform
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              // bf16(acc) (the reference's first rounding point), bias, GELU
+              uint32_t w = pack_bf16x2(__uint_as_float(v[h2][j]), __uint_as_float(v[h2][j + 1]));
+              if (p.bias != nullptr) w = pack_bf16x2(__fadd_rn(lo_bf16(w), bias_n), __fadd_rn(hi_bf16(w), bias_n));
+              if (p.epi == LTXQ_EPI_GELU) w = gelu_tab_x2(w, gtab);
+              stw[j * 32 + lane] = static_cast<uint16_t>(w & 0xFFFFu);
+              stw[(j + 1) * 32 + lane] = static_cast<uint16_t>(w >> 16);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int pass = 0; pass < 4; ++pass) {
+              const int jr = (lane >> 2) + 8 * pass;
+              const uint4 a = *reinterpret_cast<const uint4*>(stw + jr * 32 + (lane & 3) * 8);
+              if (m_c + jr < p.M && nf < p.N) {
+                uint32_t uw[4] = {a.x, a.y, a.z, a.w};
+                epi_row_store(p, uw, m_c + jr, nf, g8b, gated, two_round, gate_bcast);
+              }
+            }
+            __syncwarp();  // transpose tile consumed
+          }
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (tid == 0) mbar_arrive_cluster(leader_acc_empty + 8u * static_cast<uint32_t>(buf));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal or read it
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, P::kTmemCols);
+  }
+}
+
 template <int QK, int BN>
 static ltxq_status launch_cfg(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, cudaStream_t stream) {
   using PL = Plan<QK, BN, BN>;
@@ -1021,6 +1439,40 @@ static ltxq_status launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, con
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
   if (e == cudaSuccess) note_launch();
   if (ltxq_status st = cuda_check(e, "qgemm pair launch")) return st;
+  if (p.dp_tiles >= tiles) return LTXQ_OK;
+  const int64_t items = static_cast<int64_t>(tiles - p.dp_tiles) * kPairTile * (kPairTile / 8);
+  const int64_t want = (items + 255) / 256;
+  const int cap = num_sms() * 8;
+  splitk_reduce_kernel<<<static_cast<unsigned>(want < cap ? want : cap), 256, 0, stream>>>(p);
+  return launch_check("split-K reduce launch");
+}
+
+template <int QK>
+static ltxq_status launch_pair_pt(const CUtensorMap& tx, const CUtensorMap& tw, const Params& p, cudaStream_t stream) {
+  using PL = PairPlanPT<QK>;
+  auto kern = qgemm_pair_pt_kernel<QK>;
+  ltxq_status st =
+      cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem), "smem attribute");
+  if (st) return st;
+  const int tiles = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + 255) / 256);
+  const int units = p.dp_tiles + (tiles - p.dp_tiles) * p.splits;
+  const int max_clusters = num_sms() / 2;
+  const int clusters = units < max_clusters ? units : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kPairThreads);
+  cfg.dynamicSmemBytes = PL::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
+  if (e == cudaSuccess) note_launch();
+  if (ltxq_status st2 = cuda_check(e, "qgemm pretransposed launch")) return st2;
   if (p.dp_tiles >= tiles) return LTXQ_OK;
   const int64_t items = static_cast<int64_t>(tiles - p.dp_tiles) * kPairTile * (kPairTile / 8);
   const int64_t want = (items + 255) / 256;
@@ -1100,8 +1552,9 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   if (ltxq_status st = check_qweight(w, true, &R, &L)) return st;
   if (!x || !out) return fail(LTXQ_ERR_INVALID, "qlinear: x/out is NULL");
   if (M < 0) return fail(LTXQ_ERR_INVALID, "qlinear: M < 0");
-  if (w.layout != LTXQ_LAYOUT_STD)
-    return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: pretransposed weights are not supported by the GEMM yet");
+  const bool pt = w.layout == LTXQ_LAYOUT_PRETRANSPOSED;
+  if (pt && w.mode != LTXQ_MXFP8)
+    return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: pretransposed weights are mxfp8 only (the cache's only such mode)");
   const int64_t N = w.n_out, K = w.k_in;
   if (K % gemm::BK != 0) return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: K must be a multiple of 64");
   if (N % 8 != 0) return fail(LTXQ_ERR_UNSUPPORTED, "qlinear: N must be a multiple of 8");
@@ -1121,18 +1574,25 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
                            (reinterpret_cast<uintptr_t>(workspace) & 15u)))
     sched = gemm::Sched{sched.tiles, sched.tiles, 1};
   const int splits = sched.splits;
-  const int bn = splits > 1 ? 256 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+  const int bn = (splits > 1 || pt) ? 256 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
   CUtensorMap tx, tw;
   const uint32_t xbox = bn == 256 ? 128 : static_cast<uint32_t>(bn);  // the pair kernel stages half a tile per CTA
   if (ltxq_status st = encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, K * 2, gemm::BK, xbox,
                                       CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
-  const int wbytes_row = static_cast<int>(K * w.bits / 8);
-  const uint32_t wbox = qk == gemm::kAffine4 ? 32 : 64;
-  const CUtensorMapSwizzle wsw = qk == gemm::kAffine4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (ltxq_status st =
-          encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, wbytes_row, N, wbytes_row, wbox, gemm::BM, wsw))
-    return st;
+  if (pt) {
+    // W^T: [K rows][N bytes], box of 128 features x 64 K rows, unswizzled
+    if (ltxq_status st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, N, K, N, gemm::BM, gemm::BK,
+                                        CU_TENSOR_MAP_SWIZZLE_NONE))
+      return st;
+  } else {
+    const int wbytes_row = static_cast<int>(K * w.bits / 8);
+    const uint32_t wbox = qk == gemm::kAffine4 ? 32 : 64;
+    const CUtensorMapSwizzle wsw = qk == gemm::kAffine4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
+    if (ltxq_status st =
+            encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, wbytes_row, N, wbytes_row, wbox, gemm::BM, wsw))
+      return st;
+  }
 
   gemm::Params p{};
   p.M = static_cast<int>(M);
@@ -1163,6 +1623,10 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
   p.dp_tiles = sched.dp;
   p.splits = splits;
   p.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  if (pt) {
+    if (qk == gemm::kMxfp8F) return gemm::launch_pair_pt<gemm::kMxfp8F>(tx, tw, p, stream);
+    return gemm::launch_pair_pt<gemm::kMxfp8>(tx, tw, p, stream);
+  }
   switch (qk) {
     case gemm::kAffine8: return gemm::launch_qk<gemm::kAffine8>(bn, tx, tw, p, stream);
     case gemm::kAffine4: return gemm::launch_qk<gemm::kAffine4>(bn, tx, tw, p, stream);

@@ -83,6 +83,7 @@ def main(argv=None):
     ap.add_argument("--cublas", action="store_true")
     ap.add_argument("--no-split-k", action="store_true", help="give the GEMM no split-K workspace")
     ap.add_argument("--graph", action="store_true", help="device time per call from a captured CUDA graph")
+    ap.add_argument("--pretransposed", action="store_true", help="pack W^T (the cache's pretranspose mode; mxfp8)")
     args = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
@@ -95,14 +96,15 @@ def main(argv=None):
         b = (torch.randn(N, device=dev, generator=g) * 0.01).to(torch.bfloat16)
         res = torch.randn(M, N, device=dev, generator=g).to(torch.bfloat16)
         gate = torch.randn(N, device=dev, generator=g) * 0.1
-        row = {"M": M, "K": K, "N": N, "epilogue": args.epilogue, "split_k": not args.no_split_k}
+        row = {"M": M, "K": K, "N": N, "epilogue": args.epilogue, "split_k": not args.no_split_k,
+               "pretransposed": args.pretransposed}
         flops = 2.0 * M * N * K
         if args.cublas:
             t = _time(lambda: torch.nn.functional.linear(x, w, b), flush, args.iters, args.warmup)
             row["cublas_bf16"] = {"ms": t, "tflops": flops / t / 1e9}
         for name in args.modes.split(","):
             mode, bits = MODES[name]
-            ql = QuantizedLinear.from_linear(w, b, mode=mode, bits=bits)
+            ql = QuantizedLinear.from_linear(w, b, mode=mode, bits=bits, pretransposed=args.pretransposed)
             kw = {"gelu": True} if args.epilogue == "gelu" else (
                 {"residual": res, "gate": gate} if args.epilogue == "gated" else {})
             kw["split_k"] = not args.no_split_k
@@ -112,7 +114,8 @@ def main(argv=None):
                 qls = [ql] + [QuantizedLinear(ql.weight.clone(), ql.scales.clone(),
                                               None if ql.biases is None else ql.biases.clone(), ql.bias,
                                               group_size=ql.group_size, bits=ql.bits, mode=ql.mode,
-                                              in_features=ql.in_features, out_features=ql.out_features)
+                                              pretransposed=ql.pretransposed, in_features=ql.in_features,
+                                              out_features=ql.out_features)
                               for _ in range(copies - 1)]
                 t = _time_graph([lambda q=q: q(x, **kw) for q in qls], args.iters)
                 row["graph_calls"] = copies

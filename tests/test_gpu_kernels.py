@@ -547,3 +547,65 @@ def test_qlinear_hybrid_schedule(cuda, epi):
     assert_close(from_dev_bf16(a), ref, f"hybrid {epi}")
     whole = from_dev_bf16(ql(xd, split_k=False, **kw))
     assert (ulp_diff_bf16(from_dev_bf16(a), whole) > 0).mean() < 0.02
+
+
+def _pt_linear(WT_q, bias, n, k):
+    """QuantizedLinear over pretransposed mxfp8 arrays (W^T packed along N)."""
+    ltxq = _ltxq()
+    torch = _torch()
+    return ltxq.QuantizedLinear(to_dev(WT_q["weight"]), torch.from_numpy(WT_q["scales"].copy()).cuda(), None,
+                                to_dev_bf16(bias) if bias is not None else None, group_size=32, bits=8,
+                                mode="mxfp8", pretransposed=True, in_features=k, out_features=n)
+
+
+@pytest.mark.parametrize("M,split_k,epi", [(700, True, "none"), (201, True, "gelu"), (201, False, "none"),
+                                           (1152, True, "gated")])
+def test_qlinear_pretransposed_matches_oracle(cuda, M, split_k, epi):
+    """The cache's mxfp8-blocks-pretranspose layout (transformer_cache.py:177-193,
+    1240-1244): y = x @ dequant(W^T) + b, against _PretransposedQuantizedLinear's
+    composition (ref_ops.linear_pretransposed)."""
+    torch = _torch()
+    K, N = 1024, 768
+    g = rng(50)
+    x = normal_bf16(g, (M, K))
+    W = normal_bf16(g, (N, K), 0.02)
+    bias = normal_bf16(g, (N,), 0.01)
+    qT = oq.quantize(np.ascontiguousarray(W.T), "mxfp8")
+    deqT = oq.dequantize(qT, N)  # [K, N]
+    ql = _pt_linear(qT, bias, N, K)
+    xd = to_dev_bf16(x)
+    ref = ro.linear_pretransposed(x, deqT, bias)
+    kw = {"split_k": split_k}
+    if epi == "gelu":
+        kw["gelu"] = True
+        ref = ro.gelu_approx(ref)
+    elif epi == "gated":
+        res = normal_bf16(g, (M, N))
+        gate = normal_f32(g, (1, N), 0.5)
+        kw.update(residual=to_dev_bf16(res), gate=torch.from_numpy(gate).cuda())
+        ref = ro.gated_add(res, ref, gate)
+    out = from_dev_bf16(ql(xd, **kw))
+    assert_close(out, ref, f"pretransposed M={M} {epi}")
+    assert (ulp_diff_bf16(out, ref) > 0).mean() < 0.02
+
+
+@pytest.mark.parametrize("smax", [134, 246])
+@pytest.mark.parametrize("split_k", [True, False])
+def test_pretransposed_dequant_exact_through_identity(cuda, smax, split_k):
+    """x = identity: y[k, n] = dequant(W^T)[k, n] bit for bit, every finite
+    E4M3 code under scales 10..smax (the short and the general conversion)."""
+    torch = _torch()
+    K = M = 256
+    N = 512
+    codes = ((np.arange(N, dtype=np.uint32)[None, :] + 7 * np.arange(K, dtype=np.uint32)[:, None]) % 256).astype(np.uint8)
+    codes[(codes & 0x7F) == 0x7F] = 0
+    scales = (10 + (np.arange(K * (N // 32)) * 5) % (smax - 9)).astype(np.uint8).reshape(K, N // 32)
+    qT = {"weight": codes.reshape(K, N // 4, 4).copy().view(np.uint32).reshape(K, N // 4), "scales": scales,
+          "group_size": 32, "bits": 8, "mode": "mxfp8"}
+    ql = _pt_linear(qT, None, N, K)
+    assert ql.data_flags() == (1 if smax <= 134 else 0)
+    y = bf16_bits(ql(torch.eye(M, K, dtype=torch.bfloat16, device="cuda"), split_k=split_k))
+    want = f32_to_bf16_bits(oq.dequantize(qT, N))
+    both_zero = ((y & 0x7FFF) == 0) & ((want & 0x7FFF) == 0)
+    diff = (y != want) & ~both_zero
+    assert not diff.any(), (np.argwhere(diff)[:5], y[diff][:5], want[diff][:5])
