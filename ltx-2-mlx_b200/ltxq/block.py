@@ -222,21 +222,26 @@ class QAttention:
 
 
 def _cat_linears(parts: list[QuantizedLinear]) -> QuantizedLinear:
-    """Concatenate quantized linears along the output dimension (exact: each
-    packed row keeps its own groups)."""
+    """Concatenate quantized linears along the output dimension.  Exact: in the
+    standard layout each packed row keeps its own groups; in the pretransposed
+    layout (groups along the output dimension) every part's width is a whole
+    number of groups, so its columns keep theirs."""
     p0 = parts[0]
     for p in parts[1:]:
         assert p.in_features == p0.in_features and p.mode == p0.mode and p.bits == p0.bits
-        assert p.group_size == p0.group_size and not p.pretransposed
+        assert p.group_size == p0.group_size and p.pretransposed == p0.pretransposed
+    dim = 1 if p0.pretransposed else 0
+    if p0.pretransposed:
+        assert all(p.out_features % p.group_size == 0 for p in parts)
     bias = None
     if any(p.bias is not None for p in parts):
         bias = torch.cat([p.bias if p.bias is not None else torch.zeros(p.out_features, dtype=torch.bfloat16,
                                                                          device=p.weight.device) for p in parts])
     return QuantizedLinear(
-        torch.cat([p.weight for p in parts]), torch.cat([p.scales for p in parts]),
-        torch.cat([p.biases for p in parts]) if p0.biases is not None else None, bias,
-        group_size=p0.group_size, bits=p0.bits, mode=p0.mode, in_features=p0.in_features,
-        out_features=sum(p.out_features for p in parts))
+        torch.cat([p.weight for p in parts], dim), torch.cat([p.scales for p in parts], dim),
+        torch.cat([p.biases for p in parts], dim) if p0.biases is not None else None, bias,
+        group_size=p0.group_size, bits=p0.bits, mode=p0.mode, pretransposed=p0.pretransposed,
+        in_features=p0.in_features, out_features=sum(p.out_features for p in parts))
 
 
 class BasicAVTransformerBlock:
@@ -281,14 +286,15 @@ class BasicAVTransformerBlock:
     @staticmethod
     def random_parts(gen: torch.Generator, device, mode: str = "affine", bits: int = 8, group_size: int | None = None,
                      video: StreamConfig = VIDEO_22B, audio: StreamConfig = AUDIO_22B, w_std: float = 0.02,
-                     b_std: float = 0.01, t_std: float = 0.1):
+                     b_std: float = 0.01, t_std: float = 0.1, pretransposed: bool = False):
         """The per-projection quantized linears (cache base name ->
         QuantizedLinear) and fp32 tables of a random block."""
         lin = {}
         for name, (n, k) in linear_specs(video, audio).items():
             w = (torch.randn(n, k, generator=gen, device=device) * w_std).to(torch.bfloat16)
             b = (torch.randn(n, generator=gen, device=device) * b_std).to(torch.bfloat16)
-            lin[name] = QuantizedLinear.from_linear(w, b, group_size=group_size, bits=bits, mode=mode)
+            lin[name] = QuantizedLinear.from_linear(w, b, group_size=group_size, bits=bits, mode=mode,
+                                                    pretransposed=pretransposed)
             del w
         tabs = {}
         for name, shape in table_specs(video, audio).items():

@@ -7,7 +7,8 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode,bits,payload_mode", [("mxfp8", 8, "mxfp8-blocks"), ("affine", 8, "off")])
+@pytest.mark.parametrize("mode,bits,payload_mode", [("mxfp8", 8, "mxfp8-blocks"), ("affine", 8, "off"),
+                                                   ("mxfp8", 8, "mxfp8-blocks-pretranspose")])
 def test_blocks_from_cache_match_source(cuda, tmp_path, mode, bits, payload_mode):
     import torch
 
@@ -15,13 +16,16 @@ def test_blocks_from_cache_match_source(cuda, tmp_path, mode, bits, payload_mode
     from ltxq import cache as C
     from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
 
-    video = StreamConfig(1024, 8, 128, 1024)
-    audio = StreamConfig(512, 8, 64, 512)
+    pt = payload_mode == "mxfp8-blocks-pretranspose"
+    # pretransposed groups run along the output dimension, so every output
+    # width (the per-head gate logits included) is a multiple of 32
+    video = StreamConfig(2048, 32, 64, 2048) if pt else StreamConfig(1024, 8, 128, 1024)
+    audio = StreamConfig(2048, 32, 64, 2048) if pt else StreamConfig(512, 8, 64, 512)
     T, A, L = 80, 40, 24
     gen = torch.Generator(device="cuda")
     gen.manual_seed(11)
-    parts = [BasicAVTransformerBlock.random_parts(gen, "cuda", mode=mode, bits=bits, video=video, audio=audio)
-             for _ in range(2)]
+    parts = [BasicAVTransformerBlock.random_parts(gen, "cuda", mode=mode, bits=bits, video=video, audio=audio,
+                                                  pretransposed=pt) for _ in range(2)]
     state = {}
     for i, (lin, tabs) in enumerate(parts):
         state.update(C.block_state(i, lin, tabs))
