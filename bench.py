@@ -289,11 +289,26 @@ def run_reference(args):
 # ============================================================================ GPU arm
 
 
-def _step_config(world, n_blocks=STEP_BLOCKS, graph=True):
-    return {"workload": "config4_22b_denoise_step_mxfp8g32", "blocks": n_blocks, "video_tokens": STEP_T,
+STEP_QUANT = {  # --quant -> (mode, bits, workload name, description)
+    "mxfp8": ("mxfp8", 8, "config4_22b_denoise_step_mxfp8g32", "mxfp8 g32 (E4M3, E8M0 scales), all block linears"),
+    "int8": ("affine", 8, "22b_denoise_step_int8g64", "affine int8 g64 (bf16 scales/biases), all block linears"),
+    "int4": ("affine", 4, "22b_denoise_step_int4g64", "affine int4 g64 (bf16 scales/biases), all block linears"),
+}
+
+
+def _packed_bytes(quant, n, k):
+    """Packed weight + group parameters of an [n, k] linear."""
+    if quant == "mxfp8":
+        return n * k + n * k // 32
+    bits = 8 if quant == "int8" else 4
+    return n * k * bits // 8 + 2 * 2 * n * k // 64
+
+
+def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8"):
+    return {"workload": STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": STEP_T,
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
             "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
-            "quant": "mxfp8 g32 (E4M3, E8M0 scales), all block linears",
+            "quant": STEP_QUANT[quant][3],
             "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL)",
             "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
 
@@ -328,7 +343,8 @@ def run_step(args, world, rank, local, dev):
     gen = torch.Generator(device=dev)
     gen.manual_seed(2026)  # identical on every rank: weights are replicated
     n_blocks = args.blocks
-    blocks = [BasicAVTransformerBlock.random(gen, dev, mode="mxfp8") for _ in range(n_blocks)]
+    q_mode, q_bits = STEP_QUANT[args.quant][:2]
+    blocks = [BasicAVTransformerBlock.random(gen, dev, mode=q_mode, bits=q_bits) for _ in range(n_blocks)]
     weight_bytes = sum(b.nbytes() for b in blocks)
 
     def rnd(*shape, std=1.0, dtype=torch.float32):
@@ -459,18 +475,19 @@ def run_step(args, world, rank, local, dev):
         line = {
             "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks, use_graph),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks, use_graph, args.quant),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
                                "frac_of_bf16_burst_peak": achieved / tf_burst},
-            "roofline": {"bound": "tensor", "kernel": "qgemm_pair_kernel<mxfp8> (video FF project_in, GELU epilogue)",
+            "roofline": {"bound": "tensor",
+                         "kernel": f"qgemm_pair_kernel<{args.quant}> (video FF project_in, GELU epilogue)",
                          "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
                          "peak_kind": (f"{peak_kind} bf16 sustained (kernel timed inside a long step)"
                                        if peak_kind == "measured" else "fallback 1400 TFLOP/s sustained"),
-                         "traffic": _traffic(f"qgemm_pair_mxfp8_ff_in_{tl}x16384x4096"),
+                         "traffic": _traffic(f"qgemm_pair_{args.quant}_ff_in_{tl}x16384x4096"),
                          "algorithmic_per_launch": {"flops": ff_flops,
-                                                    "bytes": tl * VD * 2 + 4 * VD * VD + 4 * VD * VD // 32
+                                                    "bytes": tl * VD * 2 + _packed_bytes(args.quant, 4 * VD, VD)
                                                     + tl * 4 * VD * 2}},
             "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
                     "api": f"ltxq.block.BasicAVTransformerBlock x{n_blocks} (C ABI: ltxq_adaln_modulate, ltxq_qlinear, "
@@ -608,6 +625,8 @@ def main():
                     help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step op by op instead of replaying it as one captured CUDA graph")
+    ap.add_argument("--quant", choices=sorted(STEP_QUANT), default="mxfp8",
+                    help="block-linear quantization of the step workload (config 4 is mxfp8)")
     ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,
                     help="blocks per step (48 = the 22B model; fewer only for bounded profiler captures)")
     args = ap.parse_args()
