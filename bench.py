@@ -309,7 +309,7 @@ def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8"):
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
             "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
             "quant": STEP_QUANT[quant][3],
-            "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL)",
+            "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL, side stream)",
             "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
 
 
@@ -339,7 +339,7 @@ def run_step(args, world, rank, local, dev):
     if STEP_T % world:
         raise SystemExit(f"{STEP_T} video tokens do not split over {world} ranks")
     tl = STEP_T // world
-    shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank)
+    shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank, overlap=not args.no_overlap)
     gen = torch.Generator(device=dev)
     gen.manual_seed(2026)  # identical on every rank: weights are replicated
     n_blocks = args.blocks
@@ -625,6 +625,8 @@ def main():
                     help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     ap.add_argument("--eager", action="store_true",
                     help="launch the step op by op instead of replaying it as one captured CUDA graph")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="run the K/V all-gathers on the compute stream instead of a side stream")
     ap.add_argument("--quant", choices=sorted(STEP_QUANT), default="mxfp8",
                     help="block-linear quantization of the step workload (config 4 is mxfp8)")
     ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,

@@ -163,20 +163,66 @@ class RowShard:
     group: object = None
     world: int = 1
     rank: int = 0
+    overlap: bool = True  # run the all-gathers on a side stream (start_gather / finish_gather)
+    _comm: object = field(default=None, repr=False, compare=False)
 
     def gather_rows(self, x: torch.Tensor) -> torch.Tensor:
         """(B, T_local, C) on every rank -> (B, world * T_local, C)."""
         if self.world == 1:
             return x
+        return self.finish_gather(self.start_gather(x, overlap=False))[0]
+
+    def start_gather(self, *xs: torch.Tensor, overlap: bool | None = None) -> "PendingGather":
+        """Start the all-gathers of ``xs``.  With overlap, they run on a side
+        stream forked from the current one, and the caller's stream goes on
+        with independent work until ``finish_gather``.  Outputs are allocated
+        on the caller's stream and the inputs stay referenced until then, so
+        neither is recycled while the side stream uses them."""
+        xs = tuple(x.contiguous() for x in xs)
+        if self.world == 1:
+            return PendingGather(xs, xs, None)
         import torch.distributed as dist
 
-        x = x.contiguous()
-        b, t, c = x.shape
-        out = torch.empty((self.world * b, t, c), dtype=x.dtype, device=x.device)  # rank-major blocks
-        dist.all_gather_into_tensor(out, x, group=self.group)
-        if b == 1:
-            return out.view(1, self.world * t, c)
-        return out.view(self.world, b, t, c).permute(1, 0, 2, 3).reshape(b, self.world * t, c)
+        outs = tuple(torch.empty((self.world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+                     for x in xs)  # rank-major blocks
+        use_side = self.overlap if overlap is None else overlap
+        if not use_side:
+            for o, x in zip(outs, xs):
+                dist.all_gather_into_tensor(o, x, group=self.group)
+            return PendingGather(outs, xs, None)
+        if self._comm is None:
+            self._comm = torch.cuda.Stream(device=xs[0].device)
+        cur = torch.cuda.current_stream(xs[0].device)
+        self._comm.wait_stream(cur)
+        with torch.cuda.stream(self._comm):
+            for o, x in zip(outs, xs):
+                dist.all_gather_into_tensor(o, x, group=self.group)
+        return PendingGather(outs, xs, self._comm)
+
+    def finish_gather(self, pending: "PendingGather") -> tuple:
+        """Join the side stream and return the gathered (B, world * T, C)."""
+        if self.world == 1:
+            return pending.outs
+        if pending.stream is not None:
+            torch.cuda.current_stream(pending.outs[0].device).wait_stream(pending.stream)
+        res = []
+        for o, x in zip(pending.outs, pending.inputs):
+            b, t = x.shape[0], x.shape[1]
+            rest = tuple(x.shape[2:])
+            if b == 1:
+                res.append(o.view((1, self.world * t) + rest))
+            else:
+                res.append(o.view((self.world, b, t) + rest).transpose(0, 1).reshape((b, self.world * t) + rest))
+        return tuple(res)
+
+
+@dataclass
+class PendingGather:
+    """All-gathers in flight (``RowShard.start_gather``)."""
+
+    outs: tuple
+    inputs: tuple
+    stream: object
 
 
 @dataclass
@@ -209,11 +255,19 @@ class QAttention:
         """QK norm, RoPE, SDPA, per-head gate -> (B, T, inner) bf16.  With
         ``gather_kv`` the (rotated) K and V rows of every rank are
         all-gathered first."""
+        q, k = self.norm_rope(q, k, pe, k_pe)
+        if gather_kv is not None and gather_kv.world > 1:
+            k, v = gather_kv.finish_gather(gather_kv.start_gather(k, v, overlap=False))
+        return self.attend(q, k, v, gl)
+
+    def norm_rope(self, q, k, pe=None, k_pe=None):
+        """QK RMSNorm + split RoPE (attention.py:580-587, rope.py:53-90)."""
         q = K.qk_norm_rope(q, self.q_norm, self.heads, self.eps, pe)
         k = K.qk_norm_rope(k, self.k_norm, self.heads, self.eps, (pe if k_pe is None else k_pe) if pe is not None else None)
-        if gather_kv is not None and gather_kv.world > 1:
-            k = gather_kv.gather_rows(k)
-            v = gather_kv.gather_rows(v)
+        return q, k
+
+    def attend(self, q, k, v, gl) -> torch.Tensor:
+        """SDPA and the per-head gate of rotated Q, K and V."""
         qh, kh, vh = _heads(q, self.heads), _heads(k, self.heads), _heads(v, self.heads)
         o = F.scaled_dot_product_attention(qh, kh, vh, scale=1.0 / math.sqrt(self.d_head))
         b, h, t, d = o.shape
@@ -332,26 +386,36 @@ class BasicAVTransformerBlock:
         eps = self.norm_eps
         vx, ax = video.x.contiguous(), audio.x.contiguous()
 
-        # video self-attention (transformer.py:447-471)
+        sharded = shard is not None and shard.world > 1
+        # video self-attention (transformer.py:447-471).  In a row-sharded
+        # run its K/V all-gather overlaps the audio self- and text
+        # cross-attention, which read no video rows (same results: the two
+        # streams are independent until the audio<->video cross-attention)
         sh, sc, g = self._ada("scale_shift_table", video.timesteps, 0, 3)
         at = self.attn["attn1"]
         q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
-        o = at.core(q, k, v, gl, video.positional_embeddings, gather_kv=shard)
-        vx = at.to_out(o, residual=vx, gate=g)
+        q, k = at.norm_rope(q, k, video.positional_embeddings)
+        pend = shard.start_gather(k, v) if sharded else None
+
+        # audio self-attention + text cross-attention (transformer.py:488-527)
+        sh_a, sc_a, g_a = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
+        at_a = self.attn["audio_attn1"]
+        qa, ka, va, gla = at_a.project(K.adaln_modulate(ax, sc_a, sh_a, eps), None)
+        o = at_a.core(qa, ka, va, gla, audio.positional_embeddings)
+        ax = at_a.to_out(o, residual=ax, gate=g_a)
+        ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
+
+        if pend is not None:
+            k, v = shard.finish_gather(pend)
+        vx = at.to_out(at.attend(q, k, v, gl), residual=vx, gate=g)
 
         # video text cross-attention (transformer.py:344-387, 473-486)
         vx = self._text_ca(vx, video, "attn2", "scale_shift_table", "prompt_scale_shift_table")
 
-        # audio self-attention + text cross-attention (transformer.py:488-527)
-        sh, sc, g = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
-        at = self.attn["audio_attn1"]
-        q, k, v, gl = at.project(K.adaln_modulate(ax, sc, sh, eps), None)
-        o = at.core(q, k, v, gl, audio.positional_embeddings)
-        ax = at.to_out(o, residual=ax, gate=g)
-        ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
-
         # audio <-> video cross attention (transformer.py:529-627); both read
-        # the norms of vx / ax taken before either residual update
+        # the norms of vx / ax taken before either residual update.  The
+        # video->audio K/V (video rows) gather overlaps the audio->video
+        # attention.
         a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_audio", audio)
         g_v2a = (self.tables["scale_shift_table_a2v_ca_audio"][4][None, None] + audio.cross_gate_timestep[:, :, 0])
         v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_video", video)
@@ -359,14 +423,16 @@ class BasicAVTransformerBlock:
         at = self.attn["audio_to_video_attn"]
         q, k, v, gl = at.project(K.adaln_modulate(vx, v_sc_a2v, v_sh_a2v, eps),
                                  K.adaln_modulate(ax, a_sc_a2v, a_sh_a2v, eps))
-        o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
         at2 = self.attn["video_to_audio_attn"]
         q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
                                       K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
+        q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
+        pend2 = shard.start_gather(k2, v2) if sharded else None
+        o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
         vx = at.to_out(o, residual=vx, gate=g_a2v.contiguous())
-        o2 = at2.core(q2, k2, v2, gl2, audio.cross_positional_embeddings, video.cross_positional_embeddings,
-                      gather_kv=shard)
-        ax = at2.to_out(o2, residual=ax, gate=g_v2a.contiguous())
+        if pend2 is not None:
+            k2, v2 = shard.finish_gather(pend2)
+        ax = at2.to_out(at2.attend(q2, k2, v2, gl2), residual=ax, gate=g_v2a.contiguous())
 
         # feed-forwards (transformer.py:629-668)
         vx = self._ff(vx, video, "scale_shift_table", self.ff)

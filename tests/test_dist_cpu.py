@@ -91,6 +91,39 @@ def test_row_sharded_attention_equals_unsharded(tmp_path, world):
     assert torch.allclose(got, ref, atol=1e-5, rtol=1e-5)
 
 
+def _batch_worker(rank, world, port, out_dir):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ltx-2-mlx_b200")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from ltxq.block import RowShard
+
+    g = torch.Generator().manual_seed(7)
+    full_k = torch.randn(2, 8 * world, 6, generator=g)
+    full_v = torch.randn(2, 8 * world, 6, generator=g)
+    rows = slice(rank * 8, (rank + 1) * 8)
+    shard = RowShard(dist.group.WORLD, world, rank)
+    k, v = shard.finish_gather(shard.start_gather(full_k[:, rows], full_v[:, rows], overlap=False))
+    torch.save({"k": k, "v": v, "full_k": full_k, "full_v": full_v}, os.path.join(out_dir, f"b{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_batched_gather_restores_row_order(tmp_path):
+    """Batch 2: every rank's gathered K/V equal the unsharded tensors (the
+    rank-major blocks are put back in row order per batch entry)."""
+    world = 2
+    port = _free_port()
+    mp.start_processes(_batch_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        o = torch.load(os.path.join(tmp_path, f"b{r}.pt"))
+        assert torch.equal(o["k"], o["full_k"]) and torch.equal(o["v"], o["full_v"])
+
+
 def _lonely_worker(rank, world, port, out_dir):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
