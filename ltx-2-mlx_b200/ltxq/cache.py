@@ -302,7 +302,8 @@ def quantized_linears_from_state(state: dict, in_features: dict[str, int], paylo
         else:
             bits_b = bits or payload.get("transformer_cache_quantize_bits") or payload.get("video_ff_quantize_bits")
         gs, b = quant_defaults(m, group_size or payload.get("transformer_cache_quantize_group_size")
-                               or payload.get("video_ff_quantize_group_size"), bits_b)
+                               or payload.get("video_ff_quantize_group_size")
+                               or payload.get("block_linear_quantize_group_size"), bits_b)
         n = cols * 32 // b if pretransposed else rows
         out[base] = QuantizedLinear(arrs["weight"], arrs["scales"], arrs.get("biases"), state["bias"].get(base),
                                     group_size=gs, bits=b, mode=m, pretransposed=pretransposed,
