@@ -270,6 +270,7 @@ def run_reference(args):
     if args.workload == "step":
         value = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS / (tflops * 1e12) * 1e3
         unit, hib, cfg, scaling = "ms/step", False, _step_config(world), "strong"
+        cfg["execution"] = "host cores: the oracle port (numpy, BLAS on every core)"
         desc = (f"one full-width block on {sample} of 9216 video tokens per step, extrapolated to 48 blocks x "
                 f"9216 tokens by linear FLOPs (attention excluded)")
     else:
