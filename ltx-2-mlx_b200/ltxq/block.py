@@ -378,7 +378,7 @@ class BasicAVTransformerBlock:
         """get_ada_values (transformer.py:286-309) -> list of (B, 1, C) fp32."""
         t = self.tables[table][start:end]
         vals = t[None, None] + ts[:, :, start:end]
-        return [vals[:, :, i].contiguous() for i in range(end - start)]
+        return [vals[:, :, i] for i in range(end - start)]  # views: the kernels take strided vectors
 
     def __call__(self, video: TransformerArgs, audio: TransformerArgs, shard: RowShard | None = None):
         """One block.  With ``shard``, ``video`` holds this rank's rows (and
@@ -430,10 +430,10 @@ class BasicAVTransformerBlock:
         q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
         pend2 = shard.start_gather(k2, v2) if sharded else None
         o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
-        vx = at.to_out(o, residual=vx, gate=g_a2v.contiguous())
+        vx = at.to_out(o, residual=vx, gate=g_a2v)
         if pend2 is not None:
             k2, v2 = shard.finish_gather(pend2)
-        ax = at2.to_out(at2.attend(q2, k2, v2, gl2), residual=ax, gate=g_v2a.contiguous())
+        ax = at2.to_out(at2.attend(q2, k2, v2, gl2), residual=ax, gate=g_v2a)
 
         # feed-forwards (transformer.py:629-668)
         vx = self._ff(vx, video, "scale_shift_table", self.ff)
@@ -443,7 +443,7 @@ class BasicAVTransformerBlock:
     def _ada_cross(self, table: str, args: TransformerArgs):
         """get_av_ca_ada_values (transformer.py:311-342) scale/shift rows."""
         t = self.tables[table][:4][None, None] + args.cross_scale_shift_timestep
-        return [t[:, :, i].contiguous() for i in range(4)]
+        return [t[:, :, i] for i in range(4)]
 
     def _text_ca(self, x, args: TransformerArgs, name: str, table: str, prompt_table: str,
                  shard: RowShard | None = None):
@@ -455,7 +455,7 @@ class BasicAVTransformerBlock:
         eps = self.norm_eps
         sh_q, sc_q, g = self._ada(table, args.timesteps, 6, 9)
         kv = self.tables[prompt_table][None, None] + args.prompt_timestep
-        shift_kv, scale_kv = kv[:, :, 0].contiguous(), kv[:, :, 1].contiguous()
+        shift_kv, scale_kv = kv[:, :, 0], kv[:, :, 1]
         at = self.attn[name]
         inner = at.heads * at.d_head
         ctx = args.context

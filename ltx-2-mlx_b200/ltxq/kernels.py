@@ -37,21 +37,26 @@ def vec_arg(v: torch.Tensor, rows_shape: tuple[int, ...], C: int, name: str, kee
         raise ValueError(f"{name} dtype must be bfloat16 or float32, got {v.dtype}")
     if v.shape[-1] != C:
         raise ValueError(f"{name} last dim {v.shape[-1]} != {C}")
-    v = v.contiguous()
+    if v.stride(-1) != 1:
+        v = v.contiguous()
     keep.append(v)
     lead = tuple(v.shape[:-1])
     numel_lead = 1
     for d in lead:
         numel_lead *= d
-    if numel_lead == 1:
+    if numel_lead == 1:  # one vector for all rows (a strided view is used in place)
         return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, 0, 0)
     rows = 1
     for d in rows_shape:
         rows *= d
     if numel_lead == rows:  # (B, T, C): one vector per row
+        if not v.is_contiguous():
+            v = v.contiguous()
+            keep.append(v)
         return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, 1, C)
     if len(rows_shape) >= 2 and len(lead) >= 1 and lead[0] == rows_shape[0] and numel_lead == rows_shape[0]:
-        return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, rows // rows_shape[0], C)  # (B, 1, C)
+        # (B, 1, C): one vector per batch entry, B vectors at the view's batch stride
+        return _lib.Vec(v.data_ptr(), _DT[v.dtype], 0, rows // rows_shape[0], v.stride(0))
     raise ValueError(f"{name} shape {tuple(v.shape)} does not broadcast against {rows_shape + (C,)}")
 
 

@@ -609,3 +609,29 @@ def test_pretransposed_dequant_exact_through_identity(cuda, smax, split_k):
     both_zero = ((y & 0x7FFF) == 0) & ((want & 0x7FFF) == 0)
     diff = (y != want) & ~both_zero
     assert not diff.any(), (np.argwhere(diff)[:5], y[diff][:5], want[diff][:5])
+
+
+def test_strided_vector_views_match_contiguous(cuda):
+    """AdaLN vectors and gates given as strided views of a (B, 1, 9, C) table
+    sum (the block's get_ada_values slices, transformer.py:286-309) give the
+    same bits as contiguous copies, per batch entry."""
+    torch = _torch()
+    ltxq = _ltxq()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(60)
+    B, T, C = 2, 96, 1024
+    x = torch.randn(B, T, C, generator=g, device="cuda").to(torch.bfloat16)
+    vals = torch.randn(B, 1, 9, C, generator=g, device="cuda") * 0.1
+    sc, sh = vals[:, :, 1], vals[:, :, 0]
+    assert not sc.is_contiguous()
+    a = ltxq.adaln_modulate(x, sc, sh, 1e-6)
+    b = ltxq.adaln_modulate(x, sc.contiguous(), sh.contiguous(), 1e-6)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    W = normal_bf16(rng(61), (512, C), 0.02)
+    q = oq.quantize(W, "mxfp8")
+    ql = qlinear_from_oracle(q, None, 512, C)
+    res = torch.randn(B, T, 512, generator=g, device="cuda").to(torch.bfloat16)
+    gv = (torch.randn(B, 1, 9, 512, generator=g, device="cuda") * 0.5)[:, :, 2]
+    y1 = ql(a, residual=res, gate=gv)
+    y2 = ql(a, residual=res, gate=gv.contiguous())
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
