@@ -403,15 +403,14 @@ class BasicAVTransformerBlock:
         qa, ka, va, gla = at_a.project(K.adaln_modulate(ax, sc_a, sh_a, eps), None)
         o = at_a.core(qa, ka, va, gla, audio.positional_embeddings)
         ax = at_a.to_out(o, residual=ax, gate=g_a)
-        ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table",
-                           shard)
+        ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
 
         if pend is not None:
             k, v = shard.finish_gather(pend)
         vx = at.to_out(at.attend(q, k, v, gl), residual=vx, gate=g)
 
         # video text cross-attention (transformer.py:344-387, 473-486)
-        vx = self._text_ca(vx, video, "attn2", "scale_shift_table", "prompt_scale_shift_table", shard)
+        vx = self._text_ca(vx, video, "attn2", "scale_shift_table", "prompt_scale_shift_table")
 
         # audio <-> video cross attention (transformer.py:529-627); both read
         # the norms of vx / ax taken before either residual update.  The
@@ -445,33 +444,19 @@ class BasicAVTransformerBlock:
         t = self.tables[table][:4][None, None] + args.cross_scale_shift_timestep
         return [t[:, :, i] for i in range(4)]
 
-    def _text_ca(self, x, args: TransformerArgs, name: str, table: str, prompt_table: str,
-                 shard: RowShard | None = None):
+    def _text_ca(self, x, args: TransformerArgs, name: str, table: str, prompt_table: str):
         """Text cross-attention (transformer.py:344-387).  The text context is
-        the same on every rank, so a row-sharded run splits its K/V
-        projection: each rank projects L / world context rows, and the rows
-        are all-gathered (on the side stream, overlapping the query
-        projection).  No RoPE here; the K RMSNorm is row-local."""
+        the same on every rank and its K/V projection runs replicated:
+        splitting it across 8 ranks and all-gathering the rows measured
+        slower (the gathers' latency exceeded the ~0.1 ms of GEMM saved)."""
         eps = self.norm_eps
         sh_q, sc_q, g = self._ada(table, args.timesteps, 6, 9)
         kv = self.tables[prompt_table][None, None] + args.prompt_timestep
         shift_kv, scale_kv = kv[:, :, 0], kv[:, :, 1]
         at = self.attn[name]
-        inner = at.heads * at.d_head
-        ctx = args.context
-        split = shard is not None and shard.world > 1 and ctx.shape[1] % shard.world == 0
-        if split:
-            rows = ctx.shape[1] // shard.world
-            ctx = ctx[:, shard.rank * rows:(shard.rank + 1) * rows]
-        kvp = at.kv_proj(K.adaln_modulate(ctx, scale_kv, shift_kv, eps, "none"))
-        k = K.qk_norm_rope(kvp[..., :inner], at.k_norm, at.heads, at.eps, None)
-        v = kvp[..., inner:]
-        pend = shard.start_gather(k, v) if split else None
-        y = at.q_proj(K.adaln_modulate(x, sc_q, sh_q, eps))
-        q = K.qk_norm_rope(y[..., :inner], at.q_norm, at.heads, at.eps, None)
-        if pend is not None:
-            k, v = shard.finish_gather(pend)
-        o = at.attend(q, k, v, y[..., inner:])
+        q, k, v, gl = at.project(K.adaln_modulate(x, sc_q, sh_q, eps),
+                                 K.adaln_modulate(args.context, scale_kv, shift_kv, eps, "none"))
+        o = at.core(q, k, v, gl)
         return at.to_out(o, residual=x, gate=g, gate_then_add=True)
 
     def _ff(self, x, args: TransformerArgs, table: str, ff):
