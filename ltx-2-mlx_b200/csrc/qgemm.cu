@@ -640,8 +640,14 @@ struct Epi8 {
       for (int k = 0; k < 4; ++k) u[k] = pack_bf16x2(a[2 * k], a[2 * k + 1]);  // exact: a is bf16-valued
     }
     if (p.epi == LTXQ_EPI_GELU) {
+      if (gtab != nullptr) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) u[k] = gelu_tab_x2(u[k], gtab);
+        for (int k = 0; k < 4; ++k) u[k] = gelu_tab_x2(u[k], gtab);
+      } else {  // no table: the same function evaluated directly
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          u[k] = pack_bf16x2(gelu_ref(lo_bf16(u[k])), gelu_ref(hi_bf16(u[k])));
+      }
     }
     const int64_t off = static_cast<int64_t>(m) * p.N + nf;
     if (gated) {
@@ -698,15 +704,13 @@ __device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const u
 // token row, 8 features).
 constexpr int kPairTile = 256;  // features and tokens per pair-kernel tile
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
-  __shared__ uint16_t gtab[2 * kGeluN];
-  if (p.epi == LTXQ_EPI_GELU) {
-    gelu_tab_fill(gtab, threadIdx.x, blockDim.x);
-    __syncthreads();
-  }
+  // GELU is evaluated directly here (a handful of elements per thread: a
+  // per-block table would cost more to build than it saves)
   const int n_pt = (p.N + kPairTile - 1) / kPairTile;
   const int tiles = n_pt * ((p.M + kPairTile - 1) / kPairTile);
   const int64_t items = static_cast<int64_t>(tiles - p.dp_tiles) * kPairTile * (kPairTile / 8);
   constexpr size_t kTileElems = static_cast<size_t>(kPairTile) * kPairTile;
+  constexpr int kBatch = 4;  // splits whose partials are loaded before they are added (loads in flight)
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int ti = static_cast<int>(it / (kPairTile * (kPairTile / 8)));
@@ -717,20 +721,31 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
     const int nf = (tile % n_pt) * kPairTile + f;
     if (m >= p.M || nf >= p.N) continue;
     const float* src = p.partial + static_cast<size_t>(ti) * p.splits * kTileElems + j * kPairTile + f;
-    float a[8];
-    {
-      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src));
-      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + 4));
-      a[0] = lo.x; a[1] = lo.y; a[2] = lo.z; a[3] = lo.w;
-      a[4] = hi.x; a[5] = hi.y; a[6] = hi.z; a[7] = hi.w;
-    }
-    for (int sp = 1; sp < p.splits; ++sp) {
-      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src + sp * kTileElems));
-      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + sp * kTileElems + 4));
-      a[0] = __fadd_rn(a[0], lo.x); a[1] = __fadd_rn(a[1], lo.y);
-      a[2] = __fadd_rn(a[2], lo.z); a[3] = __fadd_rn(a[3], lo.w);
-      a[4] = __fadd_rn(a[4], hi.x); a[5] = __fadd_rn(a[5], hi.y);
-      a[6] = __fadd_rn(a[6], hi.z); a[7] = __fadd_rn(a[7], hi.w);
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int sp0 = 0; sp0 < p.splits; sp0 += kBatch) {
+      float4 lo[kBatch], hi[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        if (sp0 + b < p.splits) {
+          lo[b] = __ldcg(reinterpret_cast<const float4*>(src + (sp0 + b) * kTileElems));
+          hi[b] = __ldcg(reinterpret_cast<const float4*>(src + (sp0 + b) * kTileElems + 4));
+        }
+      }
+      // added in split order; split 0 starts the sum (0 + x = x exactly, -0 aside: the
+      // first partial is taken as is)
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        if (sp0 + b >= p.splits) break;
+        if (sp0 + b == 0) {
+          a[0] = lo[b].x; a[1] = lo[b].y; a[2] = lo[b].z; a[3] = lo[b].w;
+          a[4] = hi[b].x; a[5] = hi[b].y; a[6] = hi[b].z; a[7] = hi[b].w;
+        } else {
+          a[0] = __fadd_rn(a[0], lo[b].x); a[1] = __fadd_rn(a[1], lo[b].y);
+          a[2] = __fadd_rn(a[2], lo[b].z); a[3] = __fadd_rn(a[3], lo[b].w);
+          a[4] = __fadd_rn(a[4], hi[b].x); a[5] = __fadd_rn(a[5], hi[b].y);
+          a[6] = __fadd_rn(a[6], hi[b].z); a[7] = __fadd_rn(a[7], hi[b].w);
+        }
+      }
     }
 #pragma unroll
     for (int k = 0; k < 8; k += 2) {
@@ -740,7 +755,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
     }
     Epi8 e;
     e.init(p, nf);
-    e.store(p, a, m, nf, gtab);
+    e.store(p, a, m, nf, nullptr);
   }
 }
 
