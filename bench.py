@@ -2,8 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload step|ff]
 
-Default workload "step" (the metric's own
-configuration): one 22B-shaped denoise step -- 48 random-init audio-video
+Default workload "step" (benchmark config 4, the configuration the
+headline metric is quoted on): one 22B-shaped denoise step -- 48 random-init audio-video
 blocks, every block linear quantized mxfp8 (group 32, E8M0 scales) on the
 GPU from bf16 weights ~N(0, 0.02), 1024x576x121 frames -> 9216 video tokens
 (d 4096, 32 heads x 128), 201 audio tokens (d 2048, 32 x 64), 1024 text tokens

@@ -23,7 +23,7 @@ Restates the checkpoint side of LTX_2_MLX/loader:
 
 Beyond the reference's modes (off, mxfp8-blocks, mxfp8-blocks-pretranspose),
 ``affine=(bits, group_size)`` quantizes the block linears with MLX affine
-int8 / int4 (the layout BASELINE's configs 1-3 and 5 use); the payload then
+int8 / int4 (the layout of benchmark configs 1-3 and 5); the payload then
 records ``block_linear_quantize = "affine"`` with its bits and group size.
 """
 

@@ -69,7 +69,7 @@ def modulate(normed_bf16, scale, shift, vec_bf16: bool = False):
 def adaln(x, scale, shift, eps: float = EPS, norm: str = "rms", vec_bf16: bool = False):
     """``_adaln_inline`` (transformer.py:21-37) / ``_adaln_norm_mlx``
     (fused_ops.py:192-201): RMSNorm then modulate.  ``norm="layer"`` gives the
-    non-affine LayerNorm variant BASELINE config 1 names."""
+    non-affine LayerNorm variant that benchmark config 1 names."""
     nrm = rms_norm(x, eps) if norm == "rms" else layer_norm(x, eps)
     return modulate(nrm, scale, shift, vec_bf16)
 
@@ -167,7 +167,7 @@ def feed_forward(x_bf16, w_in, b_in, w_out, b_out):
 
 def adaln_linear_gated(x, scale, shift, gate, w_deq, bias, eps: float = EPS,
                        norm: str = "rms", vec_bf16: bool = False):
-    """``out = x + gate * (modulate(norm(x)) @ W^T + b)``
+    """Benchmark config 1: ``out = x + gate * (modulate(norm(x)) @ W^T + b)``
     with the reference's rounding points."""
     a = adaln(x, scale, shift, eps, norm, vec_bf16)
     y = linear(a, w_deq, bias)
@@ -176,7 +176,7 @@ def adaln_linear_gated(x, scale, shift, gate, w_deq, bias, eps: float = EPS,
 
 def ff_sublayer(x, scale, shift, gate, w_in, b_in, w_out, b_out, eps: float = EPS,
                 norm: str = "rms", vec_bf16: bool = False):
-    """BASELINE config 2 / transformer.py:629-650: AdaLN -> FF -> gated add."""
+    """Benchmark config 2 / transformer.py:629-650: AdaLN -> FF -> gated add."""
     a = adaln(x, scale, shift, eps, norm, vec_bf16)
     y = feed_forward(a, w_in, b_in, w_out, b_out)
     return gated_add(x, y, gate, vec_bf16)
@@ -201,7 +201,7 @@ def cosine(a, b) -> float:
 
 
 def max_abs_rel(a, ref) -> float:
-    """max|a - ref| / max|ref| (the BASELINE tolerance measure)."""
+    """max|a - ref| / max|ref| (the path's stated tolerance measure: <= 2e-2)."""
     a = np.asarray(a, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.abs(a - ref).max() / max(np.abs(ref).max(), 1e-30))

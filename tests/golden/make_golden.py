@@ -74,7 +74,7 @@ def oracle_vectors() -> dict[str, np.ndarray]:
         out[f"affine{bits}_scales"] = qa["scales"]
         out[f"affine{bits}_biases"] = qa["biases"]
         out[f"affine{bits}_dequant"] = f32_to_bf16_bits(oq.dequantize(qa, 256))
-    # BASELINE config 1 structure at a small size: x + gate * (mod(LN(x)) @ W^T + b)
+    # benchmark config 1 structure at a small size: x + gate * (mod(LN(x)) @ W^T + b)
     x = ro.rbf16(g.standard_normal((8, 256)).astype(np.float32))
     sc = ro.rbf16(g.standard_normal((1, 256)).astype(np.float32) * np.float32(0.1))
     sh = ro.rbf16(g.standard_normal((1, 256)).astype(np.float32) * np.float32(0.1))

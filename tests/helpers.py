@@ -1,5 +1,5 @@
 """Shared test helpers: seeded inputs (numpy PCG64 -> fp32 -> bf16 RNE, the
-generator BASELINE's configs are drawn with) and numpy <-> torch moves."""
+generator the benchmark configs are drawn with) and numpy <-> torch moves."""
 
 from __future__ import annotations
 

@@ -1,6 +1,6 @@
 """GPU parity of the CUDA path against the numpy oracle, through the C ABI.
 
-Bars: dequantized weights and quantizer outputs
+Bars (the path's stated parity requirements): dequantized weights and quantizer outputs
 bit-exact; elementwise kernels bit-exact (same rounding points, fp64 row
 statistics); GEMM outputs within max-abs-rel <= 2e-2 and cosine >= 0.9995 of
 the reference composition (in practice within 1 bf16 ulp on almost every
@@ -379,7 +379,7 @@ def test_split_k_deterministic(cuda):
 
 
 def test_adaln_qlinear_gated_config1_small(cuda):
-    """BASELINE config 1 structure at a reduced M (full size in test_gpu_configs)."""
+    """Benchmark config 1 structure (fused AdaLN + int8 linear + gated residual) at a reduced M."""
     torch = _torch()
     g = rng(0)
     M, C = 256, 1024
