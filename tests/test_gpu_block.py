@@ -149,3 +149,58 @@ def test_step_graph_replay_matches_eager(cuda):
     assert torch.equal(ga_x.view(torch.int16), ea.x.view(torch.int16))
     g.release()
     assert ltxq._lib.device_error() == 0
+
+
+def test_av_block_batch2_matches_oracle_per_entry(cuda):
+    """Batch 2 (the cond/uncond pair of classifier-free guidance): per-batch
+    AdaLN vectors, RoPE tables and contexts; each batch entry equals the
+    oracle block run on that entry alone."""
+    import torch
+
+    import ltxq
+    from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
+
+    video = StreamConfig(1024, 8, 128, 1024)
+    audio = StreamConfig(512, 8, 64, 512)
+    T, A, L = 96, 40, 32
+    mode, bits = "mxfp8", 8
+    p_oracle, quant, tables = _params(video, audio, mode, bits, seed=33)
+    g = rng(34)
+    lin = {}
+    for name, (q, b) in quant.items():
+        lin[name] = ltxq.QuantizedLinear(to_dev(q["weight"]), torch.from_numpy(q["scales"].copy()).cuda(), None,
+                                         to_dev_bf16(b), group_size=32, bits=8, mode=mode)
+    blk = BasicAVTransformerBlock(lin, {k: torch.from_numpy(v).cuda() for k, v in tables.items()}, video, audio)
+
+    def stream(cfg, tokens):
+        return {
+            "x": normal_bf16(g, (tokens, cfg.dim)),
+            "context": normal_bf16(g, (L, cfg.context_dim)),
+            "timesteps": normal_f32(g, (9, cfg.dim), 0.1),
+            "prompt": normal_f32(g, (2, cfg.dim), 0.1),
+            "cross_ss": normal_f32(g, (4, cfg.dim), 0.1),
+            "cross_gate": normal_f32(g, (1, cfg.dim), 0.1),
+            "pe": _rope(g, cfg.heads, tokens, cfg.d_head),
+            "cross_pe": _rope(g, audio.heads, tokens, audio.d_head),
+        }
+
+    entries = [(stream(video, T), stream(audio, A)) for _ in range(2)]
+
+    def args(ds):
+        f = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+        st = lambda key: torch.stack([f(d[key]) for d in ds])  # noqa: E731
+        pe = tuple(torch.stack([f(d["pe"][i]) for d in ds]) for i in range(2))
+        cpe = tuple(torch.stack([f(d["cross_pe"][i]) for d in ds]) for i in range(2))
+        return TransformerArgs(x=torch.stack([to_dev_bf16(d["x"]) for d in ds]),
+                               context=torch.stack([to_dev_bf16(d["context"]) for d in ds]),
+                               timesteps=st("timesteps")[:, None], positional_embeddings=pe,
+                               cross_positional_embeddings=cpe, cross_scale_shift_timestep=st("cross_ss")[:, None],
+                               cross_gate_timestep=st("cross_gate")[:, None], prompt_timestep=st("prompt")[:, None])
+
+    ov, oa = blk(args([e[0] for e in entries]), args([e[1] for e in entries]))
+    for bi, (vs, as_) in enumerate(entries):
+        ref_v, ref_a = ob.block(p_oracle, vs, as_, heads_v=video.heads, heads_a=audio.heads)
+        for got, ref, what in ((from_dev_bf16(ov.x[bi]), ref_v, "video"), (from_dev_bf16(oa.x[bi]), ref_a, "audio")):
+            mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
+            assert mar <= 2e-2 and cos >= 0.9995, f"entry {bi} {what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
+    assert ltxq._lib.device_error() == 0
