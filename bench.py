@@ -310,7 +310,8 @@ def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8"):
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
             "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
             "quant": STEP_QUANT[quant][3],
-            "parallelism": f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL, side stream)",
+            "parallelism": (f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL, side stream)"
+                            if world > 1 else "single GPU (no collective)"),
             "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
 
 
