@@ -305,10 +305,10 @@ def _packed_bytes(quant, n, k):
     return n * k * bits // 8 + 2 * 2 * n * k // 64
 
 
-def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8"):
-    return {"workload": STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": STEP_T,
+def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8", video_tokens=STEP_T):
+    return {"workload": STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": video_tokens,
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
-            "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": STEP_T,
+            "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": video_tokens,
             "quant": STEP_QUANT[quant][3],
             "parallelism": (f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL, side stream)"
                             if world > 1 else "single GPU (no collective)"),
@@ -338,9 +338,10 @@ def run_step(args, world, rank, local, dev):
     from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, RowShard, TransformerArgs
     from ltxq.graph import StepGraph
 
-    if STEP_T % world:
-        raise SystemExit(f"{STEP_T} video tokens do not split over {world} ranks")
-    tl = STEP_T // world
+    T = args.video_tokens
+    if T % world:
+        raise SystemExit(f"{T} video tokens do not split over {world} ranks")
+    tl = T // world
     shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank, overlap=not args.no_overlap)
     gen = torch.Generator(device=dev)
     gen.manual_seed(2026)  # identical on every rank: weights are replicated
@@ -356,10 +357,10 @@ def run_step(args, world, rank, local, dev):
         ang = torch.rand(1, heads, t, d // 2, generator=gen, device=dev) * 6.2831853
         return torch.cos(ang), torch.sin(ang)
 
-    vx_full = rnd(1, STEP_T, VD, dtype=torch.bfloat16)
+    vx_full = rnd(1, T, VD, dtype=torch.bfloat16)
     ax = rnd(1, STEP_A, AD, dtype=torch.bfloat16)
-    pe_v = rope(VIDEO_22B.heads, STEP_T, VIDEO_22B.d_head)
-    cpe_v = rope(AUDIO_22B.heads, STEP_T, AUDIO_22B.d_head)
+    pe_v = rope(VIDEO_22B.heads, T, VIDEO_22B.d_head)
+    cpe_v = rope(AUDIO_22B.heads, T, AUDIO_22B.d_head)
     rows = slice(rank * tl, (rank + 1) * tl)
     video = TransformerArgs(
         x=vx_full[:, rows].contiguous(), context=rnd(1, STEP_L, VD, dtype=torch.bfloat16),
@@ -470,14 +471,14 @@ def run_step(args, world, rank, local, dev):
 
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = _peaks()
-        lin_flops = step_linear_flops(STEP_T, STEP_A, STEP_L) * n_blocks
+        lin_flops = step_linear_flops(T, STEP_A, STEP_L) * n_blocks
         ff_flops = 2.0 * tl * VD * 4 * VD
         achieved = ff_flops / (ff_avg / 1e3) / 1e12
         h2d = vx_host.numel() * 2 + ax_host.numel() * 2
         line = {
             "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks, use_graph, args.quant),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks, use_graph, args.quant, T),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
@@ -631,6 +632,8 @@ def main():
                     help="run the K/V all-gathers on the compute stream instead of a side stream")
     ap.add_argument("--quant", choices=sorted(STEP_QUANT), default="mxfp8",
                     help="block-linear quantization of the step workload (config 4 is mxfp8)")
+    ap.add_argument("--video-tokens", type=int, default=STEP_T,
+                    help="video tokens of the step (9216 = config 4; fewer only to study per-rank shapes on one GPU)")
     ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,
                     help="blocks per step (48 = the 22B model; fewer only for bounded profiler captures)")
     args = ap.parse_args()
