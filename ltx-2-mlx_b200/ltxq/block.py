@@ -199,6 +199,35 @@ class RowShard:
                 dist.all_gather_into_tensor(o, x, group=self.group)
         return PendingGather(outs, xs, self._comm)
 
+    def all_to_all(self, x: torch.Tensor) -> torch.Tensor:
+        """Equal-split all-to-all along dim 0 (block g goes to rank g)."""
+        import torch.distributed as dist
+
+        out = torch.empty_like(x)
+        dist.all_to_all_single(out, x, group=self.group)
+        return out
+
+    def start_all_to_all(self, x: torch.Tensor) -> "PendingGather":
+        """``all_to_all`` on the side stream; ``finish_all_to_all`` joins it."""
+        import torch.distributed as dist
+
+        x = x.contiguous()
+        out = torch.empty_like(x)
+        if not self.overlap:
+            dist.all_to_all_single(out, x, group=self.group)
+            return PendingGather((out,), None, None)
+        if self._comm is None:
+            self._comm = torch.cuda.Stream(device=x.device)
+        self._comm.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(self._comm):
+            dist.all_to_all_single(out, x, group=self.group)
+        return PendingGather((out,), (x,), self._comm)
+
+    def finish_all_to_all(self, pending: "PendingGather") -> torch.Tensor:
+        if pending.stream is not None:
+            torch.cuda.current_stream(pending.outs[0].device).wait_stream(pending.stream)
+        return pending.outs[0]
+
     def finish_gather(self, pending: "PendingGather") -> tuple:
         """Join the side stream and return the gathered (B, world * T, C)."""
         if self.world == 1:
@@ -223,6 +252,45 @@ class PendingGather:
     outs: tuple
     inputs: tuple
     stream: object
+
+
+def heads_to_ranks(x: torch.Tensor, world: int, heads: int) -> torch.Tensor:
+    """(B, T_local, H*D) -> the all-to-all send layout [world, B, T_local,
+    H/world, D]: block g holds the heads rank g attends over."""
+    b, t, w = x.shape
+    d = w // heads
+    return x.view(b, t, world, heads // world, d).permute(2, 0, 1, 3, 4).contiguous()
+
+
+def ranks_to_sequence(y: torch.Tensor) -> torch.Tensor:
+    """All-to-all receive layout [world (source = token block), B, T_local,
+    H/world, D] -> (B, H/world, world*T_local, D), tokens in global order."""
+    w, b, t, h, d = y.shape
+    return y.permute(1, 3, 0, 2, 4).reshape(b, h, w * t, d)
+
+
+def sequence_to_ranks(o: torch.Tensor, world: int) -> torch.Tensor:
+    """(B, H/world, T, D) attention output -> the send layout [world (dest =
+    token block), B, H/world, T/world, D]."""
+    b, h, t, d = o.shape
+    return o.view(b, h, world, t // world, d).permute(2, 0, 1, 3, 4).contiguous()
+
+
+def ranks_to_heads(y: torch.Tensor) -> torch.Tensor:
+    """Receive layout [world (source = head group), B, H/world, T_local, D] ->
+    (B, T_local, H*D) with head group g at heads g*H/world ..."""
+    w, b, h, t, d = y.shape
+    return y.permute(1, 3, 0, 2, 4).reshape(b, t, w * h * d)
+
+
+def merge_attention_partials(outs: torch.Tensor, lses: torch.Tensor) -> torch.Tensor:
+    """Softmax attention over a key set split into parts: outs [P, ..., Lq, D]
+    (each part's normalized output) and lses [P, ..., Lq] (each part's
+    natural-log sum of exp scores) -> the output over all keys,
+    sum_p exp(lse_p - L) out_p with L = logsumexp_p(lse_p), in fp32."""
+    lse = torch.logsumexp(lses, dim=0)
+    w = torch.exp(lses - lse.unsqueeze(0)).unsqueeze(-1)
+    return (w * outs.float()).sum(dim=0)
 
 
 @dataclass
@@ -273,6 +341,41 @@ class QAttention:
         b, h, t, d = o.shape
         o = o.transpose(1, 2).reshape(b, t, h * d)
         return K.head_gate(o, gl.contiguous(), self.heads)
+
+    def attend_head_parallel(self, qkv_recv: torch.Tensor, gl, shard: "RowShard") -> torch.Tensor:
+        """Row-sharded self-attention in head-parallel form: ``qkv_recv`` is
+        the all-to-all of [world, 3, B, T_local, H/world, D] (Q, K, V of
+        ``heads_to_ranks``; this rank now holds H/world heads over all T
+        tokens); SDPA runs on those heads and a second all-to-all returns
+        every rank its token rows.  Each rank sends and receives (world-1)/world
+        of its own Q, K, V and output rows, instead of receiving every other
+        rank's K and V."""
+        q, k, v = (ranks_to_sequence(qkv_recv[:, i]) for i in range(3))
+        o = F.scaled_dot_product_attention(q, k, v, scale=1.0 / math.sqrt(self.d_head))
+        back = shard.all_to_all(sequence_to_ranks(o, shard.world))
+        return K.head_gate(ranks_to_heads(back), gl.contiguous(), self.heads)
+
+    def attend_split_keys(self, q, k_local, v_local, gl, shard: "RowShard") -> torch.Tensor:
+        """Attention of replicated queries over keys / values sharded by rows:
+        each rank attends over its own rows (memory-efficient SDPA, which also
+        returns the log-sum-exp), the small per-rank outputs are
+        all-gathered and merged (``merge_attention_partials``)."""
+        import torch.distributed as dist
+
+        qh, kh, vh = _heads(q, self.heads), _heads(k_local, self.heads), _heads(v_local, self.heads)
+        o, lse = torch.ops.aten._scaled_dot_product_efficient_attention(
+            qh, kh, vh, None, True, 0.0, False, scale=1.0 / math.sqrt(self.d_head))[:2]
+        lq = qh.shape[2]
+        part = torch.cat([o.float().flatten(), lse[..., :lq].float().flatten()])
+        parts = torch.empty(shard.world * part.numel(), dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(parts, part, group=shard.group)  # flat: valid for NCCL and gloo
+        parts = parts.view(shard.world, -1)
+        n_o = o.numel()
+        outs = parts[:, :n_o].view((shard.world,) + tuple(o.shape))
+        lses = parts[:, n_o:].view((shard.world,) + tuple(o.shape[:-1]))
+        merged = merge_attention_partials(outs, lses).to(torch.bfloat16)
+        b, h, t, d = merged.shape
+        return K.head_gate(merged.transpose(1, 2).reshape(b, t, h * d), gl.contiguous(), self.heads)
 
 
 def _cat_linears(parts: list[QuantizedLinear]) -> QuantizedLinear:
@@ -388,14 +491,21 @@ class BasicAVTransformerBlock:
 
         sharded = shard is not None and shard.world > 1
         # video self-attention (transformer.py:447-471).  In a row-sharded
-        # run its K/V all-gather overlaps the audio self- and text
-        # cross-attention, which read no video rows (same results: the two
-        # streams are independent until the audio<->video cross-attention)
+        # run its Q/K/V all-to-all (head-parallel attention; an all-gather of
+        # K/V when the heads do not split evenly) overlaps the audio self- and
+        # text cross-attention, which read no video rows (same results: the
+        # two streams are independent until the audio<->video cross-attention)
         sh, sc, g = self._ada("scale_shift_table", video.timesteps, 0, 3)
         at = self.attn["attn1"]
         q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
         q, k = at.norm_rope(q, k, video.positional_embeddings)
-        pend = shard.start_gather(k, v) if sharded else None
+        head_par = sharded and at.heads % shard.world == 0
+        pend = None
+        if head_par:  # head-parallel attention: Q/K/V all-to-all, then SDPA on H/world heads
+            qkv = torch.stack([heads_to_ranks(t_, shard.world, at.heads) for t_ in (q, k, v)], dim=1)
+            pend = shard.start_all_to_all(qkv)
+        elif sharded:
+            pend = shard.start_gather(k, v)
 
         # audio self-attention + text cross-attention (transformer.py:488-527)
         sh_a, sc_a, g_a = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
@@ -405,9 +515,13 @@ class BasicAVTransformerBlock:
         ax = at_a.to_out(o, residual=ax, gate=g_a)
         ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
 
-        if pend is not None:
-            k, v = shard.finish_gather(pend)
-        vx = at.to_out(at.attend(q, k, v, gl), residual=vx, gate=g)
+        if head_par:
+            o = at.attend_head_parallel(shard.finish_all_to_all(pend), gl, shard)
+        else:
+            if pend is not None:
+                k, v = shard.finish_gather(pend)
+            o = at.attend(q, k, v, gl)
+        vx = at.to_out(o, residual=vx, gate=g)
 
         # video text cross-attention (transformer.py:344-387, 473-486)
         vx = self._text_ca(vx, video, "attn2", "scale_shift_table", "prompt_scale_shift_table")
@@ -427,12 +541,14 @@ class BasicAVTransformerBlock:
         q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
                                       K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
         q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
-        pend2 = shard.start_gather(k2, v2) if sharded else None
         o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
         vx = at.to_out(o, residual=vx, gate=g_a2v)
-        if pend2 is not None:
-            k2, v2 = shard.finish_gather(pend2)
-        ax = at2.to_out(at2.attend(q2, k2, v2, gl2), residual=ax, gate=g_v2a)
+        # video->audio: the audio queries are on every rank, the video keys
+        # are split by rows; each rank attends over its rows and the partial
+        # results merge by their log-sum-exp (a ~1 MB exchange instead of an
+        # all-gather of the video K/V)
+        o2 = at2.attend_split_keys(q2, k2, v2, gl2, shard) if sharded else at2.attend(q2, k2, v2, gl2)
+        ax = at2.to_out(o2, residual=ax, gate=g_v2a)
 
         # feed-forwards (transformer.py:629-668)
         vx = self._ff(vx, video, "scale_shift_table", self.ff)

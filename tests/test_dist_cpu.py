@@ -142,3 +142,68 @@ def test_missing_rank_times_out_on_host(tmp_path):
     mp.start_processes(_lonely_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     assert os.path.exists(os.path.join(tmp_path, "error"))
     assert not os.path.exists(os.path.join(tmp_path, "joined"))
+
+
+def _hp_worker(rank, world, port, out_dir):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "ltx-2-mlx_b200")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from ltxq.block import (RowShard, heads_to_ranks, merge_attention_partials, ranks_to_heads,
+                            ranks_to_sequence, sequence_to_ranks)
+
+    q, k, v, _, heads = _case()
+    q, k, v = q.float(), k.float(), v.float()
+    T = q.shape[1]
+    tl = T // world
+    rows = slice(rank * tl, (rank + 1) * tl)
+    shard = RowShard(dist.group.WORLD, world, rank, overlap=False)
+    # head-parallel self-attention: Q/K/V rows -> heads, attention, back to rows
+    send = torch.stack([heads_to_ranks(t[:, rows].contiguous(), world, heads) for t in (q, k, v)], dim=1)
+    recv = shard.all_to_all(send)
+    qh, kh, vh = (ranks_to_sequence(recv[:, i]) for i in range(3))
+    o = torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)
+    hp = ranks_to_heads(shard.all_to_all(sequence_to_ranks(o, world)))
+    # replicated queries over row-split keys, merged by log-sum-exp
+    d = q.shape[2] // heads
+    qf = q.view(1, T, heads, d).transpose(1, 2)
+    kl = k[:, rows].reshape(1, tl, heads, d).transpose(1, 2)
+    vl = v[:, rows].reshape(1, tl, heads, d).transpose(1, 2)
+    sc = (qf @ kl.transpose(-1, -2)) / d ** 0.5
+    lse = torch.logsumexp(sc, dim=-1)
+    part_o = torch.softmax(sc, dim=-1) @ vl
+    outs = torch.empty(world * part_o.numel())
+    lses = torch.empty(world * lse.numel())
+    dist.all_gather_into_tensor(outs, part_o.contiguous().flatten())
+    dist.all_gather_into_tensor(lses, lse.contiguous().flatten())
+    merged = merge_attention_partials(outs.view((world,) + tuple(part_o.shape)),
+                                      lses.view((world,) + tuple(lse.shape)))
+    torch.save({"hp": hp, "merged": merged}, os.path.join(out_dir, f"hp{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_parallel_and_split_key_attention(tmp_path, world):
+    """The two sharded attention forms of the block: head-parallel
+    self-attention (all-to-all of Q/K/V rows to heads and back) equals the
+    unsharded attention on each rank's rows; replicated queries over row-split
+    keys, merged by log-sum-exp, equal attention over all keys."""
+    port = _free_port()
+    mp.start_processes(_hp_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method="spawn")
+    q, k, v, _, heads = _case()
+    q, k, v = q.float(), k.float(), v.float()
+    full = _attention(q, k, v, heads)
+    T = q.shape[1]
+    tl = T // world
+    d = q.shape[2] // heads
+    ref_merged = torch.nn.functional.scaled_dot_product_attention(
+        q.view(1, T, heads, d).transpose(1, 2), k.view(1, T, heads, d).transpose(1, 2),
+        v.view(1, T, heads, d).transpose(1, 2))
+    for r in range(world):
+        o = torch.load(os.path.join(tmp_path, f"hp{r}.pt"))
+        assert torch.allclose(o["hp"], full[:, r * tl:(r + 1) * tl], atol=1e-5, rtol=1e-5)
+        assert torch.allclose(o["merged"], ref_merged, atol=1e-5, rtol=1e-5)

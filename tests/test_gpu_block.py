@@ -204,3 +204,34 @@ def test_av_block_batch2_matches_oracle_per_entry(cuda):
             mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
             assert mar <= 2e-2 and cos >= 0.9995, f"entry {bi} {what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
     assert ltxq._lib.device_error() == 0
+
+
+def test_split_key_merge_matches_full_attention(cuda):
+    """The log-sum-exp the video->audio split-key attention merges with (from
+    the memory-efficient SDPA, natural log, padded query dimension) gives
+    the full attention: two key halves merged vs SDPA over all keys."""
+    import math
+
+    import torch
+    import torch.nn.functional as F
+
+    from ltxq.block import merge_attention_partials
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(70)
+    B, H, Lq, Lk, D = 1, 32, 201, 2304, 64
+    q = torch.randn(B, H, Lq, D, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, H, Lk, D, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, H, Lk, D, generator=g, device="cuda").to(torch.bfloat16)
+    sc = 1.0 / math.sqrt(D)
+    outs, lses = [], []
+    for part in range(2):
+        ks, vs = k[:, :, part * Lk // 2:(part + 1) * Lk // 2], v[:, :, part * Lk // 2:(part + 1) * Lk // 2]
+        o, lse = torch.ops.aten._scaled_dot_product_efficient_attention(q, ks, vs, None, True, 0.0, False,
+                                                                        scale=sc)[:2]
+        outs.append(o.float())
+        lses.append(lse[..., :Lq].float())
+    merged = merge_attention_partials(torch.stack(outs), torch.stack(lses))
+    full = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), scale=sc)
+    err = (merged - full).abs().max().item() / full.abs().max().item()
+    assert err < 1e-2, err
