@@ -305,13 +305,19 @@ def _packed_bytes(quant, n, k):
     return n * k * bits // 8 + 2 * 2 * n * k // 64
 
 
-def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8", video_tokens=STEP_T):
+_EXCHANGE = {"gather": "video self-attention K/V all-gather", "head_parallel": "video self-attention Q/K/V and "
+             "output all-to-all (head-parallel)", "split_keys": "video->audio local keys merged by log-sum-exp"}
+
+
+def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8", video_tokens=STEP_T,
+                 self_attention="gather", v2a="gather"):
+    v2a_text = "video->audio K/V all-gather" if v2a == "gather" else _EXCHANGE[v2a]
     return {"workload": STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": video_tokens,
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
             "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": video_tokens,
             "quant": STEP_QUANT[quant][3],
-            "parallelism": (f"video rows sharded x{world}, weights replicated, K/V all-gather (NCCL, side stream)"
-                            if world > 1 else "single GPU (no collective)"),
+            "parallelism": (f"video rows sharded x{world}, weights replicated, {_EXCHANGE[self_attention]}, "
+                            f"{v2a_text} (NCCL)" if world > 1 else "single GPU (no collective)"),
             "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
 
 
@@ -342,7 +348,8 @@ def run_step(args, world, rank, local, dev):
     if T % world:
         raise SystemExit(f"{T} video tokens do not split over {world} ranks")
     tl = T // world
-    shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank, overlap=not args.no_overlap)
+    shard = RowShard(torch.distributed.group.WORLD if world > 1 else None, world, rank, overlap=not args.no_overlap,
+                     self_attention=args.self_attention, v2a=args.v2a)
     gen = torch.Generator(device=dev)
     gen.manual_seed(2026)  # identical on every rank: weights are replicated
     n_blocks = args.blocks
@@ -478,7 +485,8 @@ def run_step(args, world, rank, local, dev):
         line = {
             "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _step_config(world, n_blocks, use_graph, args.quant, T),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": _step_config(world, n_blocks, use_graph, args.quant, T, args.self_attention, args.v2a),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
@@ -630,6 +638,10 @@ def main():
                     help="launch the step op by op instead of replaying it as one captured CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
                     help="run the K/V all-gathers on the compute stream instead of a side stream")
+    ap.add_argument("--self-attention", choices=["gather", "head_parallel"], default="gather",
+                    help="row-sharded video self-attention: K/V all-gather, or Q/K/V all-to-all over heads")
+    ap.add_argument("--v2a", choices=["gather", "split_keys"], default="gather",
+                    help="row-sharded video->audio attention: K/V all-gather, or local keys merged by log-sum-exp")
     ap.add_argument("--quant", choices=sorted(STEP_QUANT), default="mxfp8",
                     help="block-linear quantization of the step workload (config 4 is mxfp8)")
     ap.add_argument("--video-tokens", type=int, default=STEP_T,

@@ -164,6 +164,13 @@ class RowShard:
     world: int = 1
     rank: int = 0
     overlap: bool = True  # run the all-gathers on a side stream (start_gather / finish_gather)
+    # video self-attention exchange: "gather" (all-gather K/V, attend the
+    # local query rows) or "head_parallel" (all-to-all Q/K/V, attend H/world
+    # heads over all rows, all-to-all the output back)
+    self_attention: str = "gather"
+    # video->audio keys: "gather" (all-gather the video K/V) or "split_keys"
+    # (attend the local rows, merge the partial outputs by log-sum-exp)
+    v2a: str = "gather"
     _comm: object = field(default=None, repr=False, compare=False)
 
     def gather_rows(self, x: torch.Tensor) -> torch.Tensor:
@@ -499,7 +506,7 @@ class BasicAVTransformerBlock:
         at = self.attn["attn1"]
         q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
         q, k = at.norm_rope(q, k, video.positional_embeddings)
-        head_par = sharded and at.heads % shard.world == 0
+        head_par = sharded and shard.self_attention == "head_parallel" and at.heads % shard.world == 0
         pend = None
         if head_par:  # head-parallel attention: Q/K/V all-to-all, then SDPA on H/world heads
             qkv = torch.stack([heads_to_ranks(t_, shard.world, at.heads) for t_ in (q, k, v)], dim=1)
@@ -541,13 +548,20 @@ class BasicAVTransformerBlock:
         q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
                                       K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
         q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
+        split_keys = sharded and shard.v2a == "split_keys"
+        pend2 = shard.start_gather(k2, v2) if sharded and not split_keys else None
         o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
         vx = at.to_out(o, residual=vx, gate=g_a2v)
         # video->audio: the audio queries are on every rank, the video keys
-        # are split by rows; each rank attends over its rows and the partial
-        # results merge by their log-sum-exp (a ~1 MB exchange instead of an
-        # all-gather of the video K/V)
-        o2 = at2.attend_split_keys(q2, k2, v2, gl2, shard) if sharded else at2.attend(q2, k2, v2, gl2)
+        # are split by rows.  "split_keys": each rank attends over its rows
+        # and the partial results merge by their log-sum-exp (a ~1 MB exchange
+        # instead of an all-gather of the video K/V)
+        if split_keys:
+            o2 = at2.attend_split_keys(q2, k2, v2, gl2, shard)
+        else:
+            if pend2 is not None:
+                k2, v2 = shard.finish_gather(pend2)
+            o2 = at2.attend(q2, k2, v2, gl2)
         ax = at2.to_out(o2, residual=ax, gate=g_v2a)
 
         # feed-forwards (transformer.py:629-668)

@@ -62,7 +62,7 @@ def _rows(args, lo, hi):
                                                           for c in args.cross_positional_embeddings))
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, self_attention, v2a):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -78,7 +78,7 @@ def _worker(rank, world, port, out_dir):
     blocks, v, a = _build(dev)
     T = v.x.shape[1]
     tl = T // world
-    shard = RowShard(dist.group.WORLD, world, rank)
+    shard = RowShard(dist.group.WORLD, world, rank, self_attention=self_attention, v2a=v2a)
     vv, aa = _rows(v, rank * tl, (rank + 1) * tl), a
     for b in blocks:
         vv, aa = b(vv, aa, shard)
@@ -89,10 +89,12 @@ def _worker(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_row_sharded_block_matches_unsharded(cuda, tmp_path):
+@pytest.mark.parametrize("self_attention,v2a", [("gather", "gather"), ("head_parallel", "split_keys")])
+def test_row_sharded_block_matches_unsharded(cuda, tmp_path, self_attention, v2a):
     world = 2
     port = _free_port()
-    mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(world, port, str(tmp_path), self_attention, v2a), nprocs=world, join=True,
+                       start_method="spawn")
     from oracle import ref_ops as ro
 
     blocks, v, a = _build(torch.device("cuda", 0))
