@@ -26,6 +26,15 @@
  *                           projections (prologue-fused quantized linear)
  *   ltxq_feed_forward    <- model/transformer/feed_forward.py:64-112
  *                           FeedForward.__call__ + transformer.py:629-650
+ *   ltxq_denoise_update  <- one step of the AV CFG denoise loop after the
+ *                           transformer passes (pipelines/av_pipeline.py:
+ *                           700-752): X0Model.denoise (model/transformer/
+ *                           model.py:1527-1533), CFGGuider / STGGuider.guide
+ *                           (components/guiders.py:24-28, 79-83), the
+ *                           gradient-estimation blend (av_pipeline.py:
+ *                           725-731), post_process_latent (pipelines/
+ *                           common.py:169-191) and EulerDiffusionStep.step
+ *                           (components/diffusion_steps.py:19-70)
  */
 #ifndef LTXQ_H
 #define LTXQ_H
@@ -204,6 +213,44 @@ ltxq_status ltxq_feed_forward(const void* x, int64_t M, const ltxq_prologue* pro
                               const ltxq_qweight* w_in, const ltxq_qweight* w_out,
                               const ltxq_epilogue* epi, void* out, void* workspace,
                               size_t workspace_bytes, void* stream);
+
+/* ---- denoise step ----------------------------------------------------- */
+/* Scalars of one step.  sigma is the schedule's current value (> 0),
+ * sigma_next the next (>= 0).  cfg_scale == 1 disables CFG (v_uncond
+ * unused), stg_scale == 0 disables STG (v_perturbed unused), ge_gamma <= 0
+ * disables the gradient-estimation blend.  The host rounds the scalar
+ * factors to fp32 after their double arithmetic (cfg_scale - 1,
+ * sigma_next / sigma), as the reference's Python scalars meet its fp32
+ * arrays. */
+typedef struct {
+  float sigma;
+  float sigma_next;
+  double cfg_scale;
+  double stg_scale;
+  double ge_gamma;
+  int32_t have_prev; /* ge: prev_velocity holds the previous step's velocity */
+  int32_t pad_;
+} ltxq_denoise_params;
+
+/* One stream's update after the transformer passes of a step, fused in
+ * fp32 with one bf16 rounding at the end:
+ *   d    = latent - ts * v_cond             (ts = sigma, or mask * sigma)
+ *   d   += (cfg_scale - 1) * (d - (latent - ts * v_uncond))
+ *   d   += stg_scale * (d - (latent - ts * v_perturbed))
+ *   ge:  v = (latent - d) / sigma; if have_prev: d = latent - (gamma * (v - prev) + prev) * sigma;
+ *        prev_velocity = v
+ *   mask: d = d * mask + clean * (1 - mask)
+ *   out = bf16(d + (sigma_next / sigma) * (latent - d))
+ * latent, v_*, clean_latent, out: bf16 [batch, tokens, channels]
+ * contiguous, 16-byte aligned, channels % 8 == 0; denoise_mask: f32
+ * [batch, tokens] or NULL (uniform); clean_latent required with a mask;
+ * prev_velocity: f32 [batch, tokens, channels], read and written when
+ * ge_gamma > 0 (NULL otherwise).  out may alias latent. */
+ltxq_status ltxq_denoise_update(const void* latent, const void* v_cond, const void* v_uncond,
+                                const void* v_perturbed, const float* denoise_mask,
+                                const void* clean_latent, float* prev_velocity, int64_t batch,
+                                int64_t tokens, int64_t channels, const ltxq_denoise_params* p,
+                                void* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -59,6 +59,18 @@ class Prologue(ctypes.Structure):
     _fields_ = [("norm", c_int32), ("eps", c_float), ("scale", Vec), ("shift", Vec)]
 
 
+class DenoiseParams(ctypes.Structure):
+    _fields_ = [
+        ("sigma", c_float),
+        ("sigma_next", c_float),
+        ("cfg_scale", ctypes.c_double),
+        ("stg_scale", ctypes.c_double),
+        ("ge_gamma", ctypes.c_double),
+        ("have_prev", c_int32),
+        ("pad_", c_int32),
+    ]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "ltxq_last_error": (c_char_p, []),
@@ -84,6 +96,8 @@ SIGNATURES = {
                                              POINTER(Epilogue), c_void_p, c_void_p]),
     "ltxq_feed_forward": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(QWeight),
                                     POINTER(Epilogue), c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ltxq_denoise_update": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                      c_int64, c_int64, POINTER(DenoiseParams), c_void_p, c_void_p]),
 }
 
 _lib = None

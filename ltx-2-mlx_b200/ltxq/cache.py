@@ -314,12 +314,19 @@ def quantized_linears_from_state(state: dict, in_features: dict[str, int], paylo
 def blocks_from_cache(cache_file, device="cuda", video=None, audio=None, blocks=None):
     """``BasicAVTransformerBlock`` list from a cache on disk (single file or
     shards, ``metadata.json`` beside it when present)."""
+    cache_file = Path(cache_file)
+    return blocks_from_weights(load_cache_weights(cache_file, device), read_metadata(cache_file.parent), video,
+                               audio, blocks)
+
+
+def blocks_from_weights(weights: dict[str, torch.Tensor], payload: dict | None = None, video=None, audio=None,
+                        blocks=None):
+    """``BasicAVTransformerBlock`` list from loaded cache entries (keys of
+    other modules are ignored)."""
     from .block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, linear_specs
 
     video, audio = video or VIDEO_22B, audio or AUDIO_22B
-    cache_file = Path(cache_file)
-    payload = read_metadata(cache_file.parent)
-    by_block = split_block_state(load_cache_weights(cache_file, device))
+    by_block = split_block_state(weights)
     kdims = {base: k for base, (_, k) in linear_specs(video, audio).items()}
     idx = sorted(by_block) if blocks is None else list(blocks)
     out = []

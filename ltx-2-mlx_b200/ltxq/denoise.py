@@ -1,0 +1,247 @@
+"""Denoise loop of the audio-video pipeline around ``LTXAVModel``.
+
+Mirrors the reference's sampling components:
+
+* sigma schedules: ``DISTILLED_SIGMA_VALUES`` / ``STAGE_2_DISTILLED_SIGMA_VALUES``
+  and ``LTX2Scheduler`` (LTX_2_MLX/components/schedulers.py:13-140);
+* ``CFGGuider`` / ``STGGuider`` (components/guiders.py:10-92), as scale
+  holders with the reference's ``enabled()`` rules;
+* ``denoise_update``: everything a step does after its transformer passes
+  (velocity -> denoised, CFG, STG, gradient estimation, the denoise-mask
+  blend, the Euler step; pipelines/av_pipeline.py:700-752) as ONE CUDA
+  kernel launch per stream (``ltxq_denoise_update``), bit-identical to the
+  reference's fp32 op sequence;
+* ``denoise_av``: ``_denoise_loop_cfg_av`` (av_pipeline.py:625-756).  The
+  positive and negative (CFG) passes run as one transformer pass over a
+  batch of 2B: the weights stream from HBM once per step instead of twice.
+  With ``graph=True`` the model call is captured once as a CUDA graph and
+  replayed every step.
+
+Not built: the STG perturbed pass (it needs blocks that skip attention
+modules, ``BatchedPerturbationConfig``), the Heun stepper and the
+non-AV / two-stage pipelines.  ``denoise_update`` still takes a perturbed
+velocity from a caller that has one.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, replace
+
+import numpy as np
+import torch
+
+from . import _lib
+from .kernels import _require_cuda, _stream
+
+DISTILLED_SIGMA_VALUES = (1.0, 0.99375, 0.9875, 0.98125, 0.975, 0.909375, 0.725, 0.421875, 0.0)
+STAGE_2_DISTILLED_SIGMA_VALUES = (0.909375, 0.725, 0.421875, 0.0)
+BASE_SHIFT_ANCHOR = 1024
+MAX_SHIFT_ANCHOR = 4096
+
+
+def ltx2_scheduler(steps: int, tokens: int | None = None, max_shift: float = 2.05, base_shift: float = 0.95,
+                   stretch: bool = True, terminal: float = 0.1) -> np.ndarray:
+    """LTX2Scheduler.execute (schedulers.py:20-95): fp32 sigmas (steps + 1,)
+    shifted by the token count (``prod(latent.shape[2:])``, 4096 when not
+    given) and stretched so that the last non-zero sigma is ``terminal``.
+    Host arithmetic in fp32 with the reference's operation order."""
+    f = np.float32
+    tokens = MAX_SHIFT_ANCHOR if tokens is None else tokens
+    n = steps + 1
+    t = np.arange(n, dtype=f) / f(max(steps, 1))  # linspace(1, 0, n) = 1 * (1 - t) + 0 * t
+    sig = (f(1.0) - t).astype(f)
+    slope = (max_shift - base_shift) / (MAX_SHIFT_ANCHOR - BASE_SHIFT_ANCHOR)
+    shift = math.exp(tokens * slope + (base_shift - slope * BASE_SHIFT_ANCHOR))
+    nz = sig != 0
+    out = np.zeros(n, dtype=f)
+    out[nz] = f(shift) / (f(shift) + (f(1.0) / sig[nz] - f(1.0)))
+    if stretch and steps > 0:
+        # steps == 1 stretches by 0 (NaN first sigma), as the reference does
+        one_minus = (f(1.0) - out).astype(f)
+        scale = f(float(one_minus[steps - 1]) / (1.0 - terminal))
+        keep = out != 0
+        with np.errstate(divide="ignore", invalid="ignore"):
+            out[keep] = f(1.0) - one_minus[keep] / scale
+    return out.astype(f)
+
+
+def sigma_schedule(num_steps: int, distilled: bool = False, tokens: int | None = None) -> np.ndarray:
+    """get_sigma_schedule (schedulers.py:121-140)."""
+    if distilled:
+        return np.asarray(DISTILLED_SIGMA_VALUES, dtype=np.float32)
+    return ltx2_scheduler(num_steps, tokens)
+
+
+@dataclass(frozen=True)
+class CFGGuider:
+    """Classifier-free guidance: cond + (scale - 1) * (cond - uncond)."""
+
+    scale: float
+
+    def enabled(self) -> bool:
+        return self.scale != 1.0
+
+
+@dataclass(frozen=True)
+class STGGuider:
+    """Spatio-temporal guidance: pos + scale * (pos - perturbed)."""
+
+    scale: float
+
+    def enabled(self) -> bool:
+        return self.scale != 0.0
+
+
+@dataclass
+class LatentState:
+    """One stream's latent (bf16 (B, T, 128)), its denoise mask (fp32
+    (B, T), None = all tokens denoised) and the clean latent the mask blends
+    back in (bf16, with a mask)."""
+
+    latent: torch.Tensor
+    denoise_mask: torch.Tensor | None = None
+    clean_latent: torch.Tensor | None = None
+
+    def timesteps(self, sigma: float) -> torch.Tensor:
+        """``modality_from_state`` (pipelines/common.py:207-250): fp32 (B,)
+        full of sigma for a uniform mask, else mask * sigma per token."""
+        b = self.latent.shape[0]
+        full = torch.full((b,), sigma, dtype=torch.float32, device=self.latent.device)
+        if self.denoise_mask is None:
+            return full
+        return self.denoise_mask.float() * full[:, None]
+
+
+def _bf16_3d(t: torch.Tensor, name: str) -> torch.Tensor:
+    _require_cuda(t, name)
+    if t.dtype != torch.bfloat16 or t.dim() != 3 or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous bf16 (B, T, C) tensor")
+    return t
+
+
+def denoise_update(latent: torch.Tensor, v_cond: torch.Tensor, sigma: float, sigma_next: float,
+                   v_uncond: torch.Tensor | None = None, cfg_scale: float = 1.0,
+                   v_perturbed: torch.Tensor | None = None, stg_scale: float = 0.0,
+                   denoise_mask: torch.Tensor | None = None, clean_latent: torch.Tensor | None = None,
+                   prev_velocity: torch.Tensor | None = None, ge_gamma: float = 0.0, have_prev: bool = False,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """The latent after one step, from the step's velocities (bf16 (B, T,
+    C)); see ``ltxq_denoise_update``.  ``prev_velocity`` (fp32 (B, T, C)) is
+    read when ``have_prev`` and overwritten with this step's velocity when
+    ``ge_gamma > 0``.  ``out`` may be ``latent`` (in-place)."""
+    latent = _bf16_3d(latent, "latent")
+    shape = tuple(latent.shape)
+    if v_cond is None:
+        raise ValueError("v_cond is required")
+    for t, name in ((v_cond, "v_cond"), (v_uncond, "v_uncond"), (v_perturbed, "v_perturbed"),
+                    (clean_latent, "clean_latent"), (out, "out")):
+        if t is not None and tuple(_bf16_3d(t, name).shape) != shape:
+            raise ValueError(f"{name} shape {tuple(t.shape)} != latent shape {shape}")
+    if denoise_mask is not None:
+        _require_cuda(denoise_mask, "denoise_mask")
+        if denoise_mask.dtype != torch.float32 or tuple(denoise_mask.shape) != shape[:2]:
+            raise ValueError("denoise_mask must be fp32 (B, T)")
+        denoise_mask = denoise_mask.contiguous()
+    if prev_velocity is not None:
+        _require_cuda(prev_velocity, "prev_velocity")
+        if prev_velocity.dtype != torch.float32 or tuple(prev_velocity.shape) != shape or \
+                not prev_velocity.is_contiguous():
+            raise ValueError("prev_velocity must be a contiguous fp32 tensor of the latent's shape")
+    if out is None:
+        out = torch.empty_like(latent)
+    p = _lib.DenoiseParams(float(sigma), float(sigma_next), float(cfg_scale), float(stg_scale), float(ge_gamma),
+                           1 if have_prev else 0, 0)
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.check(_lib.load().ltxq_denoise_update(
+        latent.data_ptr(), v_cond.data_ptr(), ptr(v_uncond), ptr(v_perturbed), ptr(denoise_mask), ptr(clean_latent),
+        ptr(prev_velocity), shape[0], shape[1], shape[2], ctypes.byref(p), out.data_ptr(), _stream()),
+        "denoise_update")
+    return out
+
+
+def _batch2(t):
+    """[t; t] along the batch dimension (a tuple of tables element-wise)."""
+    if isinstance(t, tuple):
+        return tuple(_batch2(x) for x in t)
+    return torch.cat([t, t], dim=0)
+
+
+def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_context: torch.Tensor,
+               audio_context: torch.Tensor, video_pe: tuple, audio_pe: tuple, video_cross_pe: tuple,
+               audio_cross_pe: tuple, negative_video_context: torch.Tensor | None = None,
+               negative_audio_context: torch.Tensor | None = None, video_guider: CFGGuider = CFGGuider(1.0),
+               audio_guider: CFGGuider = CFGGuider(1.0), ge_gamma: float = 0.0, shard=None, graph: bool = False,
+               callback=None) -> tuple[LatentState, LatentState]:
+    """``_denoise_loop_cfg_av`` (av_pipeline.py:625-756) over ``model`` (an
+    ``LTXAVModel``): per step one transformer pass (2B rows when either
+    guider is enabled: positive then negative contexts), then one
+    ``denoise_update`` per stream.  Gradient estimation (``ge_gamma``)
+    applies to the video stream, as in the reference.  With a row shard,
+    ``video`` holds this rank's rows."""
+    from .model import Modality
+
+    sig = np.asarray(sigmas, dtype=np.float32)
+    steps = len(sig) - 1
+    need_cfg = video_guider.enabled() or audio_guider.enabled()
+    if need_cfg and (negative_video_context is None or negative_audio_context is None):
+        raise ValueError("CFG needs the negative video and audio contexts")
+    b = video.latent.shape[0]
+    if need_cfg:
+        vctx = torch.cat([video_context, negative_video_context])
+        actx = torch.cat([audio_context, negative_audio_context])
+        vpe, ape, vcpe, acpe = (_batch2(t) for t in (video_pe, audio_pe, video_cross_pe, audio_cross_pe))
+    else:
+        vctx, actx, vpe, ape, vcpe, acpe = video_context, audio_context, video_pe, audio_pe, video_cross_pe, \
+            audio_cross_pe
+    rep = 2 if need_cfg else 1
+    dev = video.latent.device
+    # the model's per-step inputs live in fixed buffers (what a captured graph reads)
+    v_in = torch.empty((rep * b,) + tuple(video.latent.shape[1:]), dtype=torch.bfloat16, device=dev)
+    a_in = torch.empty((rep * b,) + tuple(audio.latent.shape[1:]), dtype=torch.bfloat16, device=dev)
+    vt_shape = (rep * b,) if video.denoise_mask is None else (rep * b, video.latent.shape[1])
+    at_shape = (rep * b,) if audio.denoise_mask is None else (rep * b, audio.latent.shape[1])
+    v_t = torch.empty(vt_shape, dtype=torch.float32, device=dev)
+    a_t = torch.empty(at_shape, dtype=torch.float32, device=dev)
+    v_s = torch.empty((rep * b,), dtype=torch.float32, device=dev)
+
+    def run(v_in, a_in, v_t, a_t, v_s):
+        return model(Modality(v_in, v_t, vctx, vpe, vcpe, sigma=v_s),
+                     Modality(a_in, a_t, actx, ape, acpe, sigma=v_s), shard)
+
+    prev = torch.empty(video.latent.shape, dtype=torch.float32, device=dev) if ge_gamma > 0 else None
+    step_graph = None
+    for i in range(steps):
+        sigma, sigma_next = float(sig[i]), float(sig[i + 1])
+        for dst, st in ((v_in, video), (a_in, audio)):
+            for r in range(rep):
+                dst[r * b:(r + 1) * b].copy_(st.latent)
+        for dst, st in ((v_t, video), (a_t, audio)):
+            ts = st.timesteps(sigma)
+            for r in range(rep):
+                dst[r * b:(r + 1) * b].copy_(ts)
+        v_s.fill_(sigma)
+        if graph:
+            if step_graph is None:
+                from .graph import StepGraph
+
+                step_graph = StepGraph(run, v_in, a_in, v_t, a_t, v_s)
+            vv, av = step_graph.replay()
+        else:
+            vv, av = run(v_in, a_in, v_t, a_t, v_s)
+        vc, ac = vv[:b], av[:b]
+        vu, au = (vv[b:], av[b:]) if need_cfg else (None, None)
+        new_v = denoise_update(video.latent, vc, sigma, sigma_next, v_uncond=vu,
+                               cfg_scale=video_guider.scale if need_cfg else 1.0,
+                               denoise_mask=video.denoise_mask, clean_latent=video.clean_latent,
+                               prev_velocity=prev, ge_gamma=ge_gamma, have_prev=i > 0)
+        new_a = denoise_update(audio.latent, ac, sigma, sigma_next, v_uncond=au,
+                               cfg_scale=audio_guider.scale if need_cfg else 1.0,
+                               denoise_mask=audio.denoise_mask, clean_latent=audio.clean_latent)
+        video, audio = replace(video, latent=new_v), replace(audio, latent=new_a)
+        if callback is not None:
+            callback(i + 1, steps)
+    if step_graph is not None:
+        step_graph.release()
+    return video, audio

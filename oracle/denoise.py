@@ -1,0 +1,225 @@
+"""CPU oracle for the callers around the block loop: the model's input and
+output stages and one denoise step (TEST INFRASTRUCTURE ONLY; see the
+package docstring).
+
+Restates, in numpy fp32 with the reference's rounding points:
+
+* the sigma schedules (LTX_2_MLX/components/schedulers.py:13-140);
+* the sinusoidal timestep embedding and the AdaLN MLP
+  (model/transformer/timestep_embedding.py:8-201).  Their inputs are fp32,
+  so MLX promotes the bf16 weights and the MLP runs in fp32;
+* the velocity -> denoised conversion (model/transformer/model.py:1489-1540,
+  ``X0Model``), the CFG / STG guiders (components/guiders.py:10-92), the
+  gradient-estimation velocity blend and the mask blend of the AV CFG loop
+  (pipelines/av_pipeline.py:700-740, pipelines/common.py:169-204), and the
+  Euler step (components/diffusion_steps.py:19-70);
+* the video / audio output head (model/transformer/model.py:1312-1340).
+
+Every fp32 operation below is one IEEE round-to-nearest operation, as in
+MLX's elementwise kernels.  A Python float scalar meets an fp32 array as an
+fp32 value (MLX's weak scalar promotion), so scalar factors are rounded to
+fp32 once, after their double-precision arithmetic.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .bf16 import rbf16
+from .ref_ops import adaln
+
+F32 = np.float32
+
+# components/schedulers.py:100-118
+DISTILLED_SIGMA_VALUES = [1.0, 0.99375, 0.9875, 0.98125, 0.975, 0.909375, 0.725, 0.421875, 0.0]
+STAGE_2_DISTILLED_SIGMA_VALUES = [0.909375, 0.725, 0.421875, 0.0]
+
+
+def ltx2_sigmas(steps: int, tokens: int = 4096, max_shift: float = 2.05, base_shift: float = 0.95,
+                stretch: bool = True, terminal: float = 0.1) -> np.ndarray:
+    """LTX2Scheduler.execute (schedulers.py:20-95), fp32 array math: linspace
+    in fp32, shift from a linear fit on the token count, sigmoid-like
+    transform, stretch so that the last non-zero sigma equals ``terminal``."""
+    # mx.linspace(1, 0, n) as MLX's lerp form start * (1 - t) + stop * t with
+    # t = i / (n - 1) in fp32 (ends exactly at 1 and 0; the interior values'
+    # last bit is not pinned by a reference test)
+    t = (np.arange(steps + 1, dtype=F32) / F32(max(steps, 1))).astype(F32)
+    sig = (F32(1.0) - t).astype(F32)
+    mm = (max_shift - base_shift) / (4096 - 1024)
+    b = base_shift - mm * 1024
+    exp_shift = F32(math.exp(tokens * mm + b))
+    with np.errstate(divide="ignore"):
+        inv = np.where(sig != 0, F32(1.0) / sig, F32(0.0)).astype(F32) - F32(1.0)
+    tr = np.where(sig != 0, exp_shift / (exp_shift + inv), F32(0.0)).astype(F32)
+    if stretch and steps > 0:
+        om = (F32(1.0) - tr).astype(F32)
+        last = float(om[steps - 1])
+        factor = F32(last / (1.0 - terminal))
+        with np.errstate(divide="ignore", invalid="ignore"):
+            st = (F32(1.0) - om / factor).astype(F32)
+        tr = np.where(tr != 0, st, tr).astype(F32)
+    return tr.astype(F32)
+
+
+def timestep_embedding(t, dim: int = 256, max_period: int = 10000) -> np.ndarray:
+    """get_timestep_embedding with flip_sin_to_cos=True, shift 0, scale 1
+    (timestep_embedding.py:8-58, Timesteps :61-84): [cos | sin] of t * freq."""
+    half = dim // 2
+    expo = (F32(-math.log(max_period)) * np.arange(half, dtype=F32)).astype(F32) / F32(half)
+    freq = np.exp(expo.astype(np.float64)).astype(F32)
+    arg = (np.asarray(t, dtype=F32)[:, None] * freq[None, :]).astype(F32)
+    s = np.sin(arg.astype(np.float64)).astype(F32)
+    c = np.cos(arg.astype(np.float64)).astype(F32)
+    return np.concatenate([c, s], axis=-1)
+
+
+def _silu(x):
+    x = x.astype(np.float64)
+    return (x / (1.0 + np.exp(-x))).astype(F32)
+
+
+def _linear_f32(x, w, b):
+    return (x.astype(np.float64) @ np.asarray(w, np.float64).T + np.asarray(b, np.float64)).astype(F32)
+
+
+def ada_single(p: dict, t) -> tuple[np.ndarray, np.ndarray]:
+    """AdaLayerNormSingle (timestep_embedding.py:165-201) on fp32 timesteps:
+    (emb [N, n*D], embedded_timestep [N, D]), both fp32.  ``p`` holds
+    linear_1 / linear_2 / linear weights and biases (bf16 values)."""
+    h = timestep_embedding(t)
+    h = _linear_f32(h, p["linear_1.weight"], p["linear_1.bias"])
+    h = _silu(h)
+    emb_t = _linear_f32(h, p["linear_2.weight"], p["linear_2.bias"])
+    out = _linear_f32(_silu(emb_t), p["linear.weight"], p["linear.bias"])
+    return out, emb_t
+
+
+def linear_bf16(x, w, b):
+    """bf16 nn.Linear: fp32 accumulation, one rounding."""
+    return rbf16(_linear_f32(x, w, b))
+
+
+def output_head(x, table, embedded, w, b, eps: float = 1e-6):
+    """_process_video_output / _process_audio_output (model.py:1312-1340):
+    shift/scale = bf16(table + embedded_timestep); LayerNorm (no affine,
+    bf16 out); x * (1 + scale) + shift in bf16 ops; proj_out.  ``x`` [B, T,
+    D] bf16 values, ``embedded`` [B, 1, D] fp32."""
+    ss = rbf16((np.asarray(table, F32)[None, None] + np.asarray(embedded, F32)[:, :, None, :]).astype(F32))
+    y = adaln(x, ss[:, :, 1], ss[:, :, 0], eps, norm="layer", vec_bf16=True)
+    return linear_bf16(y, w, b)
+
+
+def _x0(x, ts, v):
+    """X0Model.denoise (model.py:1527-1533): latent - timesteps * velocity."""
+    return (x - (ts * v).astype(F32)).astype(F32)
+
+
+def denoise_update(latent, v_cond, sigma: float, sigma_next: float, v_uncond=None, cfg_scale: float = 1.0,
+                   v_perturbed=None, stg_scale: float = 0.0, denoise_mask=None, clean_latent=None,
+                   prev_velocity=None, ge_gamma: float = 0.0):
+    """One step of the AV CFG loop for one stream (av_pipeline.py:672-740):
+    X0 of each pass, CFG, STG, gradient estimation, mask blend, Euler step.
+    Arrays are [B, T, C] (bf16 values as fp32); ``denoise_mask`` [B, T] fp32.
+    Returns (new latent as bf16 values, this step's velocity or None)."""
+    x = np.asarray(latent, F32)
+    sig = F32(sigma)
+    ts = sig if denoise_mask is None else (np.asarray(denoise_mask, F32) * sig).astype(F32)[..., None]
+    d = _x0(x, ts, np.asarray(v_cond, F32))
+    if v_uncond is not None and cfg_scale != 1.0:  # CFGGuider.guide (guiders.py:24-28)
+        u = _x0(x, ts, np.asarray(v_uncond, F32))
+        d = (d + (F32(cfg_scale - 1.0) * (d - u).astype(F32)).astype(F32)).astype(F32)
+    if v_perturbed is not None and stg_scale != 0.0:  # STGGuider.guide (guiders.py:79-83)
+        pt = _x0(x, ts, np.asarray(v_perturbed, F32))
+        d = (d + (F32(stg_scale) * (d - pt).astype(F32)).astype(F32)).astype(F32)
+    cur = None
+    if ge_gamma > 0 and sigma > 0:  # av_pipeline.py:725-731
+        cur = ((x - d).astype(F32) / sig).astype(F32)
+        if prev_velocity is not None:
+            total = ((F32(ge_gamma) * (cur - prev_velocity).astype(F32)).astype(F32) + prev_velocity).astype(F32)
+            d = (x - (total * sig).astype(F32)).astype(F32)
+    if denoise_mask is not None:  # post_process_latent (common.py:169-191)
+        m = np.asarray(denoise_mask, F32)[..., None]
+        clean = np.asarray(clean_latent, F32)
+        d = ((d * m).astype(F32) + (clean * (F32(1.0) - m).astype(F32)).astype(F32)).astype(F32)
+    ratio = F32(float(sigma_next) / float(sigma))  # EulerDiffusionStep.step (diffusion_steps.py:62-68)
+    out = (d + (ratio * (x - d).astype(F32)).astype(F32)).astype(F32)
+    return rbf16(out), cur
+
+
+# non-block module prefixes of the reference model (model/transformer/model.py:640-712)
+MODEL_PREFIXES = {
+    "video": dict(patchify="patchify_proj", adaln="adaln_single", prompt="prompt_adaln_single",
+                  cross_ss="av_ca_video_scale_shift_adaln_single", cross_gate="av_ca_a2v_gate_adaln_single",
+                  table="scale_shift_table", proj_out="proj_out"),
+    "audio": dict(patchify="audio_patchify_proj", adaln="audio_adaln_single", prompt="audio_prompt_adaln_single",
+                  cross_ss="av_ca_audio_scale_shift_adaln_single", cross_gate="av_ca_v2a_gate_adaln_single",
+                  table="audio_scale_shift_table", proj_out="audio_proj_out"),
+}
+
+
+def _ada_params(mp: dict, prefix: str) -> dict:
+    return {"linear_1.weight": mp[f"{prefix}.emb.timestep_embedder.linear_1.weight"],
+            "linear_1.bias": mp[f"{prefix}.emb.timestep_embedder.linear_1.bias"],
+            "linear_2.weight": mp[f"{prefix}.emb.timestep_embedder.linear_2.weight"],
+            "linear_2.bias": mp[f"{prefix}.emb.timestep_embedder.linear_2.bias"],
+            "linear.weight": mp[f"{prefix}.linear.weight"], "linear.bias": mp[f"{prefix}.linear.bias"]}
+
+
+def _prepare(mp: dict, which: str, s: dict, cross_sigma: float, ts_mult: float, av_ca_mult: float):
+    """MultiModalTransformerArgsPreprocessor.prepare (model.py:270-340,
+    454-505) for one batch row with uniform timesteps (= sigma)."""
+    p = MODEL_PREFIXES[which]
+    d = np.asarray(mp[f"{p['patchify']}.weight"]).shape[0]
+    scaled = (np.array([s["sigma"]], F32) * F32(ts_mult)).astype(F32)
+    emb, emb_t = ada_single(_ada_params(mp, p["adaln"]), scaled)
+    prompt, _ = ada_single(_ada_params(mp, p["prompt"]), scaled)
+    css, _ = ada_single(_ada_params(mp, p["cross_ss"]), scaled)
+    cg, _ = ada_single(_ada_params(mp, p["cross_gate"]),
+                       (np.array([cross_sigma], F32) * F32(av_ca_mult)).astype(F32))
+    x = linear_bf16(s["latent"], mp[f"{p['patchify']}.weight"], mp[f"{p['patchify']}.bias"])
+    args = {"x": x, "context": s["context"], "timesteps": emb.reshape(9, d), "pe": s["pe"],
+            "cross_pe": s["cross_pe"], "cross_ss": css.reshape(4, d), "cross_gate": cg.reshape(1, d),
+            "prompt": prompt.reshape(2, d)}
+    return args, emb_t
+
+
+def model_forward(blocks_p: list, mp: dict, video: dict, audio: dict, heads_v: int, heads_a: int,
+                  ts_mult: float = 1000.0, av_ca_mult: float = 1000.0, eps: float = 1e-6):
+    """LTXModel.__call__ (model.py:1343-1487) for one batch row: preprocess
+    both streams, the blocks (``oracle.block.block``), the output heads.
+    ``video`` / ``audio``: latent (T, 128) bf16 values, sigma (float),
+    context, pe, cross_pe.  Returns the (video, audio) velocities."""
+    from .block import block
+
+    va, vt = _prepare(mp, "video", video, audio["sigma"], ts_mult, av_ca_mult)
+    aa, at = _prepare(mp, "audio", audio, video["sigma"], ts_mult, av_ca_mult)
+    for p in blocks_p:
+        vx, ax = block(p, va, aa, heads_v=heads_v, heads_a=heads_a, eps=eps)
+        va, aa = dict(va, x=vx), dict(aa, x=ax)
+    outs = []
+    for which, args, emb_t in (("video", va, vt), ("audio", aa, at)):
+        p = MODEL_PREFIXES[which]
+        outs.append(output_head(args["x"][None], mp[p["table"]], emb_t[None], mp[f"{p['proj_out']}.weight"],
+                                mp[f"{p['proj_out']}.bias"], eps)[0])
+    return outs[0], outs[1]
+
+
+def denoise_loop_av(model_fn, video_latent, audio_latent, sigmas, cfg_video: float = 1.0, cfg_audio: float = 1.0):
+    """_denoise_loop_cfg_av (av_pipeline.py:625-756) without STG, gradient
+    estimation or masks: ``model_fn(video_latent, audio_latent, sigma,
+    negative)`` -> (video velocity, audio velocity) for one batch row; the
+    negative pass runs when either scale is not 1.  Returns the final
+    (video, audio) latents."""
+    need_cfg = cfg_video != 1.0 or cfg_audio != 1.0
+    sig = np.asarray(sigmas, dtype=F32)
+    for i in range(len(sig) - 1):
+        s, sn = float(sig[i]), float(sig[i + 1])
+        vc, ac = model_fn(video_latent, audio_latent, s, False)
+        vu = au = None
+        if need_cfg:
+            vu, au = model_fn(video_latent, audio_latent, s, True)
+        video_latent = denoise_update(video_latent, vc, s, sn, v_uncond=vu, cfg_scale=cfg_video if need_cfg else 1.0)[0]
+        audio_latent = denoise_update(audio_latent, ac, s, sn, v_uncond=au, cfg_scale=cfg_audio if need_cfg else 1.0)[0]
+    return video_latent, audio_latent

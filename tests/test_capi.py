@@ -66,3 +66,26 @@ def test_argument_validation_without_gpu(lib):
     pro = _lib.Prologue(_lib.NORM_RMS, 1e-6, _lib.Vec(16, _lib.F32, 0, 0, 0), _lib.Vec(16, _lib.F32, 0, 0, 0))
     st = lib.ltxq_adaln_modulate(16, _lib.BF16, 4, 12, ctypes.byref(pro), 16, None)
     assert st == _lib.ERR_UNSUPPORTED  # C % 8 != 0
+
+
+def test_denoise_update_validation_without_gpu(lib):
+    """ltxq_denoise_update rejects bad scalars / shapes / missing operands
+    before any CUDA call, and an empty latent is a no-op."""
+    from ltxq import _lib
+
+    def call(p, latent=16, v_cond=16, v_uncond=None, b=1, t=4, c=8, out=16, mask=None, clean=None, prev=None):
+        return lib.ltxq_denoise_update(latent, v_cond, v_uncond, None, mask, clean, prev, b, t, c,
+                                       None if p is None else ctypes.byref(p), out, None)
+
+    ok = _lib.DenoiseParams(0.5, 0.25, 1.0, 0.0, 0.0, 0, 0)
+    assert call(None) == _lib.ERR_INVALID
+    assert call(_lib.DenoiseParams(0.0, 0.0, 1.0, 0.0, 0.0, 0, 0)) == _lib.ERR_INVALID  # sigma must be > 0
+    assert b"sigma" in lib.ltxq_last_error()
+    assert call(_lib.DenoiseParams(0.5, -0.1, 1.0, 0.0, 0.0, 0, 0)) == _lib.ERR_INVALID
+    assert call(ok, c=12) == _lib.ERR_UNSUPPORTED  # channels % 8
+    assert call(ok, latent=None) == _lib.ERR_INVALID
+    assert call(_lib.DenoiseParams(0.5, 0.25, 3.0, 0.0, 0.0, 0, 0)) == _lib.ERR_INVALID  # CFG needs v_uncond
+    assert call(_lib.DenoiseParams(0.5, 0.25, 1.0, 0.0, 1.5, 0, 0)) == _lib.ERR_INVALID  # ge needs prev_velocity
+    assert call(ok, mask=16) == _lib.ERR_INVALID  # a mask needs the clean latent
+    assert call(ok, latent=24) == _lib.ERR_UNSUPPORTED  # 16-byte alignment
+    assert call(ok, latent=None, v_cond=None, out=None, b=0) == _lib.OK  # empty: nothing to do

@@ -1,0 +1,111 @@
+"""CPU tests of the denoise-loop host logic and its oracle: the sigma
+schedules (the properties the reference's tests/test_scheduler.py checks,
+and the ltxq host code against the oracle restatement bit for bit), and
+identities of the oracle's fused step (components/diffusion_steps.py,
+components/guiders.py, pipelines/common.py) that pin its op order."""
+
+import numpy as np
+import pytest
+
+from helpers import normal_bf16, rng
+from oracle import denoise as od
+from oracle.bf16 import rbf16
+
+
+@pytest.mark.parametrize("steps", [1, 2, 8, 10, 20, 25, 30, 40, 50])
+@pytest.mark.parametrize("tokens", [None, 1024, 3456, 9216, 61152])
+def test_ltx2_scheduler_matches_oracle(steps, tokens):
+    from ltxq.denoise import ltx2_scheduler
+
+    got = ltx2_scheduler(steps, tokens)
+    ref = od.ltx2_sigmas(steps, 4096 if tokens is None else tokens)
+    assert got.dtype == np.float32 and got.shape == (steps + 1,)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("steps", [10, 20, 30, 50])
+def test_ltx2_scheduler_properties(steps):
+    """tests/test_scheduler.py:20-105 of the reference: length, monotone,
+    starts positive, ends at 0, within [0, 10]; and the stretch puts the last
+    non-zero sigma at the terminal value."""
+    from ltxq.denoise import ltx2_scheduler
+
+    s = ltx2_scheduler(steps)
+    assert len(s) == steps + 1
+    assert np.all(s[:-1] >= s[1:])
+    assert s[0] > 0 and s[-1] == 0.0
+    assert np.all(s >= 0) and np.all(s <= 10)
+    assert abs(float(s[-2]) - 0.1) < 1e-6
+    assert np.array_equal(s, ltx2_scheduler(steps))
+
+
+def test_distilled_schedules():
+    """tests/test_scheduler.py:108-147: 9 and 4 values, decreasing, ending
+    at exactly 0, stage 2 below stage 1."""
+    from ltxq.denoise import DISTILLED_SIGMA_VALUES, STAGE_2_DISTILLED_SIGMA_VALUES, sigma_schedule
+
+    assert list(DISTILLED_SIGMA_VALUES) == od.DISTILLED_SIGMA_VALUES
+    assert list(STAGE_2_DISTILLED_SIGMA_VALUES) == od.STAGE_2_DISTILLED_SIGMA_VALUES
+    for vals, n in ((DISTILLED_SIGMA_VALUES, 9), (STAGE_2_DISTILLED_SIGMA_VALUES, 4)):
+        v = np.asarray(vals)
+        assert len(v) == n and v[-1] == 0.0 and np.all(v[:-1] >= v[1:])
+    assert max(STAGE_2_DISTILLED_SIGMA_VALUES[:-1]) < max(DISTILLED_SIGMA_VALUES[:-1])
+    d = sigma_schedule(8, distilled=True)
+    assert d.dtype == np.float32 and np.array_equal(d, np.asarray(DISTILLED_SIGMA_VALUES, np.float32))
+
+
+def _inputs(shape, seed=0):
+    g = rng(seed)
+    return [normal_bf16(g, shape) for _ in range(4)]
+
+
+def test_oracle_step_is_the_euler_lerp_of_the_x0():
+    """No guidance: out = bf16(d + r (x - d)) with d = x - sigma v, the
+    reference's X0Model then EulerDiffusionStep."""
+    x, v, _, _ = _inputs((2, 40, 128))
+    s, sn = 0.909375, 0.725
+    got, cur = od.denoise_update(x, v, s, sn)
+    d = (x - (np.float32(s) * v).astype(np.float32)).astype(np.float32)
+    r = np.float32(sn / s)
+    ref = rbf16((d + (r * (x - d).astype(np.float32)).astype(np.float32)).astype(np.float32))
+    assert cur is None
+    assert np.array_equal(got, ref)
+
+
+def test_oracle_final_step_returns_the_x0():
+    """sigma_next = 0 (the last step): the result is bf16 of the denoised
+    sample (tests/test_scheduler.py:197-213 exercises this step)."""
+    x, v, u, _ = _inputs((1, 64, 128), 1)
+    got, _ = od.denoise_update(x, v, 0.421875, 0.0, v_uncond=u, cfg_scale=3.0)
+    d = (x - (np.float32(0.421875) * v).astype(np.float32)).astype(np.float32)
+    du = (x - (np.float32(0.421875) * u).astype(np.float32)).astype(np.float32)
+    d = (d + (np.float32(2.0) * (d - du).astype(np.float32)).astype(np.float32)).astype(np.float32)
+    assert np.array_equal(got, rbf16(d))
+    assert np.all(np.isfinite(got))
+
+
+def test_oracle_guidance_degenerate_cases():
+    """CFG scale 1 and STG scale 0 are the unguided step; a full mask is the
+    unmasked step; gradient estimation without history only records the
+    velocity."""
+    x, v, u, p = _inputs((2, 24, 64), 2)
+    base, _ = od.denoise_update(x, v, 0.98125, 0.975)
+    assert np.array_equal(od.denoise_update(x, v, 0.98125, 0.975, v_uncond=u, cfg_scale=1.0)[0], base)
+    assert np.array_equal(od.denoise_update(x, v, 0.98125, 0.975, v_perturbed=p, stg_scale=0.0)[0], base)
+    ones = np.ones((2, 24), np.float32)
+    clean = normal_bf16(rng(3), (2, 24, 64))
+    assert np.array_equal(od.denoise_update(x, v, 0.98125, 0.975, denoise_mask=ones, clean_latent=clean)[0], base)
+    got, cur = od.denoise_update(x, v, 0.98125, 0.975, ge_gamma=2.0)
+    assert np.array_equal(got, base)
+    assert cur.shape == x.shape and cur.dtype == np.float32
+
+
+def test_oracle_zero_mask_keeps_the_clean_latent_at_the_end():
+    """mask 0 tokens take the clean latent as their denoised value; with
+    sigma_next = 0 the result is the clean latent."""
+    x, v, _, _ = _inputs((1, 32, 128), 4)
+    clean = normal_bf16(rng(5), (1, 32, 128))
+    mask = np.zeros((1, 32), np.float32)
+    mask[:, 16:] = 1.0
+    got, _ = od.denoise_update(x, v, 0.725, 0.0, denoise_mask=mask, clean_latent=clean)
+    assert np.array_equal(got[:, :16], clean[:, :16])

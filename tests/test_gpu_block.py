@@ -6,39 +6,11 @@ rounding points and every epilogue/prologue form are those of the 22B block).
 import numpy as np
 import pytest
 
-from helpers import from_dev_bf16, normal_bf16, normal_f32, rng, to_dev, to_dev_bf16
+from helpers import block_params, from_dev_bf16, gpu_block, normal_bf16, normal_f32, rng, rope_np, to_dev_bf16
 from oracle import block as ob
-from oracle import quant as oq
 from oracle import ref_ops as ro
 
 pytestmark = pytest.mark.gpu
-
-
-def _params(video, audio, mode, bits, seed=30):
-    from ltxq.block import linear_specs, table_specs
-
-    g = rng(seed)
-    p_oracle, quant = {}, {}
-    for name, (n, k) in linear_specs(video, audio).items():
-        w = normal_bf16(g, (n, k), 0.02)
-        b = normal_bf16(g, (n,), 0.01)
-        q = oq.quantize(w, mode, 32 if mode == "mxfp8" else 64, bits)
-        quant[name] = (q, b)
-        p_oracle[f"{name}.weight"] = oq.dequantize(q, k)
-        p_oracle[f"{name}.bias"] = b
-    tables = {}
-    for name, shape in table_specs(video, audio).items():
-        t = normal_f32(g, shape, 0.1)
-        if name.endswith("norm.weight"):
-            t = (1.0 + t).astype(np.float32)
-        tables[name] = t
-        p_oracle[name] = t
-    return p_oracle, quant, tables
-
-
-def _rope(g, heads, t, d):
-    ang = g.uniform(0, 6.28, (heads, t, d // 2)).astype(np.float32)
-    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 
 @pytest.mark.parametrize("mode,bits", [("affine", 8), ("mxfp8", 8)])
@@ -46,19 +18,14 @@ def test_av_block_matches_oracle(cuda, mode, bits):
     import torch
 
     import ltxq
-    from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
+    from ltxq.block import StreamConfig, TransformerArgs
 
     video = StreamConfig(1024, 8, 128, 1024)
     audio = StreamConfig(512, 8, 64, 512)
     T, A, L = 160, 72, 48
-    p_oracle, quant, tables = _params(video, audio, mode, bits)
+    p_oracle, quant, tables = block_params(video, audio, mode, bits)
     g = rng(31)
-    lin = {}
-    for name, (q, b) in quant.items():
-        s = to_dev(q["scales"]) if mode == "affine" else torch.from_numpy(q["scales"].copy()).cuda()
-        lin[name] = ltxq.QuantizedLinear(to_dev(q["weight"]), s, to_dev(q["biases"]) if mode == "affine" else None,
-                                         to_dev_bf16(b), group_size=q["group_size"], bits=q["bits"], mode=mode)
-    blk = BasicAVTransformerBlock(lin, {k: torch.from_numpy(v).cuda() for k, v in tables.items()}, video, audio)
+    blk = gpu_block(quant, tables, video, audio, mode)
 
     def stream(cfg, tokens, ctx_tokens, heads_cross):
         d = {
@@ -68,8 +35,8 @@ def test_av_block_matches_oracle(cuda, mode, bits):
             "prompt": normal_f32(g, (2, cfg.dim), 0.1),
             "cross_ss": normal_f32(g, (4, cfg.dim), 0.1),
             "cross_gate": normal_f32(g, (1, cfg.dim), 0.1),
-            "pe": _rope(g, cfg.heads, tokens, cfg.d_head),
-            "cross_pe": _rope(g, heads_cross, tokens, audio.d_head),
+            "pe": rope_np(g, cfg.heads, tokens, cfg.d_head),
+            "cross_pe": rope_np(g, heads_cross, tokens, audio.d_head),
         }
         return d
 
@@ -158,19 +125,15 @@ def test_av_block_batch2_matches_oracle_per_entry(cuda):
     import torch
 
     import ltxq
-    from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
+    from ltxq.block import StreamConfig, TransformerArgs
 
     video = StreamConfig(1024, 8, 128, 1024)
     audio = StreamConfig(512, 8, 64, 512)
     T, A, L = 96, 40, 32
     mode, bits = "mxfp8", 8
-    p_oracle, quant, tables = _params(video, audio, mode, bits, seed=33)
+    p_oracle, quant, tables = block_params(video, audio, mode, bits, seed=33)
     g = rng(34)
-    lin = {}
-    for name, (q, b) in quant.items():
-        lin[name] = ltxq.QuantizedLinear(to_dev(q["weight"]), torch.from_numpy(q["scales"].copy()).cuda(), None,
-                                         to_dev_bf16(b), group_size=32, bits=8, mode=mode)
-    blk = BasicAVTransformerBlock(lin, {k: torch.from_numpy(v).cuda() for k, v in tables.items()}, video, audio)
+    blk = gpu_block(quant, tables, video, audio, mode)
 
     def stream(cfg, tokens):
         return {
@@ -180,8 +143,8 @@ def test_av_block_batch2_matches_oracle_per_entry(cuda):
             "prompt": normal_f32(g, (2, cfg.dim), 0.1),
             "cross_ss": normal_f32(g, (4, cfg.dim), 0.1),
             "cross_gate": normal_f32(g, (1, cfg.dim), 0.1),
-            "pe": _rope(g, cfg.heads, tokens, cfg.d_head),
-            "cross_pe": _rope(g, audio.heads, tokens, audio.d_head),
+            "pe": rope_np(g, cfg.heads, tokens, cfg.d_head),
+            "cross_pe": rope_np(g, audio.heads, tokens, audio.d_head),
         }
 
     entries = [(stream(video, T), stream(audio, A)) for _ in range(2)]
