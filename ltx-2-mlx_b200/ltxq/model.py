@@ -45,8 +45,9 @@ def timestep_embedding(t: torch.Tensor, dim: int = TIMESTEP_CHANNELS, max_period
     [cos | sin] (get_timestep_embedding with flip_sin_to_cos=True and no
     frequency shift, timestep_embedding.py:8-58)."""
     half = dim // 2
-    expo = torch.arange(half, dtype=torch.float32, device=t.device) * torch.tensor(
-        -math.log(max_period), dtype=torch.float32, device=t.device)
+    # the Python scalar enters the fp32 kernel as fp32 (no host->device copy,
+    # so the call is CUDA-graph capturable)
+    expo = torch.arange(half, dtype=torch.float32, device=t.device) * (-math.log(max_period))
     freq = torch.exp(expo / half)
     arg = t.float()[:, None] * freq[None, :]
     return torch.cat([torch.cos(arg), torch.sin(arg)], dim=-1)
