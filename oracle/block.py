@@ -79,16 +79,18 @@ def attention(p, name, x, context=None, pe=None, k_pe=None, heads=32, eps=1e-6):
 
 
 def ada(table, ts, start, end):
-    """get_ada_values (transformer.py:286-309): fp32 table rows + timestep rows."""
-    return [np.asarray(table[i], np.float32) + np.asarray(ts[i], np.float32) for i in range(start, end)]
+    """get_ada_values (transformer.py:286-309): fp32 table rows + timestep
+    rows; ``ts`` is (rows, C) for the row, or (T, rows, C) per token."""
+    ts = np.asarray(ts, np.float32)
+    return [np.asarray(table[i], np.float32) + ts[..., i, :] for i in range(start, end)]
 
 
 def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
     """BasicAVTransformerBlock.__call__ for one batch row.
 
-    video / audio: dicts with x (T, C), context (L, Cctx), timesteps (9, C),
-    pe (cos, sin), cross_pe (cos, sin), cross_ss (4, C), cross_gate (1, C),
-    prompt (2, C).  Returns (vx, ax)."""
+    video / audio: dicts with x (T, C), context (L, Cctx), timesteps (9, C)
+    or per token (T, 9, C), pe (cos, sin), cross_pe (cos, sin), cross_ss
+    (4, C) or (T, 4, C), cross_gate (1, C), prompt (2, C).  Returns (vx, ax)."""
     vx, ax = video["x"], audio["x"]
     # video self-attention (transformer.py:447-471)
     sh, sc, g = ada(p["scale_shift_table"], video["timesteps"], 0, 3)
@@ -96,7 +98,7 @@ def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
     vx = ro.gated_add(vx, attention(p, "attn1", nv, pe=video["pe"], heads=heads_v, eps=eps), g)
     # video text cross-attention (transformer.py:344-387, 473-486)
     sh_q, sc_q, g = ada(p["scale_shift_table"], video["timesteps"], 6, 9)
-    kv = [np.asarray(p["prompt_scale_shift_table"][i], np.float32) + video["prompt"][i] for i in range(2)]
+    kv = ada(p["prompt_scale_shift_table"], video["prompt"], 0, 2)
     a_in = ro.adaln(vx, sc_q, sh_q, eps)
     enc = ro.modulate(video["context"], kv[1], kv[0])
     vx = ro.gate_then_add(vx, attention(p, "attn2", a_in, context=enc, heads=heads_v, eps=eps), g)
@@ -105,7 +107,7 @@ def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
     na = ro.adaln(ax, sc, sh, eps)
     ax = ro.gated_add(ax, attention(p, "audio_attn1", na, pe=audio["pe"], heads=heads_a, eps=eps), g)
     sh_q, sc_q, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 6, 9)
-    kv = [np.asarray(p["audio_prompt_scale_shift_table"][i], np.float32) + audio["prompt"][i] for i in range(2)]
+    kv = ada(p["audio_prompt_scale_shift_table"], audio["prompt"], 0, 2)
     a_in = ro.adaln(ax, sc_q, sh_q, eps)
     enc = ro.modulate(audio["context"], kv[1], kv[0])
     ax = ro.gate_then_add(ax, attention(p, "audio_attn2", a_in, context=enc, heads=heads_a, eps=eps), g)
@@ -113,10 +115,10 @@ def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
     vn3 = ro.rms_norm(vx, eps)
     an3 = ro.rms_norm(ax, eps)
     ta, tv = p["scale_shift_table_a2v_ca_audio"], p["scale_shift_table_a2v_ca_video"]
-    a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = [ta[i] + audio["cross_ss"][i] for i in range(4)]
-    g_v2a = ta[4] + audio["cross_gate"][0]
-    v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = [tv[i] + video["cross_ss"][i] for i in range(4)]
-    g_a2v = tv[4] + video["cross_gate"][0]
+    a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = ada(ta, audio["cross_ss"], 0, 4)
+    g_v2a = ta[4] + np.asarray(audio["cross_gate"], np.float32)[..., 0, :]
+    v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = ada(tv, video["cross_ss"], 0, 4)
+    g_a2v = tv[4] + np.asarray(video["cross_gate"], np.float32)[..., 0, :]
     vxs = ro.modulate(vn3, v_sc_a2v, v_sh_a2v)
     axs = ro.modulate(an3, a_sc_a2v, a_sh_a2v)
     out = attention(p, "audio_to_video_attn", vxs, context=axs, pe=video["cross_pe"], k_pe=audio["cross_pe"],

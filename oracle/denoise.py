@@ -169,18 +169,22 @@ def _ada_params(mp: dict, prefix: str) -> dict:
 
 def _prepare(mp: dict, which: str, s: dict, cross_sigma: float, ts_mult: float, av_ca_mult: float):
     """MultiModalTransformerArgsPreprocessor.prepare (model.py:270-340,
-    454-505) for one batch row with uniform timesteps (= sigma)."""
+    454-505) for one batch row: timesteps uniform (= sigma) or per token
+    (``s["timesteps"]`` (T,) fp32, the denoise mask times sigma)."""
     p = MODEL_PREFIXES[which]
     d = np.asarray(mp[f"{p['patchify']}.weight"]).shape[0]
-    scaled = (np.array([s["sigma"]], F32) * F32(ts_mult)).astype(F32)
+    sig = (np.array([s["sigma"]], F32) * F32(ts_mult)).astype(F32)
+    per_token = s.get("timesteps") is not None
+    scaled = (np.asarray(s["timesteps"], F32) * F32(ts_mult)).astype(F32) if per_token else sig
     emb, emb_t = ada_single(_ada_params(mp, p["adaln"]), scaled)
-    prompt, _ = ada_single(_ada_params(mp, p["prompt"]), scaled)
+    prompt, _ = ada_single(_ada_params(mp, p["prompt"]), sig)
     css, _ = ada_single(_ada_params(mp, p["cross_ss"]), scaled)
     cg, _ = ada_single(_ada_params(mp, p["cross_gate"]),
                        (np.array([cross_sigma], F32) * F32(av_ca_mult)).astype(F32))
     x = linear_bf16(s["latent"], mp[f"{p['patchify']}.weight"], mp[f"{p['patchify']}.bias"])
-    args = {"x": x, "context": s["context"], "timesteps": emb.reshape(9, d), "pe": s["pe"],
-            "cross_pe": s["cross_pe"], "cross_ss": css.reshape(4, d), "cross_gate": cg.reshape(1, d),
+    lead = (-1,) if per_token else ()
+    args = {"x": x, "context": s["context"], "timesteps": emb.reshape(lead + (9, d)), "pe": s["pe"],
+            "cross_pe": s["cross_pe"], "cross_ss": css.reshape(lead + (4, d)), "cross_gate": cg.reshape(1, d),
             "prompt": prompt.reshape(2, d)}
     return args, emb_t
 
@@ -190,7 +194,8 @@ def model_forward(blocks_p: list, mp: dict, video: dict, audio: dict, heads_v: i
     """LTXModel.__call__ (model.py:1343-1487) for one batch row: preprocess
     both streams, the blocks (``oracle.block.block``), the output heads.
     ``video`` / ``audio``: latent (T, 128) bf16 values, sigma (float),
-    context, pe, cross_pe.  Returns the (video, audio) velocities."""
+    optional per-token timesteps (T,), context, pe, cross_pe.  Returns the
+    (video, audio) velocities."""
     from .block import block
 
     va, vt = _prepare(mp, "video", video, audio["sigma"], ts_mult, av_ca_mult)

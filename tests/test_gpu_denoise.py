@@ -146,6 +146,39 @@ def test_model_matches_oracle(cuda):
     assert ltxq._lib.device_error() == 0
 
 
+def test_model_per_token_timesteps_matches_oracle(cuda):
+    """A non-uniform denoise mask (conditioning tokens at mask 0): per-token
+    video timesteps (mask * sigma) run the AdaLN MLPs per token and give
+    per-token AdaLN vectors in every block and in the output head."""
+    import torch
+
+    import ltxq
+    from ltxq.model import Modality
+
+    model, blocks_p, mp, video, audio = _model_case(seed=60)
+    g = rng(61)
+    T, A, L = 64, 32, 24
+    vs = _stream_inputs(g, video, T, L, audio.heads, audio.d_head)
+    as_ = _stream_inputs(g, audio, A, L, audio.heads, audio.d_head)
+    sigma = 0.725
+    mask = np.ones(T, np.float32)
+    mask[:16] = 0.0
+    mask[16:24] = 0.5
+    ts = (mask * np.float32(sigma)).astype(np.float32)
+    ref_v, ref_a = od.model_forward(blocks_p, mp, dict(vs, sigma=sigma, timesteps=ts), dict(as_, sigma=sigma),
+                                    video.heads, audio.heads)
+    sig = torch.full((1,), sigma, dtype=torch.float32, device="cuda")
+    vm = Modality(to_dev_bf16(vs["latent"])[None], _f32_dev(ts)[None], to_dev_bf16(vs["context"])[None],
+                  _pe_dev(vs["pe"]), _pe_dev(vs["cross_pe"]), sigma=sig)
+    am = Modality(to_dev_bf16(as_["latent"])[None], sig, to_dev_bf16(as_["context"])[None], _pe_dev(as_["pe"]),
+                  _pe_dev(as_["cross_pe"]), sigma=sig)
+    ov, oa = model(vm, am)
+    for got, ref, what in ((from_dev_bf16(ov[0]), ref_v, "video"), (from_dev_bf16(oa[0]), ref_a, "audio")):
+        mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
+        assert mar <= 2e-2 and cos >= 0.9995, f"{what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
+    assert ltxq._lib.device_error() == 0
+
+
 def test_denoise_loop_cfg_matches_oracle_and_graph_replay(cuda):
     """Two steps of the AV CFG loop (positive and negative passes batched
     into one batch-2 transformer pass) against the oracle loop, which runs
