@@ -490,11 +490,19 @@ class BasicAVTransformerBlock:
         vals = t[None, None] + ts[:, :, start:end]
         return [vals[:, :, i] for i in range(end - start)]  # views: the kernels take strided vectors
 
-    def __call__(self, video: TransformerArgs, audio: TransformerArgs, shard: RowShard | None = None):
+    def __call__(self, video: TransformerArgs, audio: TransformerArgs, shard: RowShard | None = None,
+                 skip: frozenset = frozenset()):
         """One block.  With ``shard``, ``video`` holds this rank's rows (and
-        the matching rows of its RoPE tables); the result keeps that split."""
+        the matching rows of its RoPE tables); the result keeps that split.
+        ``skip`` names attention sub-layers to leave out (``PerturbationType``
+        values of ``ltxq.perturbations``: a perturbed pass for STG,
+        transformer.py:429-444, 455-457, 496-497, 574-575, 603-604)."""
         eps = self.norm_eps
         vx, ax = video.x.contiguous(), audio.x.contiguous()
+        run_v = "skip_video_self_attn" not in skip
+        run_a = "skip_audio_self_attn" not in skip
+        run_a2v = "skip_a2v_cross_attn" not in skip
+        run_v2a = "skip_v2a_cross_attn" not in skip
 
         sharded = shard is not None and shard.world > 1
         # video self-attention (transformer.py:447-471).  In a row-sharded
@@ -502,33 +510,36 @@ class BasicAVTransformerBlock:
         # K/V when the heads do not split evenly) overlaps the audio self- and
         # text cross-attention, which read no video rows (same results: the
         # two streams are independent until the audio<->video cross-attention)
-        sh, sc, g = self._ada("scale_shift_table", video.timesteps, 0, 3)
         at = self.attn["attn1"]
-        q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
-        q, k = at.norm_rope(q, k, video.positional_embeddings)
         head_par = sharded and shard.self_attention == "head_parallel" and at.heads % shard.world == 0
         pend = None
-        if head_par:  # head-parallel attention: Q/K/V all-to-all, then SDPA on H/world heads
-            qkv = torch.stack([heads_to_ranks(t_, shard.world, at.heads) for t_ in (q, k, v)], dim=1)
-            pend = shard.start_all_to_all(qkv)
-        elif sharded:
-            pend = shard.start_gather(k, v)
+        if run_v:
+            sh, sc, g = self._ada("scale_shift_table", video.timesteps, 0, 3)
+            q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
+            q, k = at.norm_rope(q, k, video.positional_embeddings)
+            if head_par:  # head-parallel attention: Q/K/V all-to-all, then SDPA on H/world heads
+                qkv = torch.stack([heads_to_ranks(t_, shard.world, at.heads) for t_ in (q, k, v)], dim=1)
+                pend = shard.start_all_to_all(qkv)
+            elif sharded:
+                pend = shard.start_gather(k, v)
 
         # audio self-attention + text cross-attention (transformer.py:488-527)
-        sh_a, sc_a, g_a = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
-        at_a = self.attn["audio_attn1"]
-        qa, ka, va, gla = at_a.project(K.adaln_modulate(ax, sc_a, sh_a, eps), None)
-        o = at_a.core(qa, ka, va, gla, audio.positional_embeddings)
-        ax = at_a.to_out(o, residual=ax, gate=g_a)
+        if run_a:
+            sh_a, sc_a, g_a = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
+            at_a = self.attn["audio_attn1"]
+            qa, ka, va, gla = at_a.project(K.adaln_modulate(ax, sc_a, sh_a, eps), None)
+            o = at_a.core(qa, ka, va, gla, audio.positional_embeddings)
+            ax = at_a.to_out(o, residual=ax, gate=g_a)
         ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
 
-        if head_par:
-            o = at.attend_head_parallel(shard.finish_all_to_all(pend), gl, shard)
-        else:
-            if pend is not None:
-                k, v = shard.finish_gather(pend)
-            o = at.attend(q, k, v, gl)
-        vx = at.to_out(o, residual=vx, gate=g)
+        if run_v:
+            if head_par:
+                o = at.attend_head_parallel(shard.finish_all_to_all(pend), gl, shard)
+            else:
+                if pend is not None:
+                    k, v = shard.finish_gather(pend)
+                o = at.attend(q, k, v, gl)
+            vx = at.to_out(o, residual=vx, gate=g)
 
         # video text cross-attention (transformer.py:344-387, 473-486)
         vx = self._text_ca(vx, video, "attn2", "scale_shift_table", "prompt_scale_shift_table")
@@ -542,27 +553,32 @@ class BasicAVTransformerBlock:
         v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_video", video)
         g_a2v = (self.tables["scale_shift_table_a2v_ca_video"][4][None, None] + video.cross_gate_timestep[:, :, 0])
         at = self.attn["audio_to_video_attn"]
-        q, k, v, gl = at.project(K.adaln_modulate(vx, v_sc_a2v, v_sh_a2v, eps),
-                                 K.adaln_modulate(ax, a_sc_a2v, a_sh_a2v, eps))
+        if run_a2v:
+            q, k, v, gl = at.project(K.adaln_modulate(vx, v_sc_a2v, v_sh_a2v, eps),
+                                     K.adaln_modulate(ax, a_sc_a2v, a_sh_a2v, eps))
         at2 = self.attn["video_to_audio_attn"]
-        q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
-                                      K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
-        q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
         split_keys = sharded and shard.v2a == "split_keys"
-        pend2 = shard.start_gather(k2, v2) if sharded and not split_keys else None
-        o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
-        vx = at.to_out(o, residual=vx, gate=g_a2v)
+        pend2 = None
+        if run_v2a:
+            q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
+                                          K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
+            q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
+            pend2 = shard.start_gather(k2, v2) if sharded and not split_keys else None
+        if run_a2v:
+            o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
+            vx = at.to_out(o, residual=vx, gate=g_a2v)
         # video->audio: the audio queries are on every rank, the video keys
         # are split by rows.  "split_keys": each rank attends over its rows
         # and the partial results merge by their log-sum-exp (a ~1 MB exchange
         # instead of an all-gather of the video K/V)
-        if split_keys:
-            o2 = at2.attend_split_keys(q2, k2, v2, gl2, shard)
-        else:
-            if pend2 is not None:
-                k2, v2 = shard.finish_gather(pend2)
-            o2 = at2.attend(q2, k2, v2, gl2)
-        ax = at2.to_out(o2, residual=ax, gate=g_v2a)
+        if run_v2a:
+            if split_keys:
+                o2 = at2.attend_split_keys(q2, k2, v2, gl2, shard)
+            else:
+                if pend2 is not None:
+                    k2, v2 = shard.finish_gather(pend2)
+                o2 = at2.attend(q2, k2, v2, gl2)
+            ax = at2.to_out(o2, residual=ax, gate=g_v2a)
 
         # feed-forwards (transformer.py:629-668)
         vx = self._ff(vx, video, "scale_shift_table", self.ff)

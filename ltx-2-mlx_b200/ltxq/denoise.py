@@ -17,10 +17,13 @@ Mirrors the reference's sampling components:
   With ``graph=True`` the model call is captured once as a CUDA graph and
   replayed every step.
 
-Not built: the STG perturbed pass (it needs blocks that skip attention
-modules, ``BatchedPerturbationConfig``), the Heun stepper and the
-non-AV / two-stage pipelines.  ``denoise_update`` still takes a perturbed
-velocity from a caller that has one.
+With an ``STGGuider`` and a ``BatchedPerturbationConfig``
+(``ltxq.perturbations``), each step also runs the perturbed pass (the
+positive inputs through blocks that skip the perturbed attention
+sub-layers) until ``stg_cutoff`` of the steps, and the video update adds
+the STG term after CFG, as av_pipeline.py:709-720 does.
+
+Not built: the Heun stepper and the non-AV / two-stage pipelines.
 """
 
 from __future__ import annotations
@@ -172,14 +175,17 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
                audio_context: torch.Tensor, video_pe: tuple, audio_pe: tuple, video_cross_pe: tuple,
                audio_cross_pe: tuple, negative_video_context: torch.Tensor | None = None,
                negative_audio_context: torch.Tensor | None = None, video_guider: CFGGuider = CFGGuider(1.0),
-               audio_guider: CFGGuider = CFGGuider(1.0), ge_gamma: float = 0.0, shard=None, graph: bool = False,
+               audio_guider: CFGGuider = CFGGuider(1.0), ge_gamma: float = 0.0, stg_guider: STGGuider | None = None,
+               stg_perturbations=None, stg_cutoff: float = 1.0, shard=None, graph: bool = False,
                callback=None) -> tuple[LatentState, LatentState]:
     """``_denoise_loop_cfg_av`` (av_pipeline.py:625-756) over ``model`` (an
     ``LTXAVModel``): per step one transformer pass (2B rows when either
     guider is enabled: positive then negative contexts), then one
     ``denoise_update`` per stream.  Gradient estimation (``ge_gamma``)
-    applies to the video stream, as in the reference.  With a row shard,
-    ``video`` holds this rank's rows."""
+    applies to the video stream, as in the reference.  The STG pass (when
+    ``stg_guider`` is enabled and ``stg_perturbations`` given) is a separate
+    batch-B pass: its blocks skip sub-layers for the whole batch.  With a row
+    shard, ``video`` holds this rank's rows."""
     from .model import Modality
 
     sig = np.asarray(sigmas, dtype=np.float32)
@@ -210,8 +216,14 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
         return model(Modality(v_in, v_t, vctx, vpe, vcpe, sigma=v_s),
                      Modality(a_in, a_t, actx, ape, acpe, sigma=v_s), shard)
 
+    def run_perturbed(v_in, a_in, v_t, a_t, v_s):
+        return model(Modality(v_in, v_t, video_context, video_pe, video_cross_pe, sigma=v_s),
+                     Modality(a_in, a_t, audio_context, audio_pe, audio_cross_pe, sigma=v_s), shard,
+                     stg_perturbations)
+
+    stg_on = stg_guider is not None and stg_guider.enabled() and stg_perturbations is not None
     prev = torch.empty(video.latent.shape, dtype=torch.float32, device=dev) if ge_gamma > 0 else None
-    step_graph = None
+    step_graph = stg_graph = None
     for i in range(steps):
         sigma, sigma_next = float(sig[i]), float(sig[i + 1])
         for dst, st in ((v_in, video), (a_in, audio)):
@@ -232,8 +244,21 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
             vv, av = run(v_in, a_in, v_t, a_t, v_s)
         vc, ac = vv[:b], av[:b]
         vu, au = (vv[b:], av[b:]) if need_cfg else (None, None)
+        stg_active = stg_on and (i + 1) / steps <= stg_cutoff  # av_pipeline.py:709-714
+        vp = None
+        if stg_active:  # the positive rows of the input buffers, through the perturbed blocks
+            pos = (v_in[:b], a_in[:b], v_t[:b], a_t[:b], v_s[:b])
+            if graph:
+                if stg_graph is None:
+                    from .graph import StepGraph
+
+                    stg_graph = StepGraph(run_perturbed, *pos)
+                vp = stg_graph.replay()[0]
+            else:
+                vp = run_perturbed(*pos)[0]
         new_v = denoise_update(video.latent, vc, sigma, sigma_next, v_uncond=vu,
-                               cfg_scale=video_guider.scale if need_cfg else 1.0,
+                               cfg_scale=video_guider.scale if need_cfg else 1.0, v_perturbed=vp,
+                               stg_scale=stg_guider.scale if stg_active else 0.0,
                                denoise_mask=video.denoise_mask, clean_latent=video.clean_latent,
                                prev_velocity=prev, ge_gamma=ge_gamma, have_prev=i > 0)
         new_a = denoise_update(audio.latent, ac, sigma, sigma_next, v_uncond=au,
@@ -242,6 +267,7 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
         video, audio = replace(video, latent=new_v), replace(audio, latent=new_a)
         if callback is not None:
             callback(i + 1, steps)
-    if step_graph is not None:
-        step_graph.release()
+    for gr in (step_graph, stg_graph):
+        if gr is not None:
+            gr.release()
     return video, audio

@@ -242,15 +242,18 @@ class LTXAVModel:
         y = K.adaln_modulate(x, ss[:, :, 1], ss[:, :, 0], self.norm_eps, norm="layer")
         return F.linear(y, s.proj_out_w, s.proj_out_b)
 
-    def __call__(self, video: Modality, audio: Modality, shard: RowShard | None = None):
+    def __call__(self, video: Modality, audio: Modality, shard: RowShard | None = None, perturbations=None):
         """(video velocity, audio velocity).  With a row shard, ``video``
         holds this rank's latent rows (and their RoPE rows); the video
-        velocity keeps that split, the audio velocity is replicated."""
+        velocity keeps that split, the audio velocity is replicated.
+        ``perturbations`` (``ltxq.perturbations.BatchedPerturbationConfig``)
+        makes this the perturbed pass of STG guidance."""
         shard = shard if shard is not None else self.shard
         va = self._prepare(self.video, video, audio)
         aa = self._prepare(self.audio, audio, video)
-        for blk in self.blocks:
-            va, aa = blk(va, aa, shard)
+        for i, blk in enumerate(self.blocks):
+            skip = perturbations.skipped(i) if perturbations is not None else frozenset()
+            va, aa = blk(va, aa, shard, skip)
         return self._output(self.video, va.x, va.embedded_timestep), self._output(self.audio, aa.x,
                                                                                   aa.embedded_timestep)
 

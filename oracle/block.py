@@ -85,17 +85,21 @@ def ada(table, ts, start, end):
     return [np.asarray(table[i], np.float32) + ts[..., i, :] for i in range(start, end)]
 
 
-def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
-    """BasicAVTransformerBlock.__call__ for one batch row.
+def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6, skip=frozenset()):
+    """BasicAVTransformerBlock.__call__ for one batch row.  ``skip`` holds
+    the perturbed sub-layers ("skip_video_self_attn", "skip_audio_self_attn",
+    "skip_a2v_cross_attn", "skip_v2a_cross_attn"; transformer.py:429-444),
+    which leave their stream's residual unchanged.
 
     video / audio: dicts with x (T, C), context (L, Cctx), timesteps (9, C)
     or per token (T, 9, C), pe (cos, sin), cross_pe (cos, sin), cross_ss
     (4, C) or (T, 4, C), cross_gate (1, C), prompt (2, C).  Returns (vx, ax)."""
     vx, ax = video["x"], audio["x"]
     # video self-attention (transformer.py:447-471)
-    sh, sc, g = ada(p["scale_shift_table"], video["timesteps"], 0, 3)
-    nv = ro.adaln(vx, sc, sh, eps)
-    vx = ro.gated_add(vx, attention(p, "attn1", nv, pe=video["pe"], heads=heads_v, eps=eps), g)
+    if "skip_video_self_attn" not in skip:
+        sh, sc, g = ada(p["scale_shift_table"], video["timesteps"], 0, 3)
+        nv = ro.adaln(vx, sc, sh, eps)
+        vx = ro.gated_add(vx, attention(p, "attn1", nv, pe=video["pe"], heads=heads_v, eps=eps), g)
     # video text cross-attention (transformer.py:344-387, 473-486)
     sh_q, sc_q, g = ada(p["scale_shift_table"], video["timesteps"], 6, 9)
     kv = ada(p["prompt_scale_shift_table"], video["prompt"], 0, 2)
@@ -103,9 +107,10 @@ def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
     enc = ro.modulate(video["context"], kv[1], kv[0])
     vx = ro.gate_then_add(vx, attention(p, "attn2", a_in, context=enc, heads=heads_v, eps=eps), g)
     # audio self-attention + text cross-attention (transformer.py:488-527)
-    sh, sc, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 0, 3)
-    na = ro.adaln(ax, sc, sh, eps)
-    ax = ro.gated_add(ax, attention(p, "audio_attn1", na, pe=audio["pe"], heads=heads_a, eps=eps), g)
+    if "skip_audio_self_attn" not in skip:
+        sh, sc, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 0, 3)
+        na = ro.adaln(ax, sc, sh, eps)
+        ax = ro.gated_add(ax, attention(p, "audio_attn1", na, pe=audio["pe"], heads=heads_a, eps=eps), g)
     sh_q, sc_q, g = ada(p["audio_scale_shift_table"], audio["timesteps"], 6, 9)
     kv = ada(p["audio_prompt_scale_shift_table"], audio["prompt"], 0, 2)
     a_in = ro.adaln(ax, sc_q, sh_q, eps)
@@ -119,16 +124,19 @@ def block(p, video, audio, heads_v=32, heads_a=32, eps=1e-6):
     g_v2a = ta[4] + np.asarray(audio["cross_gate"], np.float32)[..., 0, :]
     v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = ada(tv, video["cross_ss"], 0, 4)
     g_a2v = tv[4] + np.asarray(video["cross_gate"], np.float32)[..., 0, :]
-    vxs = ro.modulate(vn3, v_sc_a2v, v_sh_a2v)
-    axs = ro.modulate(an3, a_sc_a2v, a_sh_a2v)
-    out = attention(p, "audio_to_video_attn", vxs, context=axs, pe=video["cross_pe"], k_pe=audio["cross_pe"],
-                    heads=heads_a, eps=eps)
-    vx_new = ro.gated_add(vx, out, g_a2v)
-    axs = ro.modulate(an3, a_sc_v2a, a_sh_v2a)
-    vxs = ro.modulate(vn3, v_sc_v2a, v_sh_v2a)
-    out = attention(p, "video_to_audio_attn", axs, context=vxs, pe=audio["cross_pe"], k_pe=video["cross_pe"],
-                    heads=heads_a, eps=eps)
-    ax = ro.gated_add(ax, out, g_v2a)
+    vx_new = vx
+    if "skip_a2v_cross_attn" not in skip:
+        vxs = ro.modulate(vn3, v_sc_a2v, v_sh_a2v)
+        axs = ro.modulate(an3, a_sc_a2v, a_sh_a2v)
+        out = attention(p, "audio_to_video_attn", vxs, context=axs, pe=video["cross_pe"], k_pe=audio["cross_pe"],
+                        heads=heads_a, eps=eps)
+        vx_new = ro.gated_add(vx, out, g_a2v)
+    if "skip_v2a_cross_attn" not in skip:
+        axs = ro.modulate(an3, a_sc_v2a, a_sh_v2a)
+        vxs = ro.modulate(vn3, v_sc_v2a, v_sh_v2a)
+        out = attention(p, "video_to_audio_attn", axs, context=vxs, pe=audio["cross_pe"], k_pe=video["cross_pe"],
+                        heads=heads_a, eps=eps)
+        ax = ro.gated_add(ax, out, g_v2a)
     vx = vx_new
     # feed-forwards (transformer.py:629-668)
     sh, sc, g = ada(p["scale_shift_table"], video["timesteps"], 3, 6)

@@ -190,18 +190,20 @@ def _prepare(mp: dict, which: str, s: dict, cross_sigma: float, ts_mult: float, 
 
 
 def model_forward(blocks_p: list, mp: dict, video: dict, audio: dict, heads_v: int, heads_a: int,
-                  ts_mult: float = 1000.0, av_ca_mult: float = 1000.0, eps: float = 1e-6):
+                  ts_mult: float = 1000.0, av_ca_mult: float = 1000.0, eps: float = 1e-6, skips=None):
     """LTXModel.__call__ (model.py:1343-1487) for one batch row: preprocess
     both streams, the blocks (``oracle.block.block``), the output heads.
     ``video`` / ``audio``: latent (T, 128) bf16 values, sigma (float),
     optional per-token timesteps (T,), context, pe, cross_pe.  Returns the
-    (video, audio) velocities."""
+    (video, audio) velocities.  ``skips``: block index -> the sub-layers a
+    perturbed (STG) pass skips there."""
     from .block import block
 
     va, vt = _prepare(mp, "video", video, audio["sigma"], ts_mult, av_ca_mult)
     aa, at = _prepare(mp, "audio", audio, video["sigma"], ts_mult, av_ca_mult)
-    for p in blocks_p:
-        vx, ax = block(p, va, aa, heads_v=heads_v, heads_a=heads_a, eps=eps)
+    for i, p in enumerate(blocks_p):
+        skip = (skips or {}).get(i, frozenset())
+        vx, ax = block(p, va, aa, heads_v=heads_v, heads_a=heads_a, eps=eps, skip=skip)
         va, aa = dict(va, x=vx), dict(aa, x=ax)
     outs = []
     for which, args, emb_t in (("video", va, vt), ("audio", aa, at)):
@@ -211,20 +213,28 @@ def model_forward(blocks_p: list, mp: dict, video: dict, audio: dict, heads_v: i
     return outs[0], outs[1]
 
 
-def denoise_loop_av(model_fn, video_latent, audio_latent, sigmas, cfg_video: float = 1.0, cfg_audio: float = 1.0):
-    """_denoise_loop_cfg_av (av_pipeline.py:625-756) without STG, gradient
+def denoise_loop_av(model_fn, video_latent, audio_latent, sigmas, cfg_video: float = 1.0, cfg_audio: float = 1.0,
+                    stg_scale: float = 0.0, stg_cutoff: float = 1.0):
+    """_denoise_loop_cfg_av (av_pipeline.py:625-756) without gradient
     estimation or masks: ``model_fn(video_latent, audio_latent, sigma,
-    negative)`` -> (video velocity, audio velocity) for one batch row; the
-    negative pass runs when either scale is not 1.  Returns the final
-    (video, audio) latents."""
+    pass_)`` -> (video velocity, audio velocity) for one batch row, pass_ in
+    {"positive", "negative", "perturbed"}; the negative pass runs when either
+    scale is not 1, the perturbed (STG) pass while stg_scale != 0 and
+    (step + 1) / steps <= stg_cutoff (av_pipeline.py:709-720).  Returns the
+    final (video, audio) latents."""
     need_cfg = cfg_video != 1.0 or cfg_audio != 1.0
     sig = np.asarray(sigmas, dtype=F32)
-    for i in range(len(sig) - 1):
+    steps = len(sig) - 1
+    for i in range(steps):
         s, sn = float(sig[i]), float(sig[i + 1])
-        vc, ac = model_fn(video_latent, audio_latent, s, False)
-        vu = au = None
+        vc, ac = model_fn(video_latent, audio_latent, s, "positive")
+        vu = au = vp = None
         if need_cfg:
-            vu, au = model_fn(video_latent, audio_latent, s, True)
-        video_latent = denoise_update(video_latent, vc, s, sn, v_uncond=vu, cfg_scale=cfg_video if need_cfg else 1.0)[0]
+            vu, au = model_fn(video_latent, audio_latent, s, "negative")
+        stg = stg_scale != 0.0 and (i + 1) / steps <= stg_cutoff
+        if stg:
+            vp, _ = model_fn(video_latent, audio_latent, s, "perturbed")
+        video_latent = denoise_update(video_latent, vc, s, sn, v_uncond=vu, cfg_scale=cfg_video if need_cfg else 1.0,
+                                      v_perturbed=vp, stg_scale=stg_scale if stg else 0.0)[0]
         audio_latent = denoise_update(audio_latent, ac, s, sn, v_uncond=au, cfg_scale=cfg_audio if need_cfg else 1.0)[0]
     return video_latent, audio_latent

@@ -109,3 +109,20 @@ def test_oracle_zero_mask_keeps_the_clean_latent_at_the_end():
     mask[:, 16:] = 1.0
     got, _ = od.denoise_update(x, v, 0.725, 0.0, denoise_mask=mask, clean_latent=clean)
     assert np.array_equal(got[:, :16], clean[:, :16])
+
+
+def test_perturbation_config():
+    """components/perturbations.py semantics: a block skips a sub-layer only
+    when every sample is perturbed for it; blocks=None means every block."""
+    from ltxq.perturbations import (BatchedPerturbationConfig, Perturbation, PerturbationConfig, PerturbationType,
+                                    create_batched_stg_config)
+
+    stg = create_batched_stg_config(2, blocks=[3, 5])
+    assert stg.skipped(3) == frozenset({"skip_video_self_attn"}) and stg.skipped(4) == frozenset()
+    every = create_batched_stg_config(1)
+    assert all(every.skipped(i) == frozenset({"skip_video_self_attn"}) for i in range(48))
+    mixed = BatchedPerturbationConfig([PerturbationConfig([Perturbation(PerturbationType.SKIP_V2A_CROSS_ATTN)]),
+                                       PerturbationConfig.empty()])
+    assert not mixed.all_in_batch(PerturbationType.SKIP_V2A_CROSS_ATTN, 0) and mixed.skipped(0) == frozenset()
+    assert BatchedPerturbationConfig.empty(3).skipped(0) == frozenset()
+    assert not create_batched_stg_config(1, skip_video_self_attn=False).skipped(0)

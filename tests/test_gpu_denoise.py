@@ -198,7 +198,8 @@ def test_denoise_loop_cfg_matches_oracle_and_graph_replay(cuda):
     sigmas = np.asarray([1.0, 0.909375, 0.725], np.float32)
     cfg_v, cfg_a = 2.0, 1.5
 
-    def oracle_model(vl, al, s, negative):
+    def oracle_model(vl, al, s, pass_):
+        negative = pass_ == "negative"
         v_in = dict(vs, latent=vl, sigma=s, context=neg_v if negative else vs["context"])
         a_in = dict(as_, latent=al, sigma=s, context=neg_a if negative else as_["context"])
         return od.model_forward(blocks_p, mp, v_in, a_in, video.heads, audio.heads)
@@ -222,4 +223,93 @@ def test_denoise_loop_cfg_matches_oracle_and_graph_replay(cuda):
                            (from_dev_bf16(outs[0][1][0]), ref_a, "audio")):
         mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
         assert mar <= 2e-2 and cos >= 0.9995, f"{what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
+    assert ltxq._lib.device_error() == 0
+
+
+SKIPS = {0: frozenset({"skip_video_self_attn", "skip_audio_self_attn"}),
+         1: frozenset({"skip_a2v_cross_attn", "skip_v2a_cross_attn"})}
+
+
+def _perturbations(batch):
+    from ltxq.perturbations import BatchedPerturbationConfig, Perturbation, PerturbationConfig, PerturbationType
+
+    cfg = PerturbationConfig([Perturbation(PerturbationType.SKIP_VIDEO_SELF_ATTN, [0]),
+                              Perturbation(PerturbationType.SKIP_AUDIO_SELF_ATTN, [0]),
+                              Perturbation(PerturbationType.SKIP_A2V_CROSS_ATTN, [1]),
+                              Perturbation(PerturbationType.SKIP_V2A_CROSS_ATTN, [1])])
+    return BatchedPerturbationConfig([cfg] * batch)
+
+
+def test_model_perturbed_pass_matches_oracle(cuda):
+    """The STG perturbed pass: block 0 skips both self-attentions, block 1
+    both audio<->video cross-attentions; against the oracle with the same
+    skips."""
+    import torch
+
+    import ltxq
+    from ltxq.model import Modality
+
+    model, blocks_p, mp, video, audio = _model_case(seed=70)
+    g = rng(71)
+    T, A, L = 64, 32, 24
+    vs = _stream_inputs(g, video, T, L, audio.heads, audio.d_head)
+    as_ = _stream_inputs(g, audio, A, L, audio.heads, audio.d_head)
+    sigma = 0.98125
+    ref_v, ref_a = od.model_forward(blocks_p, mp, dict(vs, sigma=sigma), dict(as_, sigma=sigma), video.heads,
+                                    audio.heads, skips=SKIPS)
+    sig = torch.full((1,), sigma, dtype=torch.float32, device="cuda")
+    vm = Modality(to_dev_bf16(vs["latent"])[None], sig, to_dev_bf16(vs["context"])[None], _pe_dev(vs["pe"]),
+                  _pe_dev(vs["cross_pe"]), sigma=sig)
+    am = Modality(to_dev_bf16(as_["latent"])[None], sig, to_dev_bf16(as_["context"])[None], _pe_dev(as_["pe"]),
+                  _pe_dev(as_["cross_pe"]), sigma=sig)
+    ov, oa = model(vm, am, perturbations=_perturbations(1))
+    full_v, _ = model(vm, am)
+    for got, ref, what in ((from_dev_bf16(ov[0]), ref_v, "video"), (from_dev_bf16(oa[0]), ref_a, "audio")):
+        mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
+        assert mar <= 2e-2 and cos >= 0.9995, f"{what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
+    assert not torch.equal(full_v.view(torch.int16), ov.view(torch.int16))  # the skips change the result
+    assert ltxq._lib.device_error() == 0
+
+
+def test_denoise_loop_stg_matches_oracle(cuda):
+    """Two steps of the loop with CFG and STG (the perturbed pass in the
+    first step only: cutoff 0.5) against the oracle loop, eager and with
+    both passes replayed as CUDA graphs."""
+    import ltxq
+    from ltxq.denoise import CFGGuider, LatentState, STGGuider, denoise_av
+
+    model, blocks_p, mp, video, audio = _model_case(seed=80)
+    g = rng(81)
+    T, A, L = 64, 32, 24
+    vs = _stream_inputs(g, video, T, L, audio.heads, audio.d_head)
+    as_ = _stream_inputs(g, audio, A, L, audio.heads, audio.d_head)
+    neg_v = normal_bf16(g, (L, video.context_dim))
+    neg_a = normal_bf16(g, (L, audio.context_dim))
+    sigmas = np.asarray([1.0, 0.909375, 0.725], np.float32)
+
+    def oracle_model(vl, al, s, pass_):
+        negative = pass_ == "negative"
+        v_in = dict(vs, latent=vl, sigma=s, context=neg_v if negative else vs["context"])
+        a_in = dict(as_, latent=al, sigma=s, context=neg_a if negative else as_["context"])
+        return od.model_forward(blocks_p, mp, v_in, a_in, video.heads, audio.heads,
+                                skips=SKIPS if pass_ == "perturbed" else None)
+
+    ref_v, ref_a = od.denoise_loop_av(oracle_model, vs["latent"], as_["latent"], sigmas, 2.0, 1.5, stg_scale=1.0,
+                                      stg_cutoff=0.5)
+    outs = []
+    for graph in (False, True):
+        fv, fa = denoise_av(model, LatentState(to_dev_bf16(vs["latent"])[None]),
+                            LatentState(to_dev_bf16(as_["latent"])[None]), sigmas, to_dev_bf16(vs["context"])[None],
+                            to_dev_bf16(as_["context"])[None], _pe_dev(vs["pe"]), _pe_dev(as_["pe"]),
+                            _pe_dev(vs["cross_pe"]), _pe_dev(as_["cross_pe"]),
+                            negative_video_context=to_dev_bf16(neg_v)[None],
+                            negative_audio_context=to_dev_bf16(neg_a)[None], video_guider=CFGGuider(2.0),
+                            audio_guider=CFGGuider(1.5), stg_guider=STGGuider(1.0), stg_perturbations=_perturbations(1),
+                            stg_cutoff=0.5, graph=graph)
+        outs.append((from_dev_bf16(fv.latent[0]), from_dev_bf16(fa.latent[0])))
+    for got, ref, what in ((outs[0][0], ref_v, "video"), (outs[0][1], ref_a, "audio")):
+        mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
+        assert mar <= 2e-2 and cos >= 0.9995, f"{what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
+    for a, b in zip(outs[0], outs[1]):
+        assert ro.max_abs_rel(b, a) <= 2e-3
     assert ltxq._lib.device_error() == 0
