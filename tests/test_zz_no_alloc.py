@@ -12,7 +12,6 @@ used by the other parity tests.  The file is named to be collected last.
 
 import ctypes
 
-import numpy as np
 import pytest
 
 from helpers import from_dev_bf16, normal_bf16, normal_f32, rng, to_dev, to_dev_bf16
