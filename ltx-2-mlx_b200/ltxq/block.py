@@ -155,10 +155,12 @@ def _heads(x: torch.Tensor, heads: int) -> torch.Tensor:
 @dataclass
 class RowShard:
     """Video-token row sharding over a process group (one rank per GPU):
-    every linear, modulate and residual is row-local; attention K/V computed
-    from video rows are all-gathered (NCCL over NVLink) before the attention
-    that reads all video keys -- video self-attention and video->audio
-    cross-attention.  Audio and text rows are replicated."""
+    every linear, modulate and residual is row-local; by default the
+    attention K/V computed from video rows are all-gathered (NCCL over
+    NVLink) before the attention that reads all video keys -- video
+    self-attention and video->audio cross-attention (``self_attention`` and
+    ``v2a`` select the other exchanges).  Audio and text rows are
+    replicated."""
 
     group: object = None
     world: int = 1
@@ -506,10 +508,11 @@ class BasicAVTransformerBlock:
 
         sharded = shard is not None and shard.world > 1
         # video self-attention (transformer.py:447-471).  In a row-sharded
-        # run its Q/K/V all-to-all (head-parallel attention; an all-gather of
-        # K/V when the heads do not split evenly) overlaps the audio self- and
-        # text cross-attention, which read no video rows (same results: the
-        # two streams are independent until the audio<->video cross-attention)
+        # run its exchange -- the K/V all-gather, or with self_attention =
+        # "head_parallel" (and heads divisible by the ranks) the Q/K/V
+        # all-to-all -- overlaps the audio self- and text cross-attention,
+        # which read no video rows (same results: the two streams are
+        # independent until the audio<->video cross-attention)
         at = self.attn["attn1"]
         head_par = sharded and shard.self_attention == "head_parallel" and at.heads % shard.world == 0
         pend = None
