@@ -6,8 +6,16 @@ Host-side mirror of the reference's interfaces for the path:
   * ``ltxq.quantized_linear.QuantizedLinear`` (MLX nn.QuantizedLinear and
     loader/transformer_cache.py:177-193 _PretransposedQuantizedLinear)
   * ``ltxq.feed_forward.FeedForward`` (model/transformer/feed_forward.py)
-All compute runs in ``libltxq.so`` (hand-written CUDA for sm_100a) through
-its C ABI (include/ltxq.h); there is no CPU fallback.
+  * ``ltxq.block.BasicAVTransformerBlock`` / ``TransformerArgs``
+    (model/transformer/transformer.py), ``ltxq.block.RowShard`` (video rows
+    over several GPUs)
+  * ``ltxq.model.LTXAVModel`` (model/transformer/model.py LTXModel) and
+    ``ltxq.denoise`` / ``ltxq.perturbations`` (the AV denoise loop, sigma
+    schedules, guiders, STG perturbations of components/ and pipelines/)
+  * ``ltxq.cache`` / ``ltxq.cache_build`` (loader/transformer_cache.py)
+The block linears, modulates, gates and the denoise update run in
+``libltxq.so`` (hand-written CUDA for sm_100a) through its C ABI
+(include/ltxq.h); there is no CPU fallback.
 """
 
 from . import _lib
