@@ -1,4 +1,4 @@
-"""CPU (gloo, world size 2 and 4) checks of the multi-GPU row sharding.
+"""CPU (gloo, world size 2 to 8) checks of the multi-GPU row sharding.
 
 The block shards video tokens by rows; every per-row op stays local and the
 K/V rows that attention reads from all ranks are all-gathered
@@ -78,7 +78,7 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_row_sharded_attention_equals_unsharded(tmp_path, world):
     port = _free_port()
     mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method="spawn")

@@ -78,3 +78,25 @@ def test_timestep_embedding_and_adaln_mlp_match_the_oracle(t):
     ref_out, ref_t = od.ada_single(p, np.asarray(t, np.float32))
     assert np.allclose(out.numpy(), ref_out, rtol=1e-4, atol=1e-5)
     assert np.allclose(emb_t.numpy(), ref_t, rtol=1e-4, atol=1e-5)
+
+
+def test_v2_architecture_structure():
+    """The LTX-2.3 (V2) structure the reference's tests/test_v2_architecture.py
+    pins: 9-row AdaLN tables (6 base + 3 for the text cross-attention query),
+    2-row prompt tables for the context K/V modulation, a per-head gate
+    projection in every attention module, and no caption projection in the
+    model."""
+    from ltxq.block import AUDIO_22B, VIDEO_22B, attention_dims, linear_specs, table_specs
+    from ltxq.cache import QUANTIZED_BLOCK_LINEAR_BASES
+    from ltxq.model import model_param_specs
+
+    tabs = table_specs()
+    assert tabs["scale_shift_table"] == (9, VIDEO_22B.dim) and tabs["audio_scale_shift_table"] == (9, AUDIO_22B.dim)
+    assert tabs["prompt_scale_shift_table"] == (2, VIDEO_22B.dim)
+    assert tabs["scale_shift_table_a2v_ca_video"] == (5, VIDEO_22B.dim)
+    lin = linear_specs()
+    for name in ("attn1", "attn2", "audio_attn1", "audio_attn2", "audio_to_video_attn", "video_to_audio_attn"):
+        qd, _, heads, _ = attention_dims(name, VIDEO_22B, AUDIO_22B)
+        assert lin[f"{name}.to_gate_logits"] == (heads, qd)
+    assert sorted(lin) == sorted(QUANTIZED_BLOCK_LINEAR_BASES) and len(lin) == 34
+    assert not any("caption_projection" in k for k in model_param_specs())
