@@ -207,3 +207,29 @@ def test_head_parallel_and_split_key_attention(tmp_path, world):
         o = torch.load(os.path.join(tmp_path, f"hp{r}.pt"))
         assert torch.allclose(o["hp"], full[:, r * tl:(r + 1) * tl], atol=1e-5, rtol=1e-5)
         assert torch.allclose(o["merged"], ref_merged, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_head_parallel_layouts_with_an_emulated_all_to_all(world):
+    """heads_to_ranks -> all-to-all -> ranks_to_sequence gives each rank its
+    H/world heads over all tokens in global order, and sequence_to_ranks ->
+    all-to-all -> ranks_to_heads gives each rank back its token rows with all
+    heads; the all-to-all is emulated in process (block g of rank r's send
+    buffer becomes block r of rank g's receive buffer)."""
+    from ltxq.block import heads_to_ranks, ranks_to_heads, ranks_to_sequence, sequence_to_ranks
+
+    B, T, H, D = 2, 48, 8, 16
+    g = torch.Generator().manual_seed(world)
+    x = torch.randn(B, T, H * D, generator=g)
+    tl = T // world
+    sends = [heads_to_ranks(x[:, r * tl:(r + 1) * tl].contiguous(), world, H) for r in range(world)]
+    recvs = [torch.stack([sends[src][dst] for src in range(world)]) for dst in range(world)]
+    full = x.view(B, T, H, D).transpose(1, 2)  # (B, H, T, D)
+    hw = H // world
+    for r in range(world):
+        seq = ranks_to_sequence(recvs[r])
+        assert torch.equal(seq, full[:, r * hw:(r + 1) * hw])
+    outs = [sequence_to_ranks(full[:, r * hw:(r + 1) * hw].contiguous(), world) for r in range(world)]
+    backs = [torch.stack([outs[src][dst] for src in range(world)]) for dst in range(world)]
+    for r in range(world):
+        assert torch.equal(ranks_to_heads(backs[r]), x[:, r * tl:(r + 1) * tl])
