@@ -233,3 +233,23 @@ def test_head_parallel_layouts_with_an_emulated_all_to_all(world):
     backs = [torch.stack([outs[src][dst] for src in range(world)]) for dst in range(world)]
     for r in range(world):
         assert torch.equal(ranks_to_heads(backs[r]), x[:, r * tl:(r + 1) * tl])
+
+
+@pytest.mark.parametrize("parts", [1, 3, 8])
+def test_lse_merge_of_key_partitions(parts):
+    """merge_attention_partials over any number of key partitions (uneven
+    ones included) equals attention over all keys."""
+    from ltxq.block import merge_attention_partials
+
+    g = torch.Generator().manual_seed(parts)
+    B, H, Lq, Lk, D = 1, 4, 20, 64, 16
+    q, k, v = (torch.randn(B, H, n, D, generator=g) for n in (Lq, Lk, Lk))
+    bounds = torch.linspace(0, Lk, parts + 1).round().long().tolist()
+    outs, lses = [], []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        sc = (q @ k[:, :, a:b].transpose(-1, -2)) / D ** 0.5
+        lses.append(torch.logsumexp(sc, dim=-1))
+        outs.append(torch.softmax(sc, dim=-1) @ v[:, :, a:b])
+    merged = merge_attention_partials(torch.stack(outs), torch.stack(lses))
+    full = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    assert torch.allclose(merged, full, atol=1e-5, rtol=1e-5)
