@@ -22,7 +22,8 @@ and the MLPs run in fp32 (torch fp32 GEMMs, a few rows each).  ``patchify_proj``
 and ``proj_out`` are plain bf16 linears (cuBLAS through torch); the LayerNorm +
 modulate of the head is ``ltxq_adaln_modulate``.  RoPE tables are taken
 precomputed (``Modality.positional_embeddings``, as the reference accepts
-them); the rotary precompute itself is not part of this package.
+them) or built from ``Modality.positions`` (``ltxq.rope``, the reference's
+``_prepare_positional_embeddings`` / ``_prepare_cross_positional_embeddings``).
 """
 
 from __future__ import annotations
@@ -34,6 +35,7 @@ import torch
 import torch.nn.functional as F
 
 from . import kernels as K
+from . import rope as R
 from .block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, RowShard, StreamConfig, TransformerArgs
 
 TIMESTEP_CHANNELS = 256  # PixArtAlphaCombinedTimestepSizeEmbeddings.time_proj (timestep_embedding.py:139)
@@ -88,16 +90,19 @@ class Modality:
     """One stream's model input (the reference's ``Modality``): bf16 latent
     (B, T, 128); fp32 timesteps (B,) or per token (B, T); text context (B, L,
     C_ctx); RoPE (cos, sin) tables for self-attention and for the
-    cross-modal attention; fp32 sigma (B,) (the timesteps when None)."""
+    cross-modal attention, or None to build them from ``positions`` (fp32
+    token bounds (B, n_dims, T, 2), ``ltxq.rope.video_positions`` /
+    ``audio_positions``); fp32 sigma (B,) (the timesteps when None)."""
 
     latent: torch.Tensor
     timesteps: torch.Tensor
     context: torch.Tensor
-    positional_embeddings: tuple
-    cross_positional_embeddings: tuple
+    positional_embeddings: tuple | None = None
+    cross_positional_embeddings: tuple | None = None
     sigma: torch.Tensor | None = None
     context_mask: torch.Tensor | None = None
     enabled: bool = True
+    positions: torch.Tensor | None = None
 
 
 @dataclass
@@ -179,6 +184,7 @@ class LTXAVModel:
     timestep_scale_multiplier: float = 1000.0
     av_ca_timestep_scale_multiplier: float = 1000.0
     norm_eps: float = 1e-6
+    use_double_precision_rope: bool = False  # the checkpoint config's frequencies_precision == "float64"
     shard: RowShard | None = field(default=None, repr=False)
 
     # ------------------------------------------------------------- building
@@ -212,10 +218,41 @@ class LTXAVModel:
                   for _ in range(n_blocks)]
         return cls.from_state(blocks, random_model_state(gen, device, video, audio, w_std), video, audio, **kw)
 
+    # ------------------------------------------------------------- RoPE
+    def rope_tables(self, which: str, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Self-attention RoPE tables of the "video" or "audio" stream from
+        its token bounds (``_prepare_positional_embeddings``, model.py:232-258:
+        middle of each bound, max_pos (20, 2048, 2048) / (20,))."""
+        cfg = self.video.cfg if which == "video" else self.audio.cfg
+        max_pos = R.VIDEO_MAX_POS if which == "video" else R.AUDIO_MAX_POS
+        return R.precompute_freqs_cis(positions, cfg.dim, R.THETA, max_pos, True, cfg.heads,
+                                      self.use_double_precision_rope)
+
+    def cross_rope_tables(self, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Audio<->video cross-attention RoPE tables of a stream from the
+        temporal bounds of its tokens (``_prepare_cross_positional_embeddings``,
+        model.py:396-419): audio width and heads, max_pos (20,)."""
+        a = self.audio.cfg
+        return R.precompute_freqs_cis(positions[:, 0:1], a.dim, R.THETA, R.AUDIO_MAX_POS, True, a.heads,
+                                      self.use_double_precision_rope)
+
+    def positional_tables(self, video_positions: torch.Tensor, audio_positions: torch.Tensor):
+        """(video, audio, video cross, audio cross) tables of a stage, for
+        callers that precompute them once (``denoise_av``)."""
+        return (self.rope_tables("video", video_positions), self.rope_tables("audio", audio_positions),
+                self.cross_rope_tables(video_positions), self.cross_rope_tables(audio_positions))
+
     # ------------------------------------------------------------- forward
     def _prepare(self, s: _Stream, m: Modality, cross: Modality) -> TransformerArgs:
         """MultiModalTransformerArgsPreprocessor.prepare (model.py:454-505)."""
         b = m.latent.shape[0]
+        pe, cpe = m.positional_embeddings, m.cross_positional_embeddings
+        if pe is None or cpe is None:
+            if m.positions is None:
+                raise ValueError("Modality needs RoPE tables or positions")
+            which = "video" if s is self.video else "audio"
+            pe = pe if pe is not None else self.rope_tables(which, m.positions)
+            cpe = cpe if cpe is not None else self.cross_rope_tables(m.positions)
         d = s.cfg.dim
         x = F.linear(m.latent.to(torch.bfloat16), s.patchify_w, s.patchify_b)
         ts = m.timesteps.float()
@@ -229,9 +266,8 @@ class LTXAVModel:
         csig = csig[:, 0] if csig.dim() > 1 else csig
         cgate, _ = s.cross_gate_adaln(csig * self.av_ca_timestep_scale_multiplier)
         return TransformerArgs(x=x, context=m.context.to(torch.bfloat16), timesteps=emb.view(b, -1, 9, d),
-                               positional_embeddings=m.positional_embeddings,
-                               embedded_timestep=emb_t.view(b, -1, d),
-                               cross_positional_embeddings=m.cross_positional_embeddings,
+                               positional_embeddings=pe, embedded_timestep=emb_t.view(b, -1, d),
+                               cross_positional_embeddings=cpe,
                                cross_scale_shift_timestep=css.view(b, -1, 4, d),
                                cross_gate_timestep=cgate.view(b, -1, 1, d),
                                prompt_timestep=prompt.view(b, -1, 2, d))

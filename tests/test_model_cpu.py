@@ -100,3 +100,31 @@ def test_v2_architecture_structure():
         assert lin[f"{name}.to_gate_logits"] == (heads, qd)
     assert sorted(lin) == sorted(QUANTIZED_BLOCK_LINEAR_BASES) and len(lin) == 34
     assert not any("caption_projection" in k for k in model_param_specs())
+
+
+def test_model_rope_tables_from_positions():
+    """LTXAVModel builds the four RoPE tables of a stage from the token
+    bounds as the reference's preprocessors do: video (dim 4096, 32 heads,
+    max_pos (20, 2048, 2048)), audio and both cross tables (audio width and
+    heads, max_pos (20,), temporal bounds only)."""
+    from oracle import rope as orope
+
+    from ltxq.block import StreamConfig
+    from ltxq.model import LTXAVModel, random_model_state
+    from ltxq.rope import audio_positions, video_positions
+
+    video, audio = StreamConfig(256, 4, 64, 256), StreamConfig(128, 4, 32, 128)
+    g = torch.Generator()
+    g.manual_seed(4)
+    model = LTXAVModel.from_state([], random_model_state(g, "cpu", video, audio), video, audio,
+                                  use_double_precision_rope=True)
+    vpos, apos = video_positions(1, 2, 3, 4, 24.0), audio_positions(1, 9)
+    (vc, vs), (ac, as_), (vcc, vcs), (acc, acs) = model.positional_tables(vpos, apos)
+    refs = [orope.precompute_freqs_cis(vpos.numpy(), 256, 10000.0, [20, 2048, 2048], True, 4, True),
+            orope.precompute_freqs_cis(apos.numpy(), 128, 10000.0, [20], True, 4, True),
+            orope.precompute_freqs_cis(vpos[:, 0:1].numpy(), 128, 10000.0, [20], True, 4, True),
+            orope.precompute_freqs_cis(apos.numpy(), 128, 10000.0, [20], True, 4, True)]
+    for (c, s), (rc, rs) in zip(((vc, vs), (ac, as_), (vcc, vcs), (acc, acs)), refs):
+        assert c.shape == rc.shape
+        assert np.max(np.abs(c.numpy() - rc)) <= 1e-6 and np.max(np.abs(s.numpy() - rs)) <= 1e-6
+    assert vc.shape == (1, 4, 24, 32) and vcc.shape == (1, 4, 24, 16) and ac.shape == (1, 4, 9, 16)
