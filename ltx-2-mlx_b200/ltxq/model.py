@@ -245,7 +245,7 @@ class LTXAVModel:
     # ------------------------------------------------------------- forward
     def _prepare(self, s: _Stream, m: Modality, cross: Modality) -> TransformerArgs:
         """MultiModalTransformerArgsPreprocessor.prepare (model.py:454-505)."""
-        if m.context_mask is not None:  # the reference's pipelines pass None (pipelines/common.py:240-242)
+        if m.context_mask is not None:  # the reference's pipelines pass None (pipelines/common.py:242-249, 285-292)
             raise ValueError("text-context attention masks are not supported")
         if not m.enabled:
             raise ValueError("both streams run in every call: a disabled modality is not supported")
