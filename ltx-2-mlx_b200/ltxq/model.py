@@ -313,3 +313,24 @@ def random_model_state(gen: torch.Generator, device, video: StreamConfig = VIDEO
         else:
             out[key] = (t * w_std).to(torch.bfloat16)
     return out
+
+
+class X0Model:
+    """X0Model (model.py:1489-1540): the denoised predictions
+    ``latent - timesteps * velocity`` (fp32, as the reference's bf16 latent
+    and fp32 timesteps promote) instead of the velocities.  The denoise loop
+    (``ltxq.denoise.denoise_av``) fuses this step into ``ltxq_denoise_update``;
+    this wrapper serves callers that want the reference's interface."""
+
+    def __init__(self, velocity_model):
+        self.velocity_model = velocity_model
+
+    @staticmethod
+    def denoise(m: Modality, velocity: torch.Tensor) -> torch.Tensor:
+        t = m.timesteps.float()
+        t = t[:, None, None] if t.dim() == 1 else t[:, :, None]
+        return m.latent - t * velocity
+
+    def __call__(self, video: Modality, audio: Modality, shard: RowShard | None = None, perturbations=None):
+        vv, av = self.velocity_model(video, audio, shard, perturbations)
+        return self.denoise(video, vv), self.denoise(audio, av)

@@ -128,3 +128,28 @@ def test_model_rope_tables_from_positions():
         assert c.shape == rc.shape
         assert np.max(np.abs(c.numpy() - rc)) <= 1e-6 and np.max(np.abs(s.numpy() - rs)) <= 1e-6
     assert vc.shape == (1, 4, 24, 32) and vcc.shape == (1, 4, 24, 16) and ac.shape == (1, 4, 9, 16)
+
+
+def test_x0_model_matches_the_oracle_x0():
+    """X0Model.denoise: bf16 latent - fp32 timesteps * bf16 velocity in fp32,
+    uniform (B,) and per-token (B, T) timesteps."""
+    from helpers import normal_bf16, rng
+    from ltxq.model import Modality, X0Model
+
+    g = rng(9)
+    lat, vel = normal_bf16(g, (2, 6, 8)), normal_bf16(g, (2, 6, 8))
+    to_t = lambda a: torch.from_numpy(a).to(torch.bfloat16)  # noqa: E731
+    calls = []
+
+    def velocity_model(video, audio, shard, perturbations):
+        calls.append(perturbations)
+        return to_t(vel), to_t(vel)
+
+    x0 = X0Model(velocity_model)
+    for ts in (np.array([0.725, 0.5], np.float32), np.array([[0.725] * 6, [0.0] * 3 + [0.5] * 3], np.float32)):
+        m = Modality(to_t(lat), torch.from_numpy(ts), None)
+        dv, da = x0(m, m, perturbations="ptb")
+        t = ts[:, None, None] if ts.ndim == 1 else ts[:, :, None]
+        ref = (lat - (t * vel).astype(np.float32)).astype(np.float32)
+        assert dv.dtype == torch.float32 and np.array_equal(dv.numpy(), ref) and np.array_equal(da.numpy(), ref)
+    assert calls == ["ptb", "ptb"]
