@@ -79,9 +79,46 @@ def sigma_schedule(num_steps: int, distilled: bool = False, tokens: int | None =
 
 @dataclass(frozen=True)
 class CFGGuider:
-    """Classifier-free guidance: cond + (scale - 1) * (cond - uncond)."""
+    """Classifier-free guidance: cond + (scale - 1) * (cond - uncond)
+    (guiders.py:9-32).  ``guide`` works on denoised predictions (fp32 from
+    ``X0Model``); ``denoise_av`` applies the same arithmetic inside
+    ``ltxq_denoise_update``."""
 
     scale: float
+
+    def delta(self, cond: torch.Tensor, uncond: torch.Tensor) -> torch.Tensor:
+        return (self.scale - 1) * (cond - uncond)
+
+    def guide(self, cond: torch.Tensor, uncond: torch.Tensor) -> torch.Tensor:
+        return cond + self.delta(cond, uncond)
+
+    def enabled(self) -> bool:
+        return self.scale != 1.0
+
+
+def projection_coef(to_project: torch.Tensor, project_onto: torch.Tensor) -> torch.Tensor:
+    """Per-sample <a, b> / (|b|^2 + 1e-8), shape (B, 1) (guiders.py:175-192)."""
+    b = to_project.shape[0]
+    a, o = to_project.reshape(b, -1), project_onto.reshape(b, -1)
+    return (a * o).sum(dim=1, keepdim=True) / ((o * o).sum(dim=1, keepdim=True) + 1e-8)
+
+
+@dataclass(frozen=True)
+class CFGStarRescalingGuider:
+    """CFG with the unconditioned prediction rescaled onto the conditioned
+    one (guiders.py:35-62): cond + (scale - 1) * (cond - coef * uncond).
+    The per-sample coefficient is a reduction over the whole latent, so the
+    fused update does not apply it; call ``guide`` on denoised predictions."""
+
+    scale: float
+
+    def delta(self, cond: torch.Tensor, uncond: torch.Tensor) -> torch.Tensor:
+        coef = projection_coef(cond, uncond)
+        coef = coef.view((coef.shape[0],) + (1,) * (uncond.dim() - 1))
+        return (self.scale - 1) * (cond - coef * uncond)
+
+    def guide(self, cond: torch.Tensor, uncond: torch.Tensor) -> torch.Tensor:
+        return cond + self.delta(cond, uncond)
 
     def enabled(self) -> bool:
         return self.scale != 1.0
@@ -89,9 +126,16 @@ class CFGGuider:
 
 @dataclass(frozen=True)
 class STGGuider:
-    """Spatio-temporal guidance: pos + scale * (pos - perturbed)."""
+    """Spatio-temporal guidance: pos + scale * (pos - perturbed)
+    (guiders.py:65-91)."""
 
     scale: float
+
+    def delta(self, pos_denoised: torch.Tensor, perturbed_denoised: torch.Tensor) -> torch.Tensor:
+        return self.scale * (pos_denoised - perturbed_denoised)
+
+    def guide(self, pos_denoised: torch.Tensor, perturbed_denoised: torch.Tensor) -> torch.Tensor:
+        return pos_denoised + self.delta(pos_denoised, perturbed_denoised)
 
     def enabled(self) -> bool:
         return self.scale != 0.0
@@ -188,6 +232,11 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
     shard, ``video`` holds this rank's rows."""
     from .model import Modality
 
+    for gd in (video_guider, audio_guider):
+        if type(gd) is not CFGGuider:  # the fused update applies plain CFG only
+            raise ValueError(f"denoise_av takes CFGGuider guiders, got {type(gd).__name__}")
+    if stg_guider is not None and type(stg_guider) is not STGGuider:
+        raise ValueError(f"denoise_av takes an STGGuider, got {type(stg_guider).__name__}")
     sig = np.asarray(sigmas, dtype=np.float32)
     steps = len(sig) - 1
     need_cfg = video_guider.enabled() or audio_guider.enabled()

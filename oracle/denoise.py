@@ -238,3 +238,25 @@ def denoise_loop_av(model_fn, video_latent, audio_latent, sigmas, cfg_video: flo
                                       v_perturbed=vp, stg_scale=stg_scale if stg else 0.0)[0]
         audio_latent = denoise_update(audio_latent, ac, s, sn, v_uncond=au, cfg_scale=cfg_audio if need_cfg else 1.0)[0]
     return video_latent, audio_latent
+
+
+def cfg_guide(cond, uncond, scale: float):
+    """CFGGuider.guide (guiders.py:24-29), fp32."""
+    c, u = np.asarray(cond, F32), np.asarray(uncond, F32)
+    return (c + (F32(scale - 1) * (c - u).astype(F32)).astype(F32)).astype(F32)
+
+
+def stg_guide(pos, perturbed, scale: float):
+    """STGGuider.guide (guiders.py:79-83), fp32."""
+    p, q = np.asarray(pos, F32), np.asarray(perturbed, F32)
+    return (p + (F32(scale) * (p - q).astype(F32)).astype(F32)).astype(F32)
+
+
+def cfg_star_guide(cond, uncond, scale: float):
+    """CFGStarRescalingGuider.guide (guiders.py:35-62, projection_coef
+    :175-192): the per-sample coefficient in float64, the rest fp32."""
+    c, u = np.asarray(cond, F32), np.asarray(uncond, F32)
+    b = c.shape[0]
+    cf, uf = c.reshape(b, -1).astype(np.float64), u.reshape(b, -1).astype(np.float64)
+    coef = ((cf * uf).sum(1) / ((uf * uf).sum(1) + 1e-8)).astype(F32).reshape((b,) + (1,) * (c.ndim - 1))
+    return (c + (F32(scale - 1) * (c - (coef * u).astype(F32)).astype(F32)).astype(F32)).astype(F32)

@@ -126,3 +126,42 @@ def test_perturbation_config():
     assert not mixed.all_in_batch(PerturbationType.SKIP_V2A_CROSS_ATTN, 0) and mixed.skipped(0) == frozenset()
     assert BatchedPerturbationConfig.empty(3).skipped(0) == frozenset()
     assert not create_batched_stg_config(1, skip_video_self_attn=False).skipped(0)
+
+
+def test_guiders_match_the_oracle():
+    """CFGGuider / STGGuider.guide on fp32 denoised predictions bit for bit
+    (elementwise fp32), CFGStarRescalingGuider within the accumulation order
+    of its per-sample reduction."""
+    import torch
+
+    from ltxq.denoise import CFGGuider, CFGStarRescalingGuider, STGGuider
+
+    g = rng(11)
+    c, u, p = (g.standard_normal((2, 40, 16)).astype(np.float32) for _ in range(3))
+    tc, tu, tp = (torch.from_numpy(a) for a in (c, u, p))
+    assert np.array_equal(CFGGuider(3.5).guide(tc, tu).numpy(), od.cfg_guide(c, u, 3.5))
+    assert np.array_equal(STGGuider(1.25).guide(tc, tp).numpy(), od.stg_guide(c, p, 1.25))
+    got = CFGStarRescalingGuider(4.0).guide(tc, tu).numpy()
+    assert np.allclose(got, od.cfg_star_guide(c, u, 4.0), rtol=1e-5, atol=1e-5)
+    assert CFGGuider(1.0).enabled() is False and STGGuider(0.0).enabled() is False
+    assert np.array_equal(CFGGuider(1.0).guide(tc, tu).numpy(), c)  # scale 1: the conditioned prediction
+
+
+def test_cfg_guide_is_the_fused_update_arithmetic():
+    """The fused step's CFG (oracle denoise_update) equals CFGGuider.guide on
+    the X0 predictions followed by the Euler step."""
+    x, v, u, _ = _inputs((1, 20, 16), 12)
+    s, sn = 0.975, 0.909375
+    got, _ = od.denoise_update(x, v, s, sn, v_uncond=u, cfg_scale=2.5)
+    d = od.cfg_guide(od._x0(x, np.float32(s), v), od._x0(x, np.float32(s), u), 2.5)
+    r = np.float32(sn / s)
+    ref = rbf16((d + (r * (x - d).astype(np.float32)).astype(np.float32)).astype(np.float32))
+    assert np.array_equal(got, ref)
+
+
+def test_denoise_av_rejects_guiders_the_fused_update_cannot_apply():
+    from ltxq.denoise import CFGGuider, CFGStarRescalingGuider, LatentState, denoise_av
+
+    with pytest.raises(ValueError):
+        denoise_av(None, LatentState(None), LatentState(None), [1.0, 0.0], None, None, None, None, None, None,
+                   video_guider=CFGStarRescalingGuider(3.0), audio_guider=CFGGuider(1.0))
