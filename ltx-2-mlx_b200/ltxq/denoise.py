@@ -77,6 +77,48 @@ def sigma_schedule(num_steps: int, distilled: bool = False, tokens: int | None =
     return ltx2_scheduler(num_steps, tokens)
 
 
+def to_velocity(sample: torch.Tensor, sigma, denoised: torch.Tensor) -> torch.Tensor:
+    """(sample - denoised) / sigma in fp32 (core_utils.py:25-52)."""
+    if not isinstance(sigma, torch.Tensor) and sigma == 0:
+        raise ValueError("Sigma can't be 0.0")
+    s = sigma.float() if isinstance(sigma, torch.Tensor) else sigma
+    return (sample.float() - denoised.float()) / s
+
+
+class EulerDiffusionStep:
+    """EulerDiffusionStep.step (diffusion_steps.py:8-70): denoised + (sigma_next
+    / sigma) (sample - denoised) in fp32, cast to the sample's dtype.  The
+    denoise loop applies it inside ``ltxq_denoise_update``; this class serves
+    callers holding denoised predictions."""
+
+    def step(self, sample: torch.Tensor, denoised_sample: torch.Tensor, sigmas, step_index: int, *,
+             sigma: float | None = None, sigma_next: float | None = None) -> torch.Tensor:
+        sigma = float(sigmas[step_index]) if sigma is None else sigma
+        sigma_next = float(sigmas[step_index + 1]) if sigma_next is None else sigma_next
+        d = denoised_sample.float()
+        out = d + (sigma_next / sigma) * (sample.float() - d)
+        return out if sample.dtype == torch.float32 else out.to(sample.dtype)
+
+
+class HeunDiffusionStep:
+    """HeunDiffusionStep.step (diffusion_steps.py:73-130): the Euler
+    predictor, and with the denoised prediction at the predicted point the
+    average of the two velocities."""
+
+    def step(self, sample: torch.Tensor, denoised_sample: torch.Tensor, sigmas, step_index: int,
+             denoised_at_predicted: torch.Tensor | None = None) -> torch.Tensor:
+        sig = torch.as_tensor(np.asarray(sigmas, dtype=np.float32))
+        s, sn = sig[step_index], sig[step_index + 1]
+        dt = float(sn - s)
+        velocity = to_velocity(sample, s, denoised_sample)
+        predicted = sample.float() + velocity * dt
+        if denoised_at_predicted is None:
+            return predicted.to(sample.dtype)
+        v2 = to_velocity(predicted.to(sample.dtype), sn, denoised_at_predicted)
+        avg = 0.5 * (velocity + v2.float())
+        return (sample.float() + avg * dt).to(sample.dtype)
+
+
 @dataclass(frozen=True)
 class CFGGuider:
     """Classifier-free guidance: cond + (scale - 1) * (cond - uncond)

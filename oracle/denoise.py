@@ -260,3 +260,27 @@ def cfg_star_guide(cond, uncond, scale: float):
     cf, uf = c.reshape(b, -1).astype(np.float64), u.reshape(b, -1).astype(np.float64)
     coef = ((cf * uf).sum(1) / ((uf * uf).sum(1) + 1e-8)).astype(F32).reshape((b,) + (1,) * (c.ndim - 1))
     return (c + (F32(scale - 1) * (c - (coef * u).astype(F32)).astype(F32)).astype(F32)).astype(F32)
+
+
+def euler_step(sample, denoised, sigma: float, sigma_next: float):
+    """EulerDiffusionStep.step (diffusion_steps.py:19-70) for a bf16 sample:
+    bf16(d + fp32(sigma_next / sigma) (x - d))."""
+    x, d = np.asarray(sample, F32), np.asarray(denoised, F32)
+    r = F32(float(sigma_next) / float(sigma))
+    return rbf16((d + (r * (x - d).astype(F32)).astype(F32)).astype(F32))
+
+
+def heun_step(sample, denoised, sigma: float, sigma_next: float, denoised_at_predicted=None):
+    """HeunDiffusionStep.step (diffusion_steps.py:73-130) for a bf16 sample,
+    fp32 sigmas: Euler predictor; with the second prediction, the average of
+    the two velocities."""
+    x, d = np.asarray(sample, F32), np.asarray(denoised, F32)
+    s, sn = F32(sigma), F32(sigma_next)
+    dt = F32(sn - s)
+    v1 = ((x - d).astype(F32) / s).astype(F32)
+    pred = (x + (v1 * dt).astype(F32)).astype(F32)
+    if denoised_at_predicted is None:
+        return rbf16(pred)
+    v2 = ((rbf16(pred) - np.asarray(denoised_at_predicted, F32)).astype(F32) / sn).astype(F32)
+    avg = (F32(0.5) * (v1 + v2).astype(F32)).astype(F32)
+    return rbf16((x + (avg * dt).astype(F32)).astype(F32))
