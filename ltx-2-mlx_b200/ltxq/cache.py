@@ -20,9 +20,15 @@ Format (LTX_2_MLX/loader/transformer_cache.py):
 * in the ``mxfp8-blocks-pretranspose`` mode the quantized arrays are those
   of W^T (:1240-1244);
 * ``metadata.json`` beside the cache holds the build payload
-  (``_cache_payload`` :453-524): ``schema_version``,
-  ``transformer_cache_quantize`` and, when overridden,
-  ``transformer_cache_quantize_group_size`` / ``_bits``.
+  (``_cache_payload`` :453-524): ``schema_version``, the source checkpoint's
+  signature (resolved path, size, mtime in ns), ``include_audio``, the
+  layout specs, ``transformer_cache_quantize`` and, when overridden,
+  ``transformer_cache_quantize_group_size`` / ``_bits``, and
+  ``fp8_dequant_policy`` for FP8 checkpoints.  A cache is valid when that
+  file equals the payload expected for the current settings
+  (``_metadata_matches`` :979-985); its directory is
+  ``<root>/<checkpoint stem>-<first 20 hex digits of the payload's SHA-256>``
+  (``transformer_cache_paths`` :711-758, ``_payload_digest`` :542-544).
 
 safetensors itself is the public format (8-byte little-endian header length,
 a JSON header mapping names to dtype / shape / byte range plus an optional
@@ -33,6 +39,7 @@ for headers), zero-copy through ``numpy.memmap``.
 
 from __future__ import annotations
 
+import hashlib
 import json
 import os
 import re
@@ -209,6 +216,80 @@ def write_cache_weights(cache_file, tensors: dict[str, torch.Tensor],
         paths.append(cache_shard_path(cache_file, len(paths)))
         save_safetensors(paths[-1], cur)
     return paths
+
+
+def default_cache_root() -> Path:
+    """default_transformer_cache_root (transformer_cache.py:359-372):
+    $LTX_MLX_WEIGHTS_CACHE_DIR, else $LTX_MLX_TRANSFORMER_CACHE_DIR, else
+    ~/.cache/ltx-2-mlx/weights-cache."""
+    env = os.environ.get("LTX_MLX_WEIGHTS_CACHE_DIR") or os.environ.get("LTX_MLX_TRANSFORMER_CACHE_DIR")
+    return Path(env).expanduser() if env else Path.home() / ".cache" / "ltx-2-mlx" / "weights-cache"
+
+
+def file_signature(path) -> dict:
+    """The source signature of a payload (transformer_cache.py:375-382)."""
+    resolved = Path(path).expanduser().resolve()
+    st = resolved.stat()
+    return {"path": str(resolved), "size": st.st_size, "mtime_ns": st.st_mtime_ns}
+
+
+def payload_digest(payload: dict) -> str:
+    """First 20 hex digits of the SHA-256 of the compact, key-sorted JSON."""
+    encoded = json.dumps(payload, sort_keys=True, separators=(",", ":")).encode("utf-8")
+    return hashlib.sha256(encoded).hexdigest()[:20]
+
+
+def safe_stem(path) -> str:
+    stem = Path(path).stem
+    safe = "".join(ch if ch.isalnum() or ch in ("-", "_", ".") else "_" for ch in stem)
+    return safe[:80] or "transformer"
+
+
+def transformer_cache_payload(weights_path, include_audio: bool = True,
+                              transformer_cache_quantize: str = QUANTIZE_OFF, group_size: int | None = None,
+                              bits: int | None = None) -> dict:
+    """The payload the reference expects for a cache of ``weights_path``
+    built with these settings and no layout or FF-quantization overrides
+    (``_cache_payload``, transformer_cache.py:453-524)."""
+    if transformer_cache_quantize not in (QUANTIZE_OFF, QUANTIZE_MXFP8_BLOCKS, QUANTIZE_MXFP8_BLOCKS_PRETRANSPOSE):
+        raise ValueError(f"Unsupported transformer cache quantization mode: {transformer_cache_quantize}")
+    payload = {"schema_version": CACHE_SCHEMA_VERSION, "source": file_signature(weights_path),
+               "include_audio": include_audio, "video_ff_layout_specs": [], "video_ff_layout_layers": [],
+               "video_attn_layout_specs": [], "video_attn_layout_layers": []}
+    if transformer_cache_quantize != QUANTIZE_OFF:
+        payload["transformer_cache_quantize"] = transformer_cache_quantize
+        if group_size is not None:
+            payload["transformer_cache_quantize_group_size"] = group_size
+        if bits is not None:
+            payload["transformer_cache_quantize_bits"] = bits
+    try:
+        if any(d in ("F8_E4M3", "F8_E5M2") for d in read_safetensors_dtypes(weights_path).values()):
+            payload["fp8_dequant_policy"] = 2
+    except Exception:  # an unreadable source fails later, in the build, with its own error
+        pass
+    return payload
+
+
+def transformer_cache_paths(weights_path, cache_root=None, **settings) -> tuple[Path, Path, dict]:
+    """(cache file, metadata file, expected payload) where the reference
+    keeps the cache of ``weights_path`` for ``settings`` (the keyword
+    arguments of ``transformer_cache_payload``)."""
+    payload = transformer_cache_payload(weights_path, **settings)
+    root = Path(cache_root).expanduser() if cache_root else default_cache_root()
+    d = root / f"{safe_stem(weights_path)}-{payload_digest(payload)}"
+    return d / "transformer.safetensors", d / "metadata.json", payload
+
+
+def cache_is_valid(cache_file, expected_payload: dict) -> bool:
+    """The cache exists (single file or shards) and its metadata equals the
+    expected payload (``_cache_artifacts_exist`` / ``_metadata_matches``)."""
+    cache_file = Path(cache_file)
+    if not cache_file.parent.is_dir() or not (cache_file.exists() or existing_cache_shards(cache_file)):
+        return False
+    try:
+        return json.loads((cache_file.parent / "metadata.json").read_text()) == expected_payload
+    except (OSError, json.JSONDecodeError):
+        return False
 
 
 def cache_payload(transformer_cache_quantize: str = QUANTIZE_OFF, group_size: int | None = None,

@@ -19,7 +19,10 @@ Restates the checkpoint side of LTX_2_MLX/loader:
   ``__quant__.transformer_blocks.{i}.{base}.{weight,scales[,biases]}``; the
   ``mxfp8-blocks-pretranspose`` mode quantizes W^T.  Other tensors keep their
   key and dtype.  The cache is sharded at 4 GiB and ``metadata.json`` holds
-  the payload.
+  the payload the reference expects for the same checkpoint and settings
+  (``_cache_payload`` :453-524), so the reference accepts the cache as
+  valid; ``ensure_transformer_cache`` (:1749-1812) reuses a valid cache or
+  builds one in the digest-named directory the reference uses.
 
 Beyond the reference's modes (off, mxfp8-blocks, mxfp8-blocks-pretranspose),
 ``affine=(bits, group_size)`` quantizes the block linears with MLX affine
@@ -102,7 +105,8 @@ def build_transformer_cache(checkpoint, cache_file, mode: str = C.QUANTIZE_MXFP8
     """Write the cache of ``checkpoint`` (a safetensors file with
     ``model.diffusion_model.`` keys) beside ``cache_file``; returns the
     metadata payload.  ``affine=(bits, group_size)`` quantizes the block
-    linears affine instead of mxfp8."""
+    linears affine instead of mxfp8 (no reference mode: the payload adds
+    ``block_linear_quantize`` keys)."""
     from .quantized_linear import QuantizedLinear
 
     if affine is not None and mode != C.QUANTIZE_OFF:
@@ -131,11 +135,29 @@ def build_transformer_cache(checkpoint, cache_file, mode: str = C.QUANTIZE_MXFP8
         entries[f"{q}.scales"] = ql.scales
         if ql.biases is not None:
             entries[f"{q}.biases"] = ql.biases
+    payload = C.transformer_cache_payload(checkpoint, include_audio=include_audio,
+                                          transformer_cache_quantize=C.QUANTIZE_OFF if affine else mode)
     if affine is not None:
-        payload = C.cache_payload(C.QUANTIZE_OFF, block_linear_quantize="affine", block_linear_quantize_bits=affine[0],
-                                  block_linear_quantize_group_size=affine[1])
-    else:
-        payload = C.cache_payload(mode)
+        payload.update(block_linear_quantize="affine", block_linear_quantize_bits=affine[0],
+                       block_linear_quantize_group_size=affine[1])
     C.write_cache_weights(cache_file, entries, shard_limit_bytes)
     C.write_metadata(Path(cache_file).parent, payload)
     return payload
+
+
+def ensure_transformer_cache(checkpoint, cache_root=None, mode: str = C.QUANTIZE_MXFP8_BLOCKS,
+                             include_audio: bool = True, rebuild: bool = False, device="cuda",
+                             shard_limit_bytes: int = C.SHARD_LIMIT_BYTES) -> Path:
+    """The cache file of ``checkpoint`` for these settings: reused when its
+    metadata matches the expected payload (the reference's cache_mode
+    "auto"), else (or with ``rebuild``) built where the reference looks for
+    it.  Returns the cache file path (single file or shard base name)."""
+    cache_file, _, payload = C.transformer_cache_paths(checkpoint, cache_root, include_audio=include_audio,
+                                                       transformer_cache_quantize=mode)
+    if not rebuild and C.cache_is_valid(cache_file, payload):
+        return cache_file
+    got = build_transformer_cache(checkpoint, cache_file, mode=mode, include_audio=include_audio, device=device,
+                                  shard_limit_bytes=shard_limit_bytes)
+    if got != payload:  # the checkpoint changed while the cache was being built
+        raise RuntimeError(f"{checkpoint} changed during the cache build")
+    return cache_file

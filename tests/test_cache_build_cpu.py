@@ -64,3 +64,90 @@ def test_e5m2_rejected(tmp_path):
     p.write_bytes(struct.pack("<Q", len(hb)) + hb + raw[8 + n:])
     with pytest.raises(ValueError, match="E5M2"):
         list(B.iter_checkpoint_weights(p))
+
+
+def _tiny_checkpoint(path, fp8=False):
+    import torch
+
+    from ltxq import cache as C
+
+    t = {"model.diffusion_model.transformer_blocks.0.scale_shift_table": torch.zeros(9, 8),
+         "model.diffusion_model.patchify_proj.weight": torch.ones(8, 4, dtype=torch.bfloat16)}
+    if fp8:
+        t["model.diffusion_model.proj_out.weight"] = torch.zeros(4, 8, dtype=torch.float8_e4m3fn)
+    C.save_safetensors(path, t)
+    return path
+
+
+def test_transformer_cache_payload_matches_the_reference_fields(tmp_path):
+    """_cache_payload (transformer_cache.py:453-524) for the default layouts:
+    schema, source signature, include_audio, empty layout specs, the
+    quantization fields only when set (tests/test_transformer_cache.py:98-115
+    of the reference: group sizes change the payload and its digest), and
+    the FP8 dequant policy for FP8 checkpoints."""
+    import os
+
+    from ltxq import cache as C
+
+    ck = _tiny_checkpoint(tmp_path / "ckpt.safetensors")
+    p = C.transformer_cache_payload(ck, include_audio=False)
+    st = os.stat(ck)
+    assert p == {"schema_version": 1, "source": {"path": str(ck.resolve()), "size": st.st_size,
+                                                 "mtime_ns": st.st_mtime_ns},
+                 "include_audio": False, "video_ff_layout_specs": [], "video_ff_layout_layers": [],
+                 "video_attn_layout_specs": [], "video_attn_layout_layers": []}
+    a = C.transformer_cache_payload(ck, transformer_cache_quantize="mxfp8-blocks", group_size=32)
+    b = C.transformer_cache_payload(ck, transformer_cache_quantize="mxfp8-blocks", group_size=64)
+    assert a["transformer_cache_quantize_group_size"] == 32 and b["transformer_cache_quantize_group_size"] == 64
+    assert a != b and C.payload_digest(a) != C.payload_digest(b)
+    assert "fp8_dequant_policy" not in a
+    f8 = _tiny_checkpoint(tmp_path / "f8.safetensors", fp8=True)
+    assert C.transformer_cache_payload(f8)["fp8_dequant_policy"] == 2
+    with pytest.raises(ValueError):
+        C.transformer_cache_payload(ck, transformer_cache_quantize="int4")
+
+
+def test_cache_paths_and_digest(tmp_path, monkeypatch):
+    import hashlib
+
+    from ltxq import cache as C
+
+    assert C.payload_digest({"b": [], "a": 1}) == hashlib.sha256(b'{"a":1,"b":[]}').hexdigest()[:20]
+    assert C.safe_stem("/x/LTX 2.3 (22b).safetensors") == "LTX_2.3__22b_"
+    ck = _tiny_checkpoint(tmp_path / "ckpt.safetensors")
+    monkeypatch.setenv("LTX_MLX_WEIGHTS_CACHE_DIR", str(tmp_path / "root"))
+    f, meta, payload = C.transformer_cache_paths(ck, transformer_cache_quantize="mxfp8-blocks")
+    assert f.parent == tmp_path / "root" / f"ckpt-{C.payload_digest(payload)}"
+    assert f.name == "transformer.safetensors" and meta == f.parent / "metadata.json"
+    monkeypatch.delenv("LTX_MLX_WEIGHTS_CACHE_DIR")
+    monkeypatch.setenv("LTX_MLX_TRANSFORMER_CACHE_DIR", str(tmp_path / "legacy"))
+    assert C.default_cache_root() == tmp_path / "legacy"
+
+
+def test_ensure_transformer_cache_builds_reuses_and_follows_the_source(tmp_path):
+    """mode "off" needs no GPU: the first call builds (metadata = the
+    expected payload), the second reuses, a changed checkpoint gets a new
+    digest directory."""
+    import os
+    import time
+
+    from ltxq import cache as C
+    from ltxq import cache_build as CB
+
+    ck = _tiny_checkpoint(tmp_path / "ckpt.safetensors")
+    root = tmp_path / "root"
+    f1 = CB.ensure_transformer_cache(ck, root, mode="off", device="cpu")
+    _, _, payload = C.transformer_cache_paths(ck, root, transformer_cache_quantize="off")
+    assert C.cache_is_valid(f1, payload)
+    assert C.read_metadata(f1.parent) == payload
+    w = C.load_cache_weights(f1)
+    assert set(w) == {"transformer_blocks.0.scale_shift_table", "patchify_proj.weight"}
+    shard = C.existing_cache_shards(f1)[0]
+    mtime = shard.stat().st_mtime_ns
+    assert CB.ensure_transformer_cache(ck, root, mode="off", device="cpu") == f1
+    assert shard.stat().st_mtime_ns == mtime  # reused, not rebuilt
+    time.sleep(0.01)
+    os.utime(ck)  # a new source signature
+    f2 = CB.ensure_transformer_cache(ck, root, mode="off", device="cpu")
+    assert f2.parent != f1.parent and C.cache_is_valid(f2, C.transformer_cache_paths(ck, root)[2])
+    assert not C.cache_is_valid(f1, C.transformer_cache_paths(ck, root)[2])
