@@ -284,3 +284,43 @@ def heun_step(sample, denoised, sigma: float, sigma_next: float, denoised_at_pre
     v2 = ((rbf16(pred) - np.asarray(denoised_at_predicted, F32)).astype(F32) / sn).astype(F32)
     avg = (F32(0.5) * (v1 + v2).astype(F32)).astype(F32)
     return rbf16((x + (avg * dt).astype(F32)).astype(F32))
+
+
+def denoise_loop_av_general(model_fn, video_latent, audio_latent, sigmas, cfg_video: float = 1.0,
+                            cfg_audio: float = 1.0, stg_scale: float = 0.0, stg_cutoff: float = 1.0,
+                            ge_gamma: float = 0.0, video_mask=None, video_clean=None, audio_mask=None,
+                            audio_clean=None):
+    """_denoise_loop_cfg_av (av_pipeline.py:625-756) with every option:
+    ``model_fn(video_latent, audio_latent, video_timesteps, audio_timesteps,
+    pass_)`` -> velocities, timesteps fp32 (B,) or per token (B, T) (mask *
+    sigma, pipelines/common.py:194-250); gradient estimation on the video
+    stream; masks blend the clean latents back (common.py:169-191)."""
+    need_cfg = cfg_video != 1.0 or cfg_audio != 1.0
+    sig = np.asarray(sigmas, dtype=F32)
+    steps = len(sig) - 1
+    b = np.asarray(video_latent).shape[0]
+    prev = None
+
+    def ts(mask, s):
+        full = np.full((b,), F32(s), F32)
+        return full if mask is None else (np.asarray(mask, F32) * F32(s)).astype(F32)
+
+    for i in range(steps):
+        s, sn = float(sig[i]), float(sig[i + 1])
+        vt, at = ts(video_mask, s), ts(audio_mask, s)
+        vc, ac = model_fn(video_latent, audio_latent, vt, at, "positive")
+        vu = au = vp = None
+        if need_cfg:
+            vu, au = model_fn(video_latent, audio_latent, vt, at, "negative")
+        stg = stg_scale != 0.0 and (i + 1) / steps <= stg_cutoff
+        if stg:
+            vp, _ = model_fn(video_latent, audio_latent, vt, at, "perturbed")
+        new_v, cur = denoise_update(video_latent, vc, s, sn, v_uncond=vu, cfg_scale=cfg_video if need_cfg else 1.0,
+                                    v_perturbed=vp, stg_scale=stg_scale if stg else 0.0, denoise_mask=video_mask,
+                                    clean_latent=video_clean, prev_velocity=prev, ge_gamma=ge_gamma)
+        if ge_gamma > 0:
+            prev = cur
+        audio_latent = denoise_update(audio_latent, ac, s, sn, v_uncond=au, cfg_scale=cfg_audio if need_cfg else 1.0,
+                                      denoise_mask=audio_mask, clean_latent=audio_clean)[0]
+        video_latent = new_v
+    return video_latent, audio_latent
