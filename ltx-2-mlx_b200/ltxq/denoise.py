@@ -362,3 +362,98 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
         if gr is not None:
             gr.release()
     return video, audio
+
+
+def post_process_latent(denoised: torch.Tensor, denoise_mask: torch.Tensor | None,
+                        clean_latent: torch.Tensor | None) -> torch.Tensor:
+    """denoised * mask + clean * (1 - mask) (pipelines/common.py:169-191);
+    a None mask is the all-ones mask."""
+    if denoise_mask is None:
+        return denoised
+    m = denoise_mask.to(denoised.dtype)
+    m = m[..., None] if m.dim() == denoised.dim() - 1 else m
+    return denoised * m + clean_latent * (1 - m)
+
+
+def denoise_heun_av(model, video: LatentState, audio: LatentState, sigmas, video_context: torch.Tensor,
+                    audio_context: torch.Tensor, video_pe: tuple, audio_pe: tuple, video_cross_pe: tuple,
+                    audio_cross_pe: tuple, negative_video_context: torch.Tensor | None = None,
+                    negative_audio_context: torch.Tensor | None = None, video_guider=CFGGuider(1.0),
+                    audio_guider=CFGGuider(1.0), ge_gamma: float = 0.0, stg_guider: STGGuider | None = None,
+                    stg_perturbations=None, stg_cutoff: float = 1.0, shard=None,
+                    callback=None) -> tuple[LatentState, LatentState]:
+    """``_denoise_loop_heun_av`` (av_pipeline.py:758-897): per step the
+    guided X0 at the current point (CFG -- plain or ``CFGStarRescalingGuider``
+    -- STG, gradient estimation, mask blend), the Euler predictor, the guided
+    X0 at the predicted point (CFG, mask blend) and the Heun corrector
+    (``HeunDiffusionStep``).  The positive and negative passes of each point
+    run as one batch-2B transformer pass; the step arithmetic is fp32 torch
+    (X0Model, guiders, steppers), as in the reference.  At sigma_next = 0 the
+    latents become the fp32 X0, as the reference leaves them."""
+    from .model import Modality, X0Model
+
+    sig = np.asarray(sigmas, dtype=np.float32)
+    steps = len(sig) - 1
+    need_cfg = video_guider.enabled() or audio_guider.enabled()
+    if need_cfg and (negative_video_context is None or negative_audio_context is None):
+        raise ValueError("CFG needs the negative video and audio contexts")
+    b = video.latent.shape[0]
+    if need_cfg:
+        vctx = torch.cat([video_context, negative_video_context])
+        actx = torch.cat([audio_context, negative_audio_context])
+        vpe, ape, vcpe, acpe = (_batch2(t) for t in (video_pe, audio_pe, video_cross_pe, audio_cross_pe))
+    else:
+        vctx, actx, vpe, ape, vcpe, acpe = video_context, audio_context, video_pe, audio_pe, video_cross_pe, \
+            audio_cross_pe
+    rep = 2 if need_cfg else 1
+    stg_on = stg_guider is not None and stg_guider.enabled() and stg_perturbations is not None
+    heun = HeunDiffusionStep()
+
+    def guided(vlat, alat, sigma):
+        """Guided X0 predictions of both streams at (vlat, alat, sigma), and
+        the video timesteps of the point."""
+        vt, at = video.timesteps(sigma), audio.timesteps(sigma)
+        rv = lambda t: torch.cat([t] * rep) if rep > 1 else t  # noqa: E731
+        vs = torch.full((rep * b,), sigma, dtype=torch.float32, device=vlat.device)
+        vm = Modality(rv(vlat), rv(vt), vctx, vpe, vcpe, sigma=vs)
+        am = Modality(rv(alat), rv(at), actx, ape, acpe, sigma=vs)
+        dv, da = X0Model(model)(vm, am, shard)
+        if need_cfg:
+            dv = video_guider.guide(dv[:b], dv[b:])
+            da = audio_guider.guide(da[:b], da[b:])
+        return dv, da, vt, at
+
+    prev = None
+    for i in range(steps):
+        sigma, sigma_next = float(sig[i]), float(sig[i + 1])
+        x_v, x_a = video.latent, audio.latent
+        dv, da, vt, at = guided(x_v, x_a, sigma)
+        if stg_on and (i + 1) / steps <= stg_cutoff:
+            vs = torch.full((b,), sigma, dtype=torch.float32, device=x_v.device)
+            vm = Modality(x_v, vt, video_context, video_pe, video_cross_pe, sigma=vs)
+            am = Modality(x_a, at, audio_context, audio_pe, audio_cross_pe, sigma=vs)
+            dp, _ = X0Model(model)(vm, am, shard, stg_perturbations)
+            dv = stg_guider.guide(dv, dp)
+        if ge_gamma > 0 and sigma > 0:
+            cur = (x_v.float() - dv) / sigma
+            if prev is not None:
+                total = ge_gamma * (cur - prev) + prev
+                dv = x_v.float() - total * sigma
+            prev = cur
+        dv = post_process_latent(dv, video.denoise_mask, video.clean_latent)
+        da = post_process_latent(da, audio.denoise_mask, audio.clean_latent)
+        if sigma_next == 0:
+            video, audio = replace(video, latent=dv), replace(audio, latent=da)
+        else:
+            s32 = torch.tensor(sig[i])
+            dt = float(sig[i + 1] - sig[i])
+            pred_v = (x_v.float() + to_velocity(x_v, s32, dv) * dt).to(x_v.dtype)
+            pred_a = (x_a.float() + to_velocity(x_a, s32, da) * dt).to(x_a.dtype)
+            dv2, da2, _, _ = guided(pred_v, pred_a, sigma_next)
+            dv2 = post_process_latent(dv2, video.denoise_mask, video.clean_latent)
+            da2 = post_process_latent(da2, audio.denoise_mask, audio.clean_latent)
+            video = replace(video, latent=heun.step(x_v, dv, sig, i, denoised_at_predicted=dv2))
+            audio = replace(audio, latent=heun.step(x_a, da, sig, i, denoised_at_predicted=da2))
+        if callback is not None:
+            callback(i + 1, steps)
+    return video, audio

@@ -324,3 +324,72 @@ def denoise_loop_av_general(model_fn, video_latent, audio_latent, sigmas, cfg_vi
                                       denoise_mask=audio_mask, clean_latent=audio_clean)[0]
         video_latent = new_v
     return video_latent, audio_latent
+
+
+def _post_process(d, mask, clean):
+    """post_process_latent (common.py:169-191) in fp32."""
+    if mask is None:
+        return d
+    m = np.asarray(mask, F32)[..., None]
+    return ((d * m).astype(F32) + (np.asarray(clean, F32) * (F32(1.0) - m).astype(F32)).astype(F32)).astype(F32)
+
+
+def denoise_loop_heun_av(model_fn, video_latent, audio_latent, sigmas, cfg_video: float = 1.0,
+                         cfg_audio: float = 1.0, stg_scale: float = 0.0, stg_cutoff: float = 1.0,
+                         ge_gamma: float = 0.0, video_mask=None, video_clean=None, audio_mask=None,
+                         audio_clean=None):
+    """_denoise_loop_heun_av (av_pipeline.py:758-897) with ``model_fn`` as
+    in ``denoise_loop_av_general``: the guided X0 at the current point
+    (CFG, STG, gradient estimation, mask blend), the Euler predictor, the
+    guided X0 at the predicted point (CFG, mask blend) and the Heun
+    corrector; at sigma_next = 0 the latent becomes the fp32 X0."""
+    need_cfg = cfg_video != 1.0 or cfg_audio != 1.0
+    sig = np.asarray(sigmas, dtype=F32)
+    steps = len(sig) - 1
+    b = np.asarray(video_latent).shape[0]
+    prev = None
+
+    def ts(mask, s):
+        full = np.full((b,), F32(s), F32)
+        return full if mask is None else (np.asarray(mask, F32) * F32(s)).astype(F32)
+
+    def x0(lat, t, v):
+        t = t[:, None, None] if t.ndim == 1 else t[:, :, None]
+        return _x0(np.asarray(lat, F32), t, np.asarray(v, F32))
+
+    def guided(vlat, alat, s):
+        vt, at = ts(video_mask, s), ts(audio_mask, s)
+        vc, ac = model_fn(vlat, alat, vt, at, "positive")
+        dv, da = x0(vlat, vt, vc), x0(alat, at, ac)
+        if need_cfg:
+            vu, au = model_fn(vlat, alat, vt, at, "negative")
+            dv, da = cfg_guide(dv, x0(vlat, vt, vu), cfg_video), cfg_guide(da, x0(alat, at, au), cfg_audio)
+        return dv, da, vt
+
+    for i in range(steps):
+        s, sn = float(sig[i]), float(sig[i + 1])
+        dv, da, vt = guided(video_latent, audio_latent, s)
+        if stg_scale != 0.0 and (i + 1) / steps <= stg_cutoff:
+            at = ts(audio_mask, s)
+            vp, _ = model_fn(video_latent, audio_latent, vt, at, "perturbed")
+            dv = stg_guide(dv, x0(video_latent, vt, vp), stg_scale)
+        if ge_gamma > 0 and s > 0:
+            x = np.asarray(video_latent, F32)
+            cur = ((x - dv).astype(F32) / F32(s)).astype(F32)
+            if prev is not None:
+                total = ((F32(ge_gamma) * (cur - prev).astype(F32)).astype(F32) + prev).astype(F32)
+                dv = (x - (total * F32(s)).astype(F32)).astype(F32)
+            prev = cur
+        dv, da = _post_process(dv, video_mask, video_clean), _post_process(da, audio_mask, audio_clean)
+        if sn == 0:
+            video_latent, audio_latent = dv, da
+            continue
+        dt = F32(F32(sn) - F32(s))
+        pv = [rbf16((np.asarray(lat, F32) + (((np.asarray(lat, F32) - d).astype(F32) / F32(s)).astype(F32)
+                                                 * dt).astype(F32)).astype(F32)) for lat, d in ((video_latent, dv),
+                                                                                              (audio_latent, da))]
+        dv2, da2, _ = guided(pv[0], pv[1], sn)
+        dv2, da2 = _post_process(dv2, video_mask, video_clean), _post_process(da2, audio_mask, audio_clean)
+        video_latent = heun_step(video_latent, dv, s, sn, dv2)
+        audio_latent = heun_step(audio_latent, da, s, sn, da2)
+    return video_latent, audio_latent

@@ -113,3 +113,54 @@ def test_denoise_av_host_logic_matches_the_oracle_loop(monkeypatch, cfg, stg, ge
         if stg and (i + 1) / steps <= cutoff:
             expect.append((B, True))
     assert model.calls == expect
+
+
+@pytest.mark.parametrize("cfg,stg,ge,masked", [(1.0, 0.0, 0.0, False), (3.0, 0.0, 0.0, False),
+                                               (2.5, 1.0, 1.5, False), (2.0, 0.5, 2.0, True)])
+def test_denoise_heun_av_matches_the_oracle_loop(cfg, stg, ge, masked):
+    """The Heun loop (av_pipeline.py:758-897) with the same test double:
+    predictor and corrector passes, guidance, gradient estimation, masks,
+    and the last step leaving the fp32 X0 -- bit for bit against the oracle
+    loop (all of its step arithmetic is torch fp32)."""
+    from ltxq.perturbations import create_batched_stg_config
+
+    g = rng(int(cfg * 10 + stg * 7 + ge * 3) + masked + 100)
+    B, T, A, L = 2, 12, 5, 3
+    vl, al = normal_bf16(g, (B, T, C)), normal_bf16(g, (B, A, C))
+    vctx, actx, nvctx, nactx = (normal_bf16(g, (B, L, 24)) for _ in range(4))
+    vmask = amask = vclean = aclean = None
+    if masked:
+        vmask = np.ones((B, T), np.float32)
+        vmask[:, :4] = 0.0
+        amask = np.ones((B, A), np.float32)
+        amask[1, :2] = 0.25
+        vclean, aclean = normal_bf16(g, (B, T, C)), normal_bf16(g, (B, A, C))
+    sigmas = np.asarray([1.0, 0.909375, 0.725, 0.421875, 0.0], np.float32)
+    cutoff = 0.5
+
+    def model_np(vlat, alat, vt, at, pass_):
+        neg = pass_ == "negative"
+        ptb = pass_ == "perturbed"
+        return (_velocity_np(vlat, vt, nvctx if neg else vctx, 0.7, ptb),
+                _velocity_np(alat, at, nactx if neg else actx, 1.3, ptb))
+
+    a_cfg = cfg if cfg == 1.0 else 1.5
+    ref_v, ref_a = od.denoise_loop_heun_av(model_np, vl, al, sigmas, cfg, a_cfg, stg, cutoff, ge, vmask, vclean,
+                                           amask, aclean)
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    b16 = lambda a: None if a is None else t(a).to(torch.bfloat16)  # noqa: E731
+    model = FakeModel()
+    pe = (torch.zeros(1), torch.zeros(1))
+    fv, fa = D.denoise_heun_av(model, D.LatentState(b16(vl), t(vmask), b16(vclean)),
+                               D.LatentState(b16(al), t(amask), b16(aclean)), sigmas, b16(vctx), b16(actx), pe, pe,
+                               pe, pe, negative_video_context=b16(nvctx), negative_audio_context=b16(nactx),
+                               video_guider=D.CFGGuider(cfg), audio_guider=D.CFGGuider(a_cfg), ge_gamma=ge,
+                               stg_guider=D.STGGuider(stg) if stg else None,
+                               stg_perturbations=create_batched_stg_config(B) if stg else None, stg_cutoff=cutoff)
+    assert fv.latent.dtype == torch.float32  # the last step leaves the X0
+    assert np.array_equal(fv.latent.numpy(), ref_v) and np.array_equal(fa.latent.numpy(), ref_a)
+    # two transformer points per step but the last (predictor only), + the STG passes
+    steps = len(sigmas) - 1
+    n_main = 2 * steps - 1
+    n_stg = sum(1 for i in range(steps) if stg and (i + 1) / steps <= cutoff)
+    assert len(model.calls) == n_main + n_stg
