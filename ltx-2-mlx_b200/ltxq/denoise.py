@@ -4,7 +4,7 @@ Mirrors the reference's sampling components:
 
 * sigma schedules: ``DISTILLED_SIGMA_VALUES`` / ``STAGE_2_DISTILLED_SIGMA_VALUES``
   and ``LTX2Scheduler`` (LTX_2_MLX/components/schedulers.py:13-140);
-* ``CFGGuider`` / ``STGGuider`` (components/guiders.py:10-92), as scale
+* ``CFGGuider`` / ``STGGuider`` (components/guiders.py:10-87), as scale
   holders with the reference's ``enabled()`` rules;
 * ``denoise_update``: everything a step does after its transformer passes
   (velocity -> denoised, CFG, STG, gradient estimation, the denoise-mask
@@ -101,7 +101,7 @@ class EulerDiffusionStep:
 
 
 class HeunDiffusionStep:
-    """HeunDiffusionStep.step (diffusion_steps.py:73-130): the Euler
+    """HeunDiffusionStep.step (diffusion_steps.py:72-130): the Euler
     predictor, and with the denoised prediction at the predicted point the
     average of the two velocities."""
 
@@ -122,7 +122,7 @@ class HeunDiffusionStep:
 @dataclass(frozen=True)
 class CFGGuider:
     """Classifier-free guidance: cond + (scale - 1) * (cond - uncond)
-    (guiders.py:9-32).  ``guide`` works on denoised predictions (fp32 from
+    (guiders.py:10-32).  ``guide`` works on denoised predictions (fp32 from
     ``X0Model``); ``denoise_av`` applies the same arithmetic inside
     ``ltxq_denoise_update``."""
 
@@ -139,7 +139,7 @@ class CFGGuider:
 
 
 def projection_coef(to_project: torch.Tensor, project_onto: torch.Tensor) -> torch.Tensor:
-    """Per-sample <a, b> / (|b|^2 + 1e-8), shape (B, 1) (guiders.py:175-192)."""
+    """Per-sample <a, b> / (|b|^2 + 1e-8), shape (B, 1) (guiders.py:174-192)."""
     b = to_project.shape[0]
     a, o = to_project.reshape(b, -1), project_onto.reshape(b, -1)
     return (a * o).sum(dim=1, keepdim=True) / ((o * o).sum(dim=1, keepdim=True) + 1e-8)
@@ -169,7 +169,7 @@ class CFGStarRescalingGuider:
 @dataclass(frozen=True)
 class STGGuider:
     """Spatio-temporal guidance: pos + scale * (pos - perturbed)
-    (guiders.py:65-91)."""
+    (guiders.py:64-87)."""
 
     scale: float
 

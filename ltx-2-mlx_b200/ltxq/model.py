@@ -1,11 +1,11 @@
 """The velocity model around the block loop: LTXModel of
 LTX_2_MLX/model/transformer/model.py:454-1487 (AudioVideo, LTX-2.3).
 
-One call is the reference's ``LTXModel.__call__`` (model.py:1343-1487):
+One call is the reference's ``LTXModel.__call__`` (model.py:1344-1487):
 
 * preprocess each stream (``TransformerArgsPreprocessor.prepare``
-  model.py:270-340 and ``MultiModalTransformerArgsPreprocessor.prepare``
-  :454-505): ``patchify_proj`` on the latent; the AdaLN MLPs
+  model.py:285-340 and ``MultiModalTransformerArgsPreprocessor.prepare``
+  :445-505): ``patchify_proj`` on the latent; the AdaLN MLPs
   (``AdaLayerNormSingle``, timestep_embedding.py:165-201) on timesteps x 1000
   (9 rows), on sigma x 1000 for the prompt K/V modulation (2 rows), on the
   stream's own timesteps x 1000 for the cross-attention scale/shift (4 rows,
@@ -221,7 +221,7 @@ class LTXAVModel:
     # ------------------------------------------------------------- RoPE
     def rope_tables(self, which: str, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """Self-attention RoPE tables of the "video" or "audio" stream from
-        its token bounds (``_prepare_positional_embeddings``, model.py:232-258:
+        its token bounds (``_prepare_positional_embeddings``, model.py:256-283:
         middle of each bound, max_pos (20, 2048, 2048) / (20,))."""
         cfg = self.video.cfg if which == "video" else self.audio.cfg
         max_pos = R.VIDEO_MAX_POS if which == "video" else R.AUDIO_MAX_POS
@@ -231,7 +231,7 @@ class LTXAVModel:
     def cross_rope_tables(self, positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """Audio<->video cross-attention RoPE tables of a stream from the
         temporal bounds of its tokens (``_prepare_cross_positional_embeddings``,
-        model.py:396-419): audio width and heads, max_pos (20,)."""
+        model.py:392-417): audio width and heads, max_pos (20,)."""
         a = self.audio.cfg
         return R.precompute_freqs_cis(positions[:, 0:1], a.dim, R.THETA, R.AUDIO_MAX_POS, True, a.heads,
                                       self.use_double_precision_rope)
@@ -244,7 +244,7 @@ class LTXAVModel:
 
     # ------------------------------------------------------------- forward
     def _prepare(self, s: _Stream, m: Modality, cross: Modality) -> TransformerArgs:
-        """MultiModalTransformerArgsPreprocessor.prepare (model.py:454-505)."""
+        """MultiModalTransformerArgsPreprocessor.prepare (model.py:445-505)."""
         if m.context_mask is not None:  # the reference's pipelines pass None (pipelines/common.py:242-249, 285-292)
             raise ValueError("text-context attention masks are not supported")
         if not m.enabled:

@@ -2,10 +2,10 @@
 
 The reference's preprocessor builds the rotary tables from the tokens'
 positions when the caller passes none (``_prepare_positional_embeddings``
-model.py:232-258, ``_prepare_cross_positional_embeddings`` :396-419) with
+model.py:256-283, ``_prepare_cross_positional_embeddings`` :392-417) with
 ``precompute_freqs_cis`` (model/transformer/rope.py:286-338, split type).
-The positions come from the latent tools (components/patchifiers.py:124-225
-and 264-310, conditioning/tools.py:60-76): [start, end) bounds of every
+The positions come from the latent tools (components/patchifiers.py:125-225
+and 265-310, conditioning/tools.py:60-76): [start, end) bounds of every
 token, in pixels for height / width and in seconds for time.
 
 Everything here is table arithmetic in torch (fp32, or a float64 frequency
@@ -19,14 +19,14 @@ import math
 
 import torch
 
-VIDEO_MAX_POS = (20, 2048, 2048)  # LTXModel positional_embedding_max_pos default (model.py:625-626)
+VIDEO_MAX_POS = (20, 2048, 2048)  # LTXModel positional_embedding_max_pos default (model.py:615-616)
 AUDIO_MAX_POS = (20,)             # AUDIO_CROSS_PE_MAX_POS (model.py:520), also the audio stream's max_pos
 THETA = 10000.0
 
 
 def freq_grid(theta: float, n_pos_dims: int, dim: int, double: bool, device=None) -> torch.Tensor:
     """theta ** linspace(0, 1, dim // (2 n_pos_dims)) * pi / 2 as fp32
-    (rope.py:90-170); ``double`` evaluates it in float64 first, as the
+    (rope.py:92-167); ``double`` evaluates it in float64 first, as the
     reference's ``use_double_precision`` path does."""
     n = dim // (2 * n_pos_dims)
     if n <= 0:

@@ -9,7 +9,7 @@ Restates, in numpy fp32 with the reference's rounding points:
   (model/transformer/timestep_embedding.py:8-201).  Their inputs are fp32,
   so MLX promotes the bf16 weights and the MLP runs in fp32;
 * the velocity -> denoised conversion (model/transformer/model.py:1489-1540,
-  ``X0Model``), the CFG / STG guiders (components/guiders.py:10-92), the
+  ``X0Model``), the CFG / STG guiders (components/guiders.py:10-87), the
   gradient-estimation velocity blend and the mask blend of the AV CFG loop
   (pipelines/av_pipeline.py:700-740, pipelines/common.py:169-204), and the
   Euler step (components/diffusion_steps.py:19-70);
@@ -168,8 +168,8 @@ def _ada_params(mp: dict, prefix: str) -> dict:
 
 
 def _prepare(mp: dict, which: str, s: dict, cross_sigma: float, ts_mult: float, av_ca_mult: float):
-    """MultiModalTransformerArgsPreprocessor.prepare (model.py:270-340,
-    454-505) for one batch row: timesteps uniform (= sigma) or per token
+    """MultiModalTransformerArgsPreprocessor.prepare (model.py:285-340,
+    445-505) for one batch row: timesteps uniform (= sigma) or per token
     (``s["timesteps"]`` (T,) fp32, the denoise mask times sigma)."""
     p = MODEL_PREFIXES[which]
     d = np.asarray(mp[f"{p['patchify']}.weight"]).shape[0]
@@ -191,7 +191,7 @@ def _prepare(mp: dict, which: str, s: dict, cross_sigma: float, ts_mult: float, 
 
 def model_forward(blocks_p: list, mp: dict, video: dict, audio: dict, heads_v: int, heads_a: int,
                   ts_mult: float = 1000.0, av_ca_mult: float = 1000.0, eps: float = 1e-6, skips=None):
-    """LTXModel.__call__ (model.py:1343-1487) for one batch row: preprocess
+    """LTXModel.__call__ (model.py:1344-1487) for one batch row: preprocess
     both streams, the blocks (``oracle.block.block``), the output heads.
     ``video`` / ``audio``: latent (T, 128) bf16 values, sigma (float),
     optional per-token timesteps (T,), context, pe, cross_pe.  Returns the
@@ -254,7 +254,7 @@ def stg_guide(pos, perturbed, scale: float):
 
 def cfg_star_guide(cond, uncond, scale: float):
     """CFGStarRescalingGuider.guide (guiders.py:35-62, projection_coef
-    :175-192): the per-sample coefficient in float64, the rest fp32."""
+    :174-192): the per-sample coefficient in float64, the rest fp32."""
     c, u = np.asarray(cond, F32), np.asarray(uncond, F32)
     b = c.shape[0]
     cf, uf = c.reshape(b, -1).astype(np.float64), u.reshape(b, -1).astype(np.float64)
@@ -271,7 +271,7 @@ def euler_step(sample, denoised, sigma: float, sigma_next: float):
 
 
 def heun_step(sample, denoised, sigma: float, sigma_next: float, denoised_at_predicted=None):
-    """HeunDiffusionStep.step (diffusion_steps.py:73-130) for a bf16 sample,
+    """HeunDiffusionStep.step (diffusion_steps.py:72-130) for a bf16 sample,
     fp32 sigmas: Euler predictor; with the second prediction, the average of
     the two velocities."""
     x, d = np.asarray(sample, F32), np.asarray(denoised, F32)

@@ -1,9 +1,9 @@
 """RoPE table precompute and latent positions, restated in numpy (TEST
 INFRASTRUCTURE ONLY; see the package docstring).
 
-Follows LTX_2_MLX/model/transformer/rope.py:90-338 (``generate_freq_grid``,
+Follows LTX_2_MLX/model/transformer/rope.py:92-338 (``generate_freq_grid``,
 ``generate_freq_grid_float64_cpu``, ``generate_freqs``, ``split_freqs_cis``,
-``precompute_freqs_cis``), components/patchifiers.py:124-225 and 264-310
+``precompute_freqs_cis``), components/patchifiers.py:125-225 and 265-310
 (video patch bounds, pixel coordinates with the causal fix, audio timings)
 and conditioning/tools.py:60-76 (temporal positions in seconds).  fp32
 array math is one IEEE rounding per op; ``linspace(0, 1, n)`` is i / (n - 1)
@@ -22,7 +22,7 @@ F32 = np.float32
 
 
 def freq_grid(theta: float, n_pos_dims: int, dim: int, double: bool) -> np.ndarray:
-    """generate_freq_grid / generate_freq_grid_float64_cpu (rope.py:90-170):
+    """generate_freq_grid / generate_freq_grid_float64_cpu (rope.py:92-167):
     theta ** linspace(0, 1, dim // (2 n_pos_dims)) * pi / 2, fp32."""
     n = dim // (2 * n_pos_dims)
     if n <= 0:
@@ -67,7 +67,7 @@ def video_positions(batch: int, frames: int, height: int, width: int, fps: float
                     causal_fix: bool = True) -> np.ndarray:
     """(B, 3, frames * height * width, 2) fp32 [start, end) bounds of every
     latent token (patch size 1), in pixels (frames: seconds), token order
-    frame-major (patchifiers.py:124-178, 180-225; tools.py:60-76)."""
+    frame-major (patchifiers.py:125-178, 180-225; tools.py:60-76)."""
     f, h, w = np.meshgrid(np.arange(frames), np.arange(height), np.arange(width), indexing="ij")
     starts = np.stack([f, h, w]).reshape(3, -1)
     coords = np.stack([starts, starts + 1], axis=-1) * np.asarray(scale).reshape(3, 1, 1)
@@ -81,7 +81,7 @@ def video_positions(batch: int, frames: int, height: int, width: int, fps: float
 def audio_positions(batch: int, frames: int, sample_rate: int = 16000, hop_length: int = 160, downsample: int = 4,
                     is_causal: bool = True, shift: int = 0) -> np.ndarray:
     """(B, 1, frames, 2) fp32 [start, end) times in seconds of every audio
-    latent frame (patchifiers.py:264-310)."""
+    latent frame (patchifiers.py:265-310)."""
     def times(a, b):
         mel = (np.arange(a, b).astype(F32) * F32(downsample)).astype(F32)
         if is_causal:
