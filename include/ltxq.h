@@ -28,11 +28,11 @@
  *                           FeedForward.__call__ + transformer.py:629-650
  *   ltxq_denoise_update  <- one step of the AV CFG denoise loop after the
  *                           transformer passes (pipelines/av_pipeline.py:
- *                           700-752): X0Model.denoise (model/transformer/
- *                           model.py:1527-1533), CFGGuider / STGGuider.guide
+ *                           700-742): X0Model.denoise (model/transformer/
+ *                           model.py:1519-1525), CFGGuider / STGGuider.guide
  *                           (components/guiders.py:24-28, 79-83), the
  *                           gradient-estimation blend (av_pipeline.py:
- *                           725-731), post_process_latent (pipelines/
+ *                           719-725), post_process_latent (pipelines/
  *                           common.py:169-191) and EulerDiffusionStep.step
  *                           (components/diffusion_steps.py:19-70)
  */

@@ -1,8 +1,8 @@
 // denoise.cu -- the per-step latent update of the AV denoise loop, after the
-// transformer passes of a step (pipelines/av_pipeline.py:700-752): velocity
-// -> denoised (X0Model, model/transformer/model.py:1527-1533), CFG and STG
+// transformer passes of a step (pipelines/av_pipeline.py:700-742): velocity
+// -> denoised (X0Model, model/transformer/model.py:1519-1525), CFG and STG
 // guidance (components/guiders.py:24-28, 79-83), the gradient-estimation
-// velocity blend (av_pipeline.py:725-731), the denoise-mask blend
+// velocity blend (av_pipeline.py:719-725), the denoise-mask blend
 // (pipelines/common.py:169-191) and the Euler step
 // (components/diffusion_steps.py:19-70), in one pass over the latent.
 //

@@ -8,7 +8,7 @@ Mirrors the reference's sampling components:
   holders with the reference's ``enabled()`` rules;
 * ``denoise_update``: everything a step does after its transformer passes
   (velocity -> denoised, CFG, STG, gradient estimation, the denoise-mask
-  blend, the Euler step; pipelines/av_pipeline.py:700-752) as ONE CUDA
+  blend, the Euler step; pipelines/av_pipeline.py:700-742) as ONE CUDA
   kernel launch per stream (``ltxq_denoise_update``), bit-identical to the
   reference's fp32 op sequence;
 * ``denoise_av``: ``_denoise_loop_cfg_av`` (av_pipeline.py:625-756).  The
@@ -21,7 +21,7 @@ With an ``STGGuider`` and a ``BatchedPerturbationConfig``
 (``ltxq.perturbations``), each step also runs the perturbed pass (the
 positive inputs through blocks that skip the perturbed attention
 sub-layers) until ``stg_cutoff`` of the steps, and the video update adds
-the STG term after CFG, as av_pipeline.py:709-720 does.
+the STG term after CFG, as av_pipeline.py:706-717 does.
 
 Not built: the Heun stepper and the non-AV / two-stage pipelines.
 """
@@ -335,7 +335,7 @@ def denoise_av(model, video: LatentState, audio: LatentState, sigmas, video_cont
             vv, av = run(v_in, a_in, v_t, a_t, v_s)
         vc, ac = vv[:b], av[:b]
         vu, au = (vv[b:], av[b:]) if need_cfg else (None, None)
-        stg_active = stg_on and (i + 1) / steps <= stg_cutoff  # av_pipeline.py:709-714
+        stg_active = stg_on and (i + 1) / steps <= stg_cutoff  # av_pipeline.py:706-711
         vp = None
         if stg_active:  # the positive rows of the input buffers, through the perturbed blocks
             pos = (v_in[:b], a_in[:b], v_t[:b], a_t[:b], v_s[:b])

@@ -11,7 +11,7 @@ Restates, in numpy fp32 with the reference's rounding points:
 * the velocity -> denoised conversion (model/transformer/model.py:1489-1540,
   ``X0Model``), the CFG / STG guiders (components/guiders.py:10-87), the
   gradient-estimation velocity blend and the mask blend of the AV CFG loop
-  (pipelines/av_pipeline.py:700-740, pipelines/common.py:169-204), and the
+  (pipelines/av_pipeline.py:700-742, pipelines/common.py:169-204), and the
   Euler step (components/diffusion_steps.py:19-70);
 * the video / audio output head (model/transformer/model.py:1312-1340).
 
@@ -112,14 +112,14 @@ def output_head(x, table, embedded, w, b, eps: float = 1e-6):
 
 
 def _x0(x, ts, v):
-    """X0Model.denoise (model.py:1527-1533): latent - timesteps * velocity."""
+    """X0Model.denoise (model.py:1519-1525): latent - timesteps * velocity."""
     return (x - (ts * v).astype(F32)).astype(F32)
 
 
 def denoise_update(latent, v_cond, sigma: float, sigma_next: float, v_uncond=None, cfg_scale: float = 1.0,
                    v_perturbed=None, stg_scale: float = 0.0, denoise_mask=None, clean_latent=None,
                    prev_velocity=None, ge_gamma: float = 0.0):
-    """One step of the AV CFG loop for one stream (av_pipeline.py:672-740):
+    """One step of the AV CFG loop for one stream (av_pipeline.py:700-742):
     X0 of each pass, CFG, STG, gradient estimation, mask blend, Euler step.
     Arrays are [B, T, C] (bf16 values as fp32); ``denoise_mask`` [B, T] fp32.
     Returns (new latent as bf16 values, this step's velocity or None)."""
@@ -134,7 +134,7 @@ def denoise_update(latent, v_cond, sigma: float, sigma_next: float, v_uncond=Non
         pt = _x0(x, ts, np.asarray(v_perturbed, F32))
         d = (d + (F32(stg_scale) * (d - pt).astype(F32)).astype(F32)).astype(F32)
     cur = None
-    if ge_gamma > 0 and sigma > 0:  # av_pipeline.py:725-731
+    if ge_gamma > 0 and sigma > 0:  # av_pipeline.py:719-725
         cur = ((x - d).astype(F32) / sig).astype(F32)
         if prev_velocity is not None:
             total = ((F32(ge_gamma) * (cur - prev_velocity).astype(F32)).astype(F32) + prev_velocity).astype(F32)
@@ -220,7 +220,7 @@ def denoise_loop_av(model_fn, video_latent, audio_latent, sigmas, cfg_video: flo
     pass_)`` -> (video velocity, audio velocity) for one batch row, pass_ in
     {"positive", "negative", "perturbed"}; the negative pass runs when either
     scale is not 1, the perturbed (STG) pass while stg_scale != 0 and
-    (step + 1) / steps <= stg_cutoff (av_pipeline.py:709-720).  Returns the
+    (step + 1) / steps <= stg_cutoff (av_pipeline.py:706-717).  Returns the
     final (video, audio) latents."""
     need_cfg = cfg_video != 1.0 or cfg_audio != 1.0
     sig = np.asarray(sigmas, dtype=F32)
