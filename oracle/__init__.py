@@ -8,7 +8,11 @@ leg use it, and only as the checker / the timed CPU baseline.
 The oracle is a numpy restatement of the reference's MLX op composition for
 the path (LTX_2_MLX/kernels/fused_ops.py, model/transformer/transformer.py,
 model/transformer/feed_forward.py, model/transformer/attention.py,
-loader/transformer_cache.py).  MLX itself (the third-party dependency that
+loader/transformer_cache.py) and for its callers: the model's preprocess and
+output heads, RoPE tables and latent positions, the denoise step and loops,
+schedules, guiders, steppers, latent layouts and the noiser (``denoise``,
+``rope``, ``latents``; model/transformer/model.py, rope.py,
+timestep_embedding.py, components/, pipelines/av_pipeline.py).  MLX itself (the third-party dependency that
 holds ``mx.quantize`` / ``mx.quantized_matmul`` / ``mx.fast.rms_norm``,
 ``mlx>=0.31.2`` per the reference's pyproject.toml:35) is not installable
 here, so:
