@@ -72,6 +72,16 @@ def step_linear_flops(t_video: int, t_audio: int, t_text: int) -> float:
 FF_T, FF_D, FF_H = 3456, 4096, 16384
 FF_FLOPS = 2.0 * FF_T * FF_D * FF_H * 2
 
+# ---- config 1: one fused AdaLN + quantized linear + gated residual
+CFG1_M, CFG1_D = 1024, 4096
+CFG1_FLOPS = 2.0 * CFG1_M * CFG1_D * CFG1_D
+
+# ---- step-shaped workloads: --workload -> (blocks, quant, video tokens, audio tokens, batch, workload name)
+STEP_PRESETS = {
+    "config3": (1, "int8", 3456, 126, 1, "config3_av_block_int8g64_3456video_126audio"),
+    "config5": (48, "int4", 30576, 751, 2, "config5_22b_denoise_step_int4g64_batch2_30576video_751audio"),
+}
+
 
 def _peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -154,36 +164,58 @@ def _dist():
 # ============================================================================ CPU legs (oracle)
 
 
-class CpuStepSample:
-    """One full-width block on ``video_tokens`` video rows (+ 201 audio, 1024
-    text) through the oracle.  The packed mxfp8 weights are prepared once;
-    each timed run dequantizes them (the reference's quantized matmul works
-    from packed weights every call) and runs the block composition."""
+class CpuBlock:
+    """One config-4 block (d 4096 / 2048, 32 heads, every linear mxfp8 g32) on
+    the host cores through the oracle's numpy restatement of the reference
+    composition, at the full token counts: 9216 video, 201 audio and 1024 text
+    rows.  The unit of work is one of the block's seven sub-layers, attention
+    included; each call dequantizes that sub-layer's packed weights once (the
+    reference's quantized matmul works from the packed cache on every call)
+    and runs the sub-layer on all of its rows.  A block is the sum of its
+    sub-layers; a step is 48 blocks."""
 
-    def __init__(self, video_tokens: int, seed: int = 0):
+    SUBLAYERS = {  # sub-layer -> the attention / FF modules whose weights it reads
+        "video_self_attention": ("attn1",),
+        "video_text_cross_attention": ("attn2",),
+        "audio_self_attention": ("audio_attn1",),
+        "audio_text_cross_attention": ("audio_attn2",),
+        "audio_video_cross_attention": ("audio_to_video_attn", "video_to_audio_attn"),
+        "video_feed_forward": ("ff",),
+        "audio_feed_forward": ("audio_ff",),
+    }
+
+    def __init__(self, video_tokens: int = STEP_T, audio_tokens: int = STEP_A, quant: str = "mxfp8", seed: int = 0):
         import numpy as np
 
         from ltxq.block import AUDIO_22B, VIDEO_22B, linear_specs, table_specs
-        from oracle import quant as oq
-        from oracle.bf16 import rbf16
+        from oracle.bf16 import f32_to_bf16_bits, rbf16
 
-        self.video_tokens = video_tokens
+        self.video_tokens, self.audio_tokens, self.quant = video_tokens, audio_tokens, quant
         g = np.random.default_rng(seed)
         self.q = {}
         for name, (n, k) in linear_specs().items():
-            # packed mxfp8 drawn directly (finite E4M3 codes of either sign, E8M0
-            # scales around 2^-9): the timed work does not depend on the values
-            codes = (g.integers(0, 0x7F, size=(n, k), dtype=np.uint8) | (g.integers(0, 2, size=(n, k), dtype=np.uint8) << 7))
-            qq = {"mode": "mxfp8", "group_size": 32, "bits": 8,
-                  "weight": codes.view(np.uint32).reshape(n, k // 4),
-                  "scales": g.integers(112, 120, size=(n, k // 32), dtype=np.uint8)}
+            # packed arrays drawn directly (mxfp8: finite E4M3 codes of either
+            # sign, E8M0 scales around 2^-9; affine: random codes, scales and
+            # biases): the timed work does not depend on the values
+            if quant == "mxfp8":
+                codes = (g.integers(0, 0x7F, size=(n, k), dtype=np.uint8)
+                         | (g.integers(0, 2, size=(n, k), dtype=np.uint8) << 7))
+                qq = {"mode": "mxfp8", "group_size": 32, "bits": 8,
+                      "weight": codes.view(np.uint32).reshape(n, k // 4),
+                      "scales": g.integers(112, 120, size=(n, k // 32), dtype=np.uint8)}
+            else:
+                bits = 8 if quant == "int8" else 4
+                words = g.integers(0, 2 ** 32, size=(n, k * bits // 32), dtype=np.uint64).astype(np.uint32)
+                gp = lambda std: f32_to_bf16_bits(g.standard_normal((n, k // 64), dtype=np.float32) * std)  # noqa: E731
+                qq = {"mode": "affine", "group_size": 64, "bits": bits, "weight": words, "scales": gp(1e-3),
+                      "biases": gp(0.05)}
             self.q[name] = (qq, rbf16(g.standard_normal(n, dtype=np.float32) * np.float32(0.01)), k)
         self.tabs = {k: (g.standard_normal(s, dtype=np.float32) * np.float32(0.1)
                          + np.float32(1.0 if k.endswith("norm.weight") else 0.0)) for k, s in table_specs().items()}
 
-        def stream(cfg, t, cross_heads, cross_d):
+        def stream(cfg, t):
             ang = g.uniform(0, 6.28, (cfg.heads, t, cfg.d_head // 2)).astype(np.float32)
-            cang = g.uniform(0, 6.28, (cross_heads, t, cross_d // 2)).astype(np.float32)
+            cang = g.uniform(0, 6.28, (AUDIO_22B.heads, t, AUDIO_22B.d_head // 2)).astype(np.float32)
             return {"x": rbf16(g.standard_normal((t, cfg.dim), dtype=np.float32)),
                     "context": rbf16(g.standard_normal((STEP_L, cfg.context_dim), dtype=np.float32)),
                     "timesteps": (g.standard_normal((9, cfg.dim)) * 0.1).astype(np.float32),
@@ -192,24 +224,111 @@ class CpuStepSample:
                     "cross_gate": (g.standard_normal((1, cfg.dim)) * 0.1).astype(np.float32),
                     "pe": (np.cos(ang), np.sin(ang)), "cross_pe": (np.cos(cang), np.sin(cang))}
 
-        self.vs = stream(VIDEO_22B, video_tokens, AUDIO_22B.heads, AUDIO_22B.d_head)
-        self.as_ = stream(AUDIO_22B, STEP_A, AUDIO_22B.heads, AUDIO_22B.d_head)
-        self.flops = step_linear_flops(video_tokens, STEP_A, STEP_L)
+        self.vs = stream(VIDEO_22B, video_tokens)
+        self.as_ = stream(AUDIO_22B, audio_tokens)
 
-    def run(self) -> float:
-        from oracle import block as ob
+    def _weights(self, modules):
         from oracle import quant as oq
 
-        t0 = time.perf_counter()
         p = dict(self.tabs)
         for name, (qq, b, k) in self.q.items():
-            p[f"{name}.weight"] = oq.dequantize_fast(qq, k)
-            p[f"{name}.bias"] = b
-        ob.block(p, self.vs, self.as_)
+            if name.split(".")[0] in modules:
+                p[f"{name}.weight"] = oq.dequantize_fast(qq, k)
+                p[f"{name}.bias"] = b
+        return p
+
+    def run(self, sub: str) -> float:
+        """Seconds of one sub-layer (weight dequantization included)."""
+        from oracle import block as ob
+        from oracle import ref_ops as ro
+
+        vs, as_ = self.vs, self.as_
+        vx, ax = vs["x"], as_["x"]
+        t0 = time.perf_counter()
+        p = self._weights(self.SUBLAYERS[sub])
+        if sub in ("video_self_attention", "audio_self_attention"):
+            s, x, name, table = ((vs, vx, "attn1", "scale_shift_table") if sub.startswith("video")
+                                 else (as_, ax, "audio_attn1", "audio_scale_shift_table"))
+            sh, sc, g = ob.ada(p[table], s["timesteps"], 0, 3)
+            ro.gated_add(x, ob.attention(p, name, ro.adaln(x, sc, sh), pe=s["pe"]), g)
+        elif sub in ("video_text_cross_attention", "audio_text_cross_attention"):
+            s, x, name, table, prompt = ((vs, vx, "attn2", "scale_shift_table", "prompt_scale_shift_table")
+                                         if sub.startswith("video") else
+                                         (as_, ax, "audio_attn2", "audio_scale_shift_table",
+                                          "audio_prompt_scale_shift_table"))
+            sh_q, sc_q, g = ob.ada(p[table], s["timesteps"], 6, 9)
+            kv = ob.ada(p[prompt], s["prompt"], 0, 2)
+            enc = ro.modulate(s["context"], kv[1], kv[0])
+            ro.gate_then_add(x, ob.attention(p, name, ro.adaln(x, sc_q, sh_q), context=enc), g)
+        elif sub == "audio_video_cross_attention":
+            vn, an = ro.rms_norm(vx), ro.rms_norm(ax)
+            ta, tv = p["scale_shift_table_a2v_ca_audio"], p["scale_shift_table_a2v_ca_video"]
+            a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = ob.ada(ta, as_["cross_ss"], 0, 4)
+            v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = ob.ada(tv, vs["cross_ss"], 0, 4)
+            out = ob.attention(p, "audio_to_video_attn", ro.modulate(vn, v_sc_a2v, v_sh_a2v),
+                               context=ro.modulate(an, a_sc_a2v, a_sh_a2v), pe=vs["cross_pe"], k_pe=as_["cross_pe"])
+            ro.gated_add(vx, out, tv[4] + vs["cross_gate"][0])
+            out = ob.attention(p, "video_to_audio_attn", ro.modulate(an, a_sc_v2a, a_sh_v2a),
+                               context=ro.modulate(vn, v_sc_v2a, v_sh_v2a), pe=as_["cross_pe"], k_pe=vs["cross_pe"])
+            ro.gated_add(ax, out, ta[4] + as_["cross_gate"][0])
+        else:
+            s, x, table, base = ((vs, vx, "scale_shift_table", "ff") if sub.startswith("video")
+                                 else (as_, ax, "audio_scale_shift_table", "audio_ff"))
+            sh, sc, g = ob.ada(p[table], s["timesteps"], 3, 6)
+            ro.ff_sublayer(x, sc, sh, g, p[f"{base}.project_in.proj.weight"], p[f"{base}.project_in.proj.bias"],
+                           p[f"{base}.project_out.weight"], p[f"{base}.project_out.bias"])
         return time.perf_counter() - t0
 
 
-def _cpu_ff_sample(sample: int, seed: int = 1):
+def _cpu_block_rotation(blk: "CpuBlock", n_runs: int, warmup: int = 0) -> dict:
+    """Runs the block's sub-layers in turn, ``warmup`` untimed then ``n_runs``
+    timed (at least one of each), and returns each sub-layer's mean seconds."""
+    subs = list(CpuBlock.SUBLAYERS)
+    for i in range(warmup):
+        blk.run(subs[i % len(subs)])
+    times: dict = {s: [] for s in subs}
+    for i in range(max(n_runs, len(subs))):
+        s = subs[i % len(subs)]
+        times[s].append(blk.run(s))
+    return {s: sum(v) / len(v) for s, v in times.items()}
+
+
+def _cpu_block_line(per_sub: dict, blk: "CpuBlock", blocks: int = STEP_BLOCKS) -> tuple:
+    """(ms per step of ``blocks`` blocks, the cpu_baseline description) from
+    measured sub-layer seconds."""
+    block_s = sum(per_sub.values())
+    threads = os.cpu_count() or 1
+    extra = f"extrapolated x{blocks} blocks per step" if blocks > 1 else "not extrapolated"
+    desc = (f"measured: one full block ({blk.quant}; {blk.video_tokens} video, {blk.audio_tokens} audio, {STEP_L} "
+            f"text rows; attention included; weights dequantized once per sub-layer call) = {block_s:.2f} s, as "
+            f"the sum of its 7 sub-layers timed separately at full size; {extra}. oracle/ numpy restatement of the "
+            f"reference composition (BLAS on {threads} threads, elementwise ops on one)")
+    return block_s * blocks * 1e3, desc
+
+
+def _cpu_config1(norm: str = "layer"):
+    """BASELINE config 1 on the host at its full shape (not extrapolated):
+    seconds, FLOPs."""
+    import numpy as np
+
+    from oracle import quant as oq
+    from oracle import ref_ops as ro
+    from oracle.bf16 import rbf16
+
+    g = np.random.default_rng(0)
+    x = rbf16(g.standard_normal((1024, 4096), dtype=np.float32))
+    sc, sh, gt = (rbf16(g.standard_normal((1, 4096), dtype=np.float32) * np.float32(0.1)) for _ in range(3))
+    w = rbf16(g.standard_normal((4096, 4096), dtype=np.float32) * np.float32(0.02))
+    b = rbf16(g.standard_normal(4096, dtype=np.float32) * np.float32(0.01))
+    q = oq.quantize(w, "affine", 64, 8)
+    t0 = time.perf_counter()
+    ro.adaln_linear_gated(x, sc, sh, gt, oq.dequantize_fast(q, 4096), b, 1e-6, norm, vec_bf16=True)
+    return time.perf_counter() - t0, CFG1_FLOPS
+
+
+def _cpu_ff_sample(sample: int = FF_T, seed: int = 1):
+    """The config-2 FF sub-layer on ``sample`` of its rows (all 3456 by
+    default: not extrapolated): seconds, FLOPs."""
     import numpy as np
 
     from oracle import quant as oq
@@ -233,57 +352,73 @@ def _cpu_ff_sample(sample: int, seed: int = 1):
 
 
 def cpu_baseline(workload: str):
-    """Bounded CPU measurement (~10-30 s) for the cpu_baseline field."""
-    if workload == "step":
-        smp = CpuStepSample(64)
-        sec = min(smp.run() for _ in range(2))
-        tflops = smp.flops / sec / 1e12
-        ms_step = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS / (tflops * 1e12) * 1e3
-        return {"value": ms_step, "unit": "ms/step", "cores": os.cpu_count() or 1, "kind": "port",
-                "sample": f"one full-width mxfp8 block on 64 of the 9216 video tokens (+201 audio, 1024 text), "
-                          f"oracle/ numpy restatement with weights dequantized per call; {tflops * 1e3:.2f} "
-                          f"GFLOP/s of linear work, extrapolated to 48 blocks x 9216 tokens by linear FLOPs "
-                          f"(attention excluded)"}
-    sec, flops = _cpu_ff_sample(256)
-    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"256 of the {FF_T} tokens (dequantize + numpy fp32 BLAS with the reference's bf16 rounding points)"}
+    """Bounded CPU measurement for the cpu_baseline field of the GPU line."""
+    threads = os.cpu_count() or 1
+    if workload in ("step", "config3"):
+        blk = CpuBlock() if workload == "step" else CpuBlock(3456, 126, "int8")
+        blocks = STEP_BLOCKS if workload == "step" else 1
+        ms, desc = _cpu_block_line(_cpu_block_rotation(blk, 7), blk, blocks)
+        return {"value": ms, "unit": "ms/step" if blocks > 1 else "ms/block", "cores": threads, "kind": "port",
+                "sample": desc}
+    if workload == "config5":
+        return None  # hours per step on the host cores; the config-4 line carries the CPU figure
+    if workload == "config1":
+        sec, flops = _cpu_config1()
+        return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"the whole config-1 call (1024 x 4096 -> 4096, LayerNorm prologue, gated residual) in "
+                          f"{sec:.3f} s, not extrapolated"}
+    sec, flops = _cpu_ff_sample()
+    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"the whole config-2 FF sub-layer ({FF_T} tokens, int4 g64) in {sec:.2f} s, not extrapolated"}
 
 
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return
-    sample = args.cpu_sample
-    if args.workload == "ff":
-        run = lambda i: _cpu_ff_sample(sample, i)
+    threads = os.cpu_count() or 1
+    measured = None
+    if args.workload == "config5":
+        print(json.dumps({"impl": "reference", "unavailable": "config 5 on the host cores takes hours per step "
+                          "(30576 x 2 video rows); the config-4 reference line measures the same composition"}))
+        return
+    if args.workload in ("step", "config3"):
+        blk = CpuBlock() if args.workload == "step" else CpuBlock(3456, 126, "int8")
+        blocks = STEP_BLOCKS if args.workload == "step" else 1
+        per_sub = _cpu_block_rotation(blk, args.steps, args.warmup)
+        value, desc = _cpu_block_line(per_sub, blk, blocks)
+        unit, hib, scaling = ("ms/step" if blocks > 1 else "ms/block"), False, "strong"
+        cfg = (_step_config(world) if args.workload == "step" else
+               _step_config(world, 1, True, "int8", 3456, audio_tokens=126, workload=STEP_PRESETS["config3"][5]))
+        ms_step = value
+        measured = {"block_s": sum(per_sub.values()), "sublayer_s": per_sub, "blocks_per_step": blocks,
+                    "extrapolation": (f"x{blocks} blocks (every block has the same shapes)" if blocks > 1
+                                      else "none"),
+                    "timed_steps": f"each step times one sub-layer of the block in turn at full size "
+                                   f"({max(args.steps, len(CpuBlock.SUBLAYERS))} sub-layer runs)"}
     else:
-        smp = CpuStepSample(sample)
-        run = lambda i: (smp.run(), smp.flops)
-    for i in range(args.warmup):
-        run(100 + i)
-    secs, flops = [], 0.0
-    for i in range(args.steps):
-        s, flops = run(i)
-        secs.append(s)
-    sec = sum(secs) / len(secs)
-    tflops = flops / sec / 1e12
-    if args.workload == "step":
-        value = step_linear_flops(STEP_T, STEP_A, STEP_L) * STEP_BLOCKS / (tflops * 1e12) * 1e3
-        unit, hib, cfg, scaling = "ms/step", False, _step_config(world), "strong"
-        cfg["execution"] = "host cores: the oracle port (numpy, BLAS on every core)"
-        desc = (f"one full-width block on {sample} of 9216 video tokens per step, extrapolated to 48 blocks x "
-                f"9216 tokens by linear FLOPs (attention excluded)")
-    else:
-        value, unit, hib, cfg, scaling = tflops, "TFLOP/s", True, _ff_config(world), "weak"
-        desc = f"{sample} of {FF_T} tokens per step"
+        run = (lambda i: _cpu_config1()) if args.workload == "config1" else (lambda i: _cpu_ff_sample(FF_T, i))
+        for i in range(args.warmup):
+            run(100 + i)
+        secs, flops = [], 0.0
+        for i in range(args.steps):
+            s, flops = run(i)
+            secs.append(s)
+        sec = sum(secs) / len(secs)
+        value, unit, hib, scaling = flops / sec / 1e12, "TFLOP/s", True, "weak"
+        cfg = _config1_config(world) if args.workload == "config1" else _ff_config(world)
+        ms_step = sec * 1e3
+        desc = f"the whole {cfg['workload']} workload per step ({sec:.3f} s), not extrapolated"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": value if unit == "ms/step" else sec * 1e3, "higher_is_better": hib,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": hib,
         "scaling": scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
-        "cpu_baseline": {"value": value, "unit": unit, "cores": os.cpu_count() or 1, "kind": "port",
-                         "sample": desc + " (oracle/ numpy restatement of the reference composition)"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
+                         "sample": desc},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if measured is not None:
+        line["measured"] = measured
     print(json.dumps(line), flush=True)
 
 
@@ -310,15 +445,22 @@ _EXCHANGE = {"gather": "video self-attention K/V all-gather", "head_parallel": "
 
 
 def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8", video_tokens=STEP_T,
-                 self_attention="gather", v2a="gather"):
+                 self_attention="gather", v2a="gather", audio_tokens=STEP_A, batch=1, workload=None):
     v2a_text = "video->audio K/V all-gather" if v2a == "gather" else _EXCHANGE[v2a]
-    return {"workload": STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": video_tokens,
+    return {"workload": workload or STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": video_tokens,
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
-            "audio_tokens": STEP_A, "text_tokens": STEP_L, "global_batch": 1, "seq_len": video_tokens,
+            "audio_tokens": audio_tokens, "text_tokens": STEP_L, "global_batch": batch, "seq_len": video_tokens,
             "quant": STEP_QUANT[quant][3],
             "parallelism": (f"video rows sharded x{world}, weights replicated, {_EXCHANGE[self_attention]}, "
                             f"{v2a_text} (NCCL)" if world > 1 else "single GPU (no collective)"),
             "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
+
+
+def _config1_config(world):
+    return {"workload": "config1_adaln_qlinear_gated_int8g64_1024x4096x4096", "tokens": CFG1_M, "d": CFG1_D,
+            "quant": "affine int8 g64", "norm": "LayerNorm without affine, eps 1e-6", "global_batch": world,
+            "seq_len": CFG1_M, "parallelism": f"replicas{world}",
+            "l2": "flushed before every timed step (256 MiB write, outside the events)"}
 
 
 def _ff_config(world):
@@ -344,7 +486,7 @@ def run_step(args, world, rank, local, dev):
     from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, RowShard, TransformerArgs
     from ltxq.graph import StepGraph
 
-    T = args.video_tokens
+    T, A, B = args.video_tokens, args.audio_tokens, args.batch
     if T % world:
         raise SystemExit(f"{T} video tokens do not split over {world} ranks")
     tl = T // world
@@ -361,26 +503,28 @@ def run_step(args, world, rank, local, dev):
         return (torch.randn(*shape, generator=gen, device=dev) * std).to(dtype)
 
     def rope(heads, t, d):
+        # the batch entries (the CFG pair) share token positions; the tables are
+        # materialized per entry, as the kernels read them
         ang = torch.rand(1, heads, t, d // 2, generator=gen, device=dev) * 6.2831853
-        return torch.cos(ang), torch.sin(ang)
+        return tuple(f(ang).expand(B, -1, -1, -1).contiguous() for f in (torch.cos, torch.sin))
 
-    vx_full = rnd(1, T, VD, dtype=torch.bfloat16)
-    ax = rnd(1, STEP_A, AD, dtype=torch.bfloat16)
+    vx_full = rnd(B, T, VD, dtype=torch.bfloat16)
+    ax = rnd(B, A, AD, dtype=torch.bfloat16)
     pe_v = rope(VIDEO_22B.heads, T, VIDEO_22B.d_head)
     cpe_v = rope(AUDIO_22B.heads, T, AUDIO_22B.d_head)
     rows = slice(rank * tl, (rank + 1) * tl)
     video = TransformerArgs(
-        x=vx_full[:, rows].contiguous(), context=rnd(1, STEP_L, VD, dtype=torch.bfloat16),
-        timesteps=rnd(1, 1, 9, VD, std=0.1), positional_embeddings=tuple(c[:, :, rows].contiguous() for c in pe_v),
+        x=vx_full[:, rows].contiguous(), context=rnd(B, STEP_L, VD, dtype=torch.bfloat16),
+        timesteps=rnd(B, 1, 9, VD, std=0.1), positional_embeddings=tuple(c[:, :, rows].contiguous() for c in pe_v),
         cross_positional_embeddings=tuple(c[:, :, rows].contiguous() for c in cpe_v),
-        cross_scale_shift_timestep=rnd(1, 1, 4, VD, std=0.1), cross_gate_timestep=rnd(1, 1, 1, VD, std=0.1),
-        prompt_timestep=rnd(1, 1, 2, VD, std=0.1))
+        cross_scale_shift_timestep=rnd(B, 1, 4, VD, std=0.1), cross_gate_timestep=rnd(B, 1, 1, VD, std=0.1),
+        prompt_timestep=rnd(B, 1, 2, VD, std=0.1))
     audio = TransformerArgs(
-        x=ax, context=rnd(1, STEP_L, AD, dtype=torch.bfloat16), timesteps=rnd(1, 1, 9, AD, std=0.1),
-        positional_embeddings=rope(AUDIO_22B.heads, STEP_A, AUDIO_22B.d_head),
-        cross_positional_embeddings=rope(AUDIO_22B.heads, STEP_A, AUDIO_22B.d_head),
-        cross_scale_shift_timestep=rnd(1, 1, 4, AD, std=0.1), cross_gate_timestep=rnd(1, 1, 1, AD, std=0.1),
-        prompt_timestep=rnd(1, 1, 2, AD, std=0.1))
+        x=ax, context=rnd(B, STEP_L, AD, dtype=torch.bfloat16), timesteps=rnd(B, 1, 9, AD, std=0.1),
+        positional_embeddings=rope(AUDIO_22B.heads, A, AUDIO_22B.d_head),
+        cross_positional_embeddings=rope(AUDIO_22B.heads, A, AUDIO_22B.d_head),
+        cross_scale_shift_timestep=rnd(B, 1, 4, AD, std=0.1), cross_gate_timestep=rnd(B, 1, 1, AD, std=0.1),
+        prompt_timestep=rnd(B, 1, 2, AD, std=0.1))
     del vx_full, pe_v, cpe_v
     stream = torch.cuda.current_stream()
     use_graph = not args.eager
@@ -478,15 +622,17 @@ def run_step(args, world, rank, local, dev):
 
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = _peaks()
-        lin_flops = step_linear_flops(T, STEP_A, STEP_L) * n_blocks
-        ff_flops = 2.0 * tl * VD * 4 * VD
+        lin_flops = step_linear_flops(B * T, B * A, B * STEP_L) * n_blocks
+        ff_flops = 2.0 * B * tl * VD * 4 * VD
         achieved = ff_flops / (ff_avg / 1e3) / 1e12
         h2d = vx_host.numel() * 2 + ax_host.numel() * 2
         line = {
-            "metric": METRIC, "value": ms_step, "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": ms_step, "unit": "ms/block" if n_blocks == 1 else "ms/step",
+            "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": _step_config(world, n_blocks, use_graph, args.quant, T, args.self_attention, args.v2a),
+            "config": _step_config(world, n_blocks, use_graph, args.quant, T, args.self_attention, args.v2a, A, B,
+                                   args.workload_name),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
@@ -496,17 +642,17 @@ def run_step(args, world, rank, local, dev):
                          "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
                          "peak_kind": (f"{peak_kind} bf16 sustained (kernel timed inside a long step)"
                                        if peak_kind == "measured" else "fallback 1400 TFLOP/s sustained"),
-                         "traffic": _traffic(f"qgemm_pair_{args.quant}_ff_in_{tl}x16384x4096"),
+                         "traffic": _traffic(f"qgemm_pair_{args.quant}_ff_in_{B * tl}x16384x4096"),
                          "algorithmic_per_launch": {"flops": ff_flops,
-                                                    "bytes": tl * VD * 2 + _packed_bytes(args.quant, 4 * VD, VD)
-                                                    + tl * 4 * VD * 2}},
+                                                    "bytes": B * tl * VD * 2 + _packed_bytes(args.quant, 4 * VD, VD)
+                                                    + B * tl * 4 * VD * 2}},
             "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
                     "api": f"ltxq.block.BasicAVTransformerBlock x{n_blocks} (C ABI: ltxq_adaln_modulate, ltxq_qlinear, "
                            "ltxq_qk_norm_rope, ltxq_head_gate)"},
             "gpu_launches": n_launches,
             "weights_gb": weight_bytes / 1e9,
             "clocks": clk.summary(),
-            "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline("step"),
+            "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline(args.workload),
             "device_error": dev_err,
         }
         print(json.dumps(line), flush=True)
@@ -600,6 +746,114 @@ def run_ff(args, world, rank, local, dev):
         print(json.dumps(line), flush=True)
 
 
+def run_config1(args, world, rank, local, dev):
+    """out = x + gate * (modulate(LN(x)) @ W^T + b) at
+    1024 x 4096 -> 4096, affine int8 g64, bf16 vectors, through the public
+    QuantizedLinear call (ltxq_adaln_qlinear: the AdaLN pass, then the GEMM
+    with the gated residual in its epilogue).  value = quantized-GEMM TFLOP/s
+    of the whole call, summed over the replicas."""
+    import torch
+
+    import ltxq
+    from ltxq import _lib
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+
+    def randn(*shape, std=1.0, dtype=torch.bfloat16):
+        return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * std).to(dtype)
+
+    x = randn(1, CFG1_M, CFG1_D)
+    scale, shift, gate = (randn(1, CFG1_D, std=0.1) for _ in range(3))
+    ql = ltxq.QuantizedLinear.from_linear(randn(CFG1_D, CFG1_D, std=0.02), randn(CFG1_D, std=0.01), mode="affine",
+                                          bits=8, group_size=64)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def call():
+        return ql(x, residual=x, gate=gate, adaln=(scale, shift, 1e-6, "layer"))
+
+    def split(evs):  # the same two kernels, with an event between them (roofline of the GEMM)
+        evs[0].record(stream)
+        a = ltxq.adaln_modulate(x, scale, shift, 1e-6, "layer")
+        evs[1].record(stream)
+        y = ql(a, residual=x, gate=gate)
+        evs[2].record(stream)
+        return y
+
+    mk = lambda n: [torch.cuda.Event(enable_timing=True) for _ in range(n)]  # noqa: E731
+    clk = ClockSampler(local).start()
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        call()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    n_launch0 = _lib.launch_count()
+    evs = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e = mk(2)
+        e[0].record(stream)
+        call()
+        e[1].record(stream)
+        evs.append(e)
+    n_launches = _lib.launch_count() - n_launch0
+    parts = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e = mk(3)
+        split(e)
+        parts.append(e)
+    torch.cuda.synchronize()
+    clk.stop()
+    total = _max_over_ranks(sum(a.elapsed_time(b) for a, b in evs), world, dev)
+    gemm_ms = sum(e[1].elapsed_time(e[2]) for e in parts) / len(parts)
+    mod_ms = sum(e[0].elapsed_time(e[1]) for e in parts) / len(parts)
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e = []
+    for i in range(args.steps + 1):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        x_dev.copy_(x_host, non_blocking=True)
+        y = ql(x_dev, residual=x_dev, gate=gate, adaln=(scale, shift, 1e-6, "layer"))
+        out_host.copy_(y, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        if i:
+            e2e.append(e0.elapsed_time(e1))
+    e2e_total = _max_over_ranks(sum(e2e), world, dev)
+    dev_err = _lib.device_error()
+    if rank == 0:
+        hbm, tf_burst, tf_sust, peak_kind = _peaks()
+        achieved = CFG1_FLOPS / (gemm_ms / 1e3) / 1e12
+        w_bytes = _packed_bytes("int8", CFG1_D, CFG1_D) + CFG1_D * 2
+        act_bytes = CFG1_M * CFG1_D * 2 * 3  # modulated x in, residual in, out
+        line = {
+            "metric": METRIC, "value": world * CFG1_FLOPS * args.steps / (total / 1e3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": _config1_config(world),
+            "roofline": {"bound": "tensor", "kernel": "qgemm_pair_kernel<affine8> (gated-residual epilogue)",
+                         "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s", "frac": achieved / tf_burst,
+                         "peak_kind": f"{peak_kind} bf16 burst", "gemm_ms": gemm_ms,
+                         "traffic": _traffic("qgemm_pair_affine8_config1_1024x4096x4096"),
+                         "algorithmic_per_launch": {"flops": CFG1_FLOPS, "bytes": w_bytes + act_bytes}},
+            "adaln_pass": {"ms": mod_ms, "gb_per_s": CFG1_M * CFG1_D * 4 / (mod_ms / 1e3) / 1e9,
+                           "frac_of_hbm": CFG1_M * CFG1_D * 4 / (mod_ms / 1e3) / 1e9 / hbm},
+            "e2e": {"value": world * CFG1_FLOPS * len(e2e) / (e2e_total / 1e3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                    "api": "ltxq.QuantizedLinear(adaln=...) -> ltxq_adaln_qlinear"},
+            "gpu_launches": n_launches, "clocks": clk.summary(),
+            "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline("config1"),
+            "device_error": dev_err,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_ours(args):
     import torch
 
@@ -613,6 +867,8 @@ def run_ours(args):
     try:
         if args.workload == "ff":
             run_ff(args, world, rank, local, dev)
+        elif args.workload == "config1":
+            run_config1(args, world, rank, local, dev)
         else:
             run_step(args, world, rank, local, dev)
     finally:
@@ -629,8 +885,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["step", "ff"], default="step")
-    ap.add_argument("--cpu-sample", type=int, default=None)
+    ap.add_argument("--workload", choices=["step", "config1", "ff", "config3", "config5"], default="step",
+                    help="step = config 4 (the headline); config1, ff (config 2), config3 and config5 are the "
+                         "other BASELINE configurations")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
@@ -646,12 +903,16 @@ def main():
                     help="block-linear quantization of the step workload (config 4 is mxfp8)")
     ap.add_argument("--video-tokens", type=int, default=STEP_T,
                     help="video tokens of the step (9216 = config 4; fewer only to study per-rank shapes on one GPU)")
+    ap.add_argument("--audio-tokens", type=int, default=STEP_A)
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--blocks", type=int, default=STEP_BLOCKS,
                     help="blocks per step (48 = the 22B model; fewer only for bounded profiler captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.cpu_sample is None:
-        args.cpu_sample = 64 if args.workload == "step" else 256
+    args.workload_name = None
+    if args.workload in STEP_PRESETS:
+        (args.blocks, args.quant, args.video_tokens, args.audio_tokens, args.batch,
+         args.workload_name) = STEP_PRESETS[args.workload]
     if args.impl == "reference":
         run_reference(args)
     else:

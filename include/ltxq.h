@@ -134,6 +134,16 @@ ltxq_status ltxq_device_error(int32_t* code_out);
 /* Number of kernels this library has launched in this process (all devices,
  * all threads).  Host-side counter; no device synchronization. */
 uint64_t ltxq_launch_count(void);
+/* Failure-detection self-test (no counterpart in the reference, whose MLX
+ * kernels have no device-side waits).  Launches one warp that waits, through
+ * the same bounded mbarrier wait every GEMM kernel uses, on a barrier phase
+ * nothing completes; after limit_ns (1 us .. 1 s) the wait gives up, writes
+ * the device error word and the kernel returns normally.  Synchronizes
+ * `stream`.  Returns LTXQ_ERR_DEVICE when the expiry was detected and
+ * reported (the expected outcome; the word then stays set until
+ * ltxq_device_error reads and clears it), LTXQ_ERR_CUDA if it was not.
+ * Call it with the error word clear. */
+ltxq_status ltxq_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
 /* ---- bandwidth kernels ------------------------------------------------ */
 /* out[m, :] = modulate(norm(x[m, :])) for m < rows; x/out dtype x_dtype
@@ -200,8 +210,9 @@ ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pr
  * image, held by every GPU that loads the library until exit: M * K must be
  * <= 4194304 (else LTXQ_ERR_UNSUPPORTED, nothing launched).  All calls share
  * that array, so calls that overlap on the GPU race; serialize them.  The
- * first call on a device looks the array's address up (make it before any
- * stream capture).  No cudaMalloc/cudaFree or allocating routine is used. */
+ * first call on a device looks the array's address up, and so does the
+ * first call after a device reset (make those before any stream capture).
+ * No cudaMalloc/cudaFree or allocating routine is used. */
 ltxq_status ltxq_adaln_qlinear_noalloc(const void* x, int64_t M, const ltxq_prologue* pro,
                                        const ltxq_qweight* w, const ltxq_epilogue* epi, void* out,
                                        void* stream);

@@ -13,16 +13,42 @@ namespace ltxq {
 
 __device__ unsigned int g_dev_error = 0;
 
+static PFN_cuCtxGetCurrent_v4000 g_ctx_get = nullptr;
+static std::once_flag g_ctx_once;
+
+void* current_cu_context() {
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  });
+  CUcontext c = nullptr;
+  if (g_ctx_get && g_ctx_get(&c) == CUDA_SUCCESS) return c;
+  return nullptr;
+}
+
+// The error word's address per device, looked up again whenever the calling
+// thread's current context differs from the one it was looked up in.
 unsigned int* dev_error_word() {
-  static unsigned int* addr[64] = {};
+  struct Entry {
+    void* ctx;
+    unsigned int* addr;
+  };
+  static Entry cache[64] = {};
+  static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_dev_error) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<unsigned int*>(p);
-  }
-  return addr[dev];
+  std::lock_guard<std::mutex> lock(mu);
+  Entry& e = cache[dev];
+  const void* ctx = current_cu_context();
+  if (e.addr && ctx && e.ctx == ctx) return e.addr;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_dev_error) != cudaSuccess) return nullptr;
+  e.ctx = current_cu_context();  // the lookup binds the device's context if none was current
+  e.addr = static_cast<unsigned int*>(p);
+  return e.addr;
 }
 
 static std::atomic<uint64_t> g_launches{0};
@@ -87,6 +113,24 @@ int num_sms() {
   return n;
 }
 
+// One warp: lane 0 waits, through the bounded mbarrier wait of the GEMM
+// kernels, for phase 0 of a barrier that expects one arrival and never gets
+// it.  The wait gives up after limit_ns, raises the device error word and the
+// kernel returns normally (no trap, no fault): the failure-detection path of
+// every kernel, exercised on its own.
+__global__ void wait_selftest_kernel(unsigned int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, err, limit_ns);
+  __syncthreads();
+}
+
 }  // namespace ltxq
 
 extern "C" {
@@ -108,6 +152,25 @@ ltxq_status ltxq_device_error(int32_t* code_out) {
   if (st) return st;
   *code_out = static_cast<int32_t>(v);
   return LTXQ_OK;
+}
+
+ltxq_status ltxq_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  if (limit_ns < 1000ull || limit_ns > 1000000000ull)
+    return ltxq::fail(LTXQ_ERR_INVALID, "selftest_wait_timeout: limit_ns must be within [1 us, 1 s]");
+  unsigned int* err = ltxq::dev_error_word();
+  if (!err) return ltxq::fail(LTXQ_ERR_CUDA, "selftest_wait_timeout: device error word unavailable");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ltxq::wait_selftest_kernel<<<1, 32, 0, s>>>(err, limit_ns);
+  if (ltxq_status st = ltxq::launch_check("wait self-test launch")) return st;
+  if (ltxq_status st = ltxq::cuda_check(cudaStreamSynchronize(s), "wait self-test")) return st;
+  unsigned int v = 0;
+  if (ltxq_status st = ltxq::cuda_check(cudaMemcpyFromSymbol(&v, ltxq::g_dev_error, sizeof(v)), "read device error"))
+    return st;
+  if (v == 0) return ltxq::fail(LTXQ_ERR_CUDA, "selftest_wait_timeout: the wait did not report its expiry");
+  char buf[160];
+  snprintf(buf, sizeof(buf), "bounded wait expired after %llu ns as designed (device error word = %u)",
+           static_cast<unsigned long long>(limit_ns), v);
+  return ltxq::fail(LTXQ_ERR_DEVICE, buf);
 }
 
 }  // extern "C"

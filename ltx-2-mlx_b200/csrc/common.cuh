@@ -29,6 +29,12 @@ ltxq_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const vo
 
 int num_sms();
 
+// The CUDA context current on the calling thread (cuCtxGetCurrent through the
+// runtime's driver entry point), or nullptr.  Caches of device-symbol
+// addresses are keyed by it, so that an address looked up in one context is
+// never used after the device is reset and a new context loads the module.
+void* current_cu_context();
+
 // Device error word (bounded waits that expire write a code here); kernels
 // receive its address as a parameter.
 unsigned int* dev_error_word();
@@ -132,17 +138,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (after raising the CTA abort flag and the
-// device error word) if the phase does not complete within kWaitTimeoutNs,
-// or if another role of this CTA already aborted.
+// device error word) if the phase does not complete within limit_ns
+// (kWaitTimeoutNs for every production kernel), or if another role of this
+// CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned int* err) {
+                                          unsigned int* err, unsigned long long limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort_flag = 1;
         atomicCAS(err, 0u, kErrWaitTimeout);
         return false;

@@ -24,7 +24,10 @@
 //    the array, so callers must serialize them;
 //  * the first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress, once per device, with that device current) and
-//    caches it.  Make that first call before any stream capture.
+//    caches it.  Make that first call before any stream capture.  The cache
+//    is keyed by the CUDA context as well: after a cudaDeviceReset the next
+//    call looks the address up again in the new context (again outside any
+//    capture).
 //  * no cudaMalloc, cudaFree or allocating library routine is called.
 #include <mutex>
 
@@ -43,22 +46,30 @@ constexpr size_t kNoAllocScratchElems = size_t(4) << 20;  // bf16 values (8 MiB)
 // runtime's symbol lookup, never a device address.
 static __device__ __align__(256) uint16_t g_noalloc_scratch[kNoAllocScratchElems];
 
-// Device address of g_noalloc_scratch on the current device (looked up once
-// per device and cached).
+// Device address of g_noalloc_scratch on the current device: looked up once
+// per device and context, cached, and looked up again when the calling
+// thread's current context is not the one the address came from.
 static ltxq_status noalloc_scratch(void** out) {
-  static void* addr[64] = {};
+  struct Entry {
+    void* ctx;
+    void* addr;
+  };
+  static Entry cache[64] = {};
   static std::mutex mu;
   int dev = 0;
   if (ltxq_status st = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return st;
   if (dev < 0 || dev >= 64) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_qlinear_noalloc: device ordinal >= 64");
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  Entry& e = cache[dev];
+  const void* ctx = current_cu_context();
+  if (!e.addr || !ctx || e.ctx != ctx) {
     void* p = nullptr;
     if (ltxq_status st = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)"))
       return st;
-    addr[dev] = p;
+    e.ctx = current_cu_context();  // the lookup binds the device's context if none was current
+    e.addr = p;
   }
-  *out = addr[dev];
+  *out = e.addr;
   return LTXQ_OK;
 }
 

@@ -77,6 +77,7 @@ SIGNATURES = {
     "ltxq_version": (c_char_p, []),
     "ltxq_device_error": (c_int32, [POINTER(c_int32)]),
     "ltxq_launch_count": (ctypes.c_uint64, []),
+    "ltxq_selftest_wait_timeout": (c_int32, [ctypes.c_uint64, c_void_p]),
     "ltxq_qweight_scan": (c_int32, [POINTER(QWeight), POINTER(ctypes.c_uint32), c_void_p]),
     "ltxq_adaln_modulate": (c_int32, [c_void_p, c_int32, c_int64, c_int64, POINTER(Prologue), c_void_p, c_void_p]),
     "ltxq_gated_add": (c_int32, [c_void_p, c_void_p, POINTER(Vec), c_int64, c_int64, c_int32, c_void_p, c_void_p]),

@@ -23,7 +23,10 @@ positive inputs through blocks that skip the perturbed attention
 sub-layers) until ``stg_cutoff`` of the steps, and the video update adds
 the STG term after CFG, as av_pipeline.py:706-717 does.
 
-Not built: the Heun stepper and the non-AV / two-stage pipelines.
+``denoise_heun_av`` is ``_denoise_loop_heun_av`` (av_pipeline.py:758-897):
+Euler predictor and Heun corrector in fp32 torch (``HeunDiffusionStep``).
+
+Not built: the non-AV / two-stage pipelines.
 """
 
 from __future__ import annotations

@@ -11,15 +11,22 @@ import numpy as np
 
 
 def f32_to_bf16_bits(x) -> np.ndarray:
-    """RNE float32 -> bf16 bit pattern (uint16).  NaN stays a quiet NaN."""
-    x = np.array(x, dtype=np.float32, copy=True)
-    u = x.view(np.uint32).astype(np.uint64)
-    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
-    out = rounded.astype(np.uint16)
+    """RNE float32 -> bf16 bit pattern (uint16).  NaN stays a quiet NaN.
+
+    uint32 arithmetic: u + 0x7FFF + lsb cannot wrap for any non-NaN pattern
+    (the largest, -inf = 0xFF800000, stays below 2**32); NaN patterns, the
+    only ones that could wrap, are rewritten afterwards."""
+    x = np.asarray(x, dtype=np.float32, order="C")
+    u = x.view(np.uint32)
+    r = (u >> 16) & 1
+    r += u
+    r += 0x7FFF
+    r >>= 16
+    out = np.asarray(r.astype(np.uint16))
     nan = np.isnan(x)
     if nan.any():
-        out = np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), out)
-    return out
+        out[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return out[()] if out.ndim == 0 else out
 
 
 def bf16_bits_to_f32(b) -> np.ndarray:
@@ -28,8 +35,20 @@ def bf16_bits_to_f32(b) -> np.ndarray:
 
 
 def rbf16(x) -> np.ndarray:
-    """Round float32 values to the nearest bf16 value (result stays float32)."""
-    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+    """Round float32 values to the nearest bf16 value (result stays float32).
+    The same rounding as ``bf16_bits_to_f32(f32_to_bf16_bits(x))``, done in
+    place on uint32 patterns."""
+    x = np.asarray(x, dtype=np.float32, order="C")
+    u = x.view(np.uint32)
+    r = np.asarray((u >> 16) & 1)
+    r += u
+    r += 0x7FFF
+    r &= 0xFFFF0000
+    nan = np.isnan(x)
+    if nan.any():
+        r[nan] = (u[nan] & 0xFFFF0000) | 0x400000
+    out = r.view(np.float32)
+    return out[()] if out.ndim == 0 else out
 
 
 def f64_to_f32_round_to_odd(x) -> np.ndarray:

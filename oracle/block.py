@@ -44,19 +44,27 @@ def apply_split_rope(x, cos, sin, heads):
     return rbf16(out.astype(np.float32)).transpose(1, 0, 2).reshape(t, width)
 
 
-def sdpa(q, k, v, heads):
-    """mx.fast.scaled_dot_product_attention, no mask: fp32 softmax, bf16 out."""
+def sdpa(q, k, v, heads, max_scores: int = 1 << 28):
+    """mx.fast.scaled_dot_product_attention, no mask: fp32 softmax, bf16 out.
+    Heads are independent, so they are processed in groups whose score
+    matrices hold at most ``max_scores`` fp32 values (same result, bounded
+    memory at long sequences)."""
     tq, width = q.shape
     tk = k.shape[0]
     d = width // heads
     qh = np.asarray(q, np.float32).reshape(tq, heads, d).transpose(1, 0, 2)
     kh = np.asarray(k, np.float32).reshape(tk, heads, d).transpose(1, 0, 2)
     vh = np.asarray(v, np.float32).reshape(tk, heads, d).transpose(1, 0, 2)
-    s = (qh @ kh.transpose(0, 2, 1)) * np.float32(1.0 / np.sqrt(d))
-    s = s - s.max(-1, keepdims=True)
-    e = np.exp(s)
-    o = (e / e.sum(-1, keepdims=True)) @ vh
-    return rbf16(o.astype(np.float32)).transpose(1, 0, 2).reshape(tq, width)
+    o = np.empty((heads, tq, d), np.float32)
+    step = max(1, min(heads, max_scores // max(1, tq * tk)))
+    for h0 in range(0, heads, step):
+        sl = slice(h0, h0 + step)
+        s = (qh[sl] @ kh[sl].transpose(0, 2, 1)) * np.float32(1.0 / np.sqrt(d))
+        s -= s.max(-1, keepdims=True)
+        np.exp(s, out=s)
+        s /= s.sum(-1, keepdims=True)
+        o[sl] = s @ vh[sl]
+    return rbf16(o).transpose(1, 0, 2).reshape(tq, width)
 
 
 def attention(p, name, x, context=None, pe=None, k_pe=None, heads=32, eps=1e-6):

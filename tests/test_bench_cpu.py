@@ -40,3 +40,41 @@ def test_step_config_names_the_exchange():
     cfg = bench._step_config(1)
     assert cfg["workload"] == "config4_22b_denoise_step_mxfp8g32" and cfg["video_tokens"] == 9216
     assert cfg["blocks"] == 48 and cfg["audio_tokens"] == 201 and cfg["text_tokens"] == 1024
+
+
+def test_cpu_block_rotation_times_every_sublayer_and_sums_them():
+    """The reference arm's unit: each timed step runs one sub-layer of the
+    block at full size in turn; every sub-layer is timed at least once and a
+    block is the sum of the sub-layer means (a stub stands in for the numpy
+    work here)."""
+    import bench
+
+    class Stub:
+        video_tokens, audio_tokens, quant = 9216, 201, "mxfp8"
+
+        def __init__(self):
+            self.calls = []
+
+        def run(self, sub):
+            self.calls.append(sub)
+            return 1.0 + list(bench.CpuBlock.SUBLAYERS).index(sub)
+
+    stub = Stub()
+    per_sub = bench._cpu_block_rotation(stub, 3, warmup=2)
+    assert set(per_sub) == set(bench.CpuBlock.SUBLAYERS) and len(stub.calls) == 2 + 7
+    assert sum(per_sub.values()) == pytest.approx(sum(range(1, 8)))
+    ms, desc = bench._cpu_block_line(per_sub, stub, 48)
+    assert ms == pytest.approx(28.0 * 48 * 1e3) and "extrapolated x48" in desc and "attention included" in desc
+    ms1, desc1 = bench._cpu_block_line(per_sub, stub, 1)
+    assert ms1 == pytest.approx(28.0 * 1e3) and "not extrapolated" in desc1
+
+
+def test_presets_name_the_baseline_configs():
+    import bench
+
+    assert bench.STEP_PRESETS["config3"][:5] == (1, "int8", 3456, 126, 1)
+    assert bench.STEP_PRESETS["config5"][:5] == (48, "int4", 30576, 751, 2)
+    cfg = bench._step_config(1, 48, True, "int4", 30576, audio_tokens=751, batch=2,
+                             workload=bench.STEP_PRESETS["config5"][5])
+    assert cfg["global_batch"] == 2 and cfg["audio_tokens"] == 751 and cfg["workload"].startswith("config5")
+    assert bench._config1_config(1)["workload"].startswith("config1")

@@ -89,3 +89,11 @@ def test_denoise_update_validation_without_gpu(lib):
     assert call(ok, mask=16) == _lib.ERR_INVALID  # a mask needs the clean latent
     assert call(ok, latent=24) == _lib.ERR_UNSUPPORTED  # 16-byte alignment
     assert call(ok, latent=None, v_cond=None, out=None, b=0) == _lib.OK  # empty: nothing to do
+
+
+def test_selftest_limits_checked_without_gpu(lib):
+    from ltxq import _lib
+
+    assert lib.ltxq_selftest_wait_timeout(0, None) == _lib.ERR_INVALID
+    assert b"limit_ns" in lib.ltxq_last_error()
+    assert lib.ltxq_selftest_wait_timeout(2_000_000_000, None) == _lib.ERR_INVALID

@@ -6,8 +6,10 @@ pool, a plugin inside another framework's allocator, a loop where a
 cudaMalloc would synchronize the device).  Its scratch is a fixed array in the
 library's device image.  This test calls it through the C ABI twice in a row,
 with different inputs, and checks each result against the workspace-taking
-entry point ltxq_adaln_qlinear on the same inputs, within the GEMM tolerance
-used by the other parity tests.  The file is named to be collected last.
+entry point ltxq_adaln_qlinear on the same inputs and against the numpy
+oracle's AdaLN + affine int8 g64 linear + gated residual composition, within
+the GEMM tolerance used by the other parity tests.  The file is named to be
+collected last.
 """
 
 import ctypes
@@ -30,19 +32,22 @@ def _case(seed, M, K, N):
     from ltxq import _lib
 
     g = rng(seed)
-    x = to_dev_bf16(normal_bf16(g, (M, K)))
+    x_h = normal_bf16(g, (M, K))
     W = normal_bf16(g, (N, K), 0.02)
     q = oq.quantize(W, "affine", 64, 8)
+    host = {"x": x_h, "q": q, "bias": normal_bf16(g, (N,), 0.01), "scale": normal_f32(g, (K,), 0.1),
+            "shift": normal_f32(g, (K,), 0.1), "gate": normal_f32(g, (N,), 0.1), "res": normal_bf16(g, (M, N))}
     keep = {
-        "x": x,
+        "x": to_dev_bf16(x_h),
         "w": to_dev(q["weight"]),
         "s": to_dev(q["scales"]),
         "b": to_dev(q["biases"]),
-        "bias": to_dev_bf16(normal_bf16(g, (N,), 0.01)),
-        "scale": torch.from_numpy(normal_f32(g, (K,), 0.1)).cuda(),
-        "shift": torch.from_numpy(normal_f32(g, (K,), 0.1)).cuda(),
-        "gate": torch.from_numpy(normal_f32(g, (N,), 0.1)).cuda(),
-        "res": to_dev_bf16(normal_bf16(g, (M, N))),
+        "bias": to_dev_bf16(host["bias"]),
+        "scale": torch.from_numpy(host["scale"]).cuda(),
+        "shift": torch.from_numpy(host["shift"]).cuda(),
+        "gate": torch.from_numpy(host["gate"]).cuda(),
+        "res": to_dev_bf16(host["res"]),
+        "host": host,
     }
     qw = _lib.QWeight(keep["w"].data_ptr(), keep["s"].data_ptr(), keep["b"].data_ptr(), keep["bias"].data_ptr(),
                       N, K, _lib.AFFINE, 8, 64, _lib.LAYOUT_STD)
@@ -90,6 +95,12 @@ def test_no_alloc_entry_point_matches_workspace_entry_point_twice(cuda):
         torch.cuda.synchronize()
         mar, cos = ro.max_abs_rel(got, want), ro.cosine(got, want)
         assert mar <= MAX_ABS_REL and cos >= COS_MIN, f"call seed={seed}: max_abs_rel={mar:.3e} cos={cos:.6f}"
+        h = keep["host"]
+        y = ro.linear(ro.adaln(h["x"], h["scale"], h["shift"], 1e-6, "rms"), oq.dequantize(h["q"], K), h["bias"])
+        ref = ro.gated_add(h["res"], y, h["gate"])
+        for name, out in (("no-alloc", got), ("workspace", want)):
+            mar, cos = ro.max_abs_rel(out, ref), ro.cosine(out, ref)
+            assert mar <= MAX_ABS_REL and cos >= COS_MIN, f"{name} seed={seed} vs oracle: {mar:.3e} {cos:.6f}"
     assert _lib.device_error() == 0
 
 
