@@ -570,6 +570,13 @@ class BasicAVTransformerBlock:
         if run_a2v:
             o = at.core(q, k, v, gl, video.cross_positional_embeddings, audio.cross_positional_embeddings)
             vx = at.to_out(o, residual=vx, gate=g_a2v)
+        # video feed-forward (transformer.py:629-650).  It reads vx after the
+        # audio->video update and nothing of the video->audio attention (which
+        # only updates ax, from norms taken before either update), so it runs
+        # here: in a row-sharded run the video->audio K/V all-gather, started
+        # above, overlaps the block's largest GEMMs.  Same results as the
+        # reference's order.
+        vx = self._ff(vx, video, "scale_shift_table", self.ff)
         # video->audio: the audio queries are on every rank, the video keys
         # are split by rows.  "split_keys": each rank attends over its rows
         # and the partial results merge by their log-sum-exp (a ~1 MB exchange
@@ -583,8 +590,7 @@ class BasicAVTransformerBlock:
                 o2 = at2.attend(q2, k2, v2, gl2)
             ax = at2.to_out(o2, residual=ax, gate=g_v2a)
 
-        # feed-forwards (transformer.py:629-668)
-        vx = self._ff(vx, video, "scale_shift_table", self.ff)
+        # audio feed-forward (transformer.py:652-668)
         ax = self._ff(ax, audio, "audio_scale_shift_table", self.audio_ff)
         return video.replace(x=vx), audio.replace(x=ax)
 

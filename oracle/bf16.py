@@ -9,14 +9,23 @@ from __future__ import annotations
 
 import numpy as np
 
+from . import _par
+
 
 def f32_to_bf16_bits(x) -> np.ndarray:
     """RNE float32 -> bf16 bit pattern (uint16).  NaN stays a quiet NaN.
 
     uint32 arithmetic: u + 0x7FFF + lsb cannot wrap for any non-NaN pattern
     (the largest, -inf = 0xFF800000, stays below 2**32); NaN patterns, the
-    only ones that could wrap, are rewritten afterwards."""
+    only ones that could wrap, are rewritten afterwards.  Large arrays are
+    processed in row chunks on every host thread (same bits)."""
     x = np.asarray(x, dtype=np.float32, order="C")
+    if x.size >= _par.MIN_ELEMS:
+        return _par.chunked(_f32_to_bf16_bits, x)
+    return _f32_to_bf16_bits(x)
+
+
+def _f32_to_bf16_bits(x):
     u = x.view(np.uint32)
     r = (u >> 16) & 1
     r += u
@@ -39,6 +48,12 @@ def rbf16(x) -> np.ndarray:
     The same rounding as ``bf16_bits_to_f32(f32_to_bf16_bits(x))``, done in
     place on uint32 patterns."""
     x = np.asarray(x, dtype=np.float32, order="C")
+    if x.size >= _par.MIN_ELEMS:
+        return _par.chunked(_rbf16, x)
+    return _rbf16(x)
+
+
+def _rbf16(x):
     u = x.view(np.uint32)
     r = np.asarray((u >> 16) & 1)
     r += u

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import numpy as np
 
+from . import _par
 from . import ref_ops as ro
 from .bf16 import rbf16
 
@@ -44,6 +45,14 @@ def apply_split_rope(x, cos, sin, heads):
     return rbf16(out.astype(np.float32)).transpose(1, 0, 2).reshape(t, width)
 
 
+def _softmax_rows(s):
+    """Row softmax in fp32 (max-subtracted), in place on a fresh array."""
+    s = s - s.max(-1, keepdims=True)
+    np.exp(s, out=s)
+    s /= s.sum(-1, keepdims=True)
+    return s
+
+
 def sdpa(q, k, v, heads, max_scores: int = 1 << 28):
     """mx.fast.scaled_dot_product_attention, no mask: fp32 softmax, bf16 out.
     Heads are independent, so they are processed in groups whose score
@@ -60,9 +69,7 @@ def sdpa(q, k, v, heads, max_scores: int = 1 << 28):
     for h0 in range(0, heads, step):
         sl = slice(h0, h0 + step)
         s = (qh[sl] @ kh[sl].transpose(0, 2, 1)) * np.float32(1.0 / np.sqrt(d))
-        s -= s.max(-1, keepdims=True)
-        np.exp(s, out=s)
-        s /= s.sum(-1, keepdims=True)
+        s = _par.chunked(_softmax_rows, s.reshape(-1, tk)).reshape(s.shape)
         o[sl] = s @ vh[sl]
     return rbf16(o).transpose(1, 0, 2).reshape(tq, width)
 

@@ -18,6 +18,7 @@ import math
 
 import numpy as np
 
+from . import _par
 from .bf16 import rbf16
 
 EPS = 1e-6
@@ -111,9 +112,17 @@ _C_SQRT = float(rbf16(np.float32(math.sqrt(2.0 / math.pi))))
 
 def gelu_approx(x_bf16):
     """``0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x**3)))`` on a bf16
-    array: each op rounds to bf16 and the constants are bf16."""
+    array: each op rounds to bf16 and the constants are bf16.  (Large arrays
+    run in row chunks on every host thread; element-wise, so the same bits.)"""
     x = _f32(x_bf16)
-    x3 = rbf16(x.astype(np.float64) ** 3)
+    if x.size >= _par.MIN_ELEMS:
+        return _par.chunked(_gelu_approx, x)
+    return _gelu_approx(x)
+
+
+def _gelu_approx(x):
+    x64 = x.astype(np.float64)
+    x3 = rbf16(x64 * x64 * x64)  # x**3, exact in float64 for bf16 x
     t = rbf16(np.float32(_C_GELU) * x3)
     t = rbf16(x + t)
     t = rbf16(np.float32(_C_SQRT) * t)
