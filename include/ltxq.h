@@ -76,6 +76,25 @@ enum {
   LTXQ_QW_MXFP8_FINITE = 1
 };
 
+/* ltxq_qweight.compute: how a GEMM over this weight computes.
+ *  DEQUANT: the weight is dequantized to bf16 in the kernel (exact) and
+ *    multiplied by the bf16 activations on kind::f16 tensor cores; the only
+ *    difference from the reference composition is the fp32 summation order.
+ *  MX2 (mxfp8 weights): native block-scaled fp8 MMAs (kind::mxf8f6f4) on the
+ *    cache's E4M3 codes and E8M0 scales, no dequantization; the activations
+ *    are split into two MXFP8 terms x = hi + lo (per 32 K: E8M0 scale, E4M3
+ *    codes, no saturation), which keeps each to about 2^-8 of its group's
+ *    largest magnitude.
+ *  MX1 (mxfp8 weights): as MX2 with one term, about 2^-4 of the group's
+ *    largest magnitude: roughly twice the MMA rate of MX2, but it does not
+ *    meet this path's stated tolerance against the reference (opt-in).
+ * The MX modes apply to the standard layout with K a multiple of 512 and at
+ * least one 256 x 192 output tile per two SMs; other GEMMs over the same
+ * weight run the DEQUANT kernels.  The MX modes need workspace for the split
+ * activations (ltxq_qlinear_workspace_size accounts for it); given less,
+ * the GEMM runs the DEQUANT kernels. */
+enum { LTXQ_COMPUTE_DEQUANT = 0, LTXQ_COMPUTE_MX2 = 1, LTXQ_COMPUTE_MX1 = 2 };
+
 /* A quantized linear layer in the reference's MLX cache layout
  * (loader/transformer_cache.py:1238-1267, 1436-1462).
  *  affine:  weight uint32 [N, K*bits/32], scales/biases bf16 [N, K/gs]
@@ -95,7 +114,7 @@ typedef struct {
   int32_t group_size; /* 64 (affine), 32 (mxfp8) */
   int32_t layout;     /* LTXQ_LAYOUT_STD / LTXQ_LAYOUT_PRETRANSPOSED */
   uint32_t flags;     /* LTXQ_QW_* (0 = none asserted) */
-  int32_t pad_;
+  int32_t compute;    /* LTXQ_COMPUTE_*: how the GEMM computes (0 = dequantize to bf16) */
 } ltxq_qweight;
 
 /* Per-channel vectors (AdaLN scale/shift/gate).  Element (row m, channel c)
@@ -200,6 +219,21 @@ ltxq_status ltxq_qlinear(const void* x, int64_t M, const ltxq_qweight* w, const 
 ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pro,
                                const ltxq_qweight* w, const ltxq_epilogue* epi, void* out,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Activation quantization of the LTXQ_COMPUTE_MX* path (no counterpart in
+ * the reference, whose mxfp8 matmul dequantizes the weight instead): bf16
+ * x [M, K] (K % 128 == 0) -> `terms` MXFP8 terms, x = hi (+ lo).  Per group
+ * of 32 consecutive K: E8M0 scale 2^e with the smallest e >= -127 for which
+ * max|v| * 2^-e <= 448, E4M3 codes RNE(v * 2^-e); the second term quantizes
+ * the residual x - hi the same way.  Codes: [M, K] bytes per term.  Scales:
+ * in the block-scaled MMA's atom layout -- atom (k-tile j = k / 128, row
+ * tile t = m / 128) at (j * row_tiles + t) * 512 holds the scale of row
+ * t*128 + 32*m1 + m0, group 4j + k1 at byte m0*16 + m1*4 + k1; row_tiles
+ * = ceil(M / 128) + 1 (the last tile is zero rows).  ltxq_mx_split_sizes
+ * returns row_tiles and the byte sizes of one term's codes and scales. */
+size_t ltxq_mx_split_sizes(int64_t M, int64_t K, size_t* codes_bytes, size_t* scale_bytes);
+ltxq_status ltxq_mx_split(const void* x, int64_t M, int64_t K, int32_t terms, void* hi, void* lo, void* sf_hi,
+                          void* sf_lo, void* stream);
 
 /* ltxq_adaln_qlinear without a workspace argument and without allocating.
  * No counterpart in the reference.  For hosts that cannot let a library

@@ -1,0 +1,679 @@
+// mx.cu -- native block-scaled fp8 path for mxfp8 weights: tcgen05.mma
+// kind::mxf8f6f4 with E8M0 scale factors in tensor memory, no weight
+// dequantization.
+//
+// The reference's mxfp8 cache (loader/transformer_cache.py:26-33, 840-848,
+// 1436-1462) stores every block linear as E4M3 codes with one E8M0 scale per
+// 32 consecutive K -- exactly the OCP MX operand format of the tensor cores'
+// block-scaled fp8 MMA.  This path hands the packed weight to the MMA as it
+// is and converts the bf16 activations to MXFP8 first, in one or two terms:
+//
+//   x = hi + lo,  hi = MX(x),  lo = MX(x - hi)   (two terms: the default form)
+//   x ~ hi                                       (one term: faster, coarser)
+//
+// MX(v): per group of 32 consecutive K, the E8M0 scale 2^e with the smallest
+// e for which max|v| * 2^-e <= 448 (E4M3's largest value, so nothing
+// saturates) and the codes RNE_E4M3(v * 2^-e).  Both terms accumulate into
+// the same fp32 TMEM accumulator (W hi + W lo), so the two-term form keeps
+// each activation to about 2^-8 of its group's largest magnitude (a bf16
+// input has 2^-9 relative precision); the one-term form keeps about 2^-4.
+// The weight operand is exact (E4M3 times its E8M0 scale), as on the
+// dequantizing path.  From the fp32 accumulator on, the epilogue is the
+// dequantizing path's: bf16(acc), bias, GELU / gated residual with the
+// reference's rounding points.
+//
+// Kernel (persistent, clusters of two CTAs, tcgen05 cta_group::2): each tile
+// is 256 output features x 192 tokens; CTA r holds features [n0 + 128 r,
+// +128) of the weight (A, K-major, 128-byte swizzle, straight from the cache
+// by TMA) and tokens [m0 + 96 r, +96) of each activation term (B).  Per
+// 128-K stage the leader copies the scale factors into TMEM with tcgen05.cp
+// (weight scales repacked in shared memory by a helper warp from the cache's
+// row-major [N, K/32] array; activation scales written by the splitter in the
+// MMA's layout) and issues 4 MMAs (K = 32 each) per term.  Two 192-column
+// accumulators let the epilogue of one tile run while the next accumulates.
+// Every wait is bounded (common.cuh mbar_wait); no TMA load uses cluster
+// multicast.
+#include "common.cuh"
+#include "gemm_epilogue.cuh"
+
+namespace ltxq {
+namespace mx {
+
+constexpr int kGroup = 32;   // K values per E8M0 scale
+constexpr int kAtom = 512;   // scale-factor atom: 128 rows x 4 groups (one 128-K tile)
+constexpr int BM = 128;      // output features per CTA (MMA M = 256 per pair)
+constexpr int BN = 192;      // tokens per tile (MMA N)
+constexpr int BNC = BN / 2;  // tokens per CTA
+constexpr int BK = 128;      // K per stage = bytes of one fp8 row
+constexpr int kThreads = 224;  // warps 0-3 epilogue, 4 TMA, 5 MMA, 6 scale repack
+constexpr int kTmaWarp = 4, kMmaWarp = 5, kSfWarp = 6;
+constexpr uint32_t kSfaCol = 2 * BN;       // weight scale factors: 4 TMEM columns
+constexpr uint32_t kSfbCol = kSfaCol + 8;  // activation scale factors of term t: 8 columns at kSfbCol + 16 t
+constexpr uint32_t kTmemCols = 512;
+constexpr int kGroupM = 16;  // token tiles that walk a feature tile together (L2 reuse of the weight)
+
+// ---------------------------------------------------------------- numerics
+
+// E8M0 exponent of a group whose largest magnitude is amax: the smallest e
+// with amax * 2^-e <= 448, and at least -127 (the smallest E8M0 value).
+__device__ __forceinline__ int group_exp(float amax) {
+  const uint32_t b = __float_as_uint(amax);
+  const int ef = static_cast<int>(b >> 23);
+  if (ef == 0) return -127;  // zero or an fp32 subnormal
+  // amax = m 2^E, m in [1, 2): 256 m <= 448 exactly when m <= 1.75
+  const int e = ef - 127 - 8 + ((b & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+  return e < -127 ? -127 : e;
+}
+
+// 2^e for e in [-127, 127]
+__device__ __forceinline__ float exp2i(int e) {
+  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(0x00400000u);
+}
+
+// four fp32 values -> four E4M3 codes (RNE, saturating at +-448), value 0 in the low byte
+__device__ __forceinline__ uint32_t to_e4m3x4(float a0, float a1, float a2, float a3) {
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(a1), "f"(a0));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(a3), "f"(a2));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// the exact values of four E4M3 codes (code 0 = low byte)
+__device__ __forceinline__ void e4m3x4_values(uint32_t c, float (&v)[4]) {
+  uint32_t h0, h1;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h0) : "h"(static_cast<uint16_t>(c & 0xFFFFu)));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h1) : "h"(static_cast<uint16_t>(c >> 16)));
+  v[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(h0 & 0xFFFFu)));
+  v[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(h0 >> 16)));
+  v[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(h1 & 0xFFFFu)));
+  v[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(h1 >> 16)));
+}
+
+// Converts the 32 values of v (in place) to one MX term: codes c, E8M0 byte
+// s; v becomes the residual v - decode(c) * 2^e when kResidual.
+template <bool kResidual>
+__device__ __forceinline__ void mx_term(float (&v)[32], uint32_t (&c)[8], uint32_t& s) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const int e = group_exp(amax);
+  const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e, e in [-127, 121]
+  s = static_cast<uint32_t>(e + 127);
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    c[w] = to_e4m3x4(v[4 * w] * inv, v[4 * w + 1] * inv, v[4 * w + 2] * inv, v[4 * w + 3] * inv);
+  if (kResidual) {
+    const float sc = exp2i(e);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float d[4];
+      e4m3x4_values(c[w], d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[4 * w + i] = __fsub_rn(v[4 * w + i], __fmul_rn(d[i], sc));  // exact
+    }
+  }
+}
+
+// ---------------------------------------------------------------- activation splitter
+
+// One thread per group of 32 K values of a row.  Rows run over whole
+// 128-row tiles plus one spare tile (its scales are those of zero rows), so
+// that every tile the GEMM reads scale atoms from exists.  Codes: [M, K]
+// bytes row-major per term.  Scales: atom (k-tile j, row tile t) at
+// sf + (j * tiles + t) * 512 holds the scales of rows t*128 + 32*m1 + m0 for
+// groups 4j + k1 at byte m0*16 + m1*4 + k1 -- the layout tcgen05.cp.32x128b
+// .warpx4 moves into TMEM for the block-scaled MMA.
+template <int kTerms>
+__global__ void __launch_bounds__(256) mx_split_kernel(const uint16_t* __restrict__ x, int64_t M, int K,
+                                                       int64_t rows, int tiles, uint8_t* __restrict__ hi,
+                                                       uint8_t* __restrict__ lo, uint8_t* __restrict__ sf_hi,
+                                                       uint8_t* __restrict__ sf_lo) {
+  const int G = K / kGroup;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool live = t < rows * G;
+  const int64_t row = live ? t / G : 0;
+  const int g = live ? static_cast<int>(t - row * G) : 0;
+  const bool valid = live && row < M;
+  float v[32];
+  if (valid) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * K + static_cast<int64_t>(g) * kGroup);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 a = __ldg(src + q);
+      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[8 * q + 2 * i] = lo_bf16(w[i]);
+        v[8 * q + 2 * i + 1] = hi_bf16(w[i]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+  }
+  uint32_t c[8], s0 = 0, s1 = 0;
+  mx_term<kTerms == 2>(v, c, s0);
+  if (valid) {
+    uint4* dst = reinterpret_cast<uint4*>(hi + row * K + static_cast<int64_t>(g) * kGroup);
+    dst[0] = make_uint4(c[0], c[1], c[2], c[3]);
+    dst[1] = make_uint4(c[4], c[5], c[6], c[7]);
+  }
+  if (kTerms == 2) {
+    mx_term<false>(v, c, s1);
+    if (valid) {
+      uint4* dst = reinterpret_cast<uint4*>(lo + row * K + static_cast<int64_t>(g) * kGroup);
+      dst[0] = make_uint4(c[0], c[1], c[2], c[3]);
+      dst[1] = make_uint4(c[4], c[5], c[6], c[7]);
+    }
+  }
+  // lanes 4i..4i+3 hold the four groups of one 128-K tile of one row
+  // (G % 4 == 0 and a row starts at a thread index divisible by 4)
+  const int lane = threadIdx.x & 31, base = lane & ~3;
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w0 |= (__shfl_sync(0xffffffffu, s0, base + i) & 0xFFu) << (8 * i);
+    w1 |= (__shfl_sync(0xffffffffu, s1, base + i) & 0xFFu) << (8 * i);
+  }
+  if (live && (g & 3) == 0) {
+    const int64_t j = g >> 2, tile = row >> 7;
+    const int mi = static_cast<int>(row & 127);
+    const int64_t off = (j * tiles + tile) * kAtom + (mi & 31) * 16 + (mi >> 5) * 4;
+    *reinterpret_cast<uint32_t*>(sf_hi + off) = w0;
+    if (kTerms == 2) *reinterpret_cast<uint32_t*>(sf_lo + off) = w1;
+  }
+}
+
+// ---------------------------------------------------------------- PTX wrappers
+
+// cp.async.bulk (no tensor map, no multicast): `bytes` from global to this
+// CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Shared-memory descriptor of a scale-factor atom for tcgen05.cp: K-major,
+// no swizzle, 32 rows of 16 bytes (8-row core matrices 128 bytes apart).
+__device__ __forceinline__ uint64_t sf_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(128u >> 4) << 32;  // stride byte offset
+  d |= static_cast<uint64_t>(1u) << 46;         // descriptor version
+  return d;
+}
+
+// Copies a 32-row x 128-bit shared-memory matrix into TMEM lanes 0-31,
+// replicated to all four lane quarters, in both CTAs of the pair (each from
+// its own shared memory at the same offset).
+__device__ __forceinline__ void sf_copy_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Instruction descriptor of kind::mxf8f6f4 with E8M0 scales: E4M3 A and B,
+// K-major, fp32 accumulate; sf_id picks the scale byte of the 32-bit scale
+// word for both operands.
+__host__ __device__ constexpr uint32_t idesc_mx(uint32_t M, uint32_t N, uint32_t sf_id) {
+  return (sf_id << 4)          // B scale-factor byte
+         | ((N >> 3) << 17)    // N / 8
+         | (1u << 23)          // scale format: E8M0
+         | ((M >> 4) << 24)    // M / 16
+         | (sf_id << 29);      // A scale-factor byte
+}
+
+// D[tmem] (+)= (A * SFA) (B * SFB)^T on the CTA pair, both operands from
+// shared memory.
+__device__ __forceinline__ void mma_mx_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                            uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- GEMM
+
+template <int kTerms>
+struct Plan {
+  static constexpr int kA = BM * BK;        // weight tile, 16 KB
+  static constexpr int kB = BNC * BK;       // one term's activation tile, 12 KB
+  static constexpr int kSfaRaw = BM * 16;   // 16 scale bytes of each weight row
+  static constexpr int kSfb = 2 * kAtom;    // one term's scales: the two 128-token atoms a tile touches
+  static constexpr int kStage = kA + kTerms * kB + kSfaRaw + kAtom + kTerms * kSfb;
+  static constexpr int kStg = 4 * 32 * 32 * 2;  // per-warp 32 x 32 transpose tiles of the epilogue
+  static constexpr int kFixed = 1024 + kStg + 512 + gemm::kGeluTabBytes;
+  static constexpr int kStagesRaw = (227 * 1024 - kFixed) / kStage;
+  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kAOff = 0;
+  static constexpr int kBOff = kAOff + kStages * kA;  // term t, stage s at kBOff + (t * kStages + s) * kB
+  static constexpr int kSfaRawOff = kBOff + kTerms * kStages * kB;
+  static constexpr int kSfaAtomOff = kSfaRawOff + kStages * kSfaRaw;
+  static constexpr int kSfbOff = kSfaAtomOff + kStages * kAtom;  // stage s, term t at kSfbOff + (s * kTerms + t) * kSfb
+  static constexpr int kStgOff = kSfbOff + kStages * kTerms * kSfb;
+  static constexpr int kBarOff = kStgOff + kStg;
+  static constexpr int kTabOff = kBarOff + 512;
+  static constexpr int kSmem = 1024 + kTabOff + gemm::kGeluTabBytes;
+  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
+  static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kBOff % 1024 == 0, "128B-swizzle atoms need 1024-byte alignment");
+  static_assert(4 * kStages * 8 + 4 * 8 + 8 <= 512, "barrier area");
+};
+
+template <int kTerms>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_mx_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_sfa,
+                         const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
+                         const uint8_t* __restrict__ sfb_hi, const uint8_t* __restrict__ sfb_lo, int sf_tiles,
+                         const gemm::Params p) {
+  using P = Plan<kTerms>;
+  constexpr int S = P::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::kBarOff);
+  uint64_t* full = bars;           // this CTA's weight tile, weight scales and activation scales landed
+  uint64_t* bfull = bars + S;      // leader: both CTAs' activation tiles landed
+  uint64_t* aready = bars + 2 * S; // leader: both CTAs' weight scales repacked
+  uint64_t* empty = bars + 3 * S;  // stage consumed by the MMAs (commit, multicast to the pair)
+  uint64_t* acc_full = bars + 4 * S;       // [2]
+  uint64_t* acc_empty = bars + 4 * S + 2;  // [2], leader: both epilogue groups done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint16_t* gtab = reinterpret_cast<uint16_t*>(smem + P::kTabOff);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_kb = p.K / BK;
+  const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
+  const int m_t = (p.M + BN - 1) / BN;
+  const int tiles = n_pt * m_t;
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int n_clusters = static_cast<int>(gridDim.x >> 1);
+  // tile t -> (feature tile, token tile): groups of kGroupM token tiles walk
+  // the feature tiles together, so a weight tile is read by consecutive
+  // clusters while it is in L2
+  auto coords = [&](int t, int& n0, int& m0) {
+    const int span = kGroupM * n_pt;
+    const int grp = t / span;
+    const int rem_m = m_t - grp * kGroupM;
+    const int gm = rem_m < kGroupM ? rem_m : kGroupM;
+    const int w = t - grp * span;
+    n0 = (w / gm) * (2 * BM) + static_cast<int>(rank) * BM;
+    m0 = (grp * kGroupM + w % gm) * BN;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&bfull[s], 1);
+      mbar_init(&aready[s], 2);  // both CTAs' repack warps (the leader's copy is used)
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2);  // both CTAs' epilogue groups (the leader's copy is used)
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialized, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t leader_bfull = mapa_shared(smem_u32(bfull), 0);
+  const uint32_t leader_aready = mapa_shared(smem_u32(aready), 0);
+  const uint32_t leader_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      tma_prefetch_desc(&tmap_sfa);
+      tma_prefetch_desc(&tmap_hi);
+      if (kTerms == 2) tma_prefetch_desc(&tmap_lo);
+      bool ok = true;
+      int g = 0;
+      for (int t = cluster_id; t < tiles && ok; t += n_clusters) {
+        int n0, m0;
+        coords(t, n0, m0);
+        const int64_t atom0 = m0 / 128;  // first 128-token scale atom of the tile
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], P::kA + P::kSfaRaw + kTerms * P::kSfb);
+          tma_load_2d(smem + P::kAOff + s * P::kA, &tmap_w, &full[s], kb * BK, n0);
+          // 16 scale bytes per row from a 16-byte-aligned column (4 stages' worth)
+          tma_load_2d(smem + P::kSfaRawOff + s * P::kSfaRaw, &tmap_sfa, &full[s], (kb >> 2) * 16, n0);
+          const int64_t sfo = (static_cast<int64_t>(kb) * sf_tiles + atom0) * kAtom;
+          bulk_load(smem + P::kSfbOff + (s * kTerms) * P::kSfb, sfb_hi + sfo, P::kSfb, &full[s]);
+          if (kTerms == 2) bulk_load(smem + P::kSfbOff + (s * kTerms + 1) * P::kSfb, sfb_lo + sfo, P::kSfb, &full[s]);
+          // activation tiles: each CTA stages its 96 tokens; completion on the leader's barrier
+          if (leader) mbar_arrive_expect_tx(&bfull[s], 2 * kTerms * P::kB);
+          tma_load_2d_pair(smem + P::kBOff + s * P::kB, &tmap_hi, leader_bfull + 8u * s, kb * BK,
+                           m0 + static_cast<int>(rank) * BNC);
+          if (kTerms == 2)
+            tma_load_2d_pair(smem + P::kBOff + (S + s) * P::kB, &tmap_lo, leader_bfull + 8u * s, kb * BK,
+                             m0 + static_cast<int>(rank) * BNC);
+        }
+      }
+      if (*abort_flag) {
+        // give copies already in flight time to land before smem is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
+    }
+  } else if (warp == kSfWarp) {
+    // weight scales of this CTA's 128 rows -> the MMA's atom layout: atom byte
+    // m0*16 + m1*4 + k1 = scale (row m0 + 32 m1, group 4 kb + k1), i.e. the
+    // 32-bit word (kb % 4) of raw rows m0, m0 + 32, m0 + 64, m0 + 96
+    int g = 0;
+    bool ok = true;
+    for (int t = cluster_id; t < tiles && ok; t += n_clusters) {
+      for (int kb = 0; kb < num_kb; ++kb, ++g) {
+        const int s = g % S;
+        const uint32_t ph = (g / S) & 1;
+        if (!mbar_wait(&full[s], ph, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(smem + P::kSfaRawOff + s * P::kSfaRaw);
+        const int c = kb & 3;
+        const uint4 w = make_uint4(raw[lane * 4 + c], raw[(lane + 32) * 4 + c], raw[(lane + 64) * 4 + c],
+                                   raw[(lane + 96) * 4 + c]);
+        *reinterpret_cast<uint4*>(smem + P::kSfaAtomOff + s * kAtom + lane * 16) = w;
+        fence_proxy_async_smem();  // generic-proxy writes -> tcgen05.cp's reads
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&aready[s]);
+          else mbar_arrive_cluster_release(leader_aready + 8u * s);
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (leader && lane == 0) {
+      bool ok = true;
+      int it = 0, g = 0;
+      for (int t = cluster_id; t < tiles && ok; t += n_clusters, ++it) {
+        int n0, m0;
+        coords(t, n0, m0);
+        const int buf = it & 1;
+        // both epilogue groups must be done with this accumulator's previous tile
+        if (!mbar_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+        // a tile starting 64 tokens into a 128-token atom reads its scales 2 columns in
+        const uint32_t sfb_skip = (m0 & 127) ? 2u : 0u;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (g / S) & 1;
+          if (!mbar_wait(&aready[s], ph, abort_flag, p.err) || !mbar_wait(&bfull[s], ph, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          sf_copy_pair(tmem + kSfaCol, sf_desc(smem_u32(smem + P::kSfaAtomOff + s * kAtom)));
+#pragma unroll
+          for (int tm = 0; tm < kTerms; ++tm) {
+            const uint32_t src = smem_u32(smem + P::kSfbOff + (s * kTerms + tm) * P::kSfb);
+            sf_copy_pair(tmem + kSfbCol + 16u * tm, sf_desc(src));
+            sf_copy_pair(tmem + kSfbCol + 16u * tm + 4u, sf_desc(src + kAtom));
+          }
+          const uint32_t aaddr = smem_u32(smem + P::kAOff + s * P::kA);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint32_t idesc = idesc_mx(2 * BM, BN, static_cast<uint32_t>(kk));
+            const uint64_t adesc = smem_desc_sw128(aaddr + kk * 32);
+            const uint32_t sfa = (static_cast<uint32_t>(kk) << 30) | (tmem + kSfaCol);
+#pragma unroll
+            for (int tm = 0; tm < kTerms; ++tm) {
+              const uint32_t baddr = smem_u32(smem + P::kBOff + (tm * S + s) * P::kB);
+              const uint32_t sfb = (static_cast<uint32_t>(kk) << 30) | (tmem + kSfbCol + 16u * tm + sfb_skip);
+              mma_mx_pair(d, adesc, smem_desc_sw128(baddr + kk * 32), idesc, sfa, sfb,
+                          (kb != 0 || kk != 0 || tm != 0) ? 1u : 0u);
+            }
+          }
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair(&acc_full[buf], 0x3);  // accumulator of this tile ready in both CTAs
+      }
+      if (*abort_flag) {
+        // give MMAs already issued time to complete before TMEM is released
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue warps 0..3
+    const int q = warp;  // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;
+    const int tid = threadIdx.x;  // 0..127
+    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    uint16_t* stw = reinterpret_cast<uint16_t*>(smem + P::kStgOff) + q * (32 * 32);
+    const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
+    const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+    const bool gate_bcast = p.gate.rows_per_vec == 0;
+    if (p.epi == LTXQ_EPI_GELU) {
+      gemm::gelu_tab_fill(gtab, tid, 128);  // while the first tile's main loop runs
+      gemm::named_bar_sync(1, 128);
+    }
+    for (int t = cluster_id, it = 0; t < tiles; t += n_clusters, ++it) {
+      int n0, m0;
+      coords(t, n0, m0);
+      const int buf = it & 1;
+      if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, abort_flag, p.err)) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem + t_lane + static_cast<uint32_t>(buf * BN);
+      const int n = n0 + r;  // register side: this thread's feature
+      const float bias_n = (p.bias != nullptr && n < p.N) ? bf16_to_f32(__ldg(p.bias + n)) : 0.f;
+      // row side: 8 features [nf, nf + 8) of token rows (lane >> 2) + 8 i
+      const int nf = n0 + q * 32 + (lane & 3) * 8;
+      float g8b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (gated && gate_bcast && nf < p.N) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8b);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c += 2) {
+        if (m0 + c * 32 >= p.M) break;  // uniform
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(tacc + c * 32, v[0]);
+        tmem_ld_32x32b_x32(tacc + (c + 1) * 32, v[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int m_c = m0 + (c + h2) * 32;
+          if (m_c >= p.M) break;  // uniform
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            // bf16(acc) (the reference's first rounding point), bias, GELU
+            uint32_t w = pack_bf16x2(__uint_as_float(v[h2][j]), __uint_as_float(v[h2][j + 1]));
+            if (p.bias != nullptr) w = pack_bf16x2(__fadd_rn(lo_bf16(w), bias_n), __fadd_rn(hi_bf16(w), bias_n));
+            if (p.epi == LTXQ_EPI_GELU) w = gemm::gelu_tab_x2(w, gtab);
+            stw[j * 32 + lane] = static_cast<uint16_t>(w & 0xFFFFu);
+            stw[(j + 1) * 32 + lane] = static_cast<uint16_t>(w >> 16);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int jr = (lane >> 2) + 8 * pass;
+            const uint4 a = *reinterpret_cast<const uint4*>(stw + jr * 32 + (lane & 3) * 8);
+            if (m_c + jr < p.M && nf < p.N) {
+              uint32_t uw[4] = {a.x, a.y, a.z, a.w};
+              gemm::epi_row_store(p, uw, m_c + jr, nf, g8b, gated, two_round, gate_bcast);
+            }
+          }
+          __syncwarp();  // transpose tile consumed
+        }
+      }
+      tc_fence_before();
+      gemm::named_bar_sync(1, 128);
+      if (tid == 0) mbar_arrive_cluster(leader_acc_empty + 8u * static_cast<uint32_t>(buf));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal or read it
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+static size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace of the split activations: codes of each term, then the scale
+// atoms of each term.
+struct Layout {
+  int64_t k_tiles, row_tiles;  // row_tiles includes the spare tile
+  size_t codes, sf, total;
+};
+
+static Layout layout(int64_t M, int64_t K, int terms) {
+  Layout l{};
+  l.k_tiles = K / BK;
+  l.row_tiles = (M + 127) / 128 + 1;
+  l.codes = align_up(static_cast<size_t>(M) * static_cast<size_t>(K));
+  l.sf = align_up(static_cast<size_t>(l.k_tiles * l.row_tiles) * kAtom);
+  l.total = static_cast<size_t>(terms) * (l.codes + l.sf);
+  return l;
+}
+
+template <int kTerms>
+static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, const CUtensorMap& thi,
+                               const CUtensorMap& tlo, const uint8_t* sfb_hi, const uint8_t* sfb_lo, int sf_tiles,
+                               const gemm::Params& p, cudaStream_t stream) {
+  using PL = Plan<kTerms>;
+  auto kern = qgemm_mx_pair_kernel<kTerms>;
+  if (ltxq_status st = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem),
+                                  "smem attribute"))
+    return st;
+  const int tiles = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + BN - 1) / BN);
+  const int max_clusters = num_sms() / 2;
+  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = PL::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tsfa, thi, tlo, sfb_hi, sfb_lo, sf_tiles, p);
+  if (e == cudaSuccess) note_launch();
+  return cuda_check(e, "mxfp8 block-scaled GEMM launch");
+}
+
+}  // namespace mx
+
+// Whether the native block-scaled path runs this GEMM, and its workspace.
+// It needs the standard mxfp8 layout, K a multiple of 512 (the weight-scale
+// rows are read as 16-byte boxes) and at least one output tile per cluster
+// (fewer tokens run the dequantizing path's K-split schedule instead).
+size_t mx_workspace_bytes(int64_t M, const ltxq_qweight& w) {
+  if (w.compute != LTXQ_COMPUTE_MX2 && w.compute != LTXQ_COMPUTE_MX1) return 0;
+  if (w.mode != LTXQ_MXFP8 || w.layout != LTXQ_LAYOUT_STD || w.group_size != 32) return 0;
+  if (M <= 0 || w.k_in % 512 != 0 || w.n_out % 8 != 0) return 0;
+  const int64_t tiles = ((w.n_out + 2 * mx::BM - 1) / (2 * mx::BM)) * ((M + mx::BN - 1) / mx::BN);
+  if (tiles < num_sms() / 2) return 0;
+  return mx::layout(M, w.k_in, w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1).total;
+}
+
+ltxq_status launch_mx_split(const void* x, int64_t M, int64_t K, int terms, void* hi, void* lo, void* sf_hi,
+                            void* sf_lo, cudaStream_t stream) {
+  const mx::Layout l = mx::layout(M, K, terms);
+  const int64_t rows = l.row_tiles * 128;
+  const int64_t threads = rows * (K / mx::kGroup);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  if (terms == 2)
+    mx::mx_split_kernel<2><<<blocks, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(x), M, static_cast<int>(K), rows, static_cast<int>(l.row_tiles),
+        static_cast<uint8_t*>(hi), static_cast<uint8_t*>(lo), static_cast<uint8_t*>(sf_hi), static_cast<uint8_t*>(sf_lo));
+  else
+    mx::mx_split_kernel<1><<<blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(x), M, static_cast<int>(K), rows,
+                                                       static_cast<int>(l.row_tiles), static_cast<uint8_t*>(hi),
+                                                       nullptr, static_cast<uint8_t*>(sf_hi), nullptr);
+  return launch_check("mx split launch");
+}
+
+// The native path: split x into MX terms in the workspace, then the
+// block-scaled GEMM.  The caller checked the shapes, pointers, alignment and
+// epilogue and that mx_workspace_bytes(M, w) > 0 fits the workspace.
+ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, const gemm::Params& p, void* workspace,
+                              cudaStream_t stream) {
+  const int terms = w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1;
+  const int64_t K = w.k_in, N = w.n_out;
+  const mx::Layout l = mx::layout(M, K, terms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* hi = ws;
+  uint8_t* lo = ws + l.codes;
+  uint8_t* sf_hi = ws + terms * l.codes;
+  uint8_t* sf_lo = sf_hi + l.sf;
+  if (ltxq_status st = launch_mx_split(x, M, K, terms, hi, lo, sf_hi, sf_lo, stream)) return st;
+  CUtensorMap tw, tsfa, thi, tlo;
+  // weight: [N rows][K E4M3 bytes], 128-byte rows of 128 features per CTA, 128B swizzle
+  if (ltxq_status st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, K, N, K, mx::BK, mx::BM,
+                                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return st;
+  // weight scales: [N rows][K/32 bytes], boxes of 16 bytes x 128 rows
+  if (ltxq_status st = encode_tmap_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.scales, K / 32, N, K / 32, 16, mx::BM,
+                                      CU_TENSOR_MAP_SWIZZLE_NONE))
+    return st;
+  if (ltxq_status st = encode_tmap_2d(&thi, CU_TENSOR_MAP_DATA_TYPE_UINT8, hi, K, M, K, mx::BK, mx::BNC,
+                                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return st;
+  tlo = thi;
+  if (terms == 2) {
+    if (ltxq_status st = encode_tmap_2d(&tlo, CU_TENSOR_MAP_DATA_TYPE_UINT8, lo, K, M, K, mx::BK, mx::BNC,
+                                        CU_TENSOR_MAP_SWIZZLE_128B))
+      return st;
+    return mx::launch_gemm<2>(tw, tsfa, thi, tlo, sf_hi, sf_lo, static_cast<int>(l.row_tiles), p, stream);
+  }
+  (void)N;
+  return mx::launch_gemm<1>(tw, tsfa, thi, tlo, sf_hi, nullptr, static_cast<int>(l.row_tiles), p, stream);
+}
+
+}  // namespace ltxq
+
+extern "C" {
+
+size_t ltxq_mx_split_sizes(int64_t M, int64_t K, size_t* codes_bytes, size_t* scale_bytes) {
+  if (M <= 0 || K <= 0 || K % 128 != 0) return 0;
+  const ltxq::mx::Layout l = ltxq::mx::layout(M, K, 1);
+  if (codes_bytes) *codes_bytes = static_cast<size_t>(M) * static_cast<size_t>(K);
+  if (scale_bytes) *scale_bytes = static_cast<size_t>(l.k_tiles * l.row_tiles) * ltxq::mx::kAtom;
+  return l.row_tiles;
+}
+
+ltxq_status ltxq_mx_split(const void* x, int64_t M, int64_t K, int32_t terms, void* hi, void* lo, void* sf_hi,
+                          void* sf_lo, void* stream) {
+  using namespace ltxq;
+  if (!x || !hi || !sf_hi || (terms == 2 && (!lo || !sf_lo))) return fail(LTXQ_ERR_INVALID, "mx_split: NULL pointer");
+  if (terms != 1 && terms != 2) return fail(LTXQ_ERR_INVALID, "mx_split: terms must be 1 or 2");
+  if (M < 0 || K <= 0) return fail(LTXQ_ERR_INVALID, "mx_split: bad shape");
+  if (K % 128 != 0) return fail(LTXQ_ERR_UNSUPPORTED, "mx_split: K must be a multiple of 128");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo) |
+       reinterpret_cast<uintptr_t>(sf_hi) | reinterpret_cast<uintptr_t>(sf_lo)) & 15u)
+    return fail(LTXQ_ERR_UNSUPPORTED, "mx_split: pointers must be 16-byte aligned");
+  if (M == 0) return LTXQ_OK;
+  return launch_mx_split(x, M, K, terms, hi, lo, sf_hi, sf_lo, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -20,6 +20,7 @@ NORM_NONE, NORM_RMS, NORM_LAYER = 0, 1, 2
 AFFINE, MXFP8 = 0, 1
 LAYOUT_STD, LAYOUT_PRETRANSPOSED = 0, 1
 QW_MXFP8_FINITE = 1
+COMPUTE_DEQUANT, COMPUTE_MX2, COMPUTE_MX1 = 0, 1, 2
 EPI_NONE, EPI_GELU, EPI_GATED_RESIDUAL, EPI_GATE_THEN_ADD = 0, 1, 2, 3
 GATED_ADD, GATE_THEN_ADD = 0, 1
 
@@ -37,7 +38,7 @@ class QWeight(ctypes.Structure):
         ("group_size", c_int32),
         ("layout", c_int32),
         ("flags", ctypes.c_uint32),
-        ("pad_", c_int32),
+        ("compute", c_int32),
     ]
 
 
@@ -93,6 +94,9 @@ SIGNATURES = {
                                c_size_t, c_void_p]),
     "ltxq_adaln_qlinear": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(Epilogue),
                                      c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ltxq_mx_split_sizes": (c_size_t, [c_int64, c_int64, POINTER(c_size_t), POINTER(c_size_t)]),
+    "ltxq_mx_split": (c_int32, [c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p]),
     "ltxq_adaln_qlinear_noalloc": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight),
                                              POINTER(Epilogue), c_void_p, c_void_p]),
     "ltxq_feed_forward": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(QWeight),

@@ -476,6 +476,14 @@ class BasicAVTransformerBlock:
                 mods.append(at.kv_proj)
         return mods
 
+    def set_compute(self, compute: str) -> "BasicAVTransformerBlock":
+        """How every quantized GEMM of the block computes (``QuantizedLinear.
+        set_compute``): "dequant", or "mx2" / "mx1" for the native block-scaled
+        fp8 MMAs on mxfp8 weights."""
+        for ql in self.quantized_modules():
+            ql.set_compute(compute)
+        return self
+
     def nbytes(self) -> int:
         """Bytes of packed weights, group parameters and biases held."""
         total = 0

@@ -25,6 +25,10 @@ from .kernels import _require_cuda, _stream, prologue, vec_arg
 
 QUANT_DEFAULTS = {"affine": (64, 4), "mxfp8": (32, 8)}
 _MODE = {"affine": _lib.AFFINE, "mxfp8": _lib.MXFP8}
+# how the GEMM computes (include/ltxq.h LTXQ_COMPUTE_*): "dequant" (bf16
+# tensor cores over the exactly dequantized weight), "mx2" / "mx1" (native
+# block-scaled fp8 MMAs on mxfp8 weights, activations in two / one MXFP8 terms)
+COMPUTE = {"dequant": _lib.COMPUTE_DEQUANT, "mx2": _lib.COMPUTE_MX2, "mx1": _lib.COMPUTE_MX1}
 
 
 def quant_defaults(mode: str, group_size: int | None, bits: int | None) -> tuple[int, int]:
@@ -62,6 +66,16 @@ class QuantizedLinear:
             self.in_features = in_features or packed_len
         if mode == "affine" and self.biases is None:
             raise ValueError("affine quantization needs biases")
+        self.compute = "dequant"
+
+    def set_compute(self, compute: str) -> "QuantizedLinear":
+        """Select how GEMMs over this weight compute (``COMPUTE``); the MX
+        modes apply to mxfp8 weights in the standard layout, other weights
+        keep the dequantizing kernels."""
+        if compute not in COMPUTE:
+            raise ValueError(f"unknown compute mode {compute!r}")
+        self.compute = compute
+        return self
 
     # ------------------------------------------------------------------ build
     @classmethod
@@ -97,7 +111,8 @@ class QuantizedLinear:
             self.biases.data_ptr() if self.biases is not None else None,
             self.bias.data_ptr() if self.bias is not None else None,
             self.out_features, self.in_features, _MODE[self.mode], self.bits, self.group_size,
-            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD, self.data_flags())
+            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD, self.data_flags(),
+            COMPUTE[getattr(self, "compute", "dequant")])
 
     def data_flags(self) -> int:
         """LTXQ_QW_* flags of the packed data (``ltxq_qweight_scan``), cached

@@ -320,7 +320,7 @@ def _oracle_params(lin, tabs):
     return p
 
 
-def _block_case(mode, bits, T, A, L, seed):
+def _block_case(mode, bits, T, A, L, seed, compute="dequant"):
     torch = _torch()
     import ltxq
     from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, TransformerArgs
@@ -328,7 +328,7 @@ def _block_case(mode, bits, T, A, L, seed):
     gen = _gen(seed)
     lin, tabs = BasicAVTransformerBlock.random_parts(gen, "cuda", mode=mode, bits=bits)
     p = _oracle_params(lin, tabs)
-    blk = BasicAVTransformerBlock(lin, tabs, VIDEO_22B, AUDIO_22B)
+    blk = BasicAVTransformerBlock(lin, tabs, VIDEO_22B, AUDIO_22B).set_compute(compute)
 
     def stream(cfg, t):
         ang = torch.rand(1, cfg.heads, t, cfg.d_head // 2, generator=gen, device="cuda") * 6.28
@@ -360,7 +360,7 @@ def _block_case(mode, bits, T, A, L, seed):
     ref_v, ref_a = ob.block(p, hv, ha, heads_v=VIDEO_22B.heads, heads_a=AUDIO_22B.heads)
     for got, ref, what in ((got_v, ref_v, "video"), (got_a, ref_a, "audio")):
         mar, cos = ro.max_abs_rel(got, ref), ro.cosine(got, ref)
-        print(f"block {mode}{bits} T={T} A={A} {what}: max_abs_rel={mar:.2e} cos={cos:.7f}")
+        print(f"block {mode}{bits} {compute} T={T} A={A} {what}: max_abs_rel={mar:.2e} cos={cos:.7f}")
         assert mar <= MAX_ABS_REL and cos >= COS_MIN, f"{what}: max_abs_rel={mar:.3e} cos={cos:.6f}"
 
 
