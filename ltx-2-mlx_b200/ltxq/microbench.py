@@ -1,7 +1,7 @@
 """Quantized-linear microbenchmark (the analogue of the reference's
 scripts/bench_ff_microbench.py ``quant_matmul``, :451-551).
 
-    python -m ltxq.microbench --shapes 9216x4096x4096 --modes affine4,mxfp8
+    python -m ltxq.microbench --shapes 9216x4096x4096 --modes affine4,mxfp8,mxfp8_mx2
     python -m ltxq.microbench --cublas            # also time torch bf16 F.linear
 
 Each shape is MxKxN (tokens x in x out).  Prints one JSON line per shape
@@ -29,7 +29,9 @@ from .quantized_linear import QuantizedLinear
 
 DEFAULT_SHAPES = ["1024x4096x4096", "3456x4096x16384", "3456x16384x4096", "9216x4096x12288", "9216x4096x4096",
                   "9216x16384x4096", "126x2048x8192", "201x4096x2048"]
-MODES = {"affine8": ("affine", 8), "affine4": ("affine", 4), "mxfp8": ("mxfp8", 8)}
+# name -> (quantization mode, bits, compute mode)
+MODES = {"affine8": ("affine", 8, "dequant"), "affine4": ("affine", 4, "dequant"), "mxfp8": ("mxfp8", 8, "dequant"),
+         "mxfp8_mx2": ("mxfp8", 8, "mx2"), "mxfp8_mx1": ("mxfp8", 8, "mx1")}
 
 
 def _time(fn, flush, iters, warmup):
@@ -103,8 +105,9 @@ def main(argv=None):
             t = _time(lambda: torch.nn.functional.linear(x, w, b), flush, args.iters, args.warmup)
             row["cublas_bf16"] = {"ms": t, "tflops": flops / t / 1e9}
         for name in args.modes.split(","):
-            mode, bits = MODES[name]
+            mode, bits, compute = MODES[name]
             ql = QuantizedLinear.from_linear(w, b, mode=mode, bits=bits, pretransposed=args.pretransposed)
+            ql.set_compute(compute)
             kw = {"gelu": True} if args.epilogue == "gelu" else (
                 {"residual": res, "gate": gate} if args.epilogue == "gated" else {})
             kw["split_k"] = not args.no_split_k
@@ -115,7 +118,7 @@ def main(argv=None):
                                               None if ql.biases is None else ql.biases.clone(), ql.bias,
                                               group_size=ql.group_size, bits=ql.bits, mode=ql.mode,
                                               pretransposed=ql.pretransposed, in_features=ql.in_features,
-                                              out_features=ql.out_features)
+                                              out_features=ql.out_features).set_compute(compute)
                               for _ in range(copies - 1)]
                 t = _time_graph([lambda q=q: q(x, **kw) for q in qls], args.iters)
                 row["graph_calls"] = copies
