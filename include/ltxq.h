@@ -89,8 +89,9 @@ enum {
  *    largest magnitude: roughly twice the MMA rate of MX2, but it does not
  *    meet this path's stated tolerance against the reference (opt-in).
  * The MX modes apply to the standard layout with K a multiple of 512 and at
- * least one 256 x 192 output tile per two SMs; other GEMMs over the same
- * weight run the DEQUANT kernels.  The MX modes need workspace for the split
+ * least one 256 x 192 output tile per two SMs, and need the repacked weight
+ * scales (ltxq_qweight.mx_scales); other GEMMs over the same weight run the
+ * DEQUANT kernels.  The MX modes need workspace for the split
  * activations (ltxq_qlinear_workspace_size accounts for it); given less,
  * the GEMM runs the DEQUANT kernels. */
 enum { LTXQ_COMPUTE_DEQUANT = 0, LTXQ_COMPUTE_MX2 = 1, LTXQ_COMPUTE_MX1 = 2 };
@@ -115,6 +116,10 @@ typedef struct {
   int32_t layout;     /* LTXQ_LAYOUT_STD / LTXQ_LAYOUT_PRETRANSPOSED */
   uint32_t flags;     /* LTXQ_QW_* (0 = none asserted) */
   int32_t compute;    /* LTXQ_COMPUTE_*: how the GEMM computes (0 = dequantize to bf16) */
+  /* LTXQ_COMPUTE_MX*: the weight scales repacked by ltxq_mx_pack_weight_scales
+   * (16-byte aligned, ltxq_mx_weight_scales_size bytes); NULL runs the
+   * DEQUANT kernels */
+  const void* mx_scales;
 } ltxq_qweight;
 
 /* Per-channel vectors (AdaLN scale/shift/gate).  Element (row m, channel c)
@@ -232,6 +237,13 @@ ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pr
  * = ceil(M / 128) + 1 (the last tile is zero rows).  ltxq_mx_split_sizes
  * returns row_tiles and the byte sizes of one term's codes and scales. */
 size_t ltxq_mx_split_sizes(int64_t M, int64_t K, size_t* codes_bytes, size_t* scale_bytes);
+/* The weight side of LTXQ_COMPUTE_MX*: the cache's E8M0 scales [N, K/32]
+ * repacked into the same atom layout (atom (k-tile j, feature tile t) at
+ * (j * cols + t) * 512, cols = 2 * ceil(N / 256); rows >= N hold 0).  Done
+ * once per weight; the caller owns the buffer and passes it as
+ * ltxq_qweight.mx_scales.  Standard-layout mxfp8 weights with K % 512 == 0. */
+size_t ltxq_mx_weight_scales_size(const ltxq_qweight* w);
+ltxq_status ltxq_mx_pack_weight_scales(const ltxq_qweight* w, void* out, void* stream);
 ltxq_status ltxq_mx_split(const void* x, int64_t M, int64_t K, int32_t terms, void* hi, void* lo, void* sf_hi,
                           void* sf_lo, void* stream);
 

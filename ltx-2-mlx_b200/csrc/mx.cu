@@ -25,11 +25,14 @@
 // Kernel (persistent, clusters of two CTAs, tcgen05 cta_group::2): each tile
 // is 256 output features x 192 tokens; CTA r holds features [n0 + 128 r,
 // +128) of the weight (A, K-major, 128-byte swizzle, straight from the cache
-// by TMA) and tokens [m0 + 96 r, +96) of each activation term (B).  Per
-// 128-K stage the leader copies the scale factors into TMEM with tcgen05.cp
-// (weight scales repacked in shared memory by a helper warp from the cache's
-// row-major [N, K/32] array; activation scales written by the splitter in the
-// MMA's layout) and issues 4 MMAs (K = 32 each) per term.  Two 192-column
+// by TMA) and tokens [m0 + 96 r, +96) of each activation term (B).  The
+// scale factors are in the MMA's atom layout in global memory -- the
+// weight's repacked once per weight (ltxq_mx_pack_weight_scales, from the
+// cache's row-major [N, K/32]), the activations' written by the splitter --
+// so every operand of a 128-K stage, in both CTAs, arrives by TMA with its
+// completion counted on one barrier of the leader.  The leader's MMA thread
+// waits on that barrier alone, copies the scale factors into TMEM
+// (tcgen05.cp) and issues 4 MMAs (K = 32 each) per term.  Two 192-column
 // accumulators let the epilogue of one tile run while the next accumulates.
 // Every wait is bounded (common.cuh mbar_wait); no TMA load uses cluster
 // multicast.
@@ -45,8 +48,8 @@ constexpr int BM = 128;      // output features per CTA (MMA M = 256 per pair)
 constexpr int BN = 192;      // tokens per tile (MMA N)
 constexpr int BNC = BN / 2;  // tokens per CTA
 constexpr int BK = 128;      // K per stage = bytes of one fp8 row
-constexpr int kThreads = 224;  // warps 0-3 epilogue, 4 TMA, 5 MMA, 6 scale repack
-constexpr int kTmaWarp = 4, kMmaWarp = 5, kSfWarp = 6;
+constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int kTmaWarp = 4, kMmaWarp = 5;
 constexpr uint32_t kSfaCol = 2 * BN;       // weight scale factors: 4 TMEM columns
 constexpr uint32_t kSfbCol = kSfaCol + 8;  // activation scale factors of term t: 8 columns at kSfbCol + 16 t
 constexpr uint32_t kTmemCols = 512;
@@ -184,16 +187,24 @@ __global__ void __launch_bounds__(256) mx_split_kernel(const uint16_t* __restric
   }
 }
 
-// ---------------------------------------------------------------- PTX wrappers
-
-// cp.async.bulk (no tensor map, no multicast): `bytes` from global to this
-// CTA's shared memory, completion counted on `bar`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
+// Weight scales [N, K/32] (the cache's row-major E8M0 bytes) -> the same
+// atom layout: atom (k-tile j, feature tile t) at (j * cols + t) * 512, with
+// cols = 2 * ceil(N / 256) (whole CTA pairs; rows >= N hold 0, their weight
+// rows read as zeros).  One thread per (row, k-tile): one 32-bit word.
+__global__ void __launch_bounds__(256) mx_pack_scales_kernel(const uint8_t* __restrict__ s, int64_t N, int G,
+                                                             int cols, uint8_t* __restrict__ out) {
+  const int KT = G / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(cols) * 128 * KT) return;
+  const int64_t n = i / KT;
+  const int j = static_cast<int>(i - n * KT);
+  const uint32_t w = n < N ? __ldg(reinterpret_cast<const uint32_t*>(s + n * G) + j) : 0u;
+  const int m = static_cast<int>(n & 127);
+  *reinterpret_cast<uint32_t*>(out + (static_cast<int64_t>(j) * cols + (n >> 7)) * kAtom + (m & 31) * 16 +
+                               (m >> 5) * 4) = w;
 }
+
+// ---------------------------------------------------------------- PTX wrappers
 
 // Shared-memory descriptor of a scale-factor atom for tcgen05.cp: K-major,
 // no swizzle, 32 rows of 16 bytes (8-row core matrices 128 bytes apart).
@@ -241,17 +252,17 @@ template <int kTerms>
 struct Plan {
   static constexpr int kA = BM * BK;        // weight tile, 16 KB
   static constexpr int kB = BNC * BK;       // one term's activation tile, 12 KB
-  static constexpr int kSfaRaw = BM * 16;   // 16 scale bytes of each weight row
   static constexpr int kSfb = 2 * kAtom;    // one term's scales: the two 128-token atoms a tile touches
-  static constexpr int kStage = kA + kTerms * kB + kSfaRaw + kAtom + kTerms * kSfb;
+  static constexpr int kStage = kA + kTerms * kB + kAtom + kTerms * kSfb;
+  // bytes one stage lands on the leader's barrier (both CTAs)
+  static constexpr uint32_t kStageTx = 2u * (kA + kAtom + kTerms * (kB + kSfb));
   static constexpr int kStg = 4 * 32 * 32 * 2;  // per-warp 32 x 32 transpose tiles of the epilogue
   static constexpr int kFixed = 1024 + kStg + 512 + gemm::kGeluTabBytes;
   static constexpr int kStagesRaw = (227 * 1024 - kFixed) / kStage;
-  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kAOff = 0;
   static constexpr int kBOff = kAOff + kStages * kA;  // term t, stage s at kBOff + (t * kStages + s) * kB
-  static constexpr int kSfaRawOff = kBOff + kTerms * kStages * kB;
-  static constexpr int kSfaAtomOff = kSfaRawOff + kStages * kSfaRaw;
+  static constexpr int kSfaAtomOff = kBOff + kTerms * kStages * kB;
   static constexpr int kSfbOff = kSfaAtomOff + kStages * kAtom;  // stage s, term t at kSfbOff + (s * kTerms + t) * kSfb
   static constexpr int kStgOff = kSfbOff + kStages * kTerms * kSfb;
   static constexpr int kBarOff = kStgOff + kStg;
@@ -260,27 +271,26 @@ struct Plan {
   static_assert(kStages >= 3, "pipeline depth");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kBOff % 1024 == 0, "128B-swizzle atoms need 1024-byte alignment");
-  static_assert(4 * kStages * 8 + 4 * 8 + 8 <= 512, "barrier area");
+  static_assert(2 * kStages * 8 + 4 * 8 + 8 <= 512, "barrier area");
 };
 
 template <int kTerms>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_mx_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_sfa,
                          const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
-                         const uint8_t* __restrict__ sfb_hi, const uint8_t* __restrict__ sfb_lo, int sf_tiles,
+                         const __grid_constant__ CUtensorMap tmap_sfb_hi,
+                         const __grid_constant__ CUtensorMap tmap_sfb_lo, int w_atom_cols, int x_atom_cols,
                          const gemm::Params p) {
   using P = Plan<kTerms>;
   constexpr int S = P::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::kBarOff);
-  uint64_t* full = bars;           // this CTA's weight tile, weight scales and activation scales landed
-  uint64_t* bfull = bars + S;      // leader: both CTAs' activation tiles landed
-  uint64_t* aready = bars + 2 * S; // leader: both CTAs' weight scales repacked
-  uint64_t* empty = bars + 3 * S;  // stage consumed by the MMAs (commit, multicast to the pair)
-  uint64_t* acc_full = bars + 4 * S;       // [2]
-  uint64_t* acc_empty = bars + 4 * S + 2;  // [2], leader: both epilogue groups done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 4);
+  uint64_t* full = bars;           // leader: every operand of the stage landed in both CTAs
+  uint64_t* empty = bars + S;      // stage consumed by the MMAs (commit, multicast to the pair)
+  uint64_t* acc_full = bars + 2 * S;       // [2]
+  uint64_t* acc_empty = bars + 2 * S + 2;  // [2], leader: both epilogue groups done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint16_t* gtab = reinterpret_cast<uint16_t*>(smem + P::kTabOff);
 
@@ -309,9 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&bfull[s], 1);
-      mbar_init(&aready[s], 2);  // both CTAs' repack warps (the leader's copy is used)
+      mbar_init(&full[s], 1);  // the leader's arrive.expect_tx (its copy is the one used)
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -329,8 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // barriers of both CTAs initialized, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t leader_bfull = mapa_shared(smem_u32(bfull), 0);
-  const uint32_t leader_aready = mapa_shared(smem_u32(aready), 0);
+  const uint32_t leader_full = mapa_shared(smem_u32(full), 0);
   const uint32_t leader_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
 
   if (warp == kTmaWarp) {
@@ -338,13 +345,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmap_w);
       tma_prefetch_desc(&tmap_sfa);
       tma_prefetch_desc(&tmap_hi);
-      if (kTerms == 2) tma_prefetch_desc(&tmap_lo);
+      tma_prefetch_desc(&tmap_sfb_hi);
+      if (kTerms == 2) {
+        tma_prefetch_desc(&tmap_lo);
+        tma_prefetch_desc(&tmap_sfb_lo);
+      }
       bool ok = true;
       int g = 0;
       for (int t = cluster_id; t < tiles && ok; t += n_clusters) {
         int n0, m0;
         coords(t, n0, m0);
-        const int64_t atom0 = m0 / 128;  // first 128-token scale atom of the tile
+        const int atom0 = m0 / 128;  // first 128-token scale atom of the tile
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
@@ -352,53 +363,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], P::kA + P::kSfaRaw + kTerms * P::kSfb);
-          tma_load_2d(smem + P::kAOff + s * P::kA, &tmap_w, &full[s], kb * BK, n0);
-          // 16 scale bytes per row from a 16-byte-aligned column (4 stages' worth)
-          tma_load_2d(smem + P::kSfaRawOff + s * P::kSfaRaw, &tmap_sfa, &full[s], (kb >> 2) * 16, n0);
-          const int64_t sfo = (static_cast<int64_t>(kb) * sf_tiles + atom0) * kAtom;
-          bulk_load(smem + P::kSfbOff + (s * kTerms) * P::kSfb, sfb_hi + sfo, P::kSfb, &full[s]);
-          if (kTerms == 2) bulk_load(smem + P::kSfbOff + (s * kTerms + 1) * P::kSfb, sfb_lo + sfo, P::kSfb, &full[s]);
-          // activation tiles: each CTA stages its 96 tokens; completion on the leader's barrier
-          if (leader) mbar_arrive_expect_tx(&bfull[s], 2 * kTerms * P::kB);
-          tma_load_2d_pair(smem + P::kBOff + s * P::kB, &tmap_hi, leader_bfull + 8u * s, kb * BK,
-                           m0 + static_cast<int>(rank) * BNC);
-          if (kTerms == 2)
-            tma_load_2d_pair(smem + P::kBOff + (S + s) * P::kB, &tmap_lo, leader_bfull + 8u * s, kb * BK,
-                             m0 + static_cast<int>(rank) * BNC);
+          // every copy of both CTAs completes on the leader's full[s]
+          if (leader) mbar_arrive_expect_tx(&full[s], P::kStageTx);
+          const uint32_t bar = leader_full + 8u * s;
+          tma_load_2d_pair(smem + P::kAOff + s * P::kA, &tmap_w, bar, kb * BK, n0);
+          // this CTA's 128 weight rows: one scale atom (rows of 16 bytes)
+          tma_load_2d_pair(smem + P::kSfaAtomOff + s * kAtom, &tmap_sfa, bar, 0, (kb * w_atom_cols + n0 / 128) * 32);
+          const int m_cta = m0 + static_cast<int>(rank) * BNC;
+          const int sfb_row = (kb * x_atom_cols + atom0) * 32;  // the tile's two token atoms, both CTAs
+          tma_load_2d_pair(smem + P::kBOff + s * P::kB, &tmap_hi, bar, kb * BK, m_cta);
+          tma_load_2d_pair(smem + P::kSfbOff + (s * kTerms) * P::kSfb, &tmap_sfb_hi, bar, 0, sfb_row);
+          if (kTerms == 2) {
+            tma_load_2d_pair(smem + P::kBOff + (S + s) * P::kB, &tmap_lo, bar, kb * BK, m_cta);
+            tma_load_2d_pair(smem + P::kSfbOff + (s * kTerms + 1) * P::kSfb, &tmap_sfb_lo, bar, 0, sfb_row);
+          }
         }
       }
       if (*abort_flag) {
         // give copies already in flight time to land before smem is released
         const uint64_t t0 = globaltimer();
         while (globaltimer() - t0 < 50000ull) {
-        }
-      }
-    }
-  } else if (warp == kSfWarp) {
-    // weight scales of this CTA's 128 rows -> the MMA's atom layout: atom byte
-    // m0*16 + m1*4 + k1 = scale (row m0 + 32 m1, group 4 kb + k1), i.e. the
-    // 32-bit word (kb % 4) of raw rows m0, m0 + 32, m0 + 64, m0 + 96
-    int g = 0;
-    bool ok = true;
-    for (int t = cluster_id; t < tiles && ok; t += n_clusters) {
-      for (int kb = 0; kb < num_kb; ++kb, ++g) {
-        const int s = g % S;
-        const uint32_t ph = (g / S) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag, p.err)) {
-          ok = false;
-          break;
-        }
-        const uint32_t* raw = reinterpret_cast<const uint32_t*>(smem + P::kSfaRawOff + s * P::kSfaRaw);
-        const int c = kb & 3;
-        const uint4 w = make_uint4(raw[lane * 4 + c], raw[(lane + 32) * 4 + c], raw[(lane + 64) * 4 + c],
-                                   raw[(lane + 96) * 4 + c]);
-        *reinterpret_cast<uint4*>(smem + P::kSfaAtomOff + s * kAtom + lane * 16) = w;
-        fence_proxy_async_smem();  // generic-proxy writes -> tcgen05.cp's reads
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) mbar_arrive(&aready[s]);
-          else mbar_arrive_cluster_release(leader_aready + 8u * s);
         }
       }
     }
@@ -419,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
           const int s = g % S;
           const uint32_t ph = (g / S) & 1;
-          if (!mbar_wait(&aready[s], ph, abort_flag, p.err) || !mbar_wait(&bfull[s], ph, abort_flag, p.err)) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.err)) {
             ok = false;
             break;
           }
@@ -554,8 +538,8 @@ static Layout layout(int64_t M, int64_t K, int terms) {
 
 template <int kTerms>
 static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, const CUtensorMap& thi,
-                               const CUtensorMap& tlo, const uint8_t* sfb_hi, const uint8_t* sfb_lo, int sf_tiles,
-                               const gemm::Params& p, cudaStream_t stream) {
+                               const CUtensorMap& tlo, const CUtensorMap& tsfb_hi, const CUtensorMap& tsfb_lo,
+                               int w_atom_cols, int x_atom_cols, const gemm::Params& p, cudaStream_t stream) {
   using PL = Plan<kTerms>;
   auto kern = qgemm_mx_pair_kernel<kTerms>;
   if (ltxq_status st = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem),
@@ -576,7 +560,8 @@ static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, c
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tsfa, thi, tlo, sfb_hi, sfb_lo, sf_tiles, p);
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, kern, tw, tsfa, thi, tlo, tsfb_hi, tsfb_lo, w_atom_cols, x_atom_cols, p);
   if (e == cudaSuccess) note_launch();
   return cuda_check(e, "mxfp8 block-scaled GEMM launch");
 }
@@ -590,7 +575,8 @@ static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, c
 size_t mx_workspace_bytes(int64_t M, const ltxq_qweight& w) {
   if (w.compute != LTXQ_COMPUTE_MX2 && w.compute != LTXQ_COMPUTE_MX1) return 0;
   if (w.mode != LTXQ_MXFP8 || w.layout != LTXQ_LAYOUT_STD || w.group_size != 32) return 0;
-  if (M <= 0 || w.k_in % 512 != 0 || w.n_out % 8 != 0) return 0;
+  if (M <= 0 || w.k_in % 512 != 0 || w.n_out % 8 != 0 || !w.mx_scales) return 0;
+  if (reinterpret_cast<uintptr_t>(w.mx_scales) & 15u) return 0;
   const int64_t tiles = ((w.n_out + 2 * mx::BM - 1) / (2 * mx::BM)) * ((M + mx::BN - 1) / mx::BN);
   if (tiles < num_sms() / 2) return 0;
   return mx::layout(M, w.k_in, w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1).total;
@@ -627,27 +613,35 @@ ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, c
   uint8_t* sf_hi = ws + terms * l.codes;
   uint8_t* sf_lo = sf_hi + l.sf;
   if (ltxq_status st = launch_mx_split(x, M, K, terms, hi, lo, sf_hi, sf_lo, stream)) return st;
-  CUtensorMap tw, tsfa, thi, tlo;
+  CUtensorMap tw, tsfa, thi, tlo, tsbh, tsbl;
   // weight: [N rows][K E4M3 bytes], 128-byte rows of 128 features per CTA, 128B swizzle
   if (ltxq_status st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, K, N, K, mx::BK, mx::BM,
                                       CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
-  // weight scales: [N rows][K/32 bytes], boxes of 16 bytes x 128 rows
-  if (ltxq_status st = encode_tmap_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.scales, K / 32, N, K / 32, 16, mx::BM,
-                                      CU_TENSOR_MAP_SWIZZLE_NONE))
+  // scale atoms as rows of 16 bytes: one weight atom (32 rows) per CTA, two token atoms (64 rows) per tile
+  const int64_t w_cols = 2 * ((N + 255) / 256);
+  if (ltxq_status st = encode_tmap_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.mx_scales, 16, l.k_tiles * w_cols * 32,
+                                      16, 16, 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return st;
+  if (ltxq_status st = encode_tmap_2d(&tsbh, CU_TENSOR_MAP_DATA_TYPE_UINT8, sf_hi, 16, l.k_tiles * l.row_tiles * 32,
+                                      16, 16, 64, CU_TENSOR_MAP_SWIZZLE_NONE))
     return st;
   if (ltxq_status st = encode_tmap_2d(&thi, CU_TENSOR_MAP_DATA_TYPE_UINT8, hi, K, M, K, mx::BK, mx::BNC,
                                       CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
   tlo = thi;
+  tsbl = tsbh;
+  const int wc = static_cast<int>(w_cols), xc = static_cast<int>(l.row_tiles);
   if (terms == 2) {
     if (ltxq_status st = encode_tmap_2d(&tlo, CU_TENSOR_MAP_DATA_TYPE_UINT8, lo, K, M, K, mx::BK, mx::BNC,
                                         CU_TENSOR_MAP_SWIZZLE_128B))
       return st;
-    return mx::launch_gemm<2>(tw, tsfa, thi, tlo, sf_hi, sf_lo, static_cast<int>(l.row_tiles), p, stream);
+    if (ltxq_status st = encode_tmap_2d(&tsbl, CU_TENSOR_MAP_DATA_TYPE_UINT8, sf_lo, 16,
+                                        l.k_tiles * l.row_tiles * 32, 16, 16, 64, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return st;
+    return mx::launch_gemm<2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
   }
-  (void)N;
-  return mx::launch_gemm<1>(tw, tsfa, thi, tlo, sf_hi, nullptr, static_cast<int>(l.row_tiles), p, stream);
+  return mx::launch_gemm<1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
 }
 
 }  // namespace ltxq
@@ -660,6 +654,29 @@ size_t ltxq_mx_split_sizes(int64_t M, int64_t K, size_t* codes_bytes, size_t* sc
   if (codes_bytes) *codes_bytes = static_cast<size_t>(M) * static_cast<size_t>(K);
   if (scale_bytes) *scale_bytes = static_cast<size_t>(l.k_tiles * l.row_tiles) * ltxq::mx::kAtom;
   return l.row_tiles;
+}
+
+size_t ltxq_mx_weight_scales_size(const ltxq_qweight* w) {
+  if (!w || w->mode != LTXQ_MXFP8 || w->layout != LTXQ_LAYOUT_STD || w->k_in <= 0 || w->k_in % 128 != 0 ||
+      w->n_out <= 0)
+    return 0;
+  return static_cast<size_t>(w->k_in / 128) * static_cast<size_t>(2 * ((w->n_out + 255) / 256)) * ltxq::mx::kAtom;
+}
+
+ltxq_status ltxq_mx_pack_weight_scales(const ltxq_qweight* w, void* out, void* stream) {
+  using namespace ltxq;
+  if (!w || !out || !w->scales) return fail(LTXQ_ERR_INVALID, "mx_pack_weight_scales: NULL argument");
+  const size_t bytes = ltxq_mx_weight_scales_size(w);
+  if (!bytes || w->k_in % 512 != 0)
+    return fail(LTXQ_ERR_UNSUPPORTED, "mx_pack_weight_scales: mxfp8 weights, standard layout, K % 512 == 0");
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(w->scales)) & 15u)
+    return fail(LTXQ_ERR_UNSUPPORTED, "mx_pack_weight_scales: scales / out must be 16-byte aligned");
+  const int G = static_cast<int>(w->k_in / 32);
+  const int cols = static_cast<int>(2 * ((w->n_out + 255) / 256));
+  const int64_t threads = static_cast<int64_t>(cols) * 128 * (G / 4);
+  mx::mx_pack_scales_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(w->scales), w->n_out, G, cols, static_cast<uint8_t*>(out));
+  return launch_check("mx pack scales launch");
 }
 
 ltxq_status ltxq_mx_split(const void* x, int64_t M, int64_t K, int32_t terms, void* hi, void* lo, void* sf_hi,

@@ -39,6 +39,7 @@ class QWeight(ctypes.Structure):
         ("layout", c_int32),
         ("flags", ctypes.c_uint32),
         ("compute", c_int32),
+        ("mx_scales", c_void_p),
     ]
 
 
@@ -95,6 +96,8 @@ SIGNATURES = {
     "ltxq_adaln_qlinear": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(Epilogue),
                                      c_void_p, c_void_p, c_size_t, c_void_p]),
     "ltxq_mx_split_sizes": (c_size_t, [c_int64, c_int64, POINTER(c_size_t), POINTER(c_size_t)]),
+    "ltxq_mx_weight_scales_size": (c_size_t, [POINTER(QWeight)]),
+    "ltxq_mx_pack_weight_scales": (c_int32, [POINTER(QWeight), c_void_p, c_void_p]),
     "ltxq_mx_split": (c_int32, [c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p]),
     "ltxq_adaln_qlinear_noalloc": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight),

@@ -75,7 +75,30 @@ class QuantizedLinear:
         if compute not in COMPUTE:
             raise ValueError(f"unknown compute mode {compute!r}")
         self.compute = compute
+        self._mx_scales = None
+        if compute != "dequant":
+            self.mx_scales()  # packed now, not inside a later stream capture
         return self
+
+    def mx_scales(self) -> torch.Tensor | None:
+        """The weight scales repacked for the MX modes' block-scaled MMA
+        (``ltxq_mx_pack_weight_scales``), made once and again only when the
+        scale tensor changes; None where the MX modes do not apply."""
+        if getattr(self, "compute", "dequant") == "dequant" or self.mode != "mxfp8" or self.pretransposed:
+            return None
+        if self.in_features % 512 != 0:
+            return None
+        key = (self.scales.data_ptr(), self.scales._version)
+        cached = getattr(self, "_mx_scales", None)
+        if cached is None or cached[0] != key:
+            lib = _lib.load()
+            q = self._qweight_base(0, None)
+            nbytes = lib.ltxq_mx_weight_scales_size(ctypes.byref(q))
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=self.scales.device)
+            _lib.check(lib.ltxq_mx_pack_weight_scales(ctypes.byref(q), buf.data_ptr(), _stream()), "mx_pack_weight_scales")
+            cached = (key, buf)
+            self._mx_scales = cached
+        return cached[1]
 
     # ------------------------------------------------------------------ build
     @classmethod
@@ -105,14 +128,18 @@ class QuantizedLinear:
                    pretransposed=pretransposed, in_features=k_in, out_features=n_out)
 
     # ------------------------------------------------------------------ views
-    def qweight(self) -> _lib.QWeight:
+    def _qweight_base(self, flags: int, mx_scales) -> _lib.QWeight:
         return _lib.QWeight(
             self.weight.data_ptr(), self.scales.data_ptr(),
             self.biases.data_ptr() if self.biases is not None else None,
             self.bias.data_ptr() if self.bias is not None else None,
             self.out_features, self.in_features, _MODE[self.mode], self.bits, self.group_size,
-            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD, self.data_flags(),
-            COMPUTE[getattr(self, "compute", "dequant")])
+            _lib.LAYOUT_PRETRANSPOSED if self.pretransposed else _lib.LAYOUT_STD, flags,
+            COMPUTE[getattr(self, "compute", "dequant")], mx_scales)
+
+    def qweight(self) -> _lib.QWeight:
+        mx = self.mx_scales()
+        return self._qweight_base(self.data_flags(), mx.data_ptr() if mx is not None else None)
 
     def data_flags(self) -> int:
         """LTXQ_QW_* flags of the packed data (``ltxq_qweight_scan``), cached
