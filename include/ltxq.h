@@ -89,7 +89,8 @@ enum {
  *    largest magnitude: roughly twice the MMA rate of MX2, but it does not
  *    meet this path's stated tolerance against the reference (opt-in).
  * The MX modes apply to the standard layout with K a multiple of 512 and at
- * least one 256 x 192 output tile per two SMs, and need the repacked weight
+ * least one 256 x 192 output tile per two SMs (512 x 192 tiles where there
+ * are enough of those), and need the repacked weight
  * scales (ltxq_qweight.mx_scales); other GEMMs over the same weight run the
  * DEQUANT kernels.  The MX modes need workspace for the split
  * activations (ltxq_qlinear_workspace_size accounts for it); given less,
@@ -239,7 +240,7 @@ ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pr
 size_t ltxq_mx_split_sizes(int64_t M, int64_t K, size_t* codes_bytes, size_t* scale_bytes);
 /* The weight side of LTXQ_COMPUTE_MX*: the cache's E8M0 scales [N, K/32]
  * repacked into the same atom layout (atom (k-tile j, feature tile t) at
- * (j * cols + t) * 512, cols = 2 * ceil(N / 256); rows >= N hold 0).  Done
+ * (j * cols + t) * 512, cols = 4 * ceil(N / 512); rows >= N hold 0).  Done
  * once per weight; the caller owns the buffer and passes it as
  * ltxq_qweight.mx_scales.  Standard-layout mxfp8 weights with K % 512 == 0. */
 size_t ltxq_mx_weight_scales_size(const ltxq_qweight* w);

@@ -48,10 +48,6 @@ constexpr int BM = 128;      // output features per CTA (MMA M = 256 per pair)
 constexpr int BN = 192;      // tokens per tile (MMA N)
 constexpr int BNC = BN / 2;  // tokens per CTA
 constexpr int BK = 128;      // K per stage = bytes of one fp8 row
-constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 TMA, 5 MMA
-constexpr int kTmaWarp = 4, kMmaWarp = 5;
-constexpr uint32_t kSfaCol = 2 * BN;       // weight scale factors: 4 TMEM columns
-constexpr uint32_t kSfbCol = kSfaCol + 8;  // activation scale factors of term t: 8 columns at kSfbCol + 16 t
 constexpr uint32_t kTmemCols = 512;
 constexpr int kGroupM = 16;  // token tiles that walk a feature tile together (L2 reuse of the weight)
 
@@ -189,8 +185,8 @@ __global__ void __launch_bounds__(256) mx_split_kernel(const uint16_t* __restric
 
 // Weight scales [N, K/32] (the cache's row-major E8M0 bytes) -> the same
 // atom layout: atom (k-tile j, feature tile t) at (j * cols + t) * 512, with
-// cols = 2 * ceil(N / 256) (whole CTA pairs; rows >= N hold 0, their weight
-// rows read as zeros).  One thread per (row, k-tile): one 32-bit word.
+// cols = 4 * ceil(N / 512) (whole 512-feature tiles; rows >= N hold 0, their
+// weight rows read as zeros).  One thread per (row, k-tile): one 32-bit word.
 __global__ void __launch_bounds__(256) mx_pack_scales_kernel(const uint8_t* __restrict__ s, int64_t N, int G,
                                                              int cols, uint8_t* __restrict__ out) {
   const int KT = G / 4;
@@ -248,48 +244,64 @@ __device__ __forceinline__ void mma_mx_pair(uint32_t d, uint64_t adesc, uint64_t
 
 // ---------------------------------------------------------------- GEMM
 
-template <int kTerms>
+// kBlocks = 1: a tile is 256 features x 192 tokens, two accumulators per CTA
+// (the epilogue of one tile overlaps the next tile's MMAs); kBlocks = 2: a
+// tile is 512 features x 192 tokens -- each CTA holds 256 weight rows as two
+// 128-row blocks and every activation tile feeds MMAs for both, which cuts
+// the shared-cache traffic per flop by a third -- with one accumulator per
+// block and eight epilogue warps.
+template <int kTerms, int kBlocks>
 struct Plan {
-  static constexpr int kA = BM * BK;        // weight tile, 16 KB
-  static constexpr int kB = BNC * BK;       // one term's activation tile, 12 KB
-  static constexpr int kSfb = 2 * kAtom;    // one term's scales: the two 128-token atoms a tile touches
-  static constexpr int kStage = kA + kTerms * kB + kAtom + kTerms * kSfb;
+  static constexpr int kA = kBlocks * BM * BK;  // this CTA's weight rows, 16 KB per block
+  static constexpr int kB = BNC * BK;           // one term's activation tile, 12 KB
+  static constexpr int kSfa = kBlocks * kAtom;  // weight scale atoms (one per block)
+  static constexpr int kSfb = 2 * kAtom;        // one term's scales: the two 128-token atoms a tile touches
+  static constexpr int kStage = kA + kTerms * kB + kSfa + kTerms * kSfb;
   // bytes one stage lands on the leader's barrier (both CTAs)
-  static constexpr uint32_t kStageTx = 2u * (kA + kAtom + kTerms * (kB + kSfb));
-  static constexpr int kStg = 4 * 32 * 32 * 2;  // per-warp 32 x 32 transpose tiles of the epilogue
+  static constexpr uint32_t kStageTx = 2u * (kA + kSfa + kTerms * (kB + kSfb));
+  static constexpr int kEpiWarps = 4 * kBlocks;
+  static constexpr int kThreads = 32 * (kEpiWarps + 2);  // epilogue warps, then the TMA and MMA warps
+  static constexpr int kTmaWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
+  static constexpr int kAccBufs = kBlocks == 1 ? 2 : 1;
+  static constexpr int kStg = kEpiWarps * 32 * 32 * 2;  // per-warp 32 x 32 transpose tiles of the epilogue
   static constexpr int kFixed = 1024 + kStg + 512 + gemm::kGeluTabBytes;
   static constexpr int kStagesRaw = (227 * 1024 - kFixed) / kStage;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kAOff = 0;
   static constexpr int kBOff = kAOff + kStages * kA;  // term t, stage s at kBOff + (t * kStages + s) * kB
-  static constexpr int kSfaAtomOff = kBOff + kTerms * kStages * kB;
-  static constexpr int kSfbOff = kSfaAtomOff + kStages * kAtom;  // stage s, term t at kSfbOff + (s * kTerms + t) * kSfb
+  static constexpr int kSfaOff = kBOff + kTerms * kStages * kB;
+  static constexpr int kSfbOff = kSfaOff + kStages * kSfa;  // stage s, term t at kSfbOff + (s * kTerms + t) * kSfb
   static constexpr int kStgOff = kSfbOff + kStages * kTerms * kSfb;
   static constexpr int kBarOff = kStgOff + kStg;
   static constexpr int kTabOff = kBarOff + 512;
   static constexpr int kSmem = 1024 + kTabOff + gemm::kGeluTabBytes;
+  // TMEM columns: accumulators, then the scale factors
+  static constexpr uint32_t kSfaCol = 2 * BN;                // 4 columns per weight block
+  static constexpr uint32_t kSfbCol = kSfaCol + 4 * kBlocks;  // term t: 8 columns + 2 of slack at kSfbCol + 16 t
+  static_assert(kSfbCol + 16 * kTerms <= kTmemCols, "TMEM columns");
   static_assert(kStages >= 3, "pipeline depth");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   static_assert(kA % 1024 == 0 && kB % 1024 == 0 && kBOff % 1024 == 0, "128B-swizzle atoms need 1024-byte alignment");
   static_assert(2 * kStages * 8 + 4 * 8 + 8 <= 512, "barrier area");
 };
 
-template <int kTerms>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kTerms, int kBlocks>
+__global__ void __launch_bounds__(Plan<kTerms, kBlocks>::kThreads, 1)
     qgemm_mx_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_sfa,
                          const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
                          const __grid_constant__ CUtensorMap tmap_sfb_hi,
                          const __grid_constant__ CUtensorMap tmap_sfb_lo, int w_atom_cols, int x_atom_cols,
                          const gemm::Params p) {
-  using P = Plan<kTerms>;
+  using P = Plan<kTerms, kBlocks>;
   constexpr int S = P::kStages;
+  constexpr int kRows = kBlocks * BM;  // weight rows per CTA
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::kBarOff);
   uint64_t* full = bars;           // leader: every operand of the stage landed in both CTAs
   uint64_t* empty = bars + S;      // stage consumed by the MMAs (commit, multicast to the pair)
-  uint64_t* acc_full = bars + 2 * S;       // [2]
-  uint64_t* acc_empty = bars + 2 * S + 2;  // [2], leader: both epilogue groups done
+  uint64_t* acc_full = bars + 2 * S;       // [kAccBufs]
+  uint64_t* acc_empty = bars + 2 * S + 2;  // [kAccBufs], leader: both CTAs' epilogue groups done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint16_t* gtab = reinterpret_cast<uint16_t*>(smem + P::kTabOff);
@@ -299,21 +311,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int num_kb = p.K / BK;
-  const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
+  const int n_pt = (p.N + 2 * kRows - 1) / (2 * kRows);
   const int m_t = (p.M + BN - 1) / BN;
   const int tiles = n_pt * m_t;
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int n_clusters = static_cast<int>(gridDim.x >> 1);
   // tile t -> (feature tile, token tile): groups of kGroupM token tiles walk
   // the feature tiles together, so a weight tile is read by consecutive
-  // clusters while it is in L2
+  // clusters while it is in L2.  n0 = this CTA's first weight row.
   auto coords = [&](int t, int& n0, int& m0) {
     const int span = kGroupM * n_pt;
     const int grp = t / span;
     const int rem_m = m_t - grp * kGroupM;
     const int gm = rem_m < kGroupM ? rem_m : kGroupM;
     const int w = t - grp * span;
-    n0 = (w / gm) * (2 * BM) + static_cast<int>(rank) * BM;
+    n0 = (w / gm) * (2 * kRows) + static_cast<int>(rank) * kRows;
     m0 = (grp * kGroupM + w % gm) * BN;
   };
 
@@ -322,14 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);  // the leader's arrive.expect_tx (its copy is the one used)
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < P::kAccBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 2);  // both CTAs' epilogue groups (the leader's copy is used)
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == P::kMmaWarp) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
     tmem_relinquish_pair();
   }
@@ -340,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t leader_full = mapa_shared(smem_u32(full), 0);
   const uint32_t leader_acc_empty = mapa_shared(smem_u32(acc_empty), 0);
 
-  if (warp == kTmaWarp) {
+  if (warp == P::kTmaWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tmap_w);
       tma_prefetch_desc(&tmap_sfa);
@@ -367,8 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full[s], P::kStageTx);
           const uint32_t bar = leader_full + 8u * s;
           tma_load_2d_pair(smem + P::kAOff + s * P::kA, &tmap_w, bar, kb * BK, n0);
-          // this CTA's 128 weight rows: one scale atom (rows of 16 bytes)
-          tma_load_2d_pair(smem + P::kSfaAtomOff + s * kAtom, &tmap_sfa, bar, 0, (kb * w_atom_cols + n0 / 128) * 32);
+          // this CTA's weight rows: one scale atom (32 rows of 16 bytes) per block
+          tma_load_2d_pair(smem + P::kSfaOff + s * P::kSfa, &tmap_sfa, bar, 0, (kb * w_atom_cols + n0 / 128) * 32);
           const int m_cta = m0 + static_cast<int>(rank) * BNC;
           const int sfb_row = (kb * x_atom_cols + atom0) * 32;  // the tile's two token atoms, both CTAs
           tma_load_2d_pair(smem + P::kBOff + s * P::kB, &tmap_hi, bar, kb * BK, m_cta);
@@ -386,18 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == P::kMmaWarp) {
     if (leader && lane == 0) {
       bool ok = true;
       int it = 0, g = 0;
       for (int t = cluster_id; t < tiles && ok; t += n_clusters, ++it) {
         int n0, m0;
         coords(t, n0, m0);
-        const int buf = it & 1;
+        const int buf = it % P::kAccBufs;
         // both epilogue groups must be done with this accumulator's previous tile
-        if (!mbar_wait(&acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+        if (!mbar_wait(&acc_empty[buf], ((it / P::kAccBufs) & 1) ^ 1, abort_flag, p.err)) break;
         tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
         // a tile starting 64 tokens into a 128-token atom reads its scales 2 columns in
         const uint32_t sfb_skip = (m0 & 127) ? 2u : 0u;
         for (int kb = 0; kb < num_kb; ++kb, ++g) {
@@ -408,31 +419,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          sf_copy_pair(tmem + kSfaCol, sf_desc(smem_u32(smem + P::kSfaAtomOff + s * kAtom)));
+#pragma unroll
+          for (int b = 0; b < kBlocks; ++b)
+            sf_copy_pair(tmem + P::kSfaCol + 4u * b, sf_desc(smem_u32(smem + P::kSfaOff + s * P::kSfa + b * kAtom)));
 #pragma unroll
           for (int tm = 0; tm < kTerms; ++tm) {
             const uint32_t src = smem_u32(smem + P::kSfbOff + (s * kTerms + tm) * P::kSfb);
-            sf_copy_pair(tmem + kSfbCol + 16u * tm, sf_desc(src));
-            sf_copy_pair(tmem + kSfbCol + 16u * tm + 4u, sf_desc(src + kAtom));
+            sf_copy_pair(tmem + P::kSfbCol + 16u * tm, sf_desc(src));
+            sf_copy_pair(tmem + P::kSfbCol + 16u * tm + 4u, sf_desc(src + kAtom));
           }
           const uint32_t aaddr = smem_u32(smem + P::kAOff + s * P::kA);
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             const uint32_t idesc = idesc_mx(2 * BM, BN, static_cast<uint32_t>(kk));
-            const uint64_t adesc = smem_desc_sw128(aaddr + kk * 32);
-            const uint32_t sfa = (static_cast<uint32_t>(kk) << 30) | (tmem + kSfaCol);
 #pragma unroll
-            for (int tm = 0; tm < kTerms; ++tm) {
-              const uint32_t baddr = smem_u32(smem + P::kBOff + (tm * S + s) * P::kB);
-              const uint32_t sfb = (static_cast<uint32_t>(kk) << 30) | (tmem + kSfbCol + 16u * tm + sfb_skip);
-              mma_mx_pair(d, adesc, smem_desc_sw128(baddr + kk * 32), idesc, sfa, sfb,
-                          (kb != 0 || kk != 0 || tm != 0) ? 1u : 0u);
+            for (int b = 0; b < kBlocks; ++b) {
+              const uint64_t adesc = smem_desc_sw128(aaddr + b * (BM * BK) + kk * 32);
+              const uint32_t d = tmem + static_cast<uint32_t>((kBlocks == 1 ? buf : b) * BN);
+              const uint32_t sfa = (static_cast<uint32_t>(kk) << 30) | (tmem + P::kSfaCol + 4u * b);
+#pragma unroll
+              for (int tm = 0; tm < kTerms; ++tm) {
+                const uint32_t baddr = smem_u32(smem + P::kBOff + (tm * S + s) * P::kB);
+                const uint32_t sfb = (static_cast<uint32_t>(kk) << 30) | (tmem + P::kSfbCol + 16u * tm + sfb_skip);
+                mma_mx_pair(d, adesc, smem_desc_sw128(baddr + kk * 32), idesc, sfa, sfb,
+                            (kb != 0 || kk != 0 || tm != 0) ? 1u : 0u);
+              }
             }
           }
           mma_commit_pair(&empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit_pair(&acc_full[buf], 0x3);  // accumulator of this tile ready in both CTAs
+        mma_commit_pair(&acc_full[buf], 0x3);  // accumulators of this tile ready in both CTAs
       }
       if (*abort_flag) {
         // give MMAs already issued time to complete before TMEM is released
@@ -442,30 +459,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------ epilogue warps 0..3
-    const int q = warp;  // TMEM lane quarter of this warp
-    const int r = q * 32 + lane;
-    const int tid = threadIdx.x;  // 0..127
+    // ------------------------------------------------ epilogue warps
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int blk = warp >> 2;  // weight block (kBlocks == 2)
+    const int tid = threadIdx.x;  // 0 .. 128 kBlocks - 1
     const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
-    uint16_t* stw = reinterpret_cast<uint16_t*>(smem + P::kStgOff) + q * (32 * 32);
+    uint16_t* stw = reinterpret_cast<uint16_t*>(smem + P::kStgOff) + warp * (32 * 32);
     const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
     const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
     const bool gate_bcast = p.gate.rows_per_vec == 0;
     if (p.epi == LTXQ_EPI_GELU) {
-      gemm::gelu_tab_fill(gtab, tid, 128);  // while the first tile's main loop runs
-      gemm::named_bar_sync(1, 128);
+      gemm::gelu_tab_fill(gtab, tid, 32 * P::kEpiWarps);  // while the first tile's main loop runs
+      gemm::named_bar_sync(1, 32 * P::kEpiWarps);
     }
     for (int t = cluster_id, it = 0; t < tiles; t += n_clusters, ++it) {
       int n0, m0;
       coords(t, n0, m0);
-      const int buf = it & 1;
-      if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, abort_flag, p.err)) break;
+      const int buf = it % P::kAccBufs;
+      if (!mbar_wait(&acc_full[buf], (it / P::kAccBufs) & 1, abort_flag, p.err)) break;
       tc_fence_after();
-      const uint32_t tacc = tmem + t_lane + static_cast<uint32_t>(buf * BN);
-      const int n = n0 + r;  // register side: this thread's feature
+      const uint32_t tacc = tmem + t_lane + static_cast<uint32_t>((kBlocks == 1 ? buf : blk) * BN);
+      const int nb = n0 + blk * BM;  // first feature of this warp's block
+      const int n = nb + q * 32 + lane;  // register side: this thread's feature
       const float bias_n = (p.bias != nullptr && n < p.N) ? bf16_to_f32(__ldg(p.bias + n)) : 0.f;
       // row side: 8 features [nf, nf + 8) of token rows (lane >> 2) + 8 i
-      const int nf = n0 + q * 32 + (lane & 3) * 8;
+      const int nf = nb + q * 32 + (lane & 3) * 8;
       float g8b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       if (gated && gate_bcast && nf < p.N) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8b);
 #pragma unroll 1
@@ -502,14 +520,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      gemm::named_bar_sync(1, 128);
+      gemm::named_bar_sync(1, 32 * P::kEpiWarps);
       if (tid == 0) mbar_arrive_cluster(leader_acc_empty + 8u * static_cast<uint32_t>(buf));
     }
   }
 
   tc_fence_before();
   cluster_sync_all();  // no CTA leaves while its peer may still signal or read it
-  if (warp == kMmaWarp) {
+  if (warp == P::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, kTmemCols);
   }
@@ -536,21 +554,35 @@ static Layout layout(int64_t M, int64_t K, int terms) {
   return l;
 }
 
-template <int kTerms>
+// feature atoms per k-tile of the packed weight scales: whole 512-feature
+// tiles, so that both kernel forms read only atoms that exist
+static int64_t weight_atom_cols(int64_t N) { return 4 * ((N + 511) / 512); }
+
+// weight rows per cluster tile: 512 (two blocks per CTA) where that still
+// gives every cluster a tile, else 256
+static int pick_blocks(int64_t M, int64_t N) {
+  const int64_t m_t = (M + BN - 1) / BN;
+  const int clusters = num_sms() / 2;
+  if (((N + 511) / 512) * m_t >= clusters) return 2;
+  if (((N + 255) / 256) * m_t >= clusters) return 1;
+  return 0;
+}
+
+template <int kTerms, int kBlocks>
 static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, const CUtensorMap& thi,
                                const CUtensorMap& tlo, const CUtensorMap& tsfb_hi, const CUtensorMap& tsfb_lo,
                                int w_atom_cols, int x_atom_cols, const gemm::Params& p, cudaStream_t stream) {
-  using PL = Plan<kTerms>;
-  auto kern = qgemm_mx_pair_kernel<kTerms>;
+  using PL = Plan<kTerms, kBlocks>;
+  auto kern = qgemm_mx_pair_kernel<kTerms, kBlocks>;
   if (ltxq_status st = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem),
                                   "smem attribute"))
     return st;
-  const int tiles = ((p.N + 2 * BM - 1) / (2 * BM)) * ((p.M + BN - 1) / BN);
+  const int tiles = ((p.N + 2 * kBlocks * BM - 1) / (2 * kBlocks * BM)) * ((p.M + BN - 1) / BN);
   const int max_clusters = num_sms() / 2;
   const int clusters = tiles < max_clusters ? tiles : max_clusters;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(PL::kThreads);
   cfg.dynamicSmemBytes = PL::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -577,8 +609,7 @@ size_t mx_workspace_bytes(int64_t M, const ltxq_qweight& w) {
   if (w.mode != LTXQ_MXFP8 || w.layout != LTXQ_LAYOUT_STD || w.group_size != 32) return 0;
   if (M <= 0 || w.k_in % 512 != 0 || w.n_out % 8 != 0 || !w.mx_scales) return 0;
   if (reinterpret_cast<uintptr_t>(w.mx_scales) & 15u) return 0;
-  const int64_t tiles = ((w.n_out + 2 * mx::BM - 1) / (2 * mx::BM)) * ((M + mx::BN - 1) / mx::BN);
-  if (tiles < num_sms() / 2) return 0;
+  if (!mx::pick_blocks(M, w.n_out)) return 0;
   return mx::layout(M, w.k_in, w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1).total;
 }
 
@@ -613,15 +644,16 @@ ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, c
   uint8_t* sf_hi = ws + terms * l.codes;
   uint8_t* sf_lo = sf_hi + l.sf;
   if (ltxq_status st = launch_mx_split(x, M, K, terms, hi, lo, sf_hi, sf_lo, stream)) return st;
+  const int blocks = mx::pick_blocks(M, N);
   CUtensorMap tw, tsfa, thi, tlo, tsbh, tsbl;
-  // weight: [N rows][K E4M3 bytes], 128-byte rows of 128 features per CTA, 128B swizzle
-  if (ltxq_status st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, K, N, K, mx::BK, mx::BM,
-                                      CU_TENSOR_MAP_SWIZZLE_128B))
+  // weight: [N rows][K E4M3 bytes], 128-byte rows of 128 features per block, 128B swizzle
+  if (ltxq_status st = encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.weight, K, N, K, mx::BK,
+                                      mx::BM * blocks, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
-  // scale atoms as rows of 16 bytes: one weight atom (32 rows) per CTA, two token atoms (64 rows) per tile
-  const int64_t w_cols = 2 * ((N + 255) / 256);
+  // scale atoms as rows of 16 bytes: one weight atom (32 rows) per block, two token atoms (64 rows) per tile
+  const int64_t w_cols = mx::weight_atom_cols(N);
   if (ltxq_status st = encode_tmap_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.mx_scales, 16, l.k_tiles * w_cols * 32,
-                                      16, 16, 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+                                      16, 16, 32 * blocks, CU_TENSOR_MAP_SWIZZLE_NONE))
     return st;
   if (ltxq_status st = encode_tmap_2d(&tsbh, CU_TENSOR_MAP_DATA_TYPE_UINT8, sf_hi, 16, l.k_tiles * l.row_tiles * 32,
                                       16, 16, 64, CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -639,9 +671,11 @@ ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, c
     if (ltxq_status st = encode_tmap_2d(&tsbl, CU_TENSOR_MAP_DATA_TYPE_UINT8, sf_lo, 16,
                                         l.k_tiles * l.row_tiles * 32, 16, 16, 64, CU_TENSOR_MAP_SWIZZLE_NONE))
       return st;
-    return mx::launch_gemm<2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
+    return blocks == 2 ? mx::launch_gemm<2, 2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream)
+                       : mx::launch_gemm<2, 1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
   }
-  return mx::launch_gemm<1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
+  return blocks == 2 ? mx::launch_gemm<1, 2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream)
+                     : mx::launch_gemm<1, 1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
 }
 
 }  // namespace ltxq
@@ -660,7 +694,8 @@ size_t ltxq_mx_weight_scales_size(const ltxq_qweight* w) {
   if (!w || w->mode != LTXQ_MXFP8 || w->layout != LTXQ_LAYOUT_STD || w->k_in <= 0 || w->k_in % 128 != 0 ||
       w->n_out <= 0)
     return 0;
-  return static_cast<size_t>(w->k_in / 128) * static_cast<size_t>(2 * ((w->n_out + 255) / 256)) * ltxq::mx::kAtom;
+  return static_cast<size_t>(w->k_in / 128) * static_cast<size_t>(ltxq::mx::weight_atom_cols(w->n_out)) *
+         ltxq::mx::kAtom;
 }
 
 ltxq_status ltxq_mx_pack_weight_scales(const ltxq_qweight* w, void* out, void* stream) {
@@ -672,7 +707,7 @@ ltxq_status ltxq_mx_pack_weight_scales(const ltxq_qweight* w, void* out, void* s
   if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(w->scales)) & 15u)
     return fail(LTXQ_ERR_UNSUPPORTED, "mx_pack_weight_scales: scales / out must be 16-byte aligned");
   const int G = static_cast<int>(w->k_in / 32);
-  const int cols = static_cast<int>(2 * ((w->n_out + 255) / 256));
+  const int cols = static_cast<int>(mx::weight_atom_cols(w->n_out));
   const int64_t threads = static_cast<int64_t>(cols) * 128 * (G / 4);
   mx::mx_pack_scales_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(w->scales), w->n_out, G, cols, static_cast<uint8_t*>(out));
