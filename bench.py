@@ -642,18 +642,21 @@ def run_step(args, world, rank, local, dev):
             "roofline": {"bound": "tensor",
                          "kernel": (f"qgemm_pair_kernel<{args.quant}> (video FF project_in, GELU epilogue)"
                                     if args.compute == "dequant" else
-                                    f"mx_split_kernel + qgemm_mx_pair_kernel<{2 if args.compute == 'mx2' else 1}> "
-                                    "(video FF project_in, GELU epilogue)"),
+                                    f"qgemm_mx_pair_kernel<{2 if args.compute == 'mx2' else 1}> (video FF "
+                                    "project_in: MX terms in from the AdaLN pass, GELU, MX terms out)"),
                          "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
                          "peak_kind": (f"{peak_kind} bf16 sustained (kernel timed inside a long step)"
                                        if peak_kind == "measured" else "fallback 1400 TFLOP/s sustained"),
-                         "traffic": _traffic(f"qgemm_pair_{args.quant}_ff_in_{B * tl}x16384x4096"),
+                         "traffic": (_traffic(f"qgemm_pair_{args.quant}_ff_in_{B * tl}x16384x4096")
+                                     if args.compute == "dequant" else None),
                          "algorithmic_per_launch": {"flops": ff_flops,
                                                     "bytes": B * tl * VD * 2 + _packed_bytes(args.quant, 4 * VD, VD)
                                                     + B * tl * 4 * VD * 2}},
             "e2e": {"value": e2e_ms, "unit": "ms/step", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
                     "api": f"ltxq.block.BasicAVTransformerBlock x{n_blocks} (C ABI: ltxq_adaln_modulate, ltxq_qlinear, "
-                           "ltxq_qk_norm_rope, ltxq_head_gate)"},
+                           "ltxq_qk_norm_rope, ltxq_head_gate"
+                           + (", ltxq_adaln_modulate_mx, ltxq_head_gate_mx, ltxq_qlinear_mx)"
+                              if args.compute != "dequant" else ")")},
             "gpu_launches": n_launches,
             "weights_gb": weight_bytes / 1e9,
             "clocks": clk.summary(),

@@ -248,6 +248,42 @@ ltxq_status ltxq_mx_pack_weight_scales(const ltxq_qweight* w, void* out, void* s
 ltxq_status ltxq_mx_split(const void* x, int64_t M, int64_t K, int32_t terms, void* hi, void* lo, void* sf_hi,
                           void* sf_lo, void* stream);
 
+/* Activations in the MX split form (ltxq_mx_split's codes and scale-atom
+ * layout) -- the input of the block-scaled GEMMs, written directly by
+ * ltxq_adaln_modulate_mx, ltxq_head_gate_mx and ltxq_qlinear_mx's out_mx. */
+typedef struct {
+  void* hi;      /* [M, K] E4M3 codes of the first term (16-byte aligned) */
+  void* lo;      /* [M, K] codes of the second term (terms == 2) */
+  void* sf_hi;   /* scale atoms of each term (ltxq_mx_split_sizes bytes) */
+  void* sf_lo;
+  int32_t terms; /* 1 or 2 */
+  int32_t pad_;
+} ltxq_mx_act;
+
+/* 1 when the block-scaled kernels run a GEMM of M rows over `w`
+ * (LTXQ_COMPUTE_MX* with its packed scales, enough output tiles). */
+int32_t ltxq_qlinear_mx_supported(int64_t M, const ltxq_qweight* w);
+/* ltxq_qlinear from activations already in MX form (x->terms must match
+ * w->compute; ltxq_qlinear_mx_supported(M, w) must hold; no workspace).
+ * With out_mx != NULL the result (bias / GELU applied, rounded to bf16) is
+ * written as MX terms of the next GEMM's input instead of bf16 `out`
+ * (epilogue none or GELU, N % 128 == 0); out may then be NULL.  Same bits as
+ * ltxq_mx_split of the bf16 result.  The reference composition it replaces
+ * is ltxq_qlinear's (transformer_cache.py:177-193 with the block's
+ * epilogues). */
+ltxq_status ltxq_qlinear_mx(const ltxq_mx_act* x, int64_t M, const ltxq_qweight* w, const ltxq_epilogue* epi,
+                            void* out, const ltxq_mx_act* out_mx, void* stream);
+/* ltxq_adaln_modulate (bf16 x, C % 128 == 0, C <= 4096) writing its result
+ * as MX terms (`out` then unused, may be NULL) or both: bf16 to `out` when it
+ * is not NULL.  The terms are the bits ltxq_mx_split gives for the bf16
+ * result. */
+ltxq_status ltxq_adaln_modulate_mx(const void* x, int64_t rows, int64_t C, const ltxq_prologue* pro, void* out,
+                                   const ltxq_mx_act* out_mx, void* stream);
+/* ltxq_head_gate writing MX terms (heads * head_dim % 128 == 0); `out` as
+ * in ltxq_adaln_modulate_mx. */
+ltxq_status ltxq_head_gate_mx(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
+                              void* out, const ltxq_mx_act* out_mx, void* stream);
+
 /* ltxq_adaln_qlinear without a workspace argument and without allocating.
  * No counterpart in the reference.  For hosts that cannot let a library
  * allocate device memory (a runtime that owns the whole GPU's memory

@@ -9,6 +9,7 @@
 // Row statistics are accumulated in fp64 so that they are independent of the
 // reduction order.
 #include "common.cuh"
+#include "mx_act.cuh"
 
 namespace ltxq {
 
@@ -160,10 +161,13 @@ __device__ __forceinline__ uint4 pick(const uint4 (&v)[N], int j) {
   return cur;
 }
 
-template <int kCPL, int kWPR, bool kVecBf16>
+// kMx: the result is (also) written as MX terms of the next GEMM's input
+// (C % 128 == 0, so the four lanes of a quad hold one 32-channel group);
+// out may then be NULL.
+template <int kCPL, int kWPR, bool kVecBf16, bool kMx>
 __global__ void __launch_bounds__(256, 2) adaln_rows_kernel(const uint16_t* __restrict__ x, int64_t rows, int64_t C,
                                                          int norm, float eps, VecArg scale, VecArg shift,
-                                                         uint16_t* __restrict__ out) {
+                                                         uint16_t* __restrict__ out, const mx::MxOut mo) {
   __shared__ double red[8][2];
   const double inv_c = __drcp_rn(static_cast<double>(C));
   const int lane = threadIdx.x & 31;
@@ -246,7 +250,7 @@ __global__ void __launch_bounds__(256, 2) adaln_rows_kernel(const uint16_t* __re
   if (!live) return;
   const char* sc = vec_row(scale, row);
   const char* sh = vec_row(shift, row);
-  uint16_t* orow = out + row * C;
+  uint16_t* orow = out != nullptr ? out + row * C : nullptr;
   // not unrolled, so that the vector loads of one chunk are not hoisted over
   // the whole row (register pressure); the chunk is picked with selects
 #pragma unroll 1
@@ -271,7 +275,8 @@ __global__ void __launch_bounds__(256, 2) adaln_rows_kernel(const uint16_t* __re
       }
       o[i] = pack_bf16x2(e[0], e[1]);
     }
-    reinterpret_cast<uint4*>(orow)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    if (kMx) mx::mx_write8(o, row, static_cast<int64_t>(c) * 8, mo, 0xFu << (lane & ~3));
+    if (orow != nullptr) reinterpret_cast<uint4*>(orow)[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -310,8 +315,11 @@ __global__ void gated_add_kernel(const uint16_t* __restrict__ res, const uint16_
 
 // out[m, h, :] = o[m, h, :] * bf16(2 * bf16(sigmoid(logit[m, h]))); one
 // thread per 8 channels.
+// kMx: as adaln_rows_kernel's (width % 128 == 0: the grid stride and the row
+// width are multiples of 4 chunks, so a quad stays one 32-channel group).
+template <bool kMx>
 __global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ logits, int64_t rows,
-                                 int64_t heads, int64_t head_dim, uint16_t* __restrict__ out) {
+                                 int64_t heads, int64_t head_dim, uint16_t* __restrict__ out, const mx::MxOut mo) {
   const int64_t width = heads * head_dim;
   const int64_t total = rows * (width >> 3);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -327,7 +335,8 @@ __global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t*
     uint32_t r[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) r[k] = pack_bf16x2(__fmul_rn(lo_bf16(w[k]), g), __fmul_rn(hi_bf16(w[k]), g));
-    *reinterpret_cast<uint4*>(out + row * width + c) = make_uint4(r[0], r[1], r[2], r[3]);
+    if (kMx) mx::mx_write8(r, row, c, mo, 0xFu << (threadIdx.x & 28));
+    if (out != nullptr) *reinterpret_cast<uint4*>(out + row * width + c) = make_uint4(r[0], r[1], r[2], r[3]);
   }
 }
 
@@ -349,8 +358,13 @@ static ltxq_status check_vec(const ltxq_vec& v, int64_t C, const char* name) {
 }
 
 ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int64_t C, const ltxq_prologue& pro,
-                                  void* out, cudaStream_t stream) {
-  if (!x || !out) return fail(LTXQ_ERR_INVALID, "adaln_modulate: x/out is NULL");
+                                  void* out, cudaStream_t stream, const ltxq_mx_act* out_mx) {
+  if (!x || (!out && !out_mx)) return fail(LTXQ_ERR_INVALID, "adaln_modulate: x/out is NULL");
+  if (out_mx) {
+    if (!mx::act_ok(out_mx)) return fail(LTXQ_ERR_INVALID, "adaln_modulate: out_mx terms / pointers invalid");
+    if (x_dtype != LTXQ_BF16 || C % 128 != 0 || C > 4096)
+      return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: MX output needs bf16 x, C % 128 == 0 and C <= 4096");
+  }
   if (rows < 0 || C <= 0) return fail(LTXQ_ERR_INVALID, "adaln_modulate: bad shape");
   if (C % 8 != 0 || C > 8192)
     return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: C must be a multiple of 8 and <= 8192");
@@ -363,6 +377,7 @@ ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int6
   if (pro.scale.dtype != pro.shift.dtype)
     return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: scale and shift must share a dtype");
   if (!aligned16(x) || !aligned16(out)) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: x/out not 16B aligned");
+  const mx::MxOut mo = out_mx ? mx::out_of(*out_mx, rows, C) : mx::MxOut{};
   if (rows == 0) return LTXQ_OK;
   if (rows > 0x7FFFFFFF) return fail(LTXQ_ERR_UNSUPPORTED, "adaln_modulate: too many rows");
   const VecArg s = to_vec(pro.scale), t = to_vec(pro.shift);
@@ -370,16 +385,24 @@ ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int6
   if (x_dtype == LTXQ_BF16 && C <= 4096) {
     auto* xb = static_cast<const uint16_t*>(x);
     auto* ob = static_cast<uint16_t*>(out);
-#define LTXQ_ROWS(CPL, WPR)                                                                              \
-  do {                                                                                                    \
-    const unsigned blocks = static_cast<unsigned>((rows + (8 / WPR) - 1) / (8 / WPR));                    \
-    if (vb) adaln_rows_kernel<CPL, WPR, true><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob); \
-    else adaln_rows_kernel<CPL, WPR, false><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob);   \
+#define LTXQ_ROWS_MX(CPL, WPR, MX)                                                                        \
+  do {                                                                                                     \
+    const unsigned blocks = static_cast<unsigned>((rows + (8 / WPR) - 1) / (8 / WPR));                     \
+    if (vb)                                                                                                \
+      adaln_rows_kernel<CPL, WPR, true, MX><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob, mo); \
+    else                                                                                                   \
+      adaln_rows_kernel<CPL, WPR, false, MX><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob, mo); \
+  } while (0)
+#define LTXQ_ROWS(CPL, WPR)                  \
+  do {                                       \
+    if (out_mx) LTXQ_ROWS_MX(CPL, WPR, true); \
+    else LTXQ_ROWS_MX(CPL, WPR, false);       \
   } while (0)
     if (C <= 1024) LTXQ_ROWS(4, 1);
     else if (C <= 2048) LTXQ_ROWS(8, 1);
     else LTXQ_ROWS(8, 2);
 #undef LTXQ_ROWS
+#undef LTXQ_ROWS_MX
     return launch_check("adaln_modulate launch");
   }
   int threads = static_cast<int>((C + 15) / 16);
@@ -427,7 +450,15 @@ extern "C" {
 ltxq_status ltxq_adaln_modulate(const void* x, int32_t x_dtype, int64_t rows, int64_t C, const ltxq_prologue* pro,
                                 void* out, void* stream) {
   if (!pro) return ltxq::fail(LTXQ_ERR_INVALID, "adaln_modulate: prologue is NULL");
-  return ltxq::launch_adaln_modulate(x, x_dtype, rows, C, *pro, out, static_cast<cudaStream_t>(stream));
+  if (!out) return ltxq::fail(LTXQ_ERR_INVALID, "adaln_modulate: x/out is NULL");
+  return ltxq::launch_adaln_modulate(x, x_dtype, rows, C, *pro, out, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+ltxq_status ltxq_adaln_modulate_mx(const void* x, int64_t rows, int64_t C, const ltxq_prologue* pro, void* out,
+                                   const ltxq_mx_act* out_mx, void* stream) {
+  if (!pro) return ltxq::fail(LTXQ_ERR_INVALID, "adaln_modulate_mx: prologue is NULL");
+  if (!out_mx) return ltxq::fail(LTXQ_ERR_INVALID, "adaln_modulate_mx: out_mx is NULL");
+  return ltxq::launch_adaln_modulate(x, LTXQ_BF16, rows, C, *pro, out, static_cast<cudaStream_t>(stream), out_mx);
 }
 
 ltxq_status ltxq_gated_add(const void* residual, const void* branch, const ltxq_vec* gate, int64_t rows, int64_t C,
@@ -436,22 +467,45 @@ ltxq_status ltxq_gated_add(const void* residual, const void* branch, const ltxq_
   return ltxq::launch_gated_add(residual, branch, *gate, rows, C, mode, out, static_cast<cudaStream_t>(stream));
 }
 
-ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
-                           void* out, void* stream) {
-  if (!o || !logits || !out) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate: NULL tensor");
-  if (rows < 0 || heads <= 0 || head_dim <= 0) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate: bad shape");
-  if (head_dim % 8 != 0) return ltxq::fail(LTXQ_ERR_UNSUPPORTED, "head_gate: head_dim must be a multiple of 8");
+static ltxq_status head_gate(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
+                             void* out, const ltxq_mx_act* out_mx, cudaStream_t stream) {
+  using namespace ltxq;
+  if (!o || !logits || (!out && !out_mx)) return fail(LTXQ_ERR_INVALID, "head_gate: NULL tensor");
+  if (rows < 0 || heads <= 0 || head_dim <= 0) return fail(LTXQ_ERR_INVALID, "head_gate: bad shape");
+  if (head_dim % 8 != 0) return fail(LTXQ_ERR_UNSUPPORTED, "head_gate: head_dim must be a multiple of 8");
   if ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(out)) & 15u)
-    return ltxq::fail(LTXQ_ERR_UNSUPPORTED, "head_gate: o/out must be 16-byte aligned");
+    return fail(LTXQ_ERR_UNSUPPORTED, "head_gate: o/out must be 16-byte aligned");
+  if (out_mx) {
+    if (!mx::act_ok(out_mx)) return fail(LTXQ_ERR_INVALID, "head_gate: out_mx terms / pointers invalid");
+    if ((heads * head_dim) % 128 != 0)
+      return fail(LTXQ_ERR_UNSUPPORTED, "head_gate: MX output needs heads * head_dim % 128 == 0");
+  }
   if (rows == 0) return LTXQ_OK;
   const int64_t work = rows * heads * head_dim / 8;
   const int threads = 256;
   const int64_t want = (work + threads - 1) / threads;
-  const unsigned blocks = static_cast<unsigned>(want < ltxq::num_sms() * 16 ? want : ltxq::num_sms() * 16);
-  ltxq::head_gate_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(logits), rows, heads, head_dim,
-      static_cast<uint16_t*>(out));
-  return ltxq::launch_check("head_gate launch");
+  const unsigned blocks = static_cast<unsigned>(want < num_sms() * 16 ? want : num_sms() * 16);
+  auto* oi = static_cast<const uint16_t*>(o);
+  auto* li = static_cast<const uint16_t*>(logits);
+  auto* oo = static_cast<uint16_t*>(out);
+  if (out_mx)
+    head_gate_kernel<true><<<blocks, threads, 0, stream>>>(oi, li, rows, heads, head_dim, oo,
+                                                           mx::out_of(*out_mx, rows, heads * head_dim));
+  else
+    head_gate_kernel<false><<<blocks, threads, 0, stream>>>(oi, li, rows, heads, head_dim, oo, mx::MxOut{});
+  return launch_check("head_gate launch");
+}
+
+ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
+                           void* out, void* stream) {
+  if (!out) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate: NULL tensor");
+  return head_gate(o, logits, rows, heads, head_dim, out, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+ltxq_status ltxq_head_gate_mx(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
+                              void* out, const ltxq_mx_act* out_mx, void* stream) {
+  if (!out_mx) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate_mx: out_mx is NULL");
+  return head_gate(o, logits, rows, heads, head_dim, out, out_mx, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -38,80 +38,17 @@
 // multicast.
 #include "common.cuh"
 #include "gemm_epilogue.cuh"
+#include "mx_act.cuh"
 
 namespace ltxq {
 namespace mx {
 
-constexpr int kGroup = 32;   // K values per E8M0 scale
-constexpr int kAtom = 512;   // scale-factor atom: 128 rows x 4 groups (one 128-K tile)
 constexpr int BM = 128;      // output features per CTA (MMA M = 256 per pair)
 constexpr int BN = 192;      // tokens per tile (MMA N)
 constexpr int BNC = BN / 2;  // tokens per CTA
 constexpr int BK = 128;      // K per stage = bytes of one fp8 row
 constexpr uint32_t kTmemCols = 512;
 constexpr int kGroupM = 16;  // token tiles that walk a feature tile together (L2 reuse of the weight)
-
-// ---------------------------------------------------------------- numerics
-
-// E8M0 exponent of a group whose largest magnitude is amax: the smallest e
-// with amax * 2^-e <= 448, and at least -127 (the smallest E8M0 value).
-__device__ __forceinline__ int group_exp(float amax) {
-  const uint32_t b = __float_as_uint(amax);
-  const int ef = static_cast<int>(b >> 23);
-  if (ef == 0) return -127;  // zero or an fp32 subnormal
-  // amax = m 2^E, m in [1, 2): 256 m <= 448 exactly when m <= 1.75
-  const int e = ef - 127 - 8 + ((b & 0x7FFFFFu) > 0x600000u ? 1 : 0);
-  return e < -127 ? -127 : e;
-}
-
-// 2^e for e in [-127, 127]
-__device__ __forceinline__ float exp2i(int e) {
-  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23) : __uint_as_float(0x00400000u);
-}
-
-// four fp32 values -> four E4M3 codes (RNE, saturating at +-448), value 0 in the low byte
-__device__ __forceinline__ uint32_t to_e4m3x4(float a0, float a1, float a2, float a3) {
-  uint16_t lo, hi;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(a1), "f"(a0));
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(a3), "f"(a2));
-  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-}
-
-// the exact values of four E4M3 codes (code 0 = low byte)
-__device__ __forceinline__ void e4m3x4_values(uint32_t c, float (&v)[4]) {
-  uint32_t h0, h1;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h0) : "h"(static_cast<uint16_t>(c & 0xFFFFu)));
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h1) : "h"(static_cast<uint16_t>(c >> 16)));
-  v[0] = __half2float(__ushort_as_half(static_cast<unsigned short>(h0 & 0xFFFFu)));
-  v[1] = __half2float(__ushort_as_half(static_cast<unsigned short>(h0 >> 16)));
-  v[2] = __half2float(__ushort_as_half(static_cast<unsigned short>(h1 & 0xFFFFu)));
-  v[3] = __half2float(__ushort_as_half(static_cast<unsigned short>(h1 >> 16)));
-}
-
-// Converts the 32 values of v (in place) to one MX term: codes c, E8M0 byte
-// s; v becomes the residual v - decode(c) * 2^e when kResidual.
-template <bool kResidual>
-__device__ __forceinline__ void mx_term(float (&v)[32], uint32_t (&c)[8], uint32_t& s) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const int e = group_exp(amax);
-  const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e, e in [-127, 121]
-  s = static_cast<uint32_t>(e + 127);
-#pragma unroll
-  for (int w = 0; w < 8; ++w)
-    c[w] = to_e4m3x4(v[4 * w] * inv, v[4 * w + 1] * inv, v[4 * w + 2] * inv, v[4 * w + 3] * inv);
-  if (kResidual) {
-    const float sc = exp2i(e);
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      float d[4];
-      e4m3x4_values(c[w], d);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * w + i] = __fsub_rn(v[4 * w + i], __fmul_rn(d[i], sc));  // exact
-    }
-  }
-}
 
 // ---------------------------------------------------------------- activation splitter
 
@@ -291,7 +228,7 @@ __global__ void __launch_bounds__(Plan<kTerms, kBlocks>::kThreads, 1)
                          const __grid_constant__ CUtensorMap tmap_hi, const __grid_constant__ CUtensorMap tmap_lo,
                          const __grid_constant__ CUtensorMap tmap_sfb_hi,
                          const __grid_constant__ CUtensorMap tmap_sfb_lo, int w_atom_cols, int x_atom_cols,
-                         const gemm::Params p) {
+                         const gemm::Params p, const MxOut out_mx) {
   using P = Plan<kTerms, kBlocks>;
   constexpr int S = P::kStages;
   constexpr int kRows = kBlocks * BM;  // weight rows per CTA
@@ -511,9 +448,12 @@ __global__ void __launch_bounds__(Plan<kTerms, kBlocks>::kThreads, 1)
           for (int pass = 0; pass < 4; ++pass) {
             const int jr = (lane >> 2) + 8 * pass;
             const uint4 a = *reinterpret_cast<const uint4*>(stw + jr * 32 + (lane & 3) * 8);
-            if (m_c + jr < p.M && nf < p.N) {
+            if (m_c + jr < p.M && nf < p.N) {  // uniform over each lane quad (one row, one 32-feature group)
               uint32_t uw[4] = {a.x, a.y, a.z, a.w};
-              gemm::epi_row_store(p, uw, m_c + jr, nf, g8b, gated, two_round, gate_bcast);
+              if (out_mx.hi != nullptr)  // the next GEMM's input form instead of bf16 rows
+                mx_write8(uw, m_c + jr, nf, out_mx, 0xFu << (lane & ~3));
+              else
+                gemm::epi_row_store(p, uw, m_c + jr, nf, g8b, gated, two_round, gate_bcast);
             }
           }
           __syncwarp();  // transpose tile consumed
@@ -571,7 +511,8 @@ static int pick_blocks(int64_t M, int64_t N) {
 template <int kTerms, int kBlocks>
 static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, const CUtensorMap& thi,
                                const CUtensorMap& tlo, const CUtensorMap& tsfb_hi, const CUtensorMap& tsfb_lo,
-                               int w_atom_cols, int x_atom_cols, const gemm::Params& p, cudaStream_t stream) {
+                               int w_atom_cols, int x_atom_cols, const gemm::Params& p, const MxOut& out_mx,
+                               cudaStream_t stream) {
   using PL = Plan<kTerms, kBlocks>;
   auto kern = qgemm_mx_pair_kernel<kTerms, kBlocks>;
   if (ltxq_status st = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem),
@@ -593,7 +534,7 @@ static ltxq_status launch_gemm(const CUtensorMap& tw, const CUtensorMap& tsfa, c
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e =
-      cudaLaunchKernelEx(&cfg, kern, tw, tsfa, thi, tlo, tsfb_hi, tsfb_lo, w_atom_cols, x_atom_cols, p);
+      cudaLaunchKernelEx(&cfg, kern, tw, tsfa, thi, tlo, tsfb_hi, tsfb_lo, w_atom_cols, x_atom_cols, p, out_mx);
   if (e == cudaSuccess) note_launch();
   return cuda_check(e, "mxfp8 block-scaled GEMM launch");
 }
@@ -630,20 +571,15 @@ ltxq_status launch_mx_split(const void* x, int64_t M, int64_t K, int terms, void
   return launch_check("mx split launch");
 }
 
-// The native path: split x into MX terms in the workspace, then the
-// block-scaled GEMM.  The caller checked the shapes, pointers, alignment and
-// epilogue and that mx_workspace_bytes(M, w) > 0 fits the workspace.
-ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, const gemm::Params& p, void* workspace,
-                              cudaStream_t stream) {
-  const int terms = w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1;
+// The block-scaled GEMM from activations already in MX form (codes and
+// scale atoms of `terms` terms, M rows, row_tiles = ceil(M / 128) + 1).  With
+// out_mx.hi set, the epilogue writes its result as MX terms (bias / GELU
+// applied, rounded to bf16 first) instead of bf16 rows.
+static ltxq_status launch_gemm_from_terms(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi,
+                                          const uint8_t* sf_lo, int terms, int64_t M, const ltxq_qweight& w,
+                                          const gemm::Params& p, const mx::MxOut& out_mx, cudaStream_t stream) {
   const int64_t K = w.k_in, N = w.n_out;
   const mx::Layout l = mx::layout(M, K, terms);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  uint8_t* hi = ws;
-  uint8_t* lo = ws + l.codes;
-  uint8_t* sf_hi = ws + terms * l.codes;
-  uint8_t* sf_lo = sf_hi + l.sf;
-  if (ltxq_status st = launch_mx_split(x, M, K, terms, hi, lo, sf_hi, sf_lo, stream)) return st;
   const int blocks = mx::pick_blocks(M, N);
   CUtensorMap tw, tsfa, thi, tlo, tsbh, tsbl;
   // weight: [N rows][K E4M3 bytes], 128-byte rows of 128 features per block, 128B swizzle
@@ -671,16 +607,101 @@ ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, c
     if (ltxq_status st = encode_tmap_2d(&tsbl, CU_TENSOR_MAP_DATA_TYPE_UINT8, sf_lo, 16,
                                         l.k_tiles * l.row_tiles * 32, 16, 16, 64, CU_TENSOR_MAP_SWIZZLE_NONE))
       return st;
-    return blocks == 2 ? mx::launch_gemm<2, 2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream)
-                       : mx::launch_gemm<2, 1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
+    return blocks == 2 ? mx::launch_gemm<2, 2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, out_mx, stream)
+                       : mx::launch_gemm<2, 1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, out_mx, stream);
   }
-  return blocks == 2 ? mx::launch_gemm<1, 2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream)
-                     : mx::launch_gemm<1, 1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, stream);
+  return blocks == 2 ? mx::launch_gemm<1, 2>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, out_mx, stream)
+                     : mx::launch_gemm<1, 1>(tw, tsfa, thi, tlo, tsbh, tsbl, wc, xc, p, out_mx, stream);
 }
+
+// The MX terms of M rows of K values in a workspace of mx_act_bytes(M, K,
+// terms) bytes: the codes of each term, then the scale atoms of each term.
+size_t mx_act_bytes(int64_t M, int64_t K, int terms) { return mx::layout(M, K, terms).total; }
+
+ltxq_mx_act mx_workspace_act(int64_t M, int64_t K, int terms, void* workspace) {
+  const mx::Layout l = mx::layout(M, K, terms);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  ltxq_mx_act a{};
+  a.hi = ws;
+  a.lo = terms == 2 ? ws + l.codes : nullptr;
+  a.sf_hi = ws + terms * l.codes;
+  a.sf_lo = terms == 2 ? ws + terms * l.codes + l.sf : nullptr;
+  a.terms = terms;
+  return a;
+}
+
+// The native path from bf16 activations: split x into MX terms in the
+// workspace, then the block-scaled GEMM.  The caller checked the shapes,
+// pointers, alignment and epilogue and that mx_workspace_bytes(M, w) > 0 fits
+// the workspace.
+ltxq_status launch_qlinear_mx(const void* x, int64_t M, const ltxq_qweight& w, const gemm::Params& p, void* workspace,
+                              cudaStream_t stream) {
+  const int terms = w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1;
+  const ltxq_mx_act a = mx_workspace_act(M, w.k_in, terms, workspace);
+  auto* hi = static_cast<uint8_t*>(a.hi);
+  auto* lo = static_cast<uint8_t*>(a.lo);
+  auto* sf_hi = static_cast<uint8_t*>(a.sf_hi);
+  auto* sf_lo = static_cast<uint8_t*>(a.sf_lo);
+  if (ltxq_status st = launch_mx_split(x, M, w.k_in, terms, hi, lo, sf_hi, sf_lo, stream)) return st;
+  return launch_gemm_from_terms(hi, lo, sf_hi, sf_lo, terms, M, w, p, mx::MxOut{}, stream);
+}
+
+ltxq_status check_epilogue(const ltxq_epilogue* epi, int64_t M, int64_t N);
 
 }  // namespace ltxq
 
 extern "C" {
+
+int32_t ltxq_qlinear_mx_supported(int64_t M, const ltxq_qweight* w) {
+  return (w && ltxq::mx_workspace_bytes(M, *w) > 0) ? 1 : 0;
+}
+
+ltxq_status ltxq_qlinear_mx(const ltxq_mx_act* x, int64_t M, const ltxq_qweight* w, const ltxq_epilogue* epi,
+                            void* out, const ltxq_mx_act* out_mx, void* stream) {
+  using namespace ltxq;
+  if (!x || !w) return fail(LTXQ_ERR_INVALID, "qlinear_mx: NULL argument");
+  if (M < 0) return fail(LTXQ_ERR_INVALID, "qlinear_mx: M < 0");
+  if (!mx::act_ok(x)) return fail(LTXQ_ERR_INVALID, "qlinear_mx: x terms / pointers (16-byte aligned) invalid");
+  if (M > 0 && !ltxq_qlinear_mx_supported(M, w))
+    return fail(LTXQ_ERR_UNSUPPORTED,
+                "qlinear_mx: the block-scaled kernels do not run this GEMM (ltxq_qlinear_mx_supported)");
+  if ((w->compute == LTXQ_COMPUTE_MX2 ? 2 : 1) != x->terms)
+    return fail(LTXQ_ERR_INVALID, "qlinear_mx: x's term count does not match the weight's compute mode");
+  if (ltxq_status st = check_epilogue(epi, M, w->n_out)) return st;
+  if (w->bias && (reinterpret_cast<uintptr_t>(w->bias) & 15u))
+    return fail(LTXQ_ERR_UNSUPPORTED, "qlinear_mx: bias must be 16-byte aligned");
+  const int kind = epi ? epi->kind : LTXQ_EPI_NONE;
+  if (out_mx) {
+    if (!mx::act_ok(out_mx)) return fail(LTXQ_ERR_INVALID, "qlinear_mx: out_mx terms / pointers invalid");
+    if (kind != LTXQ_EPI_NONE && kind != LTXQ_EPI_GELU)
+      return fail(LTXQ_ERR_UNSUPPORTED, "qlinear_mx: MX output takes the none / GELU epilogues only");
+    if (w->n_out % 128 != 0) return fail(LTXQ_ERR_UNSUPPORTED, "qlinear_mx: MX output needs N % 128 == 0");
+  } else if (!out || (reinterpret_cast<uintptr_t>(out) & 15u)) {
+    return fail(LTXQ_ERR_INVALID, "qlinear_mx: out is NULL or not 16-byte aligned");
+  }
+  if (M == 0) return LTXQ_OK;
+  gemm::Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(w->n_out);
+  p.K = static_cast<int>(w->k_in);
+  p.gs = w->group_size;
+  p.scales = w->scales;
+  p.bias = static_cast<const uint16_t*>(w->bias);
+  p.epi = kind;
+  if (epi && (kind == LTXQ_EPI_GATED_RESIDUAL || kind == LTXQ_EPI_GATE_THEN_ADD)) {
+    p.gate = to_vec(epi->gate);
+    p.residual = static_cast<const uint16_t*>(epi->residual);
+  } else {
+    p.gate = VecArg{nullptr, LTXQ_F32, 0, 0};
+  }
+  p.out = static_cast<uint16_t*>(out);
+  p.err = dev_error_word();
+  if (!p.err) return fail(LTXQ_ERR_CUDA, "qlinear_mx: device error word unavailable");
+  const mx::MxOut om = out_mx ? mx::out_of(*out_mx, M, w->n_out) : mx::MxOut{};
+  return launch_gemm_from_terms(static_cast<const uint8_t*>(x->hi), static_cast<const uint8_t*>(x->lo),
+                                static_cast<const uint8_t*>(x->sf_hi), static_cast<const uint8_t*>(x->sf_lo), x->terms,
+                                M, *w, p, om, static_cast<cudaStream_t>(stream));
+}
 
 size_t ltxq_mx_split_sizes(int64_t M, int64_t K, size_t* codes_bytes, size_t* scale_bytes) {
   if (M <= 0 || K <= 0 || K % 128 != 0) return 0;

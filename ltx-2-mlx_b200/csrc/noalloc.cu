@@ -36,7 +36,7 @@
 namespace ltxq {
 
 ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int64_t C, const ltxq_prologue& pro,
-                                  void* out, cudaStream_t stream);
+                                  void* out, cudaStream_t stream, const ltxq_mx_act* out_mx);
 ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, const ltxq_epilogue* epi, void* out,
                            cudaStream_t stream, void* workspace, size_t workspace_bytes);
 
@@ -89,6 +89,6 @@ extern "C" ltxq_status ltxq_adaln_qlinear_noalloc(const void* x, int64_t M, cons
   void* scratch = nullptr;
   if (ltxq_status st = noalloc_scratch(&scratch)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (ltxq_status st = launch_adaln_modulate(x, LTXQ_BF16, M, w->k_in, *pro, scratch, s)) return st;
+  if (ltxq_status st = launch_adaln_modulate(x, LTXQ_BF16, M, w->k_in, *pro, scratch, s, nullptr)) return st;
   return launch_qlinear(scratch, M, *w, epi, out, s, nullptr, 0);  // unsplit: no partials
 }

@@ -34,7 +34,10 @@ namespace ltxq {
 
 ltxq_status check_qweight(const ltxq_qweight& w, bool need_data, int64_t* R, int64_t* L);
 ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int64_t C, const ltxq_prologue& pro,
-                                  void* out, cudaStream_t stream);
+                                  void* out, cudaStream_t stream, const ltxq_mx_act* out_mx);
+ltxq_status launch_mx_split(const void* x, int64_t M, int64_t K, int terms, void* hi, void* lo, void* sf_hi,
+                            void* sf_lo, cudaStream_t stream);
+ltxq_mx_act mx_workspace_act(int64_t M, int64_t K, int terms, void* workspace);
 namespace gemm {
 struct Params;
 }
@@ -1432,7 +1435,7 @@ static ltxq_status launch_qk(int bn, const CUtensorMap& tx, const CUtensorMap& t
 
 }  // namespace gemm
 
-static ltxq_status check_epilogue(const ltxq_epilogue* epi, int64_t M, int64_t N) {
+ltxq_status check_epilogue(const ltxq_epilogue* epi, int64_t M, int64_t N) {
   if (!epi) return LTXQ_OK;
   switch (epi->kind) {
     case LTXQ_EPI_NONE:
@@ -1558,6 +1561,19 @@ ltxq_status launch_qlinear(const void* x, int64_t M, const ltxq_qweight& w, cons
 
 static size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
 
+static int mx_terms(const ltxq_qweight& w) { return w.compute == LTXQ_COMPUTE_MX2 ? 2 : 1; }
+
+// the AdaLN pass can write this GEMM's block-scaled input (bf16 rows of at most 4096)
+static bool adaln_mx_fusable(int64_t M, const ltxq_qweight& w) {
+  return mx_workspace_bytes(M, w) > 0 && w.k_in <= 4096;
+}
+
+// both FF GEMMs run block-scaled; the hidden activations pass between them as MX terms
+static bool ff_mx_fusable(int64_t M, const ltxq_qweight& w_in, const ltxq_qweight& w_out) {
+  return adaln_mx_fusable(M, w_in) && mx_workspace_bytes(M, w_out) > 0 && w_in.n_out % 128 == 0 &&
+         w_out.k_in == w_in.n_out;
+}
+
 }  // namespace ltxq
 
 extern "C" {
@@ -1572,14 +1588,20 @@ size_t ltxq_qlinear_workspace_size(int64_t M, const ltxq_qweight* w) {
   return ltxq::align_up(ltxq::gemm::splitk_bytes(M, w->n_out, w->k_in));
 }
 
+// With block-scaled weights (and the AdaLN pass able to write MX terms:
+// K <= 4096) the prologue writes the GEMM's MX input directly into the
+// workspace, and in the FF the first GEMM's epilogue writes the second's.
 size_t ltxq_adaln_qlinear_workspace_size(int64_t M, const ltxq_qweight* w) {
   if (!w || M <= 0) return 0;
+  if (ltxq::adaln_mx_fusable(M, *w)) return ltxq::align_up(ltxq::mx_workspace_bytes(M, *w));
   return ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w->k_in) * 2) +
          ltxq_qlinear_workspace_size(M, w);
 }
 
 size_t ltxq_feed_forward_workspace_size(int64_t M, const ltxq_qweight* w_in, const ltxq_qweight* w_out) {
   if (!w_in || !w_out || M <= 0) return 0;
+  if (ltxq::ff_mx_fusable(M, *w_in, *w_out))
+    return ltxq::align_up(ltxq::mx_workspace_bytes(M, *w_in)) + ltxq::align_up(ltxq::mx_workspace_bytes(M, *w_out));
   const size_t a = ltxq_qlinear_workspace_size(M, w_in), b = ltxq_qlinear_workspace_size(M, w_out);
   return ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->k_in) * 2) +
          ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->n_out) * 2) + (a > b ? a : b);
@@ -1600,7 +1622,12 @@ ltxq_status ltxq_adaln_qlinear(const void* x, int64_t M, const ltxq_prologue* pr
     return ltxq::fail(LTXQ_ERR_INVALID, "adaln_qlinear: workspace too small");
   if (M == 0) return LTXQ_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w->k_in, *pro, workspace, s)) return st;
+  if (ltxq::adaln_mx_fusable(M, *w)) {
+    const ltxq_mx_act a = ltxq::mx_workspace_act(M, w->k_in, ltxq::mx_terms(*w), workspace);
+    if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w->k_in, *pro, nullptr, s, &a)) return st;
+    return ltxq_qlinear_mx(&a, M, w, epi, out, nullptr, stream);
+  }
+  if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w->k_in, *pro, workspace, s, nullptr)) return st;
   const size_t a_bytes = ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w->k_in) * 2);
   return ltxq::launch_qlinear(workspace, M, *w, epi, out, s, static_cast<char*>(workspace) + a_bytes,
                               workspace_bytes - a_bytes);
@@ -1617,14 +1644,26 @@ ltxq_status ltxq_feed_forward(const void* x, int64_t M, const ltxq_prologue* pro
   if (M == 0) return LTXQ_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
+  ltxq_epilogue gelu{};
+  gelu.kind = LTXQ_EPI_GELU;
+  if (ltxq::ff_mx_fusable(M, *w_in, *w_out)) {
+    const ltxq_mx_act a = ltxq::mx_workspace_act(M, w_in->k_in, ltxq::mx_terms(*w_in), ws);
+    const ltxq_mx_act h = ltxq::mx_workspace_act(M, w_out->k_in, ltxq::mx_terms(*w_out),
+                                                 ws + ltxq::align_up(ltxq::mx_workspace_bytes(M, *w_in)));
+    if (pro) {
+      if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w_in->k_in, *pro, nullptr, s, &a)) return st;
+    } else if (ltxq_status st = ltxq_mx_split(x, M, w_in->k_in, a.terms, a.hi, a.lo, a.sf_hi, a.sf_lo, stream)) {
+      return st;
+    }
+    if (ltxq_status st = ltxq_qlinear_mx(&a, M, w_in, &gelu, nullptr, &h, stream)) return st;
+    return ltxq_qlinear_mx(&h, M, w_out, epi, out, nullptr, stream);
+  }
   const void* a = x;
   if (pro) {
-    if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w_in->k_in, *pro, ws, s)) return st;
+    if (ltxq_status st = ltxq::launch_adaln_modulate(x, LTXQ_BF16, M, w_in->k_in, *pro, ws, s, nullptr)) return st;
     a = ws;
   }
   void* hidden = ws + ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->k_in) * 2);
-  ltxq_epilogue gelu{};
-  gelu.kind = LTXQ_EPI_GELU;
   const size_t h_bytes = ltxq::align_up(static_cast<size_t>(M) * static_cast<size_t>(w_in->n_out) * 2);
   char* part = static_cast<char*>(hidden) + h_bytes;
   const size_t part_bytes = workspace_bytes - static_cast<size_t>(part - ws);

@@ -61,6 +61,17 @@ class Prologue(ctypes.Structure):
     _fields_ = [("norm", c_int32), ("eps", c_float), ("scale", Vec), ("shift", Vec)]
 
 
+class MxAct(ctypes.Structure):
+    _fields_ = [
+        ("hi", c_void_p),
+        ("lo", c_void_p),
+        ("sf_hi", c_void_p),
+        ("sf_lo", c_void_p),
+        ("terms", c_int32),
+        ("pad_", c_int32),
+    ]
+
+
 class DenoiseParams(ctypes.Structure):
     _fields_ = [
         ("sigma", c_float),
@@ -100,6 +111,13 @@ SIGNATURES = {
     "ltxq_mx_pack_weight_scales": (c_int32, [POINTER(QWeight), c_void_p, c_void_p]),
     "ltxq_mx_split": (c_int32, [c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p]),
+    "ltxq_qlinear_mx_supported": (c_int32, [c_int64, POINTER(QWeight)]),
+    "ltxq_qlinear_mx": (c_int32, [POINTER(MxAct), c_int64, POINTER(QWeight), POINTER(Epilogue), c_void_p,
+                                  POINTER(MxAct), c_void_p]),
+    "ltxq_adaln_modulate_mx": (c_int32, [c_void_p, c_int64, c_int64, POINTER(Prologue), c_void_p, POINTER(MxAct),
+                                         c_void_p]),
+    "ltxq_head_gate_mx": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, POINTER(MxAct),
+                                    c_void_p]),
     "ltxq_adaln_qlinear_noalloc": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight),
                                              POINTER(Epilogue), c_void_p, c_void_p]),
     "ltxq_feed_forward": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(QWeight),

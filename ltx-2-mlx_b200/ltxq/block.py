@@ -349,7 +349,14 @@ class QAttention:
         o = F.scaled_dot_product_attention(qh, kh, vh, scale=1.0 / math.sqrt(self.d_head))
         b, h, t, d = o.shape
         o = o.transpose(1, 2).reshape(b, t, h * d)
-        return K.head_gate(o, gl.contiguous(), self.heads)
+        return self._gate(o, gl)
+
+    def _gate(self, o: torch.Tensor, gl: torch.Tensor):
+        """The per-head output gate, written in to_out's MX input form where
+        to_out runs block-scaled."""
+        width = o.shape[-1]
+        terms = self.to_out.mx_terms(o.numel() // width) if width % 128 == 0 else 0
+        return K.head_gate(o, gl.contiguous(), self.heads, mx_terms=terms)
 
     def attend_head_parallel(self, qkv_recv: torch.Tensor, gl, shard: "RowShard") -> torch.Tensor:
         """Row-sharded self-attention in head-parallel form: ``qkv_recv`` is
@@ -362,7 +369,7 @@ class QAttention:
         q, k, v = (ranks_to_sequence(qkv_recv[:, i]) for i in range(3))
         o = F.scaled_dot_product_attention(q, k, v, scale=1.0 / math.sqrt(self.d_head))
         back = shard.all_to_all(sequence_to_ranks(o, shard.world))
-        return K.head_gate(ranks_to_heads(back), gl.contiguous(), self.heads)
+        return self._gate(ranks_to_heads(back), gl)
 
     def attend_split_keys(self, q, k_local, v_local, gl, shard: "RowShard") -> torch.Tensor:
         """Attention of replicated queries over keys / values sharded by rows:
@@ -384,7 +391,7 @@ class QAttention:
         lses = parts[:, n_o:].view((shard.world,) + tuple(o.shape[:-1]))
         merged = merge_attention_partials(outs, lses).to(torch.bfloat16)
         b, h, t, d = merged.shape
-        return K.head_gate(merged.transpose(1, 2).reshape(b, t, h * d), gl.contiguous(), self.heads)
+        return self._gate(merged.transpose(1, 2).reshape(b, t, h * d), gl)
 
 
 def _cat_linears(parts: list[QuantizedLinear]) -> QuantizedLinear:
@@ -526,7 +533,7 @@ class BasicAVTransformerBlock:
         pend = None
         if run_v:
             sh, sc, g = self._ada("scale_shift_table", video.timesteps, 0, 3)
-            q, k, v, gl = at.project(K.adaln_modulate(vx, sc, sh, eps), None)
+            q, k, v, gl = at.project(self._mod(vx, sc, sh, at.q_proj), None)
             q, k = at.norm_rope(q, k, video.positional_embeddings)
             if head_par:  # head-parallel attention: Q/K/V all-to-all, then SDPA on H/world heads
                 qkv = torch.stack([heads_to_ranks(t_, shard.world, at.heads) for t_ in (q, k, v)], dim=1)
@@ -538,7 +545,7 @@ class BasicAVTransformerBlock:
         if run_a:
             sh_a, sc_a, g_a = self._ada("audio_scale_shift_table", audio.timesteps, 0, 3)
             at_a = self.attn["audio_attn1"]
-            qa, ka, va, gla = at_a.project(K.adaln_modulate(ax, sc_a, sh_a, eps), None)
+            qa, ka, va, gla = at_a.project(self._mod(ax, sc_a, sh_a, at_a.q_proj), None)
             o = at_a.core(qa, ka, va, gla, audio.positional_embeddings)
             ax = at_a.to_out(o, residual=ax, gate=g_a)
         ax = self._text_ca(ax, audio, "audio_attn2", "audio_scale_shift_table", "audio_prompt_scale_shift_table")
@@ -565,14 +572,14 @@ class BasicAVTransformerBlock:
         g_a2v = (self.tables["scale_shift_table_a2v_ca_video"][4][None, None] + video.cross_gate_timestep[:, :, 0])
         at = self.attn["audio_to_video_attn"]
         if run_a2v:
-            q, k, v, gl = at.project(K.adaln_modulate(vx, v_sc_a2v, v_sh_a2v, eps),
-                                     K.adaln_modulate(ax, a_sc_a2v, a_sh_a2v, eps))
+            q, k, v, gl = at.project(self._mod(vx, v_sc_a2v, v_sh_a2v, at.q_proj),
+                                     self._mod(ax, a_sc_a2v, a_sh_a2v, at.kv_proj))
         at2 = self.attn["video_to_audio_attn"]
         split_keys = sharded and shard.v2a == "split_keys"
         pend2 = None
         if run_v2a:
-            q2, k2, v2, gl2 = at2.project(K.adaln_modulate(ax, a_sc_v2a, a_sh_v2a, eps),
-                                          K.adaln_modulate(vx, v_sc_v2a, v_sh_v2a, eps))
+            q2, k2, v2, gl2 = at2.project(self._mod(ax, a_sc_v2a, a_sh_v2a, at2.q_proj),
+                                          self._mod(vx, v_sc_v2a, v_sh_v2a, at2.kv_proj))
             q2, k2 = at2.norm_rope(q2, k2, audio.cross_positional_embeddings, video.cross_positional_embeddings)
             pend2 = shard.start_gather(k2, v2) if sharded and not split_keys else None
         if run_a2v:
@@ -617,18 +624,30 @@ class BasicAVTransformerBlock:
         kv = self.tables[prompt_table][None, None] + args.prompt_timestep
         shift_kv, scale_kv = kv[:, :, 0], kv[:, :, 1]
         at = self.attn[name]
-        q, k, v, gl = at.project(K.adaln_modulate(x, sc_q, sh_q, eps),
-                                 K.adaln_modulate(args.context, scale_kv, shift_kv, eps, "none"))
+        q, k, v, gl = at.project(self._mod(x, sc_q, sh_q, at.q_proj),
+                                 self._mod(args.context, scale_kv, shift_kv, at.kv_proj, "none"))
         o = at.core(q, k, v, gl)
         return at.to_out(o, residual=x, gate=g, gate_then_add=True)
+
+    def _mod(self, x, scale, shift, consumer: QuantizedLinear, norm: str = "rms"):
+        """AdaLN modulate (transformer.py:21-37, 379) of rows that feed
+        ``consumer``: written directly in the block-scaled GEMM's MX input
+        form where that GEMM runs block-scaled (the same bits as splitting
+        the bf16 result), else as bf16."""
+        C = x.shape[-1]
+        terms = consumer.mx_terms(x.numel() // C) if K.mx_output_ok(C) and x.dtype == torch.bfloat16 else 0
+        return K.adaln_modulate(x, scale, shift, self.norm_eps, norm, mx_terms=terms)
 
     def _ff(self, x, args: TransformerArgs, table: str, ff):
         sh, sc, g = self._ada(table, args.timesteps, 3, 6)
         probe = self.probe if ff is self.ff else None
-        a = K.adaln_modulate(x, sc, sh, self.norm_eps)
+        a = self._mod(x, sc, sh, ff[0])
         if probe is not None:
             probe("ff_in_start")
-        h = ff[0](a, gelu=True)
+        # GELU(project_in) passes to project_out in its MX input form when
+        # both run block-scaled
+        h_terms = ff[1].mx_terms(a.M) if isinstance(a, K.MXActivation) and ff[1].in_features % 128 == 0 else 0
+        h = ff[0](a, gelu=True, mx_out=h_terms)
         if probe is not None:
             probe("ff_in_end")
         return ff[1](h, residual=x, gate=g)

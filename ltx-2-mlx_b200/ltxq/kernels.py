@@ -11,6 +11,7 @@ multiple of 8) runs the CUDA kernel, and anything else raises ``ValueError``.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -60,16 +61,93 @@ def vec_arg(v: torch.Tensor, rows_shape: tuple[int, ...], C: int, name: str, kee
     raise ValueError(f"{name} shape {tuple(v.shape)} does not broadcast against {rows_shape + (C,)}")
 
 
+class MXActivation:
+    """Activations in the input form of the block-scaled GEMMs
+    (``ltxq_mx_act``: per term [M, K] E4M3 codes and E8M0 scales in the MMA's
+    atom layout; ``terms`` 2 or 1).  Written by ``adaln_modulate`` /
+    ``head_gate`` with ``mx_terms`` and by ``QuantizedLinear`` with
+    ``mx_out``, read by ``QuantizedLinear``; the bits are those
+    ``ltxq_mx_split`` gives for the bf16 values.  One device buffer holds
+    every part."""
+
+    def __init__(self, rows_shape: tuple[int, ...], K: int, terms: int, device):
+        if terms not in (1, 2):
+            raise ValueError("terms must be 1 or 2")
+        self.rows_shape = tuple(rows_shape)
+        self.K = int(K)
+        self.terms = int(terms)
+        self.M = math.prod(self.rows_shape)
+        codes, sf = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        if not _lib.load().ltxq_mx_split_sizes(self.M, self.K, ctypes.byref(codes), ctypes.byref(sf)):
+            raise ValueError(f"no MX form for {self.M} x {self.K} (K % 128 == 0 and M > 0 needed)")
+        cb, sb = _align(codes.value), _align(sf.value)
+        self.buffer = torch.empty(terms * (cb + sb), dtype=torch.uint8, device=device)
+        base = self.buffer.data_ptr()
+        self._parts = (base, base + cb if terms == 2 else None, base + terms * cb,
+                       base + terms * cb + sb if terms == 2 else None)
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        return self.rows_shape + (self.K,)
+
+    @property
+    def device(self):
+        return self.buffer.device
+
+    def tensors(self) -> tuple:
+        """(hi, lo, sf_hi, sf_lo) as uint8 views of the buffer: codes [M, K],
+        scale atoms flat (ltxq_mx_split_sizes bytes); lo / sf_lo None for one
+        term."""
+        codes, sf = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _lib.load().ltxq_mx_split_sizes(self.M, self.K, ctypes.byref(codes), ctypes.byref(sf))
+        base = self.buffer.data_ptr()
+        out = []
+        for ptr, n, shape in zip(self._parts, (codes.value, codes.value, sf.value, sf.value),
+                                 ((self.M, self.K), (self.M, self.K), (-1,), (-1,))):
+            out.append(None if ptr is None else self.buffer[ptr - base:ptr - base + n].view(shape))
+        return tuple(out)
+
+    def struct(self) -> _lib.MxAct:
+        hi, lo, sf_hi, sf_lo = self._parts
+        return _lib.MxAct(hi, lo, sf_hi, sf_lo, self.terms, 0)
+
+    @classmethod
+    def split(cls, x: torch.Tensor, terms: int) -> "MXActivation":
+        """The MX form of bf16 ``x`` (``ltxq_mx_split``)."""
+        _require_cuda(x, "x")
+        if x.dtype != torch.bfloat16:
+            raise ValueError("x must be bfloat16")
+        x = x.contiguous()
+        act = cls(tuple(x.shape[:-1]), x.shape[-1], terms, x.device)
+        hi, lo, sf_hi, sf_lo = act._parts
+        _lib.check(_lib.load().ltxq_mx_split(x.data_ptr(), act.M, act.K, terms, hi, lo, sf_hi, sf_lo, _stream()),
+                   "mx_split")
+        return act
+
+
+def _align(n: int) -> int:
+    return (n + 255) & ~255
+
+
+def mx_output_ok(C: int) -> bool:
+    """Whether the row kernels (AdaLN, head gate) can write C channels in the
+    MX form (32-channel groups held by lane quads, at most 4096 channels for
+    the AdaLN pass)."""
+    return C % 128 == 0 and C <= 4096
+
+
 def prologue(norm: int, eps: float, scale, shift, rows_shape, C, keep) -> _lib.Prologue:
     return _lib.Prologue(norm, float(eps), vec_arg(scale, rows_shape, C, "scale", keep),
                          vec_arg(shift, rows_shape, C, "shift", keep))
 
 
 def adaln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, eps: float = 1e-6,
-                   norm: str = "rms") -> torch.Tensor:
+                   norm: str = "rms", mx_terms: int = 0):
     """``bf16(norm(x) * (1 + scale) + shift)`` with norm in {"rms", "layer",
     "none"}; "none" is the text cross-attention context modulation
-    (transformer.py:379)."""
+    (transformer.py:379).  ``mx_terms`` 1 or 2 returns the result as an
+    ``MXActivation`` instead (the next block-scaled GEMM's input; bf16 x,
+    ``mx_output_ok(C)``)."""
     _require_cuda(x, "x")
     if x.dtype not in _DT:
         raise ValueError(f"x dtype must be bfloat16 or float32, got {x.dtype}")
@@ -79,8 +157,14 @@ def adaln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor, ep
     keep: list = []
     nk = {"rms": _lib.NORM_RMS, "layer": _lib.NORM_LAYER, "none": _lib.NORM_NONE}[norm]
     pro = prologue(nk, eps, scale, shift, rows_shape, C, keep)
-    out = torch.empty_like(x)
     lib = _lib.load()
+    if mx_terms:
+        act = MXActivation(rows_shape, C, mx_terms, x.device)
+        st = act.struct()
+        _lib.check(lib.ltxq_adaln_modulate_mx(x.data_ptr(), act.M, C, ctypes.byref(pro), None, ctypes.byref(st),
+                                              _stream()), "adaln_modulate_mx")
+        return act
+    out = torch.empty_like(x)
     _lib.check(lib.ltxq_adaln_modulate(x.data_ptr(), _DT[x.dtype], x.numel() // C, C, ctypes.byref(pro),
                                        out.data_ptr(), _stream()), "adaln_modulate")
     return out
@@ -117,9 +201,9 @@ def gated_add_fused(residual: torch.Tensor, branch: torch.Tensor, gate: torch.Te
     return out
 
 
-def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int) -> torch.Tensor:
+def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int, mx_terms: int = 0):
     """``out * (2 * sigmoid(gate_logits))[..., None]`` per head
-    (attention.py:559-601)."""
+    (attention.py:559-601).  ``mx_terms`` as in ``adaln_modulate``."""
     _require_cuda(out, "out")
     _require_cuda(gate_logits, "gate_logits")
     if out.dtype != torch.bfloat16 or gate_logits.dtype != torch.bfloat16:
@@ -130,6 +214,12 @@ def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int) -> torch
     rows = out.numel() // width
     if gate_logits.numel() != rows * heads:
         raise ValueError("gate_logits must have one value per (row, head)")
+    if mx_terms:
+        act = MXActivation(tuple(out.shape[:-1]), width, mx_terms, out.device)
+        st = act.struct()
+        _lib.check(_lib.load().ltxq_head_gate_mx(out.data_ptr(), gate_logits.data_ptr(), rows, heads, width // heads,
+                                                 None, ctypes.byref(st), _stream()), "head_gate_mx")
+        return act
     res = torch.empty_like(out)
     _lib.check(_lib.load().ltxq_head_gate(out.data_ptr(), gate_logits.data_ptr(), rows, heads, width // heads,
                                           res.data_ptr(), _stream()), "head_gate")

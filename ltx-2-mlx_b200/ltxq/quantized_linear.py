@@ -21,7 +21,7 @@ import math
 import torch
 
 from . import _lib
-from .kernels import _require_cuda, _stream, prologue, vec_arg
+from .kernels import MXActivation, _require_cuda, _stream, prologue, vec_arg
 
 QUANT_DEFAULTS = {"affine": (64, 4), "mxfp8": (32, 8)}
 _MODE = {"affine": _lib.AFFINE, "mxfp8": _lib.MXFP8}
@@ -168,6 +168,16 @@ class QuantizedLinear:
         _lib.check(_lib.load().ltxq_dequantize(ctypes.byref(q), out.data_ptr(), _stream()), "dequantize")
         return out
 
+    def mx_terms(self, M: int) -> int:
+        """Terms of the MX input a GEMM of M rows over this weight takes (2 for
+        "mx2", 1 for "mx1"), or 0 where it runs the dequantizing kernels."""
+        if self.compute == "dequant" or M <= 0:
+            return 0
+        q = self.qweight()
+        if not _lib.load().ltxq_qlinear_mx_supported(M, ctypes.byref(q)):
+            return 0
+        return 2 if self.compute == "mx2" else 1
+
     # ---------------------------------------------------------------- forward
     def _epilogue(self, x_rows_shape, keep, gelu=False, residual=None, gate=None, gate_then_add=False):
         epi = _lib.Epilogue()
@@ -190,13 +200,22 @@ class QuantizedLinear:
 
     def __call__(self, x: torch.Tensor, *, gelu: bool = False, residual: torch.Tensor | None = None,
                  gate: torch.Tensor | None = None, gate_then_add: bool = False,
-                 adaln: tuple | None = None, split_k: bool = True) -> torch.Tensor:
+                 adaln: tuple | None = None, split_k: bool = True, mx_out: int = 0):
         """``y = x @ dequant(W).T + bias`` with optional fused consumers:
         ``gelu=True`` (project_in), ``residual``/``gate`` (gated residual add),
         and ``adaln=(scale, shift, eps[, norm])`` (the AdaLN prologue).
 
         ``split_k=False`` gives the library no workspace for split-K partials,
-        so a GEMM with few tokens runs unsplit (one pass over K per tile)."""
+        so a GEMM with few tokens runs unsplit (one pass over K per tile).
+
+        ``x`` may be an ``MXActivation`` (``mx_terms(M)`` terms): the
+        block-scaled GEMM reads it directly (``ltxq_qlinear_mx``).  With such
+        an input, ``mx_out`` 1 or 2 returns the result (bias, GELU applied) as
+        an ``MXActivation`` of that many terms for the next GEMM."""
+        if isinstance(x, MXActivation):
+            return self._call_mx(x, gelu, residual, gate, gate_then_add, mx_out)
+        if mx_out:
+            raise ValueError("mx_out needs an MXActivation input (the block-scaled kernels)")
         _require_cuda(x, "x")
         if x.dtype != torch.bfloat16:
             raise ValueError(f"x must be bfloat16, got {x.dtype}")
@@ -224,6 +243,29 @@ class QuantizedLinear:
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
             _lib.check(lib.ltxq_qlinear(x.data_ptr(), M, ctypes.byref(q), ctypes.byref(epi), out.data_ptr(),
                                         ws.data_ptr() if ws is not None else None, ws_bytes, _stream()), "qlinear")
+        return out
+
+    def _call_mx(self, x: MXActivation, gelu, residual, gate, gate_then_add, mx_out):
+        if x.K != self.in_features:
+            raise ValueError(f"x last dim {x.K} != in_features {self.in_features}")
+        if mx_out and residual is not None:
+            raise ValueError("mx_out takes the none / GELU epilogues only")
+        keep: list = []
+        epi = self._epilogue(x.rows_shape, keep, gelu, residual, gate, gate_then_add)
+        q = self.qweight()
+        xs = x.struct()
+        out = None
+        out_struct = None
+        if mx_out:
+            out = MXActivation(x.rows_shape, self.out_features, mx_out, x.device)
+            out_struct = out.struct()
+            out_ptr = None
+        else:
+            out = torch.empty(x.rows_shape + (self.out_features,), dtype=torch.bfloat16, device=x.device)
+            out_ptr = out.data_ptr()
+        _lib.check(_lib.load().ltxq_qlinear_mx(ctypes.byref(xs), x.M, ctypes.byref(q), ctypes.byref(epi), out_ptr,
+                                               ctypes.byref(out_struct) if out_struct is not None else None,
+                                               _stream()), "qlinear_mx")
         return out
 
     def __repr__(self) -> str:

@@ -68,6 +68,31 @@ def test_argument_validation_without_gpu(lib):
     assert st == _lib.ERR_UNSUPPORTED  # C % 8 != 0
 
 
+def test_mx_entry_validation_without_gpu(lib):
+    """The MX-form entry points reject bad activations / shapes before any
+    CUDA call."""
+    from ltxq import _lib
+
+    q = _lib.QWeight(16, 16, None, None, 4096, 4096, _lib.MXFP8, 8, 32, 0, 0, _lib.COMPUTE_MX2, 16)
+    epi = _lib.Epilogue()
+    assert lib.ltxq_qlinear_mx(None, 256, ctypes.byref(q), ctypes.byref(epi), 16, None, None) == _lib.ERR_INVALID
+    bad = _lib.MxAct(16, 16, 16, 16, 3, 0)  # three terms
+    assert lib.ltxq_qlinear_mx(ctypes.byref(bad), 256, ctypes.byref(q), ctypes.byref(epi), 16, None,
+                               None) == _lib.ERR_INVALID
+    odd = _lib.MxAct(24, 16, 16, 16, 2, 0)  # codes not 16-byte aligned
+    assert lib.ltxq_qlinear_mx(ctypes.byref(odd), 256, ctypes.byref(q), ctypes.byref(epi), 16, None,
+                               None) == _lib.ERR_INVALID
+    act = _lib.MxAct(16, 16, 16, 16, 2, 0)
+    pro = _lib.Prologue(_lib.NORM_RMS, 1e-6, _lib.Vec(16, _lib.F32, 0, 0, 0), _lib.Vec(16, _lib.F32, 0, 0, 0))
+    assert lib.ltxq_adaln_modulate_mx(16, 4, 4096, ctypes.byref(pro), None, None, None) == _lib.ERR_INVALID
+    assert lib.ltxq_adaln_modulate_mx(16, 4, 4160, ctypes.byref(pro), None, ctypes.byref(act),
+                                      None) == _lib.ERR_UNSUPPORTED  # C % 128 != 0
+    assert lib.ltxq_adaln_modulate_mx(16, 4, 8192, ctypes.byref(pro), None, ctypes.byref(act),
+                                      None) == _lib.ERR_UNSUPPORTED  # C > 4096
+    assert lib.ltxq_head_gate_mx(16, 16, 4, 3, 64, None, ctypes.byref(act), None) == _lib.ERR_UNSUPPORTED
+    assert lib.ltxq_head_gate_mx(16, 16, 4, 2, 64, None, None, None) == _lib.ERR_INVALID
+
+
 def test_denoise_update_validation_without_gpu(lib):
     """ltxq_denoise_update rejects bad scalars / shapes / missing operands
     before any CUDA call, and an empty latent is a no-op."""
