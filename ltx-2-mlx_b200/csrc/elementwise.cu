@@ -147,136 +147,154 @@ __device__ __forceinline__ double warp_sum(double v) {
   return v;
 }
 
-// kWPR warps per row for bf16 rows with C <= kWPR * 32 * 8 * kCPL: every
-// lane keeps kCPL 16-byte chunks (chunk lane + 32 * (wr + kWPR * j)) in
-// registers, so a row is read from HBM once with all loads in flight.  The
-// per-row fp64 partial sums of the kWPR warps meet in shared memory.
-// v[j] for a runtime j without dynamic register indexing (selects only)
-template <int N>
-__device__ __forceinline__ uint4 pick(const uint4 (&v)[N], int j) {
-  uint4 cur = v[0];
-#pragma unroll
-  for (int jj = 1; jj < N; ++jj)
-    if (jj == j) cur = v[jj];
-  return cur;
-}
+// Row tiles for bf16 rows of C <= 256 * 8 * kCPT channels: a CTA of 256
+// threads takes kR consecutive rows; thread t owns the 8-channel chunks
+// t + 256 j (j < kCPT) of every row, so all kR * kCPT 16-byte loads of a
+// thread are in flight at once, and the scale / shift entries of a chunk are
+// loaded once for the kR rows when the rows share their vectors.  RMS
+// statistics: an fp32 sum of squares per thread and row (the reference's
+// fp32 mean, up to its last ulp), added across threads in fp64 in a fixed
+// order; LayerNorm sums and centred squares in fp64.  One thread per row
+// forms 1/sqrt.  kMx: the result is written as MX terms (C % 128 == 0: the
+// four lanes of a quad hold one 32-channel group of one row) and, when
+// out != NULL, also as bf16 rows.
+constexpr int kTileThreads = 256;
 
-// kMx: the result is (also) written as MX terms of the next GEMM's input
-// (C % 128 == 0, so the four lanes of a quad hold one 32-channel group);
-// out may then be NULL.
-template <int kCPL, int kWPR, bool kVecBf16, bool kMx>
-__global__ void __launch_bounds__(256, 2) adaln_rows_kernel(const uint16_t* __restrict__ x, int64_t rows, int64_t C,
-                                                         int norm, float eps, VecArg scale, VecArg shift,
-                                                         uint16_t* __restrict__ out, const mx::MxOut mo) {
-  __shared__ double red[8][2];
+template <int kR, int kCPT, int kNorm, bool kVecBf16, bool kMx>
+__global__ void __launch_bounds__(kTileThreads, kNorm == LTXQ_NORM_LAYER ? 2 : 3)
+    adaln_tile_kernel(const uint16_t* __restrict__ x, int64_t rows, int C, float eps, VecArg scale, VecArg shift,
+                      uint16_t* __restrict__ out, const mx::MxOut mo) {
+  constexpr int kWarps = kTileThreads / 32;
+  __shared__ double red[kWarps][kR];
+  __shared__ float inv_s[kR], mu_s[kR];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kR;
+  const int nch = C >> 3;
+  uint4 v[kR][kCPT];
+#pragma unroll
+  for (int r = 0; r < kR; ++r)
+#pragma unroll
+    for (int j = 0; j < kCPT; ++j) {
+      const int c = threadIdx.x + kTileThreads * j;
+      v[r][j] = (r0 + r < rows && c < nch) ? __ldg(reinterpret_cast<const uint4*>(x + (r0 + r) * C) + c)
+                                          : make_uint4(0, 0, 0, 0);
+    }
   const double inv_c = __drcp_rn(static_cast<double>(C));
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int wr = warp % kWPR;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / kWPR) + warp / kWPR;
-  const bool live = row < rows;
-  const int nch = static_cast<int>(C >> 3);
-  const uint16_t* xr = x + (live ? row : 0) * C;
-  uint4 v[kCPL];
+  if constexpr (kNorm == LTXQ_NORM_RMS) {
 #pragma unroll
-  for (int j = 0; j < kCPL; ++j) {
-    const int c = lane + 32 * (wr + kWPR * j);
-    v[j] = (live && c < nch) ? __ldg(reinterpret_cast<const uint4*>(xr) + c) : make_uint4(0, 0, 0, 0);
-  }
-  float mu_f = 0.f, inv = 1.f;
-  if (norm != LTXQ_NORM_NONE) {
-    double s1 = 0.0, s2 = 0.0;
-#pragma unroll 1
-    for (int j = 0; j < kCPL; ++j) {
-      const uint4 cur = pick(v, j);
-      const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
+    for (int r = 0; r < kR; ++r) {
+      float q = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const double a = lo_bf16(w[i]), b = hi_bf16(w[i]);
-        s1 += a + b;
-        s2 += a * a + b * b;
+      for (int j = 0; j < kCPT; ++j) {
+        const uint32_t w[4] = {v[r][j].x, v[r][j].y, v[r][j].z, v[r][j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          q = __fmaf_rn(hi_bf16(w[i]), hi_bf16(w[i]), __fmaf_rn(lo_bf16(w[i]), lo_bf16(w[i]), q));
       }
+      const double d = warp_sum(static_cast<double>(q));
+      if (lane == 0) red[warp][r] = d;
     }
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
-    if (kWPR > 1) {
-      if (lane == 0) {
-        red[warp][0] = s1;
-        red[warp][1] = s2;
-      }
-      __syncthreads();
-      const int w0 = warp - wr;
-      s1 = 0.0;
-      s2 = 0.0;
+    __syncthreads();
+    if (threadIdx.x < kR) {
+      double t = 0.0;
 #pragma unroll
-      for (int i = 0; i < kWPR; ++i) {
-        s1 += red[w0 + i][0];
-        s2 += red[w0 + i][1];
-      }
+      for (int w = 0; w < kWarps; ++w) t += red[w][threadIdx.x];
+      const float ms = static_cast<float>(t * inv_c);
+      inv_s[threadIdx.x] = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(ms, eps))));
+      mu_s[threadIdx.x] = 0.f;
     }
-    if (norm == LTXQ_NORM_RMS) {
-      const float ms = static_cast<float>(s2 * inv_c);
-      inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(ms, eps))));
-    } else {
-      const double mu = s1 * inv_c;
+    __syncthreads();
+  } else if constexpr (kNorm == LTXQ_NORM_LAYER) {
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      double s1 = 0.0;
+#pragma unroll
+      for (int j = 0; j < kCPT; ++j) {
+        const uint32_t w[4] = {v[r][j].x, v[r][j].y, v[r][j].z, v[r][j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s1 += static_cast<double>(lo_bf16(w[i])) + static_cast<double>(hi_bf16(w[i]));
+      }
+      s1 = warp_sum(s1);
+      if (lane == 0) red[warp][r] = s1;
+    }
+    __syncthreads();
+    double mu[kR];
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      double t = 0.0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) t += red[w][r];
+      mu[r] = t * inv_c;
+    }
+    __syncthreads();  // red is reused for the centred squares
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
       double d2 = 0.0;
-#pragma unroll 1
-      for (int j = 0; j < kCPL; ++j) {
-        if (lane + 32 * (wr + kWPR * j) < nch) {
-          const uint4 cur = pick(v, j);
-          const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+      for (int j = 0; j < kCPT; ++j) {
+        if (threadIdx.x + kTileThreads * j < nch) {
+          const uint32_t w[4] = {v[r][j].x, v[r][j].y, v[r][j].z, v[r][j].w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const double a = lo_bf16(w[i]) - mu, b = hi_bf16(w[i]) - mu;
+            const double a = lo_bf16(w[i]) - mu[r], b = hi_bf16(w[i]) - mu[r];
             d2 += a * a + b * b;
           }
         }
       }
       d2 = warp_sum(d2);
-      if (kWPR > 1) {
-        __syncthreads();
-        if (lane == 0) red[warp][0] = d2;
-        __syncthreads();
-        const int w0 = warp - wr;
-        d2 = 0.0;
-#pragma unroll
-        for (int i = 0; i < kWPR; ++i) d2 += red[w0 + i][0];
-      }
-      const float var = static_cast<float>(d2 * inv_c);
-      inv = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(var, eps))));
-      mu_f = static_cast<float>(mu);
+      if (lane == 0) red[warp][r] = d2;
     }
+    __syncthreads();
+    if (threadIdx.x < kR) {
+      double t = 0.0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) t += red[w][threadIdx.x];
+      const float var = static_cast<float>(t * inv_c);
+      inv_s[threadIdx.x] = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(var, eps))));
+      mu_s[threadIdx.x] = static_cast<float>(mu[threadIdx.x]);
+    }
+    __syncthreads();
   }
-  if (!live) return;
-  const char* sc = vec_row(scale, row);
-  const char* sh = vec_row(shift, row);
-  uint16_t* orow = out != nullptr ? out + row * C : nullptr;
-  // not unrolled, so that the vector loads of one chunk are not hoisted over
-  // the whole row (register pressure); the chunk is picked with selects
-#pragma unroll 1
-  for (int j = 0; j < kCPL; ++j) {
-    const int c = lane + 32 * (wr + kWPR * j);
+  // the kR rows read the same vector entries (broadcast, or one vector per
+  // group of rows that the tile does not straddle)
+  const bool shared_vec = (scale.rows_per_vec == 0 || (scale.rows_per_vec % kR) == 0) &&
+                          (shift.rows_per_vec == 0 || (shift.rows_per_vec % kR) == 0);
+#pragma unroll
+  for (int j = 0; j < kCPT; ++j) {
+    const int c = threadIdx.x + kTileThreads * j;
     if (c >= nch) break;
-    const uint4 cur = pick(v, j);
     float s8[8], t8[8];
-    load_vec8(scale, sc, static_cast<int64_t>(c) * 8, s8);
-    load_vec8(shift, sh, static_cast<int64_t>(c) * 8, t8);
-    const uint32_t w[4] = {cur.x, cur.y, cur.z, cur.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float e[2] = {lo_bf16(w[i]), hi_bf16(w[i])};
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float n = e[h];
-        if (norm == LTXQ_NORM_RMS) n = rbf16(__fmul_rn(n, inv));
-        else if (norm == LTXQ_NORM_LAYER) n = rbf16(__fmul_rn(__fsub_rn(n, mu_f), inv));
-        e[h] = modulate1<kVecBf16>(n, s8[2 * i + h], t8[2 * i + h]);
-      }
-      o[i] = pack_bf16x2(e[0], e[1]);
+    if (shared_vec) {
+      load_vec8(scale, vec_row(scale, r0), static_cast<int64_t>(c) * 8, s8);
+      load_vec8(shift, vec_row(shift, r0), static_cast<int64_t>(c) * 8, t8);
     }
-    if (kMx) mx::mx_write8(o, row, static_cast<int64_t>(c) * 8, mo, 0xFu << (lane & ~3));
-    if (orow != nullptr) reinterpret_cast<uint4*>(orow)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      const int64_t row = r0 + r;
+      if (row >= rows) break;
+      if (!shared_vec) {
+        load_vec8(scale, vec_row(scale, row), static_cast<int64_t>(c) * 8, s8);
+        load_vec8(shift, vec_row(shift, row), static_cast<int64_t>(c) * 8, t8);
+      }
+      const float inv = kNorm == LTXQ_NORM_NONE ? 1.f : inv_s[r];
+      const float mu_f = kNorm == LTXQ_NORM_LAYER ? mu_s[r] : 0.f;
+      const uint32_t w[4] = {v[r][j].x, v[r][j].y, v[r][j].z, v[r][j].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float e[2] = {lo_bf16(w[i]), hi_bf16(w[i])};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float n = e[h];
+          if (kNorm == LTXQ_NORM_RMS) n = rbf16(__fmul_rn(n, inv));
+          else if (kNorm == LTXQ_NORM_LAYER) n = rbf16(__fmul_rn(__fsub_rn(n, mu_f), inv));
+          e[h] = modulate1<kVecBf16>(n, s8[2 * i + h], t8[2 * i + h]);
+        }
+        o[i] = pack_bf16x2(e[0], e[1]);
+      }
+      if (kMx) mx::mx_write8(o, row, static_cast<int64_t>(c) * 8, mo, 0xFu << (lane & ~3));
+      if (out != nullptr) reinterpret_cast<uint4*>(out + row * C)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
@@ -315,7 +333,7 @@ __global__ void gated_add_kernel(const uint16_t* __restrict__ res, const uint16_
 
 // out[m, h, :] = o[m, h, :] * bf16(2 * bf16(sigmoid(logit[m, h]))); one
 // thread per 8 channels.
-// kMx: as adaln_rows_kernel's (width % 128 == 0: the grid stride and the row
+// kMx: as adaln_tile_kernel's (width % 128 == 0: the grid stride and the row
 // width are multiples of 4 chunks, so a quad stays one 32-channel group).
 template <bool kMx>
 __global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ logits, int64_t rows,
@@ -385,24 +403,28 @@ ltxq_status launch_adaln_modulate(const void* x, int x_dtype, int64_t rows, int6
   if (x_dtype == LTXQ_BF16 && C <= 4096) {
     auto* xb = static_cast<const uint16_t*>(x);
     auto* ob = static_cast<uint16_t*>(out);
-#define LTXQ_ROWS_MX(CPL, WPR, MX)                                                                        \
-  do {                                                                                                     \
-    const unsigned blocks = static_cast<unsigned>((rows + (8 / WPR) - 1) / (8 / WPR));                     \
-    if (vb)                                                                                                \
-      adaln_rows_kernel<CPL, WPR, true, MX><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob, mo); \
-    else                                                                                                   \
-      adaln_rows_kernel<CPL, WPR, false, MX><<<blocks, 256, 0, stream>>>(xb, rows, C, pro.norm, pro.eps, s, t, ob, mo); \
+    const int ci = static_cast<int>(C);
+#define LTXQ_TILE_N(R, CPT, NORM)                                                                          \
+  do {                                                                                                      \
+    const unsigned blocks = static_cast<unsigned>((rows + (R) - 1) / (R));                                  \
+    if (out_mx) {                                                                                           \
+      if (vb) adaln_tile_kernel<R, CPT, NORM, true, true><<<blocks, kTileThreads, 0, stream>>>(xb, rows, ci, pro.eps, s, t, ob, mo); \
+      else adaln_tile_kernel<R, CPT, NORM, false, true><<<blocks, kTileThreads, 0, stream>>>(xb, rows, ci, pro.eps, s, t, ob, mo);  \
+    } else {                                                                                                \
+      if (vb) adaln_tile_kernel<R, CPT, NORM, true, false><<<blocks, kTileThreads, 0, stream>>>(xb, rows, ci, pro.eps, s, t, ob, mo); \
+      else adaln_tile_kernel<R, CPT, NORM, false, false><<<blocks, kTileThreads, 0, stream>>>(xb, rows, ci, pro.eps, s, t, ob, mo);  \
+    }                                                                                                       \
   } while (0)
-#define LTXQ_ROWS(CPL, WPR)                  \
-  do {                                       \
-    if (out_mx) LTXQ_ROWS_MX(CPL, WPR, true); \
-    else LTXQ_ROWS_MX(CPL, WPR, false);       \
+#define LTXQ_TILE(R, CPT)                                                       \
+  do {                                                                          \
+    if (pro.norm == LTXQ_NORM_RMS) LTXQ_TILE_N(R, CPT, LTXQ_NORM_RMS);          \
+    else if (pro.norm == LTXQ_NORM_LAYER) LTXQ_TILE_N(R, CPT, LTXQ_NORM_LAYER); \
+    else LTXQ_TILE_N(R, CPT, LTXQ_NORM_NONE);                                   \
   } while (0)
-    if (C <= 1024) LTXQ_ROWS(4, 1);
-    else if (C <= 2048) LTXQ_ROWS(8, 1);
-    else LTXQ_ROWS(8, 2);
-#undef LTXQ_ROWS
-#undef LTXQ_ROWS_MX
+    if (C <= 2048) LTXQ_TILE(8, 1);
+    else LTXQ_TILE(4, 2);
+#undef LTXQ_TILE
+#undef LTXQ_TILE_N
     return launch_check("adaln_modulate launch");
   }
   int threads = static_cast<int>((C + 15) / 16);

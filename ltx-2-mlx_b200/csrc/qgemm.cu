@@ -635,6 +635,21 @@ __device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const u
 // then the same epilogue as whole tiles.  One thread per (split tile,
 // token row, 8 features).
 constexpr int kPairTile = 256;  // features and tokens per pair-kernel tile
+constexpr int kGroupM = 16;     // token tiles that walk a feature tile together
+
+// Pair-kernel tile t -> (feature tile nt, token tile mt).  Groups of kGroupM
+// token tiles walk the feature tiles together, so the clusters that run at
+// the same time share a few weight tiles (read from HBM about once per group
+// while they sit in L2) and a group's activation rows stay L2-resident.
+__device__ __forceinline__ void pair_tile_coords(int t, int n_pt, int m_tiles, int& nt, int& mt) {
+  const int span = kGroupM * n_pt;
+  const int grp = t / span;
+  const int rem_m = m_tiles - grp * kGroupM;
+  const int gm = rem_m < kGroupM ? rem_m : kGroupM;
+  const int w = t - grp * span;
+  nt = w / gm;
+  mt = grp * kGroupM + w % gm;
+}
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
   // GELU is evaluated directly here (a handful of elements per thread: a
   // per-block table would cost more to build than it saves)
@@ -648,9 +663,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const Params p) {
     const int ti = static_cast<int>(it / (kPairTile * (kPairTile / 8)));
     const int rem = static_cast<int>(it - static_cast<int64_t>(ti) * (kPairTile * (kPairTile / 8)));
     const int j = rem / (kPairTile / 8), f = (rem % (kPairTile / 8)) * 8;
-    const int tile = p.dp_tiles + ti;
-    const int m = (tile / n_pt) * kPairTile + j;
-    const int nf = (tile % n_pt) * kPairTile + f;
+    int nt, mt;
+    pair_tile_coords(p.dp_tiles + ti, n_pt, (p.M + kPairTile - 1) / kPairTile, nt, mt);
+    const int m = mt * kPairTile + j;
+    const int nf = nt * kPairTile + f;
     if (m >= p.M || nf >= p.N) continue;
     const float* src = p.partial + static_cast<size_t>(ti) * p.splits * kTileElems + j * kPairTile + f;
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -714,7 +730,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const bool leader = rank == 0;
   const int num_kb = p.K / BK;
   const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
-  const int tiles = n_pt * ((p.M + BN - 1) / BN);
+  const int m_tiles = (p.M + BN - 1) / BN;
+  const int tiles = n_pt * m_tiles;
   // work unit u < dp: whole tile u; u >= dp: K range sp of tile
   // dp + (u - dp) / splits.  Every role walks the same units in the same order.
   const int dp = p.dp_tiles;
@@ -735,8 +752,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       kb_lo = sp * num_kb / splits;
       kb_hi = (sp + 1) * num_kb / splits;
     }
-    n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
-    m0 = (tile / n_pt) * BN;
+    int nt, mt;
+    pair_tile_coords(tile, n_pt, m_tiles, nt, mt);
+    n0 = nt * (2 * BM) + static_cast<int>(rank) * BM;
+    m0 = mt * BN;
   };
 
   if (threadIdx.x == 0) {
@@ -1080,7 +1099,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const bool leader = rank == 0;
   const int num_kb = p.K / BK;
   const int n_pt = (p.N + 2 * BM - 1) / (2 * BM);
-  const int tiles = n_pt * ((p.M + BN - 1) / BN);
+  const int m_tiles = (p.M + BN - 1) / BN;
+  const int tiles = n_pt * m_tiles;
   // work unit u < dp: whole tile u; u >= dp: K range sp of tile
   // dp + (u - dp) / splits.  Every role walks the same units in the same order.
   const int dp = p.dp_tiles;
@@ -1101,8 +1121,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       kb_lo = sp * num_kb / splits;
       kb_hi = (sp + 1) * num_kb / splits;
     }
-    n0 = (tile % n_pt) * (2 * BM) + static_cast<int>(rank) * BM;
-    m0 = (tile / n_pt) * BN;
+    int nt, mt;
+    pair_tile_coords(tile, n_pt, m_tiles, nt, mt);
+    n0 = nt * (2 * BM) + static_cast<int>(rank) * BM;
+    m0 = mt * BN;
   };
 
   if (threadIdx.x == 0) {

@@ -3,6 +3,7 @@ scripts/bench_ff_microbench.py ``quant_matmul``, :451-551).
 
     python -m ltxq.microbench --shapes 9216x4096x4096 --modes affine4,mxfp8,mxfp8_mx2
     python -m ltxq.microbench --cublas            # also time torch bf16 F.linear
+    python -m ltxq.microbench --adaln 9216x4096   # the AdaLN pass alone (bf16 / MX outputs)
 
 Each shape is MxKxN (tokens x in x out).  Prints one JSON line per shape
 with ms and TFLOP/s (2*M*N*K / time) per mode; the L2 is flushed (256 MiB
@@ -75,6 +76,30 @@ def _time_graph(fns, iters):
     return ts[len(ts) // 2]
 
 
+def _adaln(spec: str, iters: int) -> None:
+    """The AdaLN pass (RMS norm, fp32 modulate vectors) over M x C bf16 rows,
+    graph-timed over copies of x larger than the L2, with bf16 output and
+    with the output written as 2 / 1 MX terms.  Bytes per call: x read +
+    output written + the two vectors."""
+    from . import kernels as K
+
+    M, C = (int(v) for v in spec.split("x"))
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    copies = max(1, -(-(256 << 20) // (M * C * 2)))
+    xs = [torch.randn(M, C, device=dev, generator=g).to(torch.bfloat16) for _ in range(copies)]
+    sc = torch.randn(1, C, device=dev, generator=g) * 0.1
+    sh = torch.randn(1, C, device=dev, generator=g) * 0.1
+    row = {"adaln": {"M": M, "C": C, "graph_calls": copies}}
+    for name, terms in (("bf16_out", 0), ("mx2_out", 2), ("mx1_out", 1)):
+        t = _time_graph([lambda x=x: K.adaln_modulate(x, sc, sh, 1e-6, mx_terms=terms) for x in xs], iters)
+        out_bytes = M * C * (2 if terms == 0 else terms) + (M * C // 32) * terms
+        nbytes = M * C * 2 + out_bytes + 2 * C * 4
+        row[name] = {"ms": t, "gbs": nbytes / t / 1e6, "bytes": nbytes}
+    print(json.dumps(row), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(DEFAULT_SHAPES))
@@ -86,7 +111,11 @@ def main(argv=None):
     ap.add_argument("--no-split-k", action="store_true", help="give the GEMM no split-K workspace")
     ap.add_argument("--graph", action="store_true", help="device time per call from a captured CUDA graph")
     ap.add_argument("--pretransposed", action="store_true", help="pack W^T (the cache's pretranspose mode; mxfp8)")
+    ap.add_argument("--adaln", default=None, help="MxC: time the AdaLN pass instead of the GEMMs")
     args = ap.parse_args(argv)
+    if args.adaln:
+        _adaln(args.adaln, args.iters)
+        return
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
     g.manual_seed(0)
