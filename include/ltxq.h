@@ -16,6 +16,8 @@
  *                              transformer.py:387,484 text-CA gate-then-add)
  *   ltxq_head_gate       <- LTX_2_MLX/model/transformer/attention.py:559-601
  *   ltxq_qk_norm_rope    <- attention.py:320-329, 580-587 + rope.py:53-90
+ *   ltxq_attention       <- mx.fast.scaled_dot_product_attention in
+ *                           attention.py:170-302 (kernels/steel_attention.py)
  *   ltxq_quantize        <- mx.quantize at loader/transformer_cache.py:1255
  *   ltxq_dequantize      <- mx.dequantize semantics of the same cache entries
  *   ltxq_qlinear         <- nn.QuantizedLinear.__call__ /
@@ -198,6 +200,20 @@ ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int6
 ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t row_stride, int64_t heads,
                               int64_t head_dim, const float* weight, float eps, const float* cos_table,
                               const float* sin_table, int64_t pe_tokens, void* out, void* stream);
+
+/* Attention core without a mask (the block's mx.fast.scaled_dot_product_attention,
+ * model/transformer/attention.py:170-302; kernels/steel_attention.py:251-280):
+ * out[b, i, h*D:(h+1)*D] = sum_j softmax_j(q_i . k_j * scale) v_j over the
+ * kv_rows keys of batch b, per head h; fp32 scores and softmax, P rounded to
+ * bf16 for the P.V product (fp32 accumulate), one bf16 rounding of the result.
+ * q: bf16 [batch, q_rows, *] with row stride q_stride elements, head h at
+ * columns [h*D, (h+1)*D); k, v: bf16 [batch, kv_rows, *] likewise (column
+ * slices of fused projection outputs work as they are); out: contiguous bf16
+ * [batch, q_rows, heads*D].  head_dim D 64 or 128; strides multiples of 8;
+ * 16-byte aligned. */
+ltxq_status ltxq_attention(const void* q, const void* k, const void* v, int64_t batch, int64_t q_rows,
+                           int64_t kv_rows, int64_t heads, int64_t head_dim, int64_t q_stride, int64_t k_stride,
+                           int64_t v_stride, float scale, void* out, void* stream);
 
 /* ---- quantized weights ------------------------------------------------ */
 /* Quantize a bf16 weight [N, K] into the MLX cache layout described by `w`

@@ -77,9 +77,9 @@ ltxq_status cuda_check(cudaError_t e, const char* what) {
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 
-ltxq_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner_elems,
-                           uint64_t outer_rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
-                           CUtensorMapSwizzle swizzle) {
+static ltxq_status encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                               const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                               CUtensorMapSwizzle swizzle) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -90,21 +90,42 @@ ltxq_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const vo
   if (!g_encode) return fail(LTXQ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the CUDA driver");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     return fail(LTXQ_ERR_INVALID, "TMA base address must be 16-byte aligned");
-  if (row_stride_bytes % 16 != 0) return fail(LTXQ_ERR_INVALID, "TMA row stride must be a multiple of 16 bytes");
-  cuuint64_t dims[2] = {inner_elems, outer_rows};
-  cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint64_t d[3];
+  cuuint64_t st[2];
+  cuuint32_t bx[3];
+  cuuint32_t estr[3] = {1, 1, 1};
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    if (i + 1 < rank) {
+      if (strides[i] % 16 != 0) return fail(LTXQ_ERR_INVALID, "TMA strides must be multiples of 16 bytes");
+      st[i] = strides[i];
+    }
+  }
+  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    char buf[160];
-    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) dims=(%llu,%llu) box=(%u,%u)", (int)r,
-             (unsigned long long)inner_elems, (unsigned long long)outer_rows, box_inner, box_outer);
+    char buf[200];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) rank %u dims=(%llu,%llu,%llu) box=(%u,%u,%u)",
+             (int)r, rank, (unsigned long long)dims[0], (unsigned long long)dims[1],
+             (unsigned long long)(rank > 2 ? dims[2] : 1), box[0], box[1], rank > 2 ? box[2] : 1u);
     return fail(LTXQ_ERR_CUDA, buf);
   }
   return LTXQ_OK;
+}
+
+ltxq_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner_elems,
+                           uint64_t outer_rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                           CUtensorMapSwizzle swizzle) {
+  const uint64_t dims[2] = {inner_elems, outer_rows};
+  const uint64_t strides[1] = {row_stride_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return encode_tmap(map, dtype, 2, base, dims, strides, box, swizzle);
+}
+
+ltxq_status encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+                           const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle) {
+  return encode_tmap(map, dtype, 3, base, dims, strides_bytes, box, swizzle);
 }
 
 int num_sms() {

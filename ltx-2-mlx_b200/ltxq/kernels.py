@@ -226,6 +226,40 @@ def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int, mx_terms
     return res
 
 
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None) -> torch.Tensor:
+    """``softmax(q k^T * scale) v`` per head (the block's
+    ``mx.fast.scaled_dot_product_attention``, attention.py:170-302) on
+    (B, T, heads*D) rows: q (B, Tq, W), k / v (B, Tk, W), any row stride with
+    unit column stride (column slices of a fused projection are read in
+    place).  D = W / heads must be 64 or 128; scale defaults to 1/sqrt(D).
+    Returns contiguous (B, Tq, heads*D) bf16."""
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _require_cuda(t, name)
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be a (B, T, W) bfloat16 tensor with unit column stride")
+    b, tq, width = q.shape
+    if k.shape != v.shape or k.shape[0] != b or k.shape[2] != width:
+        raise ValueError("k and v must be (B, Tk, W) with q's B and W")
+    tk = k.shape[1]
+    if width % heads != 0:
+        raise ValueError("W must be a multiple of heads")
+    d = width // heads
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+
+    def rows(t):  # (B, T, W) with one row stride across batch and tokens
+        if t.stride(0) != t.shape[1] * t.stride(1):
+            t = t.contiguous()
+        return t
+
+    q, k, v = rows(q), rows(k), rows(v)
+    out = torch.empty((b, tq, width), dtype=torch.bfloat16, device=q.device)
+    _lib.check(_lib.load().ltxq_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), b, tq, tk, heads, d, q.stride(1),
+                                          k.stride(1), v.stride(1), float(scale), out.data_ptr(), _stream()),
+               "attention")
+    return out
+
+
 def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, heads: int, eps: float = 1e-6,
                  pe: tuple | None = None) -> torch.Tensor:
     """QK RMSNorm (attention.py:320-329) then split RoPE (rope.py:53-90) in one

@@ -4,6 +4,7 @@ scripts/bench_ff_microbench.py ``quant_matmul``, :451-551).
     python -m ltxq.microbench --shapes 9216x4096x4096 --modes affine4,mxfp8,mxfp8_mx2
     python -m ltxq.microbench --cublas            # also time torch bf16 F.linear
     python -m ltxq.microbench --adaln 9216x4096   # the AdaLN pass alone (bf16 / MX outputs)
+    python -m ltxq.microbench --attention 9216x9216x32x128   # attention core vs torch SDPA
 
 Each shape is MxKxN (tokens x in x out).  Prints one JSON line per shape
 with ms and TFLOP/s (2*M*N*K / time) per mode; the L2 is flushed (256 MiB
@@ -100,6 +101,31 @@ def _adaln(spec: str, iters: int) -> None:
     print(json.dumps(row), flush=True)
 
 
+def _attention(spec: str, iters: int) -> None:
+    """The attention core at Tq x Tk x heads x D: ``ltxq_attention`` and
+    torch's SDPA (cuDNN / flash) on the same bf16 inputs, graph-timed.
+    FLOP = 4 * Tq * Tk * heads * D."""
+    import math
+
+    import torch.nn.functional as F
+
+    from . import kernels as K
+
+    tq, tk, heads, d = (int(v) for v in spec.split("x"))
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q, k, v = (torch.randn(1, t, heads * d, device=dev, generator=g).to(torch.bfloat16) for t in (tq, tk, tk))
+    hv = lambda t: t.view(1, t.shape[1], heads, d).transpose(1, 2)
+    flops = 4.0 * tq * tk * heads * d
+    row = {"attention": {"Tq": tq, "Tk": tk, "heads": heads, "D": d}}
+    t = _time_graph([lambda: K.attention(q, k, v, heads)], iters)
+    row["ltxq"] = {"ms": t, "tflops": flops / t / 1e9}
+    t = _time_graph([lambda: F.scaled_dot_product_attention(hv(q), hv(k), hv(v), scale=1.0 / math.sqrt(d))], iters)
+    row["torch_sdpa"] = {"ms": t, "tflops": flops / t / 1e9}
+    print(json.dumps(row), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(DEFAULT_SHAPES))
@@ -112,9 +138,14 @@ def main(argv=None):
     ap.add_argument("--graph", action="store_true", help="device time per call from a captured CUDA graph")
     ap.add_argument("--pretransposed", action="store_true", help="pack W^T (the cache's pretranspose mode; mxfp8)")
     ap.add_argument("--adaln", default=None, help="MxC: time the AdaLN pass instead of the GEMMs")
+    ap.add_argument("--attention", default=None, help="TqxTkxHxD: time the attention core instead of the GEMMs")
     args = ap.parse_args(argv)
     if args.adaln:
         _adaln(args.adaln, args.iters)
+        return
+    if args.attention:
+        for spec in args.attention.split(","):
+            _attention(spec, args.iters)
         return
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
