@@ -446,12 +446,13 @@ _EXCHANGE = {"gather": "video self-attention K/V all-gather", "head_parallel": "
 
 def _step_config(world, n_blocks=STEP_BLOCKS, graph=True, quant="mxfp8", video_tokens=STEP_T,
                  self_attention="gather", v2a="gather", audio_tokens=STEP_A, batch=1, workload=None,
-                 compute="dequant"):
+                 compute="dequant", attention="sdpa"):
     v2a_text = "video->audio K/V all-gather" if v2a == "gather" else _EXCHANGE[v2a]
     return {"workload": workload or STEP_QUANT[quant][2], "blocks": n_blocks, "video_tokens": video_tokens,
             "execution": "one CUDA graph per step (captured once, replayed)" if graph else "eager launches",
             "audio_tokens": audio_tokens, "text_tokens": STEP_L, "global_batch": batch, "seq_len": video_tokens,
             "quant": STEP_QUANT[quant][3], "compute": compute,
+            "attention": ("torch SDPA (cuDNN)" if attention == "sdpa" else "ltxq_attention (native sm_100a)"),
             "parallelism": (f"video rows sharded x{world}, weights replicated, {_EXCHANGE[self_attention]}, "
                             f"{v2a_text} (NCCL)" if world > 1 else "single GPU (no collective)"),
             "l2": "not flushed: 19 GB of packed weights streamed per step >> 126 MB L2"}
@@ -497,7 +498,7 @@ def run_step(args, world, rank, local, dev):
     gen.manual_seed(2026)  # identical on every rank: weights are replicated
     n_blocks = args.blocks
     q_mode, q_bits = STEP_QUANT[args.quant][:2]
-    blocks = [BasicAVTransformerBlock.random(gen, dev, mode=q_mode, bits=q_bits).set_compute(args.compute)
+    blocks = [BasicAVTransformerBlock.random(gen, dev, mode=q_mode, bits=q_bits).set_compute(args.compute).set_attention(args.attention)
               for _ in range(n_blocks)]
     weight_bytes = sum(b.nbytes() for b in blocks)
 
@@ -634,7 +635,7 @@ def run_step(args, world, rank, local, dev):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": _step_config(world, n_blocks, use_graph, args.quant, T, args.self_attention, args.v2a, A, B,
-                                   args.workload_name, args.compute),
+                                   args.workload_name, args.compute, args.attention),
             "quantized_gemm": {"linear_tflop_per_step": lin_flops / 1e12,
                                "step_linear_tflops_per_s": lin_flops / (ms_step / 1e3) / 1e12,
                                "ff_in_gemm_ms": ff_avg, "ff_in_gemm_tflops": achieved,
@@ -912,6 +913,8 @@ def main():
     ap.add_argument("--video-tokens", type=int, default=STEP_T,
                     help="video tokens of the step (9216 = config 4; fewer only to study per-rank shapes on one GPU)")
     ap.add_argument("--audio-tokens", type=int, default=STEP_A)
+    ap.add_argument("--attention", choices=["sdpa", "native"], default="sdpa",
+                    help="attention core: torch SDPA (cuDNN) or this library's sm_100a kernel (ltxq_attention)")
     ap.add_argument("--compute", choices=["dequant", "mx2", "mx1"], default="dequant",
                     help="GEMM compute mode (include/ltxq.h LTXQ_COMPUTE_*): dequant = bf16 tensor cores over the "
                          "exactly dequantized weight; mx2 / mx1 = native block-scaled fp8 MMAs on mxfp8 weights with "

@@ -25,7 +25,16 @@
 //                     row's maximum grows by more than 2^8 (then O is rescaled
 //                     in TMEM, after the previous P V product completed), so
 //                     P stays below 256 and most stages touch O not at all.
+//                     A full stage after the first takes one pass over S,
+//                     with P held in registers until the maximum is known
+//                     to stay.
 //   epilogue          O / sum, rounded to bf16, one row per thread.
+// S_t(j) overwrites P_t(j-1), so it is issued once PV_t(j-1) completed.
+// Measured and not kept: 64-key stages with S double-buffered per tile (S of
+// the next stage computed during the softmax of this one) ran 20 % slower,
+// the per-stage hand-offs doubling; a quarter of the exponentials on the
+// FMA pipe (polynomial) ran 6 % slower: the softmax is issue-bound, not
+// bound by the MUFU.
 // TMEM: S_A [0, 128), S_B [128, 256), O_A [256, 256 + D), O_B [256 + D, ...).
 // Every mbarrier wait is bounded; an expired wait raises the device error
 // word and the CTA unwinds.
@@ -213,65 +222,101 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const int n_valid = min(BKV, Tk - j * BKV);
-      float mt = -INFINITY;
+      // Fast path (a full stage after the first): one pass over S, exps
+      // against the running maximum, P kept in registers and stored only if
+      // no row's maximum grew past the threshold.
+      bool redo = true;
+      float ls = 0.f;
+
+      if (j > 0 && n_valid == BKV) {
+        uint32_t pw[BKV / 2];
+        float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(s_col + c * 32, v);
-        tmem_wait_ld();
+        for (int c = 0; c < BKV / 32; c += 2) {
+          uint32_t v[2][32];  // two loads in flight per wait
+          tmem_ld_32x32b_x32(s_col + c * 32, v[0]);
+          tmem_ld_32x32b_x32(s_col + c * 32 + 32, v[1]);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < n_valid) mt = fmaxf(mt, __uint_as_float(v[i]));
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float s0 = __uint_as_float(v[h][2 * i]), s1 = __uint_as_float(v[h][2 * i + 1]);
+              mt = fmaxf(mt, fmaxf(s0, s1));
+              const float p0 = ex2(__fmaf_rn(s0, scale_log2, -m_run));
+              const float p1 = ex2(__fmaf_rn(s1, scale_log2, -m_run));
+              ls += p0 + p1;
+              pw[(c + h) * 16 + i] = pack_bf16x2(p0, p1);
+            }
+        }
+        redo = __any_sync(0xffffffffu, mt * scale_log2 > m_run + kRescaleLog2);
+        if (!redo) {
+#pragma unroll
+          for (int c = 0; c < BKV / 32; ++c) tmem_st_32x32b_x16(s_col + c * 16, pw + c * 16);
+        }
       }
-      mt *= scale_log2;
-      if (j == 0) {
-        m_run = mt;
-      } else {
-        const bool grow = mt > m_run + kRescaleLog2;
-        if (__any_sync(0xffffffffu, grow)) {
-          // O holds the products up to stage j-1: rescale it once they are complete
-          const bool done = mbar_wait(&bb.o_done[t], (j - 1) & 1, bb.abort_flag, err);
-          if (!__all_sync(0xffffffffu, done)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float f = grow ? ex2(m_run - mt) : 1.f;
+      if (redo) {
+        ls = 0.f;
+        float mt = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(o_col + c * 32, v);
-            tmem_wait_ld();
+        for (int c = 0; c < BKV / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(s_col + c * 32, v);
+          tmem_wait_ld();
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              uint32_t w[16];
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < n_valid) mt = fmaxf(mt, __uint_as_float(v[i]));
+        }
+        mt *= scale_log2;
+        if (j == 0) {
+          m_run = mt;
+        } else {
+          const bool grow = mt > m_run + kRescaleLog2;
+          if (__any_sync(0xffffffffu, grow)) {
+            // O holds the products up to stage j-1: rescale it once they are complete
+            const bool done = mbar_wait(&bb.o_done[t], (j - 1) & 1, bb.abort_flag, err);
+            if (!__all_sync(0xffffffffu, done)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const float f = grow ? ex2(m_run - mt) : 1.f;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(__uint_as_float(v[h * 16 + i]) * f);
-              tmem_st_32x32b_x16(o_col + c * 32 + h * 16, w);
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(o_col + c * 32, v);
+              tmem_wait_ld();
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(__uint_as_float(v[h * 16 + i]) * f);
+                tmem_st_32x32b_x16(o_col + c * 32 + h * 16, w);
+              }
+            }
+            if (grow) {
+              l_run *= f;
+              m_run = mt;
             }
           }
-          if (grow) {
-            l_run *= f;
-            m_run = mt;
+        }
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(s_col + c * 32, v);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = c * 32 + 2 * i;
+            const float p0 = k0 < n_valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -m_run)) : 0.f;
+            const float p1 =
+                k0 + 1 < n_valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -m_run)) : 0.f;
+            ls += p0 + p1;
+            w[i] = pack_bf16x2(p0, p1);
           }
+          tmem_st_32x32b_x16(s_col + c * 16, w);
         }
-      }
-      float ls = 0.f;
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(s_col + c * 32, v);
-        tmem_wait_ld();
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int k0 = c * 32 + 2 * i;
-          const float p0 = k0 < n_valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i]), scale_log2, -m_run)) : 0.f;
-          const float p1 = k0 + 1 < n_valid ? ex2(__fmaf_rn(__uint_as_float(v[2 * i + 1]), scale_log2, -m_run)) : 0.f;
-          ls += p0 + p1;
-          w[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st_32x32b_x16(s_col + c * 16, w);
       }
       l_run += ls;
       tmem_wait_st();

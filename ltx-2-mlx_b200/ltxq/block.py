@@ -316,6 +316,9 @@ class QAttention:
     q_norm: torch.Tensor
     k_norm: torch.Tensor
     eps: float = 1e-6
+    # "sdpa": torch's scaled_dot_product_attention (cuDNN / flash kernels);
+    # "native": this library's sm_100a kernel (ltxq_attention)
+    kernel: str = "sdpa"
 
     def project(self, x_mod: torch.Tensor, ctx_mod: torch.Tensor | None):
         inner = self.heads * self.d_head
@@ -345,6 +348,8 @@ class QAttention:
 
     def attend(self, q, k, v, gl) -> torch.Tensor:
         """SDPA and the per-head gate of rotated Q, K and V."""
+        if self.kernel == "native":
+            return self._gate(K.attention(q, k, v, self.heads, 1.0 / math.sqrt(self.d_head)), gl)
         qh, kh, vh = _heads(q, self.heads), _heads(k, self.heads), _heads(v, self.heads)
         o = F.scaled_dot_product_attention(qh, kh, vh, scale=1.0 / math.sqrt(self.d_head))
         b, h, t, d = o.shape
@@ -489,6 +494,17 @@ class BasicAVTransformerBlock:
         fp8 MMAs on mxfp8 weights."""
         for ql in self.quantized_modules():
             ql.set_compute(compute)
+        return self
+
+    def set_attention(self, core: str) -> "BasicAVTransformerBlock":
+        """The attention core of every attention sub-layer: "sdpa" (torch's
+        scaled_dot_product_attention, the default) or "native" (this
+        library's sm_100a kernel, ``ltxq_attention``).  The row-sharded
+        head-parallel and split-key forms keep torch's kernels."""
+        if core not in ("sdpa", "native"):
+            raise ValueError(f"unknown attention core {core!r}")
+        for at in self.attn.values():
+            at.kernel = core
         return self
 
     def nbytes(self) -> int:

@@ -132,3 +132,11 @@ def test_attention_rejects_bad_arguments(cuda):
     x = torch.zeros(1, 8, 96, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):
         K.attention(x, x, x, 1)  # head_dim 96
+
+
+def test_block_with_native_attention_matches_oracle(cuda):
+    """A 22B-width mxfp8 block (1024 video, 201 audio, 1024 text tokens) with
+    every attention core on the native kernel, against the oracle block."""
+    from test_gpu_shapes import _block_case
+
+    _block_case("mxfp8", 8, 1024, 201, 1024, seed=901, attention="native")

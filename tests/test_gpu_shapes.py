@@ -320,7 +320,7 @@ def _oracle_params(lin, tabs):
     return p
 
 
-def _block_case(mode, bits, T, A, L, seed, compute="dequant"):
+def _block_case(mode, bits, T, A, L, seed, compute="dequant", attention="sdpa"):
     torch = _torch()
     import ltxq
     from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, TransformerArgs
@@ -328,7 +328,7 @@ def _block_case(mode, bits, T, A, L, seed, compute="dequant"):
     gen = _gen(seed)
     lin, tabs = BasicAVTransformerBlock.random_parts(gen, "cuda", mode=mode, bits=bits)
     p = _oracle_params(lin, tabs)
-    blk = BasicAVTransformerBlock(lin, tabs, VIDEO_22B, AUDIO_22B).set_compute(compute)
+    blk = BasicAVTransformerBlock(lin, tabs, VIDEO_22B, AUDIO_22B).set_compute(compute).set_attention(attention)
 
     def stream(cfg, t):
         ang = torch.rand(1, cfg.heads, t, cfg.d_head // 2, generator=gen, device="cuda") * 6.28
