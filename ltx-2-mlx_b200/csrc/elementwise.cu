@@ -283,13 +283,17 @@ __global__ void __launch_bounds__(kTileThreads, kNorm == LTXQ_NORM_LAYER ? 2 : 3
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float e[2] = {lo_bf16(w[i]), hi_bf16(w[i])};
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float n = e[h];
-          if (kNorm == LTXQ_NORM_RMS) n = rbf16(__fmul_rn(n, inv));
-          else if (kNorm == LTXQ_NORM_LAYER) n = rbf16(__fmul_rn(__fsub_rn(n, mu_f), inv));
-          e[h] = modulate1<kVecBf16>(n, s8[2 * i + h], t8[2 * i + h]);
+        if (kNorm != LTXQ_NORM_NONE) {
+          // the norm's bf16 rounding, two values per conversion
+          const uint32_t nw = kNorm == LTXQ_NORM_RMS
+                                  ? pack_bf16x2(__fmul_rn(e[0], inv), __fmul_rn(e[1], inv))
+                                  : pack_bf16x2(__fmul_rn(__fsub_rn(e[0], mu_f), inv),
+                                                __fmul_rn(__fsub_rn(e[1], mu_f), inv));
+          e[0] = lo_bf16(nw);
+          e[1] = hi_bf16(nw);
         }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) e[h] = modulate1<kVecBf16>(e[h], s8[2 * i + h], t8[2 * i + h]);
         o[i] = pack_bf16x2(e[0], e[1]);
       }
       if (kMx) mx::mx_write8(o, row, static_cast<int64_t>(c) * 8, mo, 0xFu << (lane & ~3));
