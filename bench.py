@@ -489,6 +489,12 @@ def run_step(args, world, rank, local, dev):
     from ltxq.graph import StepGraph
 
     T, A, B = args.video_tokens, args.audio_tokens, args.batch
+    # exchange forms: at 2 GPUs the K/V all-gathers measured fastest (202.6 ms against
+    # 221.3 / 205.0), at 8 the all-to-all and split-key forms (88.5 ms against 93.1)
+    if args.self_attention == "auto":
+        args.self_attention = "head_parallel" if world >= 8 else "gather"
+    if args.v2a == "auto":
+        args.v2a = "split_keys" if world >= 8 else "gather"
     if T % world:
         raise SystemExit(f"{T} video tokens do not split over {world} ranks")
     tl = T // world
@@ -904,10 +910,12 @@ def main():
                     help="launch the step op by op instead of replaying it as one captured CUDA graph")
     ap.add_argument("--no-overlap", action="store_true",
                     help="run the K/V all-gathers on the compute stream instead of a side stream")
-    ap.add_argument("--self-attention", choices=["gather", "head_parallel"], default="gather",
-                    help="row-sharded video self-attention: K/V all-gather, or Q/K/V all-to-all over heads")
-    ap.add_argument("--v2a", choices=["gather", "split_keys"], default="gather",
-                    help="row-sharded video->audio attention: K/V all-gather, or local keys merged by log-sum-exp")
+    ap.add_argument("--self-attention", choices=["auto", "gather", "head_parallel"], default="auto",
+                    help="row-sharded video self-attention: K/V all-gather, or Q/K/V all-to-all over heads; "
+                         "auto = head_parallel on 8 or more GPUs (measured faster there), gather below")
+    ap.add_argument("--v2a", choices=["auto", "gather", "split_keys"], default="auto",
+                    help="row-sharded video->audio attention: K/V all-gather, or local keys merged by log-sum-exp; "
+                         "auto = split_keys on 8 or more GPUs, gather below")
     ap.add_argument("--quant", choices=sorted(STEP_QUANT), default="mxfp8",
                     help="block-linear quantization of the step workload (config 4 is mxfp8)")
     ap.add_argument("--video-tokens", type=int, default=STEP_T,
