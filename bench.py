@@ -481,6 +481,17 @@ def _max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def exchange_forms(world: int, self_attention: str = "auto", v2a: str = "auto") -> tuple[str, str]:
+    """The row-sharded attention exchanges; "auto" picks by GPU count: at 2 GPUs
+    the K/V all-gathers measured fastest (202.6 ms against 221.3 / 205.0), at 8
+    the Q/K/V all-to-all and the split-key form (88.5 ms against 93.1)."""
+    if self_attention == "auto":
+        self_attention = "head_parallel" if world >= 8 else "gather"
+    if v2a == "auto":
+        v2a = "split_keys" if world >= 8 else "gather"
+    return self_attention, v2a
+
+
 def run_step(args, world, rank, local, dev):
     import torch
 
@@ -489,12 +500,7 @@ def run_step(args, world, rank, local, dev):
     from ltxq.graph import StepGraph
 
     T, A, B = args.video_tokens, args.audio_tokens, args.batch
-    # exchange forms: at 2 GPUs the K/V all-gathers measured fastest (202.6 ms against
-    # 221.3 / 205.0), at 8 the all-to-all and split-key forms (88.5 ms against 93.1)
-    if args.self_attention == "auto":
-        args.self_attention = "head_parallel" if world >= 8 else "gather"
-    if args.v2a == "auto":
-        args.v2a = "split_keys" if world >= 8 else "gather"
+    args.self_attention, args.v2a = exchange_forms(world, args.self_attention, args.v2a)
     if T % world:
         raise SystemExit(f"{T} video tokens do not split over {world} ranks")
     tl = T // world

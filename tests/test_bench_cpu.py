@@ -78,3 +78,16 @@ def test_presets_name_the_baseline_configs():
                              workload=bench.STEP_PRESETS["config5"][5])
     assert cfg["global_batch"] == 2 and cfg["audio_tokens"] == 751 and cfg["workload"].startswith("config5")
     assert bench._config1_config(1)["workload"].startswith("config1")
+
+
+def test_exchange_forms_by_gpu_count():
+    """--self-attention / --v2a auto: the K/V all-gathers below 8 GPUs, the
+    all-to-all and split-key forms from 8 up; explicit choices pass through."""
+    import bench
+
+    assert bench.exchange_forms(1) == ("gather", "gather")
+    assert bench.exchange_forms(2) == ("gather", "gather")
+    assert bench.exchange_forms(4) == ("gather", "gather")
+    assert bench.exchange_forms(8) == ("head_parallel", "split_keys")
+    assert bench.exchange_forms(8, "gather", "gather") == ("gather", "gather")
+    assert bench.exchange_forms(2, "head_parallel", "split_keys") == ("head_parallel", "split_keys")

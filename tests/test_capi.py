@@ -93,6 +93,44 @@ def test_mx_entry_validation_without_gpu(lib):
     assert lib.ltxq_head_gate_mx(16, 16, 4, 2, 64, None, None, None) == _lib.ERR_INVALID
 
 
+def test_attention_validation_without_gpu(lib):
+    """ltxq_attention rejects bad shapes / strides / pointers before any CUDA
+    call, and an empty batch is a no-op."""
+    from ltxq import _lib
+
+    def call(q=16, k=16, v=16, b=1, tq=8, tk=8, h=2, d=64, qs=128, ks=128, vs=128, scale=0.125, out=16):
+        return lib.ltxq_attention(q, k, v, b, tq, tk, h, d, qs, ks, vs, scale, out, None)
+
+    assert call(q=None) == _lib.ERR_INVALID
+    assert call(d=96, qs=192, ks=192, vs=192) == _lib.ERR_UNSUPPORTED  # head_dim
+    assert call(tk=0) == _lib.ERR_INVALID
+    assert call(qs=64) == _lib.ERR_INVALID                               # stride < heads * head_dim
+    assert call(vs=132) == _lib.ERR_UNSUPPORTED                          # stride not a multiple of 8
+    assert call(out=24) == _lib.ERR_UNSUPPORTED                          # 16-byte alignment
+    assert call(scale=0.0) == _lib.ERR_INVALID
+    assert call(b=0) == _lib.OK
+
+
+def test_mx_activation_layout_on_cpu():
+    """MXActivation: one buffer holding both terms' codes and scale atoms at
+    256-byte aligned offsets, sized by ltxq_mx_split_sizes."""
+    import torch
+
+    from ltxq.kernels import MXActivation
+
+    for M, K, terms in ((201, 2048, 2), (1000, 4096, 1), (1, 128, 2)):
+        a = MXActivation((M,), K, terms, torch.device("cpu"))
+        hi, lo, sf_hi, sf_lo = a.tensors()
+        assert hi.shape == (M, K) and (lo is None) == (terms == 1)
+        row_tiles = (M + 127) // 128 + 1
+        assert sf_hi.numel() == (K // 128) * row_tiles * 512
+        base = a.buffer.data_ptr()
+        for p in a._parts:
+            assert p is None or (p - base) % 256 == 0
+        st = a.struct()
+        assert st.terms == terms and st.hi == base
+
+
 def test_denoise_update_validation_without_gpu(lib):
     """ltxq_denoise_update rejects bad scalars / shapes / missing operands
     before any CUDA call, and an empty latent is a no-op."""
