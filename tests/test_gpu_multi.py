@@ -21,7 +21,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _build(dev):
+def _build(dev, batch=1):
     from ltxq.block import BasicAVTransformerBlock, StreamConfig, TransformerArgs
 
     video = StreamConfig(1024, 8, 128, 1024)
@@ -37,21 +37,21 @@ def _build(dev):
         ang = torch.rand(1, heads, t, d // 2, generator=gen, device=dev) * 6.28
         return torch.cos(ang), torch.sin(ang)
 
-    T, A, L = 128, 40, 32
-    v = TransformerArgs(x=rnd(1, T, video.dim, dtype=torch.bfloat16), context=rnd(1, L, video.context_dim,
+    T, A, L, B = 128, 40, 32, batch  # batch 2: the CFG pair as one pass, per-batch AdaLN vectors
+    v = TransformerArgs(x=rnd(B, T, video.dim, dtype=torch.bfloat16), context=rnd(B, L, video.context_dim,
                                                                                    dtype=torch.bfloat16),
-                        timesteps=rnd(1, 1, 9, video.dim, std=0.1), positional_embeddings=rope(video.heads, T, 128),
+                        timesteps=rnd(B, 1, 9, video.dim, std=0.1), positional_embeddings=rope(video.heads, T, 128),
                         cross_positional_embeddings=rope(audio.heads, T, 64),
-                        cross_scale_shift_timestep=rnd(1, 1, 4, video.dim, std=0.1),
-                        cross_gate_timestep=rnd(1, 1, 1, video.dim, std=0.1),
-                        prompt_timestep=rnd(1, 1, 2, video.dim, std=0.1))
-    a = TransformerArgs(x=rnd(1, A, audio.dim, dtype=torch.bfloat16), context=rnd(1, L, audio.context_dim,
+                        cross_scale_shift_timestep=rnd(B, 1, 4, video.dim, std=0.1),
+                        cross_gate_timestep=rnd(B, 1, 1, video.dim, std=0.1),
+                        prompt_timestep=rnd(B, 1, 2, video.dim, std=0.1))
+    a = TransformerArgs(x=rnd(B, A, audio.dim, dtype=torch.bfloat16), context=rnd(B, L, audio.context_dim,
                                                                                    dtype=torch.bfloat16),
-                        timesteps=rnd(1, 1, 9, audio.dim, std=0.1), positional_embeddings=rope(audio.heads, A, 64),
+                        timesteps=rnd(B, 1, 9, audio.dim, std=0.1), positional_embeddings=rope(audio.heads, A, 64),
                         cross_positional_embeddings=rope(audio.heads, A, 64),
-                        cross_scale_shift_timestep=rnd(1, 1, 4, audio.dim, std=0.1),
-                        cross_gate_timestep=rnd(1, 1, 1, audio.dim, std=0.1),
-                        prompt_timestep=rnd(1, 1, 2, audio.dim, std=0.1))
+                        cross_scale_shift_timestep=rnd(B, 1, 4, audio.dim, std=0.1),
+                        cross_gate_timestep=rnd(B, 1, 1, audio.dim, std=0.1),
+                        prompt_timestep=rnd(B, 1, 2, audio.dim, std=0.1))
     return blocks, v, a
 
 
@@ -62,7 +62,7 @@ def _rows(args, lo, hi):
                                                           for c in args.cross_positional_embeddings))
 
 
-def _worker(rank, world, port, out_dir, self_attention, v2a):
+def _worker(rank, world, port, out_dir, self_attention, v2a, batch):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -75,7 +75,7 @@ def _worker(rank, world, port, out_dir, self_attention, v2a):
                             device_id=dev)
     from ltxq.block import RowShard
 
-    blocks, v, a = _build(dev)
+    blocks, v, a = _build(dev, batch)
     T = v.x.shape[1]
     tl = T // world
     shard = RowShard(dist.group.WORLD, world, rank, self_attention=self_attention, v2a=v2a)
@@ -89,15 +89,16 @@ def _worker(rank, world, port, out_dir, self_attention, v2a):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("self_attention,v2a", [("gather", "gather"), ("head_parallel", "split_keys")])
-def test_row_sharded_block_matches_unsharded(cuda, tmp_path, self_attention, v2a):
+@pytest.mark.parametrize("self_attention,v2a,batch", [("gather", "gather", 1), ("head_parallel", "split_keys", 1),
+                                                       ("gather", "gather", 2), ("head_parallel", "split_keys", 2)])
+def test_row_sharded_block_matches_unsharded(cuda, tmp_path, self_attention, v2a, batch):
     world = 2
     port = _free_port()
-    mp.start_processes(_worker, args=(world, port, str(tmp_path), self_attention, v2a), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(world, port, str(tmp_path), self_attention, v2a, batch), nprocs=world,
+                       join=True, start_method="spawn")
     from oracle import ref_ops as ro
 
-    blocks, v, a = _build(torch.device("cuda", 0))
+    blocks, v, a = _build(torch.device("cuda", 0), batch)
     for b in blocks:
         v, a = b(v, a)
     got_v = torch.cat([torch.load(os.path.join(tmp_path, f"r{r}.pt"))["v"] for r in range(world)], dim=1)
