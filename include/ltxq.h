@@ -215,6 +215,15 @@ ltxq_status ltxq_attention(const void* q, const void* k, const void* v, int64_t 
                            int64_t kv_rows, int64_t heads, int64_t head_dim, int64_t q_stride, int64_t k_stride,
                            int64_t v_stride, float scale, void* out, void* stream);
 
+/* ltxq_qk_norm_rope for Q and K of the same rows and the same RoPE tables
+ * (the self-attention's, attention.py:580-587): one pass, the tables read
+ * once for both.  heads * head_dim / 16 a multiple of 32 (at most 256);
+ * weights 16-byte aligned; otherwise as ltxq_qk_norm_rope. */
+ltxq_status ltxq_qk_norm_rope_pair(const void* q, const void* k, int64_t rows, int64_t q_stride, int64_t k_stride,
+                                   int64_t heads, int64_t head_dim, const float* q_weight, const float* k_weight,
+                                   float eps, const float* cos_table, const float* sin_table, int64_t pe_tokens,
+                                   void* q_out, void* k_out, void* stream);
+
 /* ---- quantized weights ------------------------------------------------ */
 /* Quantize a bf16 weight [N, K] into the MLX cache layout described by `w`
  * (w->weight/scales/biases are outputs here; w->bias is ignored). */

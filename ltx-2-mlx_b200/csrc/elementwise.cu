@@ -633,6 +633,173 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const uint16_t* __res
   }
 }
 
+// Tile form: a unit is (head h, 8-wide chunk c): the chunk c of both halves
+// of head h (the rotation pairs element i of the first half with element i of
+// the second).  A row has U = heads * D / 16 units (a multiple of 32); a CTA
+// of 256 threads covers 256 / U rows per pass and kR passes, so every thread
+// issues all its 16-byte row and table loads at once.  kPair: a second
+// operand (K next to Q) on the same rows, rotated by the same tables, which
+// are then read once for both.  Row statistics: an fp32 sum of squares per
+// thread, added across the row's threads in fp64 in a fixed order.
+constexpr int kRopeThreads = 256;
+
+template <int kD, int kR, bool kPair>
+__global__ void __launch_bounds__(kRopeThreads, 2)
+    qk_rope_tile_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ x2, int64_t rows,
+                        int64_t stride, int64_t stride2, int heads, const float* __restrict__ w,
+                        const float* __restrict__ w2, float eps, const float* __restrict__ cosv,
+                        const float* __restrict__ sinv, int64_t pe_tokens, uint16_t* __restrict__ out,
+                        uint16_t* __restrict__ out2) {
+  constexpr int kCh = kD / 16;  // chunks per half head
+  constexpr int kOps = kPair ? 2 : 1;
+  __shared__ double red[kR][kOps][kRopeThreads / 32];
+  __shared__ float inv_s[kR][kOps][kRopeThreads / 32];  // per row of the pass (at most 8 rows)
+  const int U = heads * kCh;
+  const int rpp = kRopeThreads / U;  // rows per pass
+  const int tid = threadIdx.x;
+  const int rr = tid / U, u = tid - rr * U;  // row within the pass, unit
+  const bool active = rr < rpp;
+  const int h = u / kCh, c = u - h * kCh;
+  const int col_lo = h * kD + 8 * c, col_hi = col_lo + kD / 2;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int wpr = U / 32;  // warps per row
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * rpp * kR;
+  const uint16_t* xs[2] = {x, x2};
+  const int64_t strides[2] = {stride, stride2};
+  uint4 lo[kR][kOps], hi[kR][kOps];
+  float4 cs[kR][2], sn[kR][2];
+#pragma unroll
+  for (int p = 0; p < kR; ++p) {
+    const int64_t row = row0 + p * rpp + rr;
+    const bool live = active && row < rows;
+#pragma unroll
+    for (int o = 0; o < kOps; ++o) {
+      const uint16_t* xr = xs[o] + (live ? row : 0) * strides[o];
+      lo[p][o] = live ? __ldg(reinterpret_cast<const uint4*>(xr + col_lo)) : make_uint4(0, 0, 0, 0);
+      hi[p][o] = live ? __ldg(reinterpret_cast<const uint4*>(xr + col_hi)) : make_uint4(0, 0, 0, 0);
+    }
+    if (cosv != nullptr && live) {
+      const int64_t b = row / pe_tokens, tt = row - b * pe_tokens;
+      const int64_t off = ((b * heads + h) * pe_tokens + tt) * (kD / 2) + 8 * c;
+      cs[p][0] = __ldg(reinterpret_cast<const float4*>(cosv + off));
+      cs[p][1] = __ldg(reinterpret_cast<const float4*>(cosv + off + 4));
+      sn[p][0] = __ldg(reinterpret_cast<const float4*>(sinv + off));
+      sn[p][1] = __ldg(reinterpret_cast<const float4*>(sinv + off + 4));
+    }
+  }
+  // per-row sums of squares: fp32 per thread, fp64 across the row's warps
+#pragma unroll
+  for (int p = 0; p < kR; ++p)
+#pragma unroll
+    for (int o = 0; o < kOps; ++o) {
+      const uint32_t a[8] = {lo[p][o].x, lo[p][o].y, lo[p][o].z, lo[p][o].w,
+                             hi[p][o].x, hi[p][o].y, hi[p][o].z, hi[p][o].w};
+      float q = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        q = __fmaf_rn(hi_bf16(a[k]), hi_bf16(a[k]), __fmaf_rn(lo_bf16(a[k]), lo_bf16(a[k]), q));
+      const double d = warp_sum(static_cast<double>(q));
+      if (lane == 0) red[p][o][warp] = d;
+    }
+  __syncthreads();
+  if (active && u % 32 == 0 && u / 32 == 0) {  // the first warp of each row of the pass
+#pragma unroll
+    for (int p = 0; p < kR; ++p)
+#pragma unroll
+      for (int o = 0; o < kOps; ++o)
+        if (lane == 0) {
+          double t = 0.0;
+          for (int i = 0; i < wpr; ++i) t += red[p][o][rr * wpr + i];
+          const float ms = static_cast<float>(t / static_cast<double>(heads * kD));
+          inv_s[p][o][rr] = static_cast<float>(rsqrt(static_cast<double>(__fadd_rn(ms, eps))));
+        }
+  }
+  __syncthreads();
+  if (!active) return;
+  const float* ws[2] = {w, w2};
+  uint16_t* outs[2] = {out, out2};
+#pragma unroll
+  for (int o = 0; o < kOps; ++o) {
+    float w1[8], w2v[8];
+    {
+      const float4 a0 = __ldg(reinterpret_cast<const float4*>(ws[o] + col_lo));
+      const float4 a1 = __ldg(reinterpret_cast<const float4*>(ws[o] + col_lo + 4));
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(ws[o] + col_hi));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(ws[o] + col_hi + 4));
+      w1[0] = a0.x; w1[1] = a0.y; w1[2] = a0.z; w1[3] = a0.w; w1[4] = a1.x; w1[5] = a1.y; w1[6] = a1.z; w1[7] = a1.w;
+      w2v[0] = b0.x; w2v[1] = b0.y; w2v[2] = b0.z; w2v[3] = b0.w; w2v[4] = b1.x; w2v[5] = b1.y; w2v[6] = b1.z;
+      w2v[7] = b1.w;
+    }
+#pragma unroll
+    for (int p = 0; p < kR; ++p) {
+      const int64_t row = row0 + p * rpp + rr;
+      if (row >= rows) break;
+      const float inv = inv_s[p][o][rr];
+      const uint32_t al[4] = {lo[p][o].x, lo[p][o].y, lo[p][o].z, lo[p][o].w};
+      const uint32_t ah[4] = {hi[p][o].x, hi[p][o].y, hi[p][o].z, hi[p][o].w};
+      float y1[8], y2[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        y1[2 * k] = lo_bf16(al[k]);
+        y1[2 * k + 1] = hi_bf16(al[k]);
+        y2[2 * k] = lo_bf16(ah[k]);
+        y2[2 * k + 1] = hi_bf16(ah[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {
+        // y = bf16(x * inv * w), two values per conversion
+        const uint32_t r1 = pack_bf16x2(__fmul_rn(__fmul_rn(y1[k], inv), w1[k]),
+                                        __fmul_rn(__fmul_rn(y1[k + 1], inv), w1[k + 1]));
+        const uint32_t r2 = pack_bf16x2(__fmul_rn(__fmul_rn(y2[k], inv), w2v[k]),
+                                        __fmul_rn(__fmul_rn(y2[k + 1], inv), w2v[k + 1]));
+        y1[k] = lo_bf16(r1);
+        y1[k + 1] = hi_bf16(r1);
+        y2[k] = lo_bf16(r2);
+        y2[k + 1] = hi_bf16(r2);
+      }
+      if (cosv != nullptr) {
+        const float cv[8] = {cs[p][0].x, cs[p][0].y, cs[p][0].z, cs[p][0].w, cs[p][1].x, cs[p][1].y, cs[p][1].z,
+                             cs[p][1].w};
+        const float sv[8] = {sn[p][0].x, sn[p][0].y, sn[p][0].z, sn[p][0].w, sn[p][1].x, sn[p][1].y, sn[p][1].z,
+                             sn[p][1].w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float a1 = y1[k], a2 = y2[k];
+          y1[k] = __fsub_rn(__fmul_rn(a1, cv[k]), __fmul_rn(a2, sv[k]));
+          y2[k] = __fadd_rn(__fmul_rn(a1, sv[k]), __fmul_rn(a2, cv[k]));
+        }
+      }
+      uint16_t* orow = outs[o] + row * static_cast<int64_t>(heads) * kD;
+      uint4 o1, o2;
+      o1.x = pack_bf16x2(y1[0], y1[1]); o1.y = pack_bf16x2(y1[2], y1[3]);
+      o1.z = pack_bf16x2(y1[4], y1[5]); o1.w = pack_bf16x2(y1[6], y1[7]);
+      o2.x = pack_bf16x2(y2[0], y2[1]); o2.y = pack_bf16x2(y2[2], y2[3]);
+      o2.z = pack_bf16x2(y2[4], y2[5]); o2.w = pack_bf16x2(y2[6], y2[7]);
+      *reinterpret_cast<uint4*>(orow + col_lo) = o1;
+      *reinterpret_cast<uint4*>(orow + col_hi) = o2;
+    }
+  }
+}
+
+constexpr int kRopeRows = 2;  // passes per CTA
+
+template <bool kPair>
+static ltxq_status launch_rope_tile(const uint16_t* x, const uint16_t* x2, int64_t rows, int64_t stride,
+                                   int64_t stride2, int heads, int D, const float* w, const float* w2, float eps,
+                                   const float* cosv, const float* sinv, int64_t pe_tokens, uint16_t* out,
+                                   uint16_t* out2, cudaStream_t s) {
+  const int U = heads * (D / 16);
+  const int64_t per_cta = static_cast<int64_t>(kRopeThreads / U) * kRopeRows;
+  const unsigned blocks = static_cast<unsigned>((rows + per_cta - 1) / per_cta);
+  if (D == 128)
+    qk_rope_tile_kernel<128, kRopeRows, kPair><<<blocks, kRopeThreads, 0, s>>>(
+        x, x2, rows, stride, stride2, heads, w, w2, eps, cosv, sinv, pe_tokens, out, out2);
+  else
+    qk_rope_tile_kernel<64, kRopeRows, kPair><<<blocks, kRopeThreads, 0, s>>>(
+        x, x2, rows, stride, stride2, heads, w, w2, eps, cosv, sinv, pe_tokens, out, out2);
+  return launch_check("qk_norm_rope launch");
+}
+
 }  // namespace ltxq
 
 extern "C" ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t row_stride, int64_t heads,
@@ -652,14 +819,50 @@ extern "C" ltxq_status ltxq_qk_norm_rope(const void* x, int64_t rows, int64_t ro
   if (!(eps >= 0.f)) return fail(LTXQ_ERR_INVALID, "qk_norm_rope: eps must be >= 0");
   if (rows == 0) return LTXQ_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
   auto* xi = static_cast<const uint16_t*>(x);
   auto* o = static_cast<uint16_t*>(out);
   const int h = static_cast<int>(heads);
+  if ((heads * (head_dim / 16)) % 32 == 0 && !(reinterpret_cast<uintptr_t>(weight) & 15u))
+    return launch_rope_tile<false>(xi, nullptr, rows, row_stride, 0, h, static_cast<int>(head_dim), weight, nullptr,
+                                   eps, cos_table, sin_table, pe_tokens, o, nullptr, s);
+  const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
   // heads per lane: heads / (32 / (D/16)), <= 32 heads
   if (head_dim == 128)
     qk_norm_rope_kernel<128, 8><<<blocks, 256, 0, s>>>(xi, rows, row_stride, h, weight, eps, cos_table, sin_table, pe_tokens, o);
   else
     qk_norm_rope_kernel<64, 4><<<blocks, 256, 0, s>>>(xi, rows, row_stride, h, weight, eps, cos_table, sin_table, pe_tokens, o);
   return launch_check("qk_norm_rope launch");
+}
+
+extern "C" ltxq_status ltxq_qk_norm_rope_pair(const void* q, const void* k, int64_t rows, int64_t q_stride,
+                                              int64_t k_stride, int64_t heads, int64_t head_dim, const float* q_weight,
+                                              const float* k_weight, float eps, const float* cos_table,
+                                              const float* sin_table, int64_t pe_tokens, void* q_out, void* k_out,
+                                              void* stream) {
+  using namespace ltxq;
+  if (!q || !k || !q_out || !k_out || !q_weight || !k_weight)
+    return fail(LTXQ_ERR_INVALID, "qk_norm_rope_pair: NULL tensor");
+  if (rows < 0 || heads <= 0 || q_stride < heads * head_dim || k_stride < heads * head_dim)
+    return fail(LTXQ_ERR_INVALID, "qk_norm_rope_pair: bad shape");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(LTXQ_ERR_UNSUPPORTED, "qk_norm_rope_pair: head_dim must be 64 or 128");
+  if ((heads * (head_dim / 16)) % 32 != 0 || heads * (head_dim / 16) > kRopeThreads)
+    return fail(LTXQ_ERR_UNSUPPORTED, "qk_norm_rope_pair: heads * head_dim / 16 must be a multiple of 32, <= 256");
+  if ((cos_table == nullptr) != (sin_table == nullptr))
+    return fail(LTXQ_ERR_INVALID, "qk_norm_rope_pair: cos/sin pairing");
+  if (cos_table && (pe_tokens <= 0 || rows % pe_tokens != 0))
+    return fail(LTXQ_ERR_INVALID, "qk_norm_rope_pair: rows must be a multiple of pe_tokens > 0");
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(q_out) |
+        reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(cos_table) |
+        reinterpret_cast<uintptr_t>(sin_table) | reinterpret_cast<uintptr_t>(q_weight) |
+        reinterpret_cast<uintptr_t>(k_weight)) & 15u) ||
+      (q_stride % 8) != 0 || (k_stride % 8) != 0)
+    return fail(LTXQ_ERR_UNSUPPORTED,
+                "qk_norm_rope_pair: tensors must be 16-byte aligned (row strides multiples of 8)");
+  if (!(eps >= 0.f)) return fail(LTXQ_ERR_INVALID, "qk_norm_rope_pair: eps must be >= 0");
+  if (rows == 0) return LTXQ_OK;
+  return launch_rope_tile<true>(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k), rows, q_stride,
+                                k_stride, static_cast<int>(heads), static_cast<int>(head_dim), q_weight, k_weight,
+                                eps, cos_table, sin_table, pe_tokens, static_cast<uint16_t*>(q_out),
+                                static_cast<uint16_t*>(k_out), static_cast<cudaStream_t>(stream));
 }

@@ -97,6 +97,8 @@ SIGNATURES = {
     "ltxq_head_gate": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "ltxq_qk_norm_rope": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p,
                                     c_void_p, c_int64, c_void_p, c_void_p]),
+    "ltxq_qk_norm_rope_pair": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                         c_void_p, c_float, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
     "ltxq_attention": (c_int32, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
                                  c_int64, c_int64, c_float, c_void_p, c_void_p]),
     "ltxq_quantize": (c_int32, [c_void_p, POINTER(QWeight), c_void_p]),

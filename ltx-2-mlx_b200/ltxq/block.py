@@ -341,7 +341,10 @@ class QAttention:
         return self.attend(q, k, v, gl)
 
     def norm_rope(self, q, k, pe=None, k_pe=None):
-        """QK RMSNorm + split RoPE (attention.py:580-587, rope.py:53-90)."""
+        """QK RMSNorm + split RoPE (attention.py:580-587, rope.py:53-90); Q and
+        K of the same rows and tables (self-attention) in one pass."""
+        if k_pe is None and q.shape == k.shape and (self.heads * self.d_head // 16) % 32 == 0:
+            return K.qk_norm_rope_pair(q, k, self.q_norm, self.k_norm, self.heads, self.eps, pe)
         q = K.qk_norm_rope(q, self.q_norm, self.heads, self.eps, pe)
         k = K.qk_norm_rope(k, self.k_norm, self.heads, self.eps, (pe if k_pe is None else k_pe) if pe is not None else None)
         return q, k

@@ -226,6 +226,38 @@ def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int, mx_terms
     return res
 
 
+def qk_norm_rope_pair(q: torch.Tensor, k: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, heads: int,
+                      eps: float = 1e-6, pe: tuple | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``qk_norm_rope`` of Q and K over the same rows and RoPE tables in one
+    pass (the tables are read once): the self-attention's Q/K norm and
+    rotation (attention.py:580-587)."""
+    for t, name in ((q, "q"), (k, "k")):
+        _require_cuda(t, name)
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.dim() != 3:
+            raise ValueError(f"{name} must be a (B, T, W) bfloat16 tensor with unit column stride")
+    if q.shape != k.shape:
+        raise ValueError("q and k must have the same shape")
+    b, t, width = q.shape
+    q = q if q.stride(0) == t * q.stride(1) else q.contiguous()
+    k = k if k.stride(0) == t * k.stride(1) else k.contiguous()
+    d = width // heads
+    wq, wk = q_weight.float().contiguous(), k_weight.float().contiguous()
+    oq = torch.empty((b, t, width), dtype=torch.bfloat16, device=q.device)
+    ok = torch.empty_like(oq)
+    cos = sin = None
+    if pe is not None:
+        cos, sin = pe[0].float().contiguous(), pe[1].float().contiguous()
+        if cos.shape != (b, heads, t, d // 2) and cos.shape != (1, heads, t, d // 2):
+            raise ValueError(f"RoPE table shape {tuple(cos.shape)} does not match {(b, heads, t, d // 2)}")
+        if cos.shape[0] != b:
+            cos, sin = cos.expand(b, -1, -1, -1).contiguous(), sin.expand(b, -1, -1, -1).contiguous()
+    _lib.check(_lib.load().ltxq_qk_norm_rope_pair(
+        q.data_ptr(), k.data_ptr(), b * t, q.stride(1), k.stride(1), heads, d, wq.data_ptr(), wk.data_ptr(),
+        float(eps), cos.data_ptr() if cos is not None else None, sin.data_ptr() if sin is not None else None, t,
+        oq.data_ptr(), ok.data_ptr(), _stream()), "qk_norm_rope_pair")
+    return oq, ok
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float | None = None) -> torch.Tensor:
     """``softmax(q k^T * scale) v`` per head (the block's
     ``mx.fast.scaled_dot_product_attention``, attention.py:170-302) on

@@ -447,7 +447,8 @@ def test_qlinear_group_sizes_and_unaligned_group_rows(cuda, gs, K, bits):
     assert (ulp_diff_bf16(out, ro.linear(x, deq, bias)) > 0).mean() < 0.01
 
 
-@pytest.mark.parametrize("heads,d,with_pe,strided", [(32, 128, True, True), (32, 64, True, False), (8, 128, False, True)])
+@pytest.mark.parametrize("heads,d,with_pe,strided", [(32, 128, True, True), (32, 64, True, False), (8, 128, False, True),
+                                                     (6, 64, True, True)])  # 6 x 64: the warp-per-row form
 def test_qk_norm_rope_matches_oracle(cuda, heads, d, with_pe, strided):
     """Fused QK RMSNorm + split RoPE against the oracle (attention.py:320-329,
     rope.py:53-90) and against the plain torch fp32 reference."""
@@ -635,3 +636,28 @@ def test_strided_vector_views_match_contiguous(cuda):
     y1 = ql(a, residual=res, gate=gv)
     y2 = ql(a, residual=res, gate=gv.contiguous())
     assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+
+
+@pytest.mark.parametrize("heads,d,batch", [(32, 128, 1), (32, 64, 2)])
+def test_qk_norm_rope_pair_equals_two_calls(cuda, heads, d, batch):
+    """ltxq_qk_norm_rope_pair (Q and K in one pass, the tables read once)
+    gives the bits of two ltxq_qk_norm_rope calls; Q strided as a column
+    slice of a fused projection output."""
+    import torch
+
+    import ltxq
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    T, W = 300, heads * d
+    fused = torch.randn(batch, T, 3 * W + 32, generator=g, device="cuda").to(torch.bfloat16)
+    q, k = fused[..., :W], fused[..., W:2 * W]
+    wq = 1.0 + 0.1 * torch.randn(W, generator=g, device="cuda")
+    wk = 1.0 + 0.1 * torch.randn(W, generator=g, device="cuda")
+    ang = torch.rand(batch, heads, T, d // 2, generator=g, device="cuda") * 6.28
+    pe = (torch.cos(ang), torch.sin(ang))
+    oq, ok = ltxq.kernels.qk_norm_rope_pair(q, k, wq, wk, heads, 1e-6, pe)
+    rq = ltxq.kernels.qk_norm_rope(q, wq, heads, 1e-6, pe)
+    rk = ltxq.kernels.qk_norm_rope(k, wk, heads, 1e-6, pe)
+    assert torch.equal(oq.view(torch.int16), rq.view(torch.int16))
+    assert torch.equal(ok.view(torch.int16), rk.view(torch.int16))
