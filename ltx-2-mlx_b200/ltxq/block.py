@@ -521,10 +521,15 @@ class BasicAVTransformerBlock:
 
     # -------------------------------------------------------------- forward
     def _ada(self, table: str, ts: torch.Tensor, start: int, end: int):
-        """get_ada_values (transformer.py:286-309) -> list of (B, 1, C) fp32."""
-        t = self.tables[table][start:end]
-        vals = t[None, None] + ts[:, :, start:end]
-        return [vals[:, :, i] for i in range(end - start)]  # views: the kernels take strided vectors
+        """get_ada_values (transformer.py:286-309) -> list of (B, 1, C) fp32.
+        All rows of a table are added to the timestep rows in one launch per
+        block call (the same elementwise fp32 adds), then sliced."""
+        key = (table, id(ts))
+        vals = self._ada_rows.get(key)
+        if vals is None:
+            vals = self.tables[table][None, None] + ts[:, :, :self.tables[table].shape[0]]
+            self._ada_rows[key] = vals
+        return [vals[:, :, i] for i in range(start, end)]  # views: the kernels take strided vectors
 
     def __call__(self, video: TransformerArgs, audio: TransformerArgs, shard: RowShard | None = None,
                  skip: frozenset = frozenset()):
@@ -534,6 +539,7 @@ class BasicAVTransformerBlock:
         values of ``ltxq.perturbations``: a perturbed pass for STG,
         transformer.py:429-444, 455-457, 496-497, 574-575, 603-604)."""
         eps = self.norm_eps
+        self._ada_rows = {}  # (table, timestep tensor) -> all rows, for this call only
         vx, ax = video.x.contiguous(), audio.x.contiguous()
         run_v = "skip_video_self_attn" not in skip
         run_a = "skip_audio_self_attn" not in skip
