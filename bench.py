@@ -280,6 +280,25 @@ class CpuBlock:
         return time.perf_counter() - t0
 
 
+def _cpu_threads() -> int:
+    """Threads of the CPU legs: the cores this process may use (oracle/_par.py)."""
+    from oracle._par import usable_cpus
+
+    return usable_cpus()
+
+
+def _limit_cpu_threads():
+    """Context that sizes the BLAS thread pools to the usable cores."""
+    try:
+        from threadpoolctl import threadpool_limits
+
+        return threadpool_limits(limits=_cpu_threads())
+    except ImportError:  # pragma: no cover - threadpoolctl is in the image
+        import contextlib
+
+        return contextlib.nullcontext()
+
+
 def _cpu_block_rotation(blk: "CpuBlock", n_runs: int, warmup: int = 0) -> dict:
     """Runs the block's sub-layers in turn, ``warmup`` untimed then ``n_runs``
     timed (at least one of each), and returns each sub-layer's mean seconds."""
@@ -290,6 +309,7 @@ def _cpu_block_rotation(blk: "CpuBlock", n_runs: int, warmup: int = 0) -> dict:
     for i in range(max(n_runs, len(subs))):
         s = subs[i % len(subs)]
         times[s].append(blk.run(s))
+        print(f"[cpu] {s}: {times[s][-1]:.2f} s on {_cpu_threads()} threads", file=sys.stderr, flush=True)
     return {s: sum(v) / len(v) for s, v in times.items()}
 
 
@@ -297,7 +317,7 @@ def _cpu_block_line(per_sub: dict, blk: "CpuBlock", blocks: int = STEP_BLOCKS) -
     """(ms per step of ``blocks`` blocks, the cpu_baseline description) from
     measured sub-layer seconds."""
     block_s = sum(per_sub.values())
-    threads = os.cpu_count() or 1
+    threads = _cpu_threads()
     extra = f"extrapolated x{blocks} blocks per step" if blocks > 1 else "not extrapolated"
     desc = (f"measured: one full block ({blk.quant}; {blk.video_tokens} video, {blk.audio_tokens} audio, {STEP_L} "
             f"text rows; attention included; weights dequantized once per sub-layer call) = {block_s:.2f} s, as "
@@ -353,7 +373,12 @@ def _cpu_ff_sample(sample: int = FF_T, seed: int = 1):
 
 def cpu_baseline(workload: str):
     """Bounded CPU measurement for the cpu_baseline field of the GPU line."""
-    threads = os.cpu_count() or 1
+    with _limit_cpu_threads():
+        return _cpu_baseline(workload)
+
+
+def _cpu_baseline(workload: str):
+    threads = _cpu_threads()
     if workload in ("step", "config3"):
         blk = CpuBlock() if workload == "step" else CpuBlock(3456, 126, "int8")
         blocks = STEP_BLOCKS if workload == "step" else 1
@@ -376,7 +401,12 @@ def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    with _limit_cpu_threads():
+        _run_reference(args, world)
+
+
+def _run_reference(args, world):
+    threads = _cpu_threads()
     measured = None
     if args.workload == "config5":
         print(json.dumps({"impl": "reference", "unavailable": "config 5 on the host cores takes hours per step "
