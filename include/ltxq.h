@@ -308,6 +308,13 @@ ltxq_status ltxq_adaln_modulate_mx(const void* x, int64_t rows, int64_t C, const
  * in ltxq_adaln_modulate_mx. */
 ltxq_status ltxq_head_gate_mx(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
                               void* out, const ltxq_mx_act* out_mx, void* stream);
+/* ltxq_head_gate / ltxq_head_gate_mx with the gate logits of row m at
+ * logits + m * logits_stride (elements, >= heads): the logits may be a
+ * column slice of a fused projection output (this library's Q|K|V|gate
+ * GEMM), where the reference computes them with their own linear
+ * (attention.py:559-601).  `out_mx` NULL: bf16 `out` only. */
+ltxq_status ltxq_head_gate_ex(const void* o, const void* logits, int64_t logits_stride, int64_t rows, int64_t heads,
+                              int64_t head_dim, void* out, const ltxq_mx_act* out_mx, void* stream);
 
 /* ltxq_adaln_qlinear without a workspace argument and without allocating.
  * No counterpart in the reference.  For hosts that cannot let a library

@@ -336,12 +336,14 @@ __global__ void gated_add_kernel(const uint16_t* __restrict__ res, const uint16_
 }
 
 // out[m, h, :] = o[m, h, :] * bf16(2 * bf16(sigmoid(logit[m, h]))); one
-// thread per 8 channels.
+// thread per 8 channels.  Row m's logits start at logits + m * lstride (a
+// column slice of a fused projection output needs no copy).
 // kMx: as adaln_tile_kernel's (width % 128 == 0: the grid stride and the row
 // width are multiples of 4 chunks, so a quad stays one 32-channel group).
 template <bool kMx>
-__global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ logits, int64_t rows,
-                                 int64_t heads, int64_t head_dim, uint16_t* __restrict__ out, const mx::MxOut mo) {
+__global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ logits, int64_t lstride,
+                                 int64_t rows, int64_t heads, int64_t head_dim, uint16_t* __restrict__ out,
+                                 const mx::MxOut mo) {
   const int64_t width = heads * head_dim;
   const int64_t total = rows * (width >> 3);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -349,7 +351,7 @@ __global__ void head_gate_kernel(const uint16_t* __restrict__ o, const uint16_t*
     const int64_t row = i / (width >> 3);
     const int64_t c = (i - row * (width >> 3)) << 3;
     const int64_t h = c / head_dim;
-    const double lg = static_cast<double>(bf16_to_f32(__ldg(logits + row * heads + h)));
+    const double lg = static_cast<double>(bf16_to_f32(__ldg(logits + row * lstride + h)));
     const float sig = rbf16(static_cast<float>(1.0 / (1.0 + exp(-lg))));
     const float g = rbf16(__fmul_rn(2.0f, sig));
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + row * width + c));
@@ -493,11 +495,13 @@ ltxq_status ltxq_gated_add(const void* residual, const void* branch, const ltxq_
   return ltxq::launch_gated_add(residual, branch, *gate, rows, C, mode, out, static_cast<cudaStream_t>(stream));
 }
 
-static ltxq_status head_gate(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
-                             void* out, const ltxq_mx_act* out_mx, cudaStream_t stream) {
+static ltxq_status head_gate(const void* o, const void* logits, int64_t lstride, int64_t rows, int64_t heads,
+                             int64_t head_dim, void* out, const ltxq_mx_act* out_mx, cudaStream_t stream) {
   using namespace ltxq;
   if (!o || !logits || (!out && !out_mx)) return fail(LTXQ_ERR_INVALID, "head_gate: NULL tensor");
   if (rows < 0 || heads <= 0 || head_dim <= 0) return fail(LTXQ_ERR_INVALID, "head_gate: bad shape");
+  if (lstride == 0) lstride = heads;
+  if (lstride < heads) return fail(LTXQ_ERR_INVALID, "head_gate: logits row stride < heads");
   if (head_dim % 8 != 0) return fail(LTXQ_ERR_UNSUPPORTED, "head_gate: head_dim must be a multiple of 8");
   if ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(out)) & 15u)
     return fail(LTXQ_ERR_UNSUPPORTED, "head_gate: o/out must be 16-byte aligned");
@@ -515,23 +519,30 @@ static ltxq_status head_gate(const void* o, const void* logits, int64_t rows, in
   auto* li = static_cast<const uint16_t*>(logits);
   auto* oo = static_cast<uint16_t*>(out);
   if (out_mx)
-    head_gate_kernel<true><<<blocks, threads, 0, stream>>>(oi, li, rows, heads, head_dim, oo,
+    head_gate_kernel<true><<<blocks, threads, 0, stream>>>(oi, li, lstride, rows, heads, head_dim, oo,
                                                            mx::out_of(*out_mx, rows, heads * head_dim));
   else
-    head_gate_kernel<false><<<blocks, threads, 0, stream>>>(oi, li, rows, heads, head_dim, oo, mx::MxOut{});
+    head_gate_kernel<false><<<blocks, threads, 0, stream>>>(oi, li, lstride, rows, heads, head_dim, oo,
+                                                            mx::MxOut{});
   return launch_check("head_gate launch");
 }
 
 ltxq_status ltxq_head_gate(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
                            void* out, void* stream) {
   if (!out) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate: NULL tensor");
-  return head_gate(o, logits, rows, heads, head_dim, out, nullptr, static_cast<cudaStream_t>(stream));
+  return head_gate(o, logits, 0, rows, heads, head_dim, out, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 ltxq_status ltxq_head_gate_mx(const void* o, const void* logits, int64_t rows, int64_t heads, int64_t head_dim,
                               void* out, const ltxq_mx_act* out_mx, void* stream) {
   if (!out_mx) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate_mx: out_mx is NULL");
-  return head_gate(o, logits, rows, heads, head_dim, out, out_mx, static_cast<cudaStream_t>(stream));
+  return head_gate(o, logits, 0, rows, heads, head_dim, out, out_mx, static_cast<cudaStream_t>(stream));
+}
+
+ltxq_status ltxq_head_gate_ex(const void* o, const void* logits, int64_t logits_stride, int64_t rows, int64_t heads,
+                              int64_t head_dim, void* out, const ltxq_mx_act* out_mx, void* stream) {
+  if (logits_stride <= 0) return ltxq::fail(LTXQ_ERR_INVALID, "head_gate_ex: logits_stride must be positive");
+  return head_gate(o, logits, logits_stride, rows, heads, head_dim, out, out_mx, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

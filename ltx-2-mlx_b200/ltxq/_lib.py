@@ -122,6 +122,8 @@ SIGNATURES = {
                                          c_void_p]),
     "ltxq_head_gate_mx": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, POINTER(MxAct),
                                     c_void_p]),
+    "ltxq_head_gate_ex": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                    POINTER(MxAct), c_void_p]),
     "ltxq_adaln_qlinear_noalloc": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight),
                                              POINTER(Epilogue), c_void_p, c_void_p]),
     "ltxq_feed_forward": (c_int32, [c_void_p, c_int64, POINTER(Prologue), POINTER(QWeight), POINTER(QWeight),

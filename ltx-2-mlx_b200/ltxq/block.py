@@ -364,7 +364,7 @@ class QAttention:
         to_out runs block-scaled."""
         width = o.shape[-1]
         terms = self.to_out.mx_terms(o.numel() // width) if width % 128 == 0 else 0
-        return K.head_gate(o, gl.contiguous(), self.heads, mx_terms=terms)
+        return K.head_gate(o, gl, self.heads, mx_terms=terms)  # gl: a column slice, read in place
 
     def attend_head_parallel(self, qkv_recv: torch.Tensor, gl, shard: "RowShard") -> torch.Tensor:
         """Row-sharded self-attention in head-parallel form: ``qkv_recv`` is

@@ -203,26 +203,34 @@ def gated_add_fused(residual: torch.Tensor, branch: torch.Tensor, gate: torch.Te
 
 def head_gate(out: torch.Tensor, gate_logits: torch.Tensor, heads: int, mx_terms: int = 0):
     """``out * (2 * sigmoid(gate_logits))[..., None]`` per head
-    (attention.py:559-601).  ``mx_terms`` as in ``adaln_modulate``."""
+    (attention.py:559-601).  ``mx_terms`` as in ``adaln_modulate``.
+    ``gate_logits`` may be a column slice of a wider tensor (rows at a
+    uniform stride, heads contiguous): it is read in place."""
     _require_cuda(out, "out")
     _require_cuda(gate_logits, "gate_logits")
     if out.dtype != torch.bfloat16 or gate_logits.dtype != torch.bfloat16:
         raise ValueError("head_gate expects bfloat16 tensors")
     out = out.contiguous()
-    gate_logits = gate_logits.contiguous()
     width = out.shape[-1]
     rows = out.numel() // width
-    if gate_logits.numel() != rows * heads:
+    if gate_logits.numel() != rows * heads or gate_logits.shape[-1] != heads:
         raise ValueError("gate_logits must have one value per (row, head)")
+    try:
+        gl = gate_logits.view(rows, heads)
+    except RuntimeError:  # rows not at one uniform stride
+        gl = gate_logits.contiguous().view(rows, heads)
+    if gl.stride(1) != 1 or (rows > 1 and gl.stride(0) < heads):
+        gl = gl.contiguous()
+    lstride = gl.stride(0) if rows > 1 else heads
     if mx_terms:
         act = MXActivation(tuple(out.shape[:-1]), width, mx_terms, out.device)
         st = act.struct()
-        _lib.check(_lib.load().ltxq_head_gate_mx(out.data_ptr(), gate_logits.data_ptr(), rows, heads, width // heads,
-                                                 None, ctypes.byref(st), _stream()), "head_gate_mx")
+        _lib.check(_lib.load().ltxq_head_gate_ex(out.data_ptr(), gl.data_ptr(), lstride, rows, heads, width // heads,
+                                                 None, ctypes.byref(st), _stream()), "head_gate_ex")
         return act
     res = torch.empty_like(out)
-    _lib.check(_lib.load().ltxq_head_gate(out.data_ptr(), gate_logits.data_ptr(), rows, heads, width // heads,
-                                          res.data_ptr(), _stream()), "head_gate")
+    _lib.check(_lib.load().ltxq_head_gate_ex(out.data_ptr(), gl.data_ptr(), lstride, rows, heads, width // heads,
+                                             res.data_ptr(), None, _stream()), "head_gate_ex")
     return res
 
 

@@ -91,6 +91,9 @@ def test_mx_entry_validation_without_gpu(lib):
                                       None) == _lib.ERR_UNSUPPORTED  # C > 4096
     assert lib.ltxq_head_gate_mx(16, 16, 4, 3, 64, None, ctypes.byref(act), None) == _lib.ERR_UNSUPPORTED
     assert lib.ltxq_head_gate_mx(16, 16, 4, 2, 64, None, None, None) == _lib.ERR_INVALID
+    assert lib.ltxq_head_gate_ex(16, 16, 1, 4, 2, 64, 16, None, None) == _lib.ERR_INVALID  # stride < heads
+    assert lib.ltxq_head_gate_ex(16, 16, 0, 4, 2, 64, 16, None, None) == _lib.ERR_INVALID  # stride not positive
+    assert lib.ltxq_head_gate_ex(16, 16, 2, 0, 2, 64, 16, None, None) == _lib.OK            # no rows: no-op
 
 
 def test_attention_validation_without_gpu(lib):

@@ -250,6 +250,36 @@ def test_head_gate_matches_oracle(cuda):
     assert ulp_diff_bf16(out, ro.head_gate(o, lg, 32)).max() <= 1
 
 
+def test_head_gate_reads_strided_logits(cuda):
+    """Gate logits as a column slice of a fused Q|K|V|gate output (rows at
+    stride 3 * width + heads, batch 2) are read in place: the result equals
+    the contiguous call bit for bit, bf16 and MX outputs alike."""
+    import torch
+
+    from ltxq import kernels as K
+
+    g = rng(81)
+    B, T, heads, d = 2, 150, 32, 128
+    W = heads * d
+    o = to_dev_bf16(normal_bf16(g, (B * T, W))).view(B, T, W)
+    fused = to_dev_bf16(normal_bf16(g, (B * T, 3 * W + heads), 2.0)).view(B, T, 3 * W + heads)
+    gl = fused[:, :, 3 * W:]
+    assert not gl.is_contiguous()
+    ref = K.head_gate(o, gl.contiguous(), heads)
+    got = K.head_gate(o, gl, heads)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    assert ulp_diff_bf16(from_dev_bf16(got).reshape(B * T, W),
+                         ro.head_gate(from_dev_bf16(o).reshape(B * T, W),
+                                      from_dev_bf16(gl.contiguous()).reshape(B * T, heads), heads)).max() <= 1
+    from test_gpu_mx_fused import _assert_same_terms
+
+    mx_ref = K.head_gate(o, gl.contiguous(), heads, mx_terms=2)
+    mx_got = K.head_gate(o, gl, heads, mx_terms=2)
+    torch.cuda.synchronize()
+    _assert_same_terms(mx_got, mx_ref, "strided-logit gate, MX out")
+
+
 # ----------------------------------------------------------------- quantized GEMM
 
 
