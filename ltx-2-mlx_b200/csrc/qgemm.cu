@@ -501,10 +501,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // multicasts stage releases and accumulator readiness to both CTAs.
 //
 // Four epilogue warps per CTA drain the 128 x 256 fp32 accumulator into a
-// bf16 shared-memory tile (the reference's first rounding point), hand TMEM
+// bf16 copy in spare TMEM columns (the reference's first rounding point;
+// TMEM -> registers -> TMEM, each thread its own lane), hand the accumulator
 // back to the MMA through the leader's acc_empty barrier, and only then apply
-// bias / GELU / gated residual and store -- overlapped with the next tile's
-// main loop.  The smem and TMEM rings continue across tiles.
+// bias / GELU / gated residual from the copy, through a 2 KB per-warp
+// transpose tile, with 16-byte row stores -- overlapped with the next tile's
+// main loop.  With no shared-memory staging tile, the operand ring gets the
+// shared memory (8 stages of 24 KB, 10 of 20 KB).  The smem and TMEM rings
+// continue across tiles.
+//
+// TMEM columns: [0, 256) fp32 accumulator (lane = feature, column = token);
+// [256, 384) the A ring (4 stages x 32 columns of bf16 pairs); [384, 512) the
+// bf16 accumulator copy (column c = tokens 2c, 2c + 1).
 constexpr int kEpiWarp0 = 10, kPairThreads = 448;  // warps 10..13: epilogue
 
 template <int QK>
@@ -512,18 +520,21 @@ struct PairPlan {
   static constexpr int BN = 256;
   static constexpr int kXStage = (BN / 2) * BK * 2;  // this CTA's half of the activation tile
   static constexpr int kWStage = BM * QTraits<QK>::kWBytes;
-  static constexpr int kEpiBytes = BN * BM * 2;      // bf16 [256 tokens][128 features]
-  static constexpr int kBudget = 224 * 1024 - kEpiBytes - 2048;
-  static constexpr int kStagesRaw = kBudget / (kXStage + kWStage);
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kEpiOff = kStages * (kXStage + kWStage);
-  static constexpr int kBarOff = kEpiOff + kEpiBytes;
+  static constexpr int kStgBytes = 4 * 32 * 32 * 2;  // per-warp 32 x 32 bf16 transpose tiles
+  static constexpr int kFixed = 1024 + kStgBytes + 512 + kGeluTabBytes;
+  static constexpr int kStagesRaw = (227 * 1024 - kFixed) / (kXStage + kWStage);
+  static constexpr int kStages = kStagesRaw > 10 ? 10 : kStagesRaw;
+  static constexpr int kStgOff = kStages * (kXStage + kWStage);
+  static constexpr int kBarOff = kStgOff + kStgBytes;
   static constexpr int kTabOff = kBarOff + 512;  // GELU table (epilogue)
   static constexpr int kSmem = 1024 + kTabOff + kGeluTabBytes;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr int kAStages = 8;
+  static constexpr int kAStages = 4;
   static constexpr uint32_t kACol = BN;
+  static constexpr uint32_t kCopyCol = BN + kAStages * 32;
+  static_assert(kCopyCol + BN / 2 <= kTmemCols, "TMEM columns");
   static_assert(kStages >= 4, "pipeline depth");
+  static_assert(4 * kStages * 8 + 2 * kAStages * 8 + 24 <= 512, "barrier block");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
@@ -593,33 +604,6 @@ struct Epi8 {
     *reinterpret_cast<uint4*>(p.out + off) = make_uint4(u[0], u[1], u[2], u[3]);
   }
 };
-
-// Epilogue math for one CTA's tile from the bf16 staging tile (token-major,
-// 128 features per token row): 128 threads, thread t owns the 8-feature
-// column chunk (t & 15) and token rows (t >> 4) + 8 i.
-__device__ __forceinline__ void epilogue_tile_from_smem(const Params& p, const uint16_t* stg, const uint16_t* gtab,
-                                                        int tid, int n0, int m0) {
-  const int f = (tid & 15) * 8;
-  const int nf = n0 + f;
-  if (nf >= p.N) return;
-  Epi8 e;
-  e.init(p, nf);
-#pragma unroll 2
-  for (int i = 0; i < 32; ++i) {
-    const int j = (tid >> 4) + 8 * i;
-    const int m = m0 + j;
-    if (m >= p.M) break;
-    const uint4 av = *reinterpret_cast<const uint4*>(stg + j * BM + f);
-    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-    float a[8];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      a[2 * k] = lo_bf16(aw[k]);
-      a[2 * k + 1] = hi_bf16(aw[k]);
-    }
-    e.store(p, a, m, nf, gtab);
-  }
-}
 
 // Split tiles: out[m, nf..nf+8) from the fp32 partial sums of a split
 // tile's K ranges, added in split order (deterministic), rounded to bf16,
@@ -711,7 +695,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = smem;
   uint8_t* ws = smem + S * P::kXStage;
-  uint16_t* stg = reinterpret_cast<uint16_t*>(smem + P::kEpiOff);
   uint16_t* gtab = reinterpret_cast<uint16_t*>(smem + P::kTabOff);
   const Bars bb = carve_bars<S, AS>(smem + P::kBarOff);
 
@@ -871,6 +854,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int r = q * 32 + lane;
     const int tid = (warp - kEpiWarp0) * 32 + lane;  // 0..127
     const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    uint16_t* stw = reinterpret_cast<uint16_t*>(smem + P::kStgOff) + q * (32 * 32);
+    const bool gated = p.epi == LTXQ_EPI_GATED_RESIDUAL || p.epi == LTXQ_EPI_GATE_THEN_ADD;
+    const bool two_round = p.epi == LTXQ_EPI_GATE_THEN_ADD || p.gate.dtype == LTXQ_BF16;
+    const bool gate_bcast = p.gate.rows_per_vec == 0;
     if (p.epi == LTXQ_EPI_GELU) {
       gelu_tab_fill(gtab, tid, 128);  // while the first tile's main loop runs
       named_bar_sync(1, 128);
@@ -906,29 +893,67 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (tid == 0) mbar_arrive_cluster(leader_acc_empty);
         continue;
       }
-      // drain: accumulator column j of TMEM lane r -> staging[j][r] as bf16(acc);
-      // two 32-column loads in flight per wait (the MMA waits on this drain)
+      // drain: fp32 accumulator columns of TMEM lane r -> bf16(acc) pairs in
+      // the copy columns of the same lane (the MMA waits on this drain only);
+      // chunks past the last token row are neither read nor written
+      const int chunks = min(BN / 32, (p.M - m0 + 31) / 32);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c += 2) {
+      for (int c = 0; c < chunks; c += 2) {
         uint32_t v[2][32];
         tmem_ld_32x32b_x32(tmem + t_lane + c * 32, v[0]);
         tmem_ld_32x32b_x32(tmem + t_lane + (c + 1) * 32, v[1]);
         tmem_wait_ld();
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t h[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const uint32_t h = pack_bf16x2(__uint_as_float(v[h2][j]), __uint_as_float(v[h2][j + 1]));
-            stg[((c + h2) * 32 + j) * BM + r] = static_cast<uint16_t>(h & 0xFFFFu);
-            stg[((c + h2) * 32 + j + 1) * BM + r] = static_cast<uint16_t>(h >> 16);
-          }
+          for (int j = 0; j < 16; ++j) h[j] = pack_bf16x2(__uint_as_float(v[h2][2 * j]), __uint_as_float(v[h2][2 * j + 1]));
+          tmem_st_32x32b_x16(tmem + t_lane + P::kCopyCol + (c + h2) * 16, h);
         }
       }
+      tmem_wait_st();
       tc_fence_before();
       named_bar_sync(1, 128);
       if (tid == 0) mbar_arrive_cluster(leader_acc_empty);  // TMEM accumulator may be overwritten
-      epilogue_tile_from_smem(p, stg, gtab, tid, n0, m0);
-      named_bar_sync(1, 128);  // staging tile consumed
+      // epilogue from the copy: thread = feature r, registers = tokens; bias
+      // and GELU in registers, a 32 x 32 transpose per warp, then 8 features
+      // of one token row per lane quad and 16-byte stores
+      const int n = n0 + r;
+      const float bias_n = (p.bias != nullptr && n < p.N) ? bf16_to_f32(__ldg(p.bias + n)) : 0.f;
+      const int nf = n0 + q * 32 + (lane & 3) * 8;
+      float g8b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (gated && gate_bcast && nf < p.N) load_vec8(p.gate, vec_row(p.gate, 0), nf, g8b);
+#pragma unroll 1
+      for (int c = 0; c < chunks; c += 2) {
+        uint32_t w2[2][16];
+        tmem_ld_32x32b_x16(tmem + t_lane + P::kCopyCol + c * 16, w2[0]);
+        tmem_ld_32x32b_x16(tmem + t_lane + P::kCopyCol + (c + 1) * 16, w2[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int m_c = m0 + (c + h2) * 32;
+          if (m_c >= p.M) break;  // uniform
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            uint32_t w = w2[h2][j];
+            if (p.bias != nullptr) w = pack_bf16x2(__fadd_rn(lo_bf16(w), bias_n), __fadd_rn(hi_bf16(w), bias_n));
+            if (p.epi == LTXQ_EPI_GELU) w = gelu_tab_x2(w, gtab);
+            stw[(2 * j) * 32 + lane] = static_cast<uint16_t>(w & 0xFFFFu);
+            stw[(2 * j + 1) * 32 + lane] = static_cast<uint16_t>(w >> 16);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int pass = 0; pass < 4; ++pass) {
+            const int jr = (lane >> 2) + 8 * pass;
+            const uint4 a = *reinterpret_cast<const uint4*>(stw + jr * 32 + (lane & 3) * 8);
+            if (m_c + jr < p.M && nf < p.N) {
+              uint32_t uw[4] = {a.x, a.y, a.z, a.w};
+              epi_row_store(p, uw, m_c + jr, nf, g8b, gated, two_round, gate_bcast);
+            }
+          }
+          __syncwarp();  // transpose tile consumed
+        }
+      }
     }
   }
 
