@@ -581,6 +581,23 @@ def run_step(args, world, rank, local, dev):
         e.record(torch.cuda.current_stream())
         ff_events.append(e)
 
+    xchg_events: list = []  # (kind, phase, event) around each exchange the compute stream waits for
+
+    def xprobe(kind, phase):
+        e = torch.cuda.Event(enable_timing=True, external=use_graph)
+        e.record(torch.cuda.current_stream())
+        xchg_events.append((kind, phase, e))
+
+    def xchg_ms() -> dict:
+        """Device ms per kind between each phase-0 and phase-1 event: how long
+        the compute stream waited for a side-stream exchange ("wait") or ran
+        one in line ("sync")."""
+        out = {"wait": 0.0, "sync": 0.0}
+        for (k0, p0, e0), (k1, p1, e1) in zip(xchg_events[0::2], xchg_events[1::2]):
+            assert k0 == k1 and (p0, p1) == (0, 1)
+            out[k0] += e0.elapsed_time(e1)
+        return out
+
     def step(v, a):
         for b in blocks:
             v, a = b(v, a, shard)
@@ -595,14 +612,17 @@ def run_step(args, world, rank, local, dev):
         # the last warm-up step runs inside StepGraph (before the capture)
         for b in blocks:
             b.probe = probe
+        shard.wait_probe = xprobe if world > 1 else None
         graph = StepGraph(step, video, audio, warmup=1)
         ff_events = ff_events[len(ff_events) - 2 * n_blocks:]  # the captured events
+        xchg_events = xchg_events[len(xchg_events) // 2:]  # warm-up pass, then the captured one
+        shard.wait_probe = None
         for b in blocks:
             b.probe = None
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    evs, ff_ms = [], []
+    evs, ff_ms, xw = [], [], []
     n_launch0 = _lib.launch_count()
     if args.profile_range:
         torch.cuda.cudart().cudaProfilerStart()
@@ -612,8 +632,10 @@ def run_step(args, world, rank, local, dev):
             e0.record(stream)
             graph.replay()
             e1.record(stream)
-            e1.synchronize()  # read this replay's FF probes
+            e1.synchronize()  # read this replay's FF and exchange probes
             ff_ms += [ff_events[i].elapsed_time(ff_events[i + 1]) for i in range(0, len(ff_events), 2)]
+            if xchg_events:
+                xw.append(xchg_ms())
         else:
             for b in blocks:
                 b.probe = probe
@@ -635,6 +657,17 @@ def run_step(args, world, rank, local, dev):
     if not use_graph:
         ff_ms = [ff_events[i].elapsed_time(ff_events[i + 1]) for i in range(0, len(ff_events), 2)]
     ff_avg = sum(ff_ms) / len(ff_ms)
+    exchange = None
+    if world > 1 and use_graph:
+        # every rank holds the same probe list (same steps, same block code)
+        wait_ms = _max_over_ranks(sum(x["wait"] for x in xw) / max(len(xw), 1), world, dev)
+        sync_ms = _max_over_ranks(sum(x["sync"] for x in xw) / max(len(xw), 1), world, dev)
+        exchange = {"self_attention": args.self_attention, "v2a": args.v2a,
+                    "exposed_wait_ms_per_step": wait_ms, "inline_collective_ms_per_step": sync_ms,
+                    "per_block_ms": (wait_ms + sync_ms) / n_blocks,
+                    "how": "CUDA events on the compute stream around each join of a side-stream collective "
+                           "(time the compute stream waited) and around each collective run in line, in the "
+                           "replayed step graph; max over ranks"}
 
     # ---- e2e through the public block API with host buffers
     vx_host = video.x.cpu().pin_memory()
@@ -702,6 +735,7 @@ def run_step(args, world, rank, local, dev):
                               if args.compute != "dequant" else ")")},
             "gpu_launches": n_launches,
             "weights_gb": weight_bytes / 1e9,
+            **({"exchange": exchange} if exchange is not None else {}),
             "clocks": clk.summary(),
             "cpu_baseline": None if (args.no_cpu_baseline or world > 1) else cpu_baseline(args.workload),
             "device_error": dev_err,

@@ -173,7 +173,17 @@ class RowShard:
     # video->audio keys: "gather" (all-gather the video K/V) or "split_keys"
     # (attend the local rows, merge the partial outputs by log-sum-exp)
     v2a: str = "gather"
+    # optional callable(kind, phase): called with phase 0 just before and 1
+    # just after each point where the caller's stream waits for an exchange
+    # ("wait": the join of a side-stream collective) or runs one in line
+    # ("sync"); a timer records device events there (bench.py: exposed
+    # exchange time per step)
+    wait_probe: object = field(default=None, repr=False, compare=False)
     _comm: object = field(default=None, repr=False, compare=False)
+
+    def _probe(self, kind: str, phase: int) -> None:
+        if self.wait_probe is not None:
+            self.wait_probe(kind, phase)
 
     def gather_rows(self, x: torch.Tensor) -> torch.Tensor:
         """(B, T_local, C) on every rank -> (B, world * T_local, C)."""
@@ -196,8 +206,10 @@ class RowShard:
                      for x in xs)  # rank-major blocks
         use_side = self.overlap if overlap is None else overlap
         if not use_side:
+            self._probe("sync", 0)
             for o, x in zip(outs, xs):
                 dist.all_gather_into_tensor(o, x, group=self.group)
+            self._probe("sync", 1)
             return PendingGather(outs, xs, None)
         if self._comm is None:
             self._comm = torch.cuda.Stream(device=xs[0].device)
@@ -213,7 +225,9 @@ class RowShard:
         import torch.distributed as dist
 
         out = torch.empty_like(x)
+        self._probe("sync", 0)
         dist.all_to_all_single(out, x, group=self.group)
+        self._probe("sync", 1)
         return out
 
     def start_all_to_all(self, x: torch.Tensor) -> "PendingGather":
@@ -223,7 +237,9 @@ class RowShard:
         x = x.contiguous()
         out = torch.empty_like(x)
         if not self.overlap:
+            self._probe("sync", 0)
             dist.all_to_all_single(out, x, group=self.group)
+            self._probe("sync", 1)
             return PendingGather((out,), None, None)
         if self._comm is None:
             self._comm = torch.cuda.Stream(device=x.device)
@@ -234,7 +250,9 @@ class RowShard:
 
     def finish_all_to_all(self, pending: "PendingGather") -> torch.Tensor:
         if pending.stream is not None:
+            self._probe("wait", 0)
             torch.cuda.current_stream(pending.outs[0].device).wait_stream(pending.stream)
+            self._probe("wait", 1)
         return pending.outs[0]
 
     def finish_gather(self, pending: "PendingGather") -> tuple:
@@ -242,7 +260,9 @@ class RowShard:
         if self.world == 1:
             return pending.outs
         if pending.stream is not None:
+            self._probe("wait", 0)
             torch.cuda.current_stream(pending.outs[0].device).wait_stream(pending.stream)
+            self._probe("wait", 1)
         res = []
         for o, x in zip(pending.outs, pending.inputs):
             b, t = x.shape[0], x.shape[1]
@@ -392,7 +412,9 @@ class QAttention:
         lq = qh.shape[2]
         part = torch.cat([o.float().flatten(), lse[..., :lq].float().flatten()])
         parts = torch.empty(shard.world * part.numel(), dtype=part.dtype, device=part.device)
+        shard._probe("sync", 0)
         dist.all_gather_into_tensor(parts, part, group=shard.group)  # flat: valid for NCCL and gloo
+        shard._probe("sync", 1)
         parts = parts.view(shard.world, -1)
         n_o = o.numel()
         outs = parts[:, :n_o].view((shard.world,) + tuple(o.shape))

@@ -161,6 +161,8 @@ def _hp_worker(rank, world, port, out_dir):
     tl = T // world
     rows = slice(rank * tl, (rank + 1) * tl)
     shard = RowShard(dist.group.WORLD, world, rank, overlap=False)
+    calls = []
+    shard.wait_probe = lambda kind, phase: calls.append((kind, phase))
     # head-parallel self-attention: Q/K/V rows -> heads, attention, back to rows
     send = torch.stack([heads_to_ranks(t[:, rows].contiguous(), world, heads) for t in (q, k, v)], dim=1)
     recv = shard.all_to_all(send)
@@ -181,7 +183,8 @@ def _hp_worker(rank, world, port, out_dir):
     dist.all_gather_into_tensor(lses, lse.contiguous().flatten())
     merged = merge_attention_partials(outs.view((world,) + tuple(part_o.shape)),
                                       lses.view((world,) + tuple(lse.shape)))
-    torch.save({"hp": hp, "merged": merged}, os.path.join(out_dir, f"hp{rank}.pt"))
+    kg = shard.gather_rows(k[:, rows].contiguous())  # in-line all-gather (overlap off)
+    torch.save({"hp": hp, "merged": merged, "calls": calls, "kg": kg}, os.path.join(out_dir, f"hp{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -191,7 +194,9 @@ def test_head_parallel_and_split_key_attention(tmp_path, world):
     """The two sharded attention forms of the block: head-parallel
     self-attention (all-to-all of Q/K/V rows to heads and back) equals the
     unsharded attention on each rank's rows; replicated queries over row-split
-    keys, merged by log-sum-exp, equal attention over all keys."""
+    keys, merged by log-sum-exp, equal attention over all keys.  The
+    exchange probe (``RowShard.wait_probe``) is called around every in-line
+    collective."""
     port = _free_port()
     mp.start_processes(_hp_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True, start_method="spawn")
     q, k, v, _, heads = _case()
@@ -207,6 +212,9 @@ def test_head_parallel_and_split_key_attention(tmp_path, world):
         o = torch.load(os.path.join(tmp_path, f"hp{r}.pt"))
         assert torch.allclose(o["hp"], full[:, r * tl:(r + 1) * tl], atol=1e-5, rtol=1e-5)
         assert torch.allclose(o["merged"], ref_merged, atol=1e-5, rtol=1e-5)
+        assert torch.equal(o["kg"], k)
+        # the exchange probe brackets each in-line collective: two all-to-alls, one all-gather
+        assert o["calls"] == [("sync", 0), ("sync", 1)] * 3
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
