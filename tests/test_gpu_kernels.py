@@ -395,6 +395,39 @@ def test_gelu_epilogue_exhaustive(cuda):
     assert ulps.max() <= 1 and (ulps > 0).sum() <= 64, ((ulps > 0).sum(), ulps.max())
 
 
+def test_gelu_epilogue_token_pairs_exhaustive(cuda):
+    """The GELU epilogue with a different input on every token: token t's
+    accumulator is the bf16 pattern t (x[t, 0] = pattern, the weight's first
+    column 1, the rest 0), so every bf16x2 word of consecutive tokens holds
+    two neighbouring patterns, and words with one half inside and one
+    outside the tabulated range occur at each range edge.  The pair kernel
+    (table, paired fast path) and the single-CTA kernel's direct evaluation
+    give identical bits."""
+    torch = _torch()
+    ltxq = _ltxq()
+    pats = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    K, N = 64, 256
+    x = torch.zeros(0x10000, K, dtype=torch.bfloat16, device="cuda")
+    x[:, 0] = torch.from_numpy(pats.view(np.int16)).cuda().view(torch.bfloat16)
+    w = torch.zeros(N, K // 4, dtype=torch.int32, device="cuda")
+    w[:, 0] = 1  # code 1 at k = 0, code 0 elsewhere
+    s = torch.ones(N, K // 64, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(N, K // 64, dtype=torch.bfloat16, device="cuda")
+    ql = ltxq.QuantizedLinear(w, s, b, None, group_size=64, bits=8, mode="affine", in_features=K, out_features=N)
+    pair = from_dev_bf16(ql(x, gelu=True))[:, :8]  # every feature alike; 8 of them
+    bits = lambda a: f32_to_bf16_bits(a)  # noqa: E731
+    assert (bits(pair) == bits(pair[:, :1])).all()
+    pair = pair[:, 0]
+    # reference: the single-CTA kernel's direct gelu_ref of every pattern (as bias, weights 0)
+    direct = from_dev_bf16(_zero_affine_linear(0x10000, 512, pats)(
+        torch.ones(64, 512, dtype=torch.bfloat16, device="cuda"), gelu=True, split_k=False))[0]
+    # the accumulator of pattern 0x8000 (-0) is +0 (-0 + 0 products); every other
+    # pattern is its own accumulator
+    keep = pats != 0x8000
+    same = (bits(pair) == bits(direct)) | (np.isnan(pair) & np.isnan(direct))
+    assert same[keep].all(), [hex(p) for p in pats[keep & ~same][:8]]
+
+
 def test_split_k_deterministic(cuda):
     """Split-K partials are summed in split order: repeated calls agree bit
     for bit."""
