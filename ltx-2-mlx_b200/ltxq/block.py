@@ -475,6 +475,7 @@ class BasicAVTransformerBlock:
         self.linears = {k: v for k, v in linears.items()
                         if not k.endswith((".to_q", ".to_k", ".to_v", ".to_gate_logits"))}
         self.probe = None  # optional callable(tag) recording events around the FF project_in GEMM
+        self._expanded: dict = {}  # AdaLN table rows broadcast to a timestep tensor's shape (_table_like)
 
     # -------------------------------------------------------------- building
     @classmethod
@@ -543,15 +544,57 @@ class BasicAVTransformerBlock:
 
     # -------------------------------------------------------------- forward
     def _ada(self, table: str, ts: torch.Tensor, start: int, end: int):
-        """get_ada_values (transformer.py:286-309) -> list of (B, 1, C) fp32.
-        All rows of a table are added to the timestep rows in one launch per
-        block call (the same elementwise fp32 adds), then sliced."""
+        """get_ada_values (transformer.py:286-309) -> list of (B, 1, C) fp32:
+        slices of the table + timestep rows that ``_ada_prepare`` added."""
         key = (table, id(ts))
         vals = self._ada_rows.get(key)
         if vals is None:
             vals = self.tables[table][None, None] + ts[:, :, :self.tables[table].shape[0]]
             self._ada_rows[key] = vals
         return [vals[:, :, i] for i in range(start, end)]  # views: the kernels take strided vectors
+
+    def _table_like(self, table: str, rows: slice, like: torch.Tensor) -> torch.Tensor:
+        """``tables[table][rows]`` broadcast to ``like``'s shape as a dense
+        tensor (kept until the table changes)."""
+        t = self.tables[table]
+        key = (table, rows.start, rows.stop, tuple(like.shape), t.data_ptr(), t._version)
+        e = self._expanded.get(key)
+        if e is None:
+            e = t[rows][None, None].expand(like.shape).contiguous()
+            self._expanded[key] = e
+        return e
+
+    def _ada_prepare(self, video: TransformerArgs, audio: TransformerArgs) -> None:
+        """Every AdaLN table + timestep sum of this block call
+        (get_ada_values / get_av_ca_ada_values, transformer.py:286-342, and
+        the text-CA prompt rows, :379) in one multi-tensor fp32 add: the same
+        elementwise adds as one ``table + timestep`` per table, one launch
+        instead of eight.  Results go to ``_ada_rows`` under (table, id of
+        the timestep tensor); a sum that does not fit (missing tensor, other
+        dtype, per-token rows) is left to the caller's own add."""
+        want = []
+        for args, base, prompt, cross in ((video, "scale_shift_table", "prompt_scale_shift_table",
+                                           "scale_shift_table_a2v_ca_video"),
+                                          (audio, "audio_scale_shift_table", "audio_prompt_scale_shift_table",
+                                           "scale_shift_table_a2v_ca_audio")):
+            n = self.tables[base].shape[0]
+            want += [(base, slice(0, n), args.timesteps, args.timesteps[:, :, :n] if args.timesteps is not None
+                      else None),
+                     (prompt, slice(0, 2), args.prompt_timestep, args.prompt_timestep),
+                     (cross, slice(0, 4), args.cross_scale_shift_timestep, args.cross_scale_shift_timestep),
+                     ((cross, "gate"), slice(4, 5), args.cross_gate_timestep, args.cross_gate_timestep)]
+        lhs, rhs, keys = [], [], []
+        for table, rows, src, ts in want:
+            name = table[0] if isinstance(table, tuple) else table
+            # per-batch rows (B, 1, R, C) only: per-token timesteps keep the broadcast add
+            if (ts is None or name not in self.tables or ts.dtype != torch.float32 or not ts.is_contiguous()
+                    or ts.dim() != 4 or ts.shape[1] != 1 or ts.shape[-2] != rows.stop - rows.start):
+                continue
+            lhs.append(self._table_like(name, rows, ts))
+            rhs.append(ts)
+            keys.append((table, id(src)))
+        for key, val in zip(keys, torch._foreach_add(lhs, rhs) if lhs else ()):
+            self._ada_rows[key] = val
 
     def __call__(self, video: TransformerArgs, audio: TransformerArgs, shard: RowShard | None = None,
                  skip: frozenset = frozenset()):
@@ -562,6 +605,7 @@ class BasicAVTransformerBlock:
         transformer.py:429-444, 455-457, 496-497, 574-575, 603-604)."""
         eps = self.norm_eps
         self._ada_rows = {}  # (table, timestep tensor) -> all rows, for this call only
+        self._ada_prepare(video, audio)
         vx, ax = video.x.contiguous(), audio.x.contiguous()
         run_v = "skip_video_self_attn" not in skip
         run_a = "skip_audio_self_attn" not in skip
@@ -614,9 +658,9 @@ class BasicAVTransformerBlock:
         # video->audio K/V (video rows) gather overlaps the audio->video
         # attention.
         a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_audio", audio)
-        g_v2a = (self.tables["scale_shift_table_a2v_ca_audio"][4][None, None] + audio.cross_gate_timestep[:, :, 0])
+        g_v2a = self._cross_gate("scale_shift_table_a2v_ca_audio", audio)
         v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a = self._ada_cross("scale_shift_table_a2v_ca_video", video)
-        g_a2v = (self.tables["scale_shift_table_a2v_ca_video"][4][None, None] + video.cross_gate_timestep[:, :, 0])
+        g_a2v = self._cross_gate("scale_shift_table_a2v_ca_video", video)
         at = self.attn["audio_to_video_attn"]
         if run_a2v:
             q, k, v, gl = at.project(self._mod(vx, v_sc_a2v, v_sh_a2v, at.q_proj),
@@ -658,8 +702,17 @@ class BasicAVTransformerBlock:
 
     def _ada_cross(self, table: str, args: TransformerArgs):
         """get_av_ca_ada_values (transformer.py:311-342) scale/shift rows."""
-        t = self.tables[table][:4][None, None] + args.cross_scale_shift_timestep
+        t = self._ada_rows.get((table, id(args.cross_scale_shift_timestep)))
+        if t is None:
+            t = self.tables[table][:4][None, None] + args.cross_scale_shift_timestep
         return [t[:, :, i] for i in range(4)]
+
+    def _cross_gate(self, table: str, args: TransformerArgs):
+        """The audio<->video gate row (transformer.py:311-342, row 4)."""
+        t = self._ada_rows.get(((table, "gate"), id(args.cross_gate_timestep)))
+        if t is None:
+            return self.tables[table][4][None, None] + args.cross_gate_timestep[:, :, 0]
+        return t[:, :, 0]
 
     def _text_ca(self, x, args: TransformerArgs, name: str, table: str, prompt_table: str):
         """Text cross-attention (transformer.py:344-387).  The text context is
@@ -668,7 +721,9 @@ class BasicAVTransformerBlock:
         slower (the gathers' latency exceeded the ~0.1 ms of GEMM saved)."""
         eps = self.norm_eps
         sh_q, sc_q, g = self._ada(table, args.timesteps, 6, 9)
-        kv = self.tables[prompt_table][None, None] + args.prompt_timestep
+        kv = self._ada_rows.get((prompt_table, id(args.prompt_timestep)))
+        if kv is None:
+            kv = self.tables[prompt_table][None, None] + args.prompt_timestep
         shift_kv, scale_kv = kv[:, :, 0], kv[:, :, 1]
         at = self.attn[name]
         q, k, v, gl = at.project(self._mod(x, sc_q, sh_q, at.q_proj),

@@ -153,3 +153,44 @@ def test_x0_model_matches_the_oracle_x0():
         ref = (lat - (t * vel).astype(np.float32)).astype(np.float32)
         assert dv.dtype == torch.float32 and np.array_equal(dv.numpy(), ref) and np.array_equal(da.numpy(), ref)
     assert calls == ["ptb", "ptb"]
+
+
+def test_adaln_table_sums_in_one_multi_tensor_add():
+    """BasicAVTransformerBlock._ada_prepare: every table + timestep sum of a
+    block call from one torch._foreach_add equals the per-table broadcast
+    add bit for bit (batch 2), and per-token timestep rows are left to the
+    broadcast add."""
+    import torch
+
+    from ltxq.block import AUDIO_22B, VIDEO_22B, BasicAVTransformerBlock, TransformerArgs, table_specs
+
+    g = torch.Generator().manual_seed(3)
+    blk = object.__new__(BasicAVTransformerBlock)  # tables only: no quantized linears (they need a GPU)
+    blk.tables = {k: torch.randn(*s, generator=g) * 0.1 for k, s in table_specs(VIDEO_22B, AUDIO_22B).items()}
+    blk._expanded = {}
+
+    def args(C, per_token=False):
+        r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+        return TransformerArgs(x=None, context=None, timesteps=r(2, 5 if per_token else 1, 9, C),
+                               positional_embeddings=None, cross_positional_embeddings=None,
+                               cross_scale_shift_timestep=r(2, 1, 4, C), cross_gate_timestep=r(2, 1, 1, C),
+                               prompt_timestep=r(2, 1, 2, C))
+
+    for per_token in (False, True):
+        video, audio = args(VIDEO_22B.dim, per_token), args(AUDIO_22B.dim)
+        blk._ada_rows = {}
+        blk._ada_prepare(video, audio)
+        assert (("scale_shift_table", id(video.timesteps)) in blk._ada_rows) == (not per_token)
+        for tab, a in (("scale_shift_table", video), ("audio_scale_shift_table", audio)):
+            got = blk._ada(tab, a.timesteps, 0, 9)
+            ref = blk.tables[tab][None, None] + a.timesteps
+            assert all(torch.equal(got[i], ref[:, :, i]) for i in range(9))
+        for tab, a in (("scale_shift_table_a2v_ca_video", video), ("scale_shift_table_a2v_ca_audio", audio)):
+            got = blk._ada_cross(tab, a)
+            ref = blk.tables[tab][:4][None, None] + a.cross_scale_shift_timestep
+            assert all(torch.equal(got[i], ref[:, :, i]) for i in range(4))
+            assert torch.equal(blk._cross_gate(tab, a),
+                               blk.tables[tab][4][None, None] + a.cross_gate_timestep[:, :, 0])
+        for tab, a in (("prompt_scale_shift_table", video), ("audio_prompt_scale_shift_table", audio)):
+            assert torch.equal(blk._ada_rows[(tab, id(a.prompt_timestep))],
+                               blk.tables[tab][None, None] + a.prompt_timestep)
