@@ -44,9 +44,11 @@ __device__ __forceinline__ void deq_affine8_word(uint32_t w, uint32_t s2, uint32
   const float q1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7651)) - kMagic;
   const float q2 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7652)) - kMagic;
   const float q3 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7653)) - kMagic;
-  // q < 256 has <= 8 significant bits: the bf16 packing is exact.
-  o01 = fma_bf16x2(s2, pack_bf16x2(q0, q1), b2);
-  o23 = fma_bf16x2(s2, pack_bf16x2(q2, q3), b2);
+  // q < 256 has <= 8 significant bits, so the low 16 bits of its fp32
+  // pattern are zero and the upper half is its exact bf16: the pairs are
+  // packed by a byte permute (integer pipe), not a conversion.
+  o01 = fma_bf16x2(s2, __byte_perm(__float_as_uint(q0), __float_as_uint(q1), 0x7632), b2);
+  o23 = fma_bf16x2(s2, __byte_perm(__float_as_uint(q2), __float_as_uint(q3), 0x7632), b2);
 }
 
 // int4: one packed word (elements k..k+7, nibble i = element k+i) -> four
