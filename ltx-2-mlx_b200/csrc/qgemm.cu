@@ -52,7 +52,7 @@ constexpr int BK = 64;   // K per pipeline stage
 constexpr int kDeqWarps = 8;  // two per TMEM lane quarter; each converts one 32-wide half of a stage
 constexpr int kTmaWarp = 8, kMmaWarp = 9, kThreads = 320;
 constexpr int kStagePitch = 136;  // epilogue staging row pitch in bf16 (128 + 8 pad)
-constexpr int kPrefetch = 4;      // scale/bias register prefetch distance (stages)
+constexpr int kPrefetch = 2;      // scale/bias register prefetch distance (stages); also the dequant loop's unroll
 
 // kMxfp8F: mxfp8 data flagged LTXQ_QW_MXFP8_FINITE (short conversion)
 enum QKind { kAffine8 = 0, kAffine4 = 1, kMxfp8 = 2, kMxfp8F = 3 };
