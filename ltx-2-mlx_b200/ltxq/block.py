@@ -555,13 +555,15 @@ class BasicAVTransformerBlock:
 
     def _table_like(self, table: str, rows: slice, like: torch.Tensor) -> torch.Tensor:
         """``tables[table][rows]`` broadcast to ``like``'s shape as a dense
-        tensor (kept until the table changes)."""
+        tensor, kept while ``tables[table]`` is the same tensor object (the
+        entry holds it) and unmodified (its in-place version counter)."""
         t = self.tables[table]
-        key = (table, rows.start, rows.stop, tuple(like.shape), t.data_ptr(), t._version)
-        e = self._expanded.get(key)
-        if e is None:
-            e = t[rows][None, None].expand(like.shape).contiguous()
-            self._expanded[key] = e
+        key = (table, rows.start, rows.stop, tuple(like.shape))
+        hit = self._expanded.get(key)
+        if hit is not None and hit[0] is t and hit[1] == t._version:
+            return hit[2]
+        e = t[rows][None, None].expand(like.shape).contiguous()
+        self._expanded[key] = (t, t._version, e)
         return e
 
     def _ada_prepare(self, video: TransformerArgs, audio: TransformerArgs) -> None:

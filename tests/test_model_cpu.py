@@ -194,3 +194,15 @@ def test_adaln_table_sums_in_one_multi_tensor_add():
         for tab, a in (("prompt_scale_shift_table", video), ("audio_prompt_scale_shift_table", audio)):
             assert torch.equal(blk._ada_rows[(tab, id(a.prompt_timestep))],
                                blk.tables[tab][None, None] + a.prompt_timestep)
+    # a table replaced by another tensor, or changed in place, is expanded again
+    video, audio = args(VIDEO_22B.dim), args(AUDIO_22B.dim)
+    for change in ("replace", "in_place"):
+        if change == "replace":
+            blk.tables["scale_shift_table"] = torch.randn(9, VIDEO_22B.dim, generator=g)
+        else:
+            blk.tables["scale_shift_table"].add_(1.0)
+        blk._ada_rows = {}
+        blk._ada_prepare(video, audio)
+        got = blk._ada("scale_shift_table", video.timesteps, 0, 9)
+        ref = blk.tables["scale_shift_table"][None, None] + video.timesteps
+        assert all(torch.equal(got[i], ref[:, :, i]) for i in range(9)), change
