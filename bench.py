@@ -511,6 +511,21 @@ def _max_over_ranks(x: float, world: int, dev) -> float:
     return float(t.item())
 
 
+def exchange_ms(events: list) -> dict:
+    """Device ms per kind between each phase-0 and phase-1 event of
+    ``RowShard.wait_probe`` records ``(kind, phase, event)``: how long the
+    compute stream waited for a side-stream exchange ("wait") or ran one in
+    line ("sync")."""
+    out = {"wait": 0.0, "sync": 0.0}
+    if len(events) % 2:
+        raise ValueError("unpaired exchange probe events")
+    for (k0, p0, e0), (k1, p1, e1) in zip(events[0::2], events[1::2]):
+        if k0 != k1 or (p0, p1) != (0, 1):
+            raise ValueError(f"exchange probe events out of order: {(k0, p0)} then {(k1, p1)}")
+        out[k0] += e0.elapsed_time(e1)
+    return out
+
+
 def exchange_forms(world: int, self_attention: str = "auto", v2a: str = "auto") -> tuple[str, str]:
     """The row-sharded attention exchanges; "auto" picks by GPU count: at 2 GPUs
     the K/V all-gathers measured fastest (202.6 ms against 221.3 / 205.0), at 8
@@ -589,14 +604,7 @@ def run_step(args, world, rank, local, dev):
         xchg_events.append((kind, phase, e))
 
     def xchg_ms() -> dict:
-        """Device ms per kind between each phase-0 and phase-1 event: how long
-        the compute stream waited for a side-stream exchange ("wait") or ran
-        one in line ("sync")."""
-        out = {"wait": 0.0, "sync": 0.0}
-        for (k0, p0, e0), (k1, p1, e1) in zip(xchg_events[0::2], xchg_events[1::2]):
-            assert k0 == k1 and (p0, p1) == (0, 1)
-            out[k0] += e0.elapsed_time(e1)
-        return out
+        return exchange_ms(xchg_events)
 
     def step(v, a):
         for b in blocks:

@@ -91,3 +91,25 @@ def test_exchange_forms_by_gpu_count():
     assert bench.exchange_forms(8) == ("head_parallel", "split_keys")
     assert bench.exchange_forms(8, "gather", "gather") == ("gather", "gather")
     assert bench.exchange_forms(2, "head_parallel", "split_keys") == ("head_parallel", "split_keys")
+
+
+def test_exchange_ms_pairs_probe_events():
+    """bench.exchange_ms: the time between each phase-0 / phase-1 probe pair
+    is summed per kind; unpaired or out-of-order records raise."""
+    import bench
+
+    class Ev:
+        def __init__(self, t):
+            self.t = t
+
+        def elapsed_time(self, other):
+            return other.t - self.t
+
+    evs = [("wait", 0, Ev(1.0)), ("wait", 1, Ev(1.5)), ("sync", 0, Ev(2.0)), ("sync", 1, Ev(2.25)),
+           ("wait", 0, Ev(3.0)), ("wait", 1, Ev(3.0))]
+    assert bench.exchange_ms(evs) == {"wait": 0.5, "sync": 0.25}
+    assert bench.exchange_ms([]) == {"wait": 0.0, "sync": 0.0}
+    with pytest.raises(ValueError):
+        bench.exchange_ms(evs[:3])
+    with pytest.raises(ValueError):
+        bench.exchange_ms([("wait", 0, Ev(0.0)), ("sync", 1, Ev(1.0))])
